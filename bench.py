@@ -1,0 +1,425 @@
+#!/usr/bin/env python
+"""Headline benchmark: quantized decode matvec (batch 1) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step = one pass of the hot path over the config-2 sweep at batch 1: Q4_K and Q6_K weights of
+2048x11008, 11008x2048 and 151936x2048 ([n_out][n_in], N(0, 0.02) quantized by the package's
+quantizer; the 151936-row LM heads are filled from a pool of quantized Gaussian blocks), and an
+f32 N(0, 1) activation vector quantized on the device to Q8_K before each product. The metric
+is weight+activation bytes streamed per second (GB/s).
+
+  value  device-resident inputs (weights in the slab layout, activations in HBM), device time
+         with CUDA events on the launching stream; the step's working set (492 MB) exceeds the
+         126 MB L2, so every matrix is re-read from HBM.
+  e2e    the same products through the reference-facing C-ABI (op_matmul: host f32 activations
+         in pinned memory, host outputs), weights resident after sdy_weights_register (the
+         counterpart of the reference's mmap); includes the H2D copy of x and the D2H of y.
+  --impl reference  the reference's own CPU kernels (oracle/_ref/libsardyne_ref.so, built from
+         its sources) on all host threads, row ranges split as its thread pool does.
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own copy of the sweep (independent
+matrices, no collective on the data path): weak scaling, value = all ranks' bytes / max time.
+"""
+import argparse
+import concurrent.futures as cf
+import ctypes
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "Q4_K/Q6_K matvec HBM GB/s (% of 8 TB/s); decode tok/s Qwen3-30B-A3B-shape"
+SHAPES = [(2048, 11008), (11008, 2048), (151936, 2048)]  # [n_out][n_in]
+FORMATS = ["Q4_K", "Q6_K"]
+TYPE_ID = {"Q4_K": 12, "Q6_K": 14, "Q8_K": 15}
+BLOCK = {"Q4_K": (256, 144), "Q6_K": (256, 210)}
+WORKLOAD = ("BASELINE config 2 at batch 1: Q4_K and Q6_K matvec over 2048x11008, 11008x2048 and "
+            "151936x2048 ([n_out][n_in]), Q8_K activations quantized on the device each product")
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def weight_bytes(fmt, n_out, n_in):
+    qk, bb = BLOCK[fmt]
+    return n_out * (n_in // qk) * bb
+
+
+def alg_bytes(fmt, n_out, n_in):
+    """Algorithmic bytes of one matvec: weights + f32 x + f32 y."""
+    return weight_bytes(fmt, n_out, n_in) + 4 * n_in + 4 * n_out
+
+
+def make_inputs(seed=0):
+    from sardyne_b200 import kquant
+    rng = np.random.default_rng(seed)
+    mats = []
+    for fmt in FORMATS:
+        for n_out, n_in in SHAPES:
+            if n_out * n_in <= 32 * 1024 * 1024:
+                w = (rng.standard_normal((n_out, n_in)) * 0.02).astype(np.float32)
+                raw = kquant.quantize(w, fmt)
+            else:
+                raw = kquant.synth_tensor(fmt, n_out, n_in, rng)
+            mats.append((fmt, n_out, n_in, np.frombuffer(raw, np.uint8).reshape(n_out, -1).copy()))
+    xs = {n_in: np.random.default_rng(1).standard_normal(n_in).astype(np.float32) for _, n_in in SHAPES}
+    return mats, xs
+
+
+# ------------------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU's clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if not self.proc:
+            return
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        rows = []
+        for line in getattr(self, "lines", []):
+            p = [v.strip() for v in line.split(",")]
+            if len(p) < 8:
+                continue
+            try:
+                rows.append((float(p[0]), float(p[1]), p[4:8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------ reference CPU arm
+
+def cpu_sample(mats, lm_head_rows=18992):
+    """Bounded sample of the same workload for the CPU: every matrix, LM heads cut to their first
+    lm_head_rows rows (1/8)."""
+    return [(fmt, min(n_out, lm_head_rows) if n_out > 100000 else n_out, n_in, w) for fmt, n_out, n_in, w in mats]
+
+
+def reference_pass(ref, sample, xs, threads, pool):
+    """One pass of the reference's CPU path: op_quantize_rows once per input, then
+    op_matmul_q_rows over `threads` contiguous row ranges (csrc/model_llama.c:569-611)."""
+    xq = {}
+    for n_in, x in xs.items():
+        buf = np.zeros(n_in // 256 * 292, np.uint8)
+        ref.op_quantize_rows(TYPE_ID["Q8_K"], x.ctypes.data, buf.ctypes.data, n_in, 0, 1)
+        xq[n_in] = buf
+    for fmt, n_out, n_in, w in sample:
+        out = np.empty(n_out, np.float32)
+        cuts = [n_out * i // threads for i in range(threads + 1)]
+        futs = [pool.submit(ref.op_matmul_q_rows, out.ctypes.data, xq[n_in].ctypes.data, w.ctypes.data,
+                            TYPE_ID[fmt], 1, n_in, n_out, cuts[i], cuts[i + 1]) for i in range(threads)]
+        for f in futs:
+            f.result()
+
+
+def sample_bytes(sample):
+    return sum(alg_bytes(fmt, n_out, n_in) for fmt, n_out, n_in, _ in sample)
+
+
+def time_reference(mats, xs, min_seconds=3.0, threads=None):
+    import oracle
+    ref = oracle.ref()
+    ref.op_set_simd(1)
+    threads = threads or os.cpu_count() or 1
+    sample = cpu_sample(mats)
+    nbytes = sample_bytes(sample)
+    best, spent, n = float("inf"), 0.0, 0
+    with cf.ThreadPoolExecutor(threads) as pool:
+        reference_pass(ref, sample, xs, threads, pool)  # warm-up
+        while spent < min_seconds or n < 3:
+            t0 = time.perf_counter()
+            reference_pass(ref, sample, xs, threads, pool)
+            dt = time.perf_counter() - t0
+            best, spent, n = min(best, dt), spent + dt, n + 1
+    return {"value": round(nbytes / best / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+            "sample": f"reference AVX2 op_quantize_rows + op_matmul_q_rows on {threads} host threads, all six "
+                      f"matrices with the LM heads cut to their first 18992 rows ({nbytes / 1e6:.0f} MB per pass), "
+                      f"best of {n} passes ({spent:.1f} s)"}
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    import oracle
+    if not oracle.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libsardyne_ref.so was not built"}))
+        return 0
+    mats, xs = make_inputs()
+    ref = oracle.ref()
+    ref.op_set_simd(1)
+    threads = os.cpu_count() or 1
+    sample = cpu_sample(mats)
+    nbytes = sample_bytes(sample)
+    with cf.ThreadPoolExecutor(threads) as pool:
+        for _ in range(args.warmup):
+            reference_pass(ref, sample, xs, threads, pool)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            reference_pass(ref, sample, xs, threads, pool)
+        dt = time.perf_counter() - t0
+    value = nbytes * args.steps / dt / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": config(),
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                             "sample": f"each step: the six matrices with LM heads cut to 18992 rows "
+                                       f"({nbytes / 1e6:.0f} MB), reference AVX2 kernels on {threads} threads"},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def config():
+    return {"workload": WORKLOAD, "formats": FORMATS, "shapes_out_in": SHAPES, "batch": 1,
+            "l2": "inputs larger than L2: 492 MB of weights per step against a 126 MB L2",
+            "weights": "N(0,0.02), package quantizer; LM heads from a pool of quantized Gaussian blocks"}
+
+
+# ------------------------------------------------------------------------------ B200 arm
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if present."""
+    p = REPO / "profiles" / "qmv_q6k_lmhead_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("dram_bytes_per_launch")
+        except (ValueError, KeyError):
+            return None
+    return None
+
+
+def run_b200(args, rank, world, local_rank):
+    import torch
+    from sardyne_b200 import capi
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    lib = capi.lib()
+    mats, xs = make_inputs()
+    stream = torch.cuda.Stream(device=dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+
+    # device-resident inputs
+    handles, d_out, d_x, d_xq = [], {}, {}, {}
+    for fmt, n_out, n_in, w in mats:
+        h = lib.sdy_qmat_upload(w.ctypes.data, TYPE_ID[fmt], n_out, n_in)
+        if not h:
+            raise RuntimeError(capi.last_error())
+        handles.append(h)
+        d_out[(fmt, n_out, n_in)] = torch.empty(n_out, dtype=torch.float32, device=dev)
+    for n_in, x in xs.items():
+        d_x[n_in] = torch.from_numpy(x).to(dev)
+        d_xq[n_in] = torch.empty(lib.sdy_xq_bytes(TYPE_ID["Q8_K"], n_in, 1), dtype=torch.uint8, device=dev)
+    dominant = max(range(len(mats)), key=lambda i: alg_bytes(*mats[i][:3]))
+    step_bytes = sum(alg_bytes(fmt, n_out, n_in) for fmt, n_out, n_in, _ in mats)
+
+    def step(ev=None):
+        for i, (fmt, n_out, n_in, _) in enumerate(mats):
+            lib.sdy_quantize_rows_dev(TYPE_ID["Q8_K"], ctypes.c_void_p(d_x[n_in].data_ptr()), 1, n_in,
+                                      ctypes.c_void_p(d_xq[n_in].data_ptr()), sp)
+            if ev is not None and i == dominant:
+                ev[0].record(stream)
+            lib.sdy_qmatvec_dev(handles[i], ctypes.c_void_p(d_xq[n_in].data_ptr()), 1,
+                                ctypes.c_void_p(d_out[(fmt, n_out, n_in)].data_ptr()), n_out, 0, n_out, sp)
+            if ev is not None and i == dominant:
+                ev[1].record(stream)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.synchronize()
+    capi.check()
+
+    # per-matrix device time (informational breakdown, separate from the timed region)
+    per = []
+    for i, (fmt, n_out, n_in, _) in enumerate(mats):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 50
+        e0.record(stream)
+        for _ in range(reps):
+            for j, (f2, o2, i2, _) in enumerate(mats):  # interleave so this matrix is cold in L2 each time
+                if j == i:
+                    continue
+                lib.sdy_qmatvec_dev(handles[j], ctypes.c_void_p(d_xq[i2].data_ptr()), 1,
+                                    ctypes.c_void_p(d_out[(f2, o2, i2)].data_ptr()), o2, 0, o2, sp)
+        e1.record(stream)
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        for _ in range(reps):
+            for j, (f2, o2, i2, _) in enumerate(mats):
+                lib.sdy_qmatvec_dev(handles[j], ctypes.c_void_p(d_xq[i2].data_ptr()), 1,
+                                    ctypes.c_void_p(d_out[(f2, o2, i2)].data_ptr()), o2, 0, o2, sp)
+        e3.record(stream)
+        torch.cuda.synchronize()
+        ms = (e2.elapsed_time(e3) - e0.elapsed_time(e1)) / reps
+        per.append({"format": fmt, "n_out": n_out, "n_in": n_in, "us": round(ms * 1e3, 2),
+                    "GB/s": round(alg_bytes(fmt, n_out, n_in) / (ms * 1e-3) / 1e9, 1)})
+
+    # timed region
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = lib.sdy_kernel_launches()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for k in range(args.steps):
+                step(evs[k])
+            end.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    launches = lib.sdy_kernel_launches() - launches0
+    capi.check()
+    ms_total = start.elapsed_time(end)
+    t = torch.tensor([ms_total], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * step_bytes * args.steps / (ms_max * 1e-3) / 1e9
+    dom_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    fmt, n_out, n_in, _ = mats[dominant]
+    peak, peak_kind = load_peaks()
+    achieved = alg_bytes(fmt, n_out, n_in) / (dom_ms * 1e-3) / 1e9
+    traffic = load_traffic()
+
+    # e2e through the reference-facing C-ABI with host buffers
+    x_pin = {n_in: torch.from_numpy(x).pin_memory() for n_in, x in xs.items()}
+    y_pin = {(fmt, n_out, n_in): torch.empty(n_out, dtype=torch.float32).pin_memory() for fmt, n_out, n_in, _ in mats}
+    for fmt, n_out, n_in, w in mats:
+        if lib.sdy_weights_register(w.ctypes.data, TYPE_ID[fmt], n_out, n_in) != 0:
+            raise RuntimeError(capi.last_error())
+
+    def e2e_step():
+        for fmt, n_out, n_in, w in mats:
+            lib.op_matmul(ctypes.c_void_p(y_pin[(fmt, n_out, n_in)].data_ptr()), ctypes.c_void_p(x_pin[n_in].data_ptr()),
+                          w.ctypes.data, TYPE_ID[fmt], 1, n_in, n_out)
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    e2e_steps = max(10, args.steps // 4)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+    capi.check()
+    # the resident product through the C-ABI equals the device-resident one
+    for fmt, n_out, n_in, _ in mats:
+        assert torch.equal(y_pin[(fmt, n_out, n_in)], d_out[(fmt, n_out, n_in)].cpu()), "e2e/device mismatch"
+    e2e_value = world * step_bytes * e2e_steps / float(te.item()) / 1e9
+    for _, _, _, w in mats:
+        lib.sdy_weights_unregister(w.ctypes.data)
+    for h in handles:
+        lib.sdy_qmat_free(h)
+
+    if rank != 0:
+        return 0
+    line = {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config(),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": f"qmv {fmt} {n_out}x{n_in} batch 1", "peak_source": peak_kind,
+                         "algorithmic_bytes": alg_bytes(fmt, n_out, n_in), "launch_us": round(dom_ms * 1e3, 2)},
+            "e2e": {"value": round(e2e_value, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": sum(4 * n_in for _, _, n_in, _ in mats),
+                    "d2h_bytes_per_step": sum(4 * n_out for _, n_out, _, _ in mats),
+                    "steps": e2e_steps, "api": "op_matmul (C-ABI), weights resident via sdy_weights_register"},
+            "gpu_launches": int(launches), "clocks": clk.summary(),
+            "frac_of_8tbs": round(value / world / 8000.0, 4), "per_matrix": per}
+    if world == 1 and not args.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = time_reference(mats, xs)
+        except OSError as e:
+            line["cpu_baseline"] = {"value": None, "unavailable": str(e)}
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+    if world > 1:
+        import datetime
+        import torch
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    try:
+        return run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

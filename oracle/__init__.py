@@ -152,6 +152,10 @@ def ref() -> ctypes.CDLL:
             "engine_n_logits": (_i32, [_vp]),
             "engine_n_past": (_i32, [_vp]),
             "engine_last_error": (ctypes.c_char_p, [_vp]),
+            "engine_model_get_info": (None, [_vp, _vp]),
+            "engine_ctx_n_threads": (_i32, [_vp]),
+            "engine_reset": (None, [_vp]),
+            "engine_truncate": (_i, [_vp, _i32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)

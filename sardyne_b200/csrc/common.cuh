@@ -1,0 +1,139 @@
+// Shared definitions for the B200 quantized-weight path: ggml type ids, block geometry, the
+// device weight layout ("slabs"), the device activation layout ("XQ"), and error plumbing.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <string>
+
+namespace sdy {
+
+// ggml type ids as stored in GGUF (reference csrc/ops.h:21-22).
+enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14,
+             T_Q8_K = 15, T_BF16 = 30 };
+
+__host__ __device__ constexpr int block_elems(int t) {
+    return (t == T_Q4_K || t == T_Q6_K || t == T_Q8_K) ? 256
+         : (t == T_Q8_0 || t == T_Q4_0 || t == T_Q5_0) ? 32 : 1;
+}
+__host__ __device__ constexpr int block_bytes(int t) {
+    return t == T_Q8_0 ? 34 : t == T_Q4_0 ? 18 : t == T_Q5_0 ? 22 : t == T_Q4_K ? 144 : t == T_Q6_K ? 210
+         : t == T_Q8_K ? 292 : t == T_F32 ? 4 : (t == T_F16 || t == T_BF16) ? 2 : 0;
+}
+inline bool is_quant_weight(int t) {
+    return t == T_Q8_0 || t == T_Q4_0 || t == T_Q5_0 || t == T_Q4_K || t == T_Q6_K;
+}
+inline bool is_float_weight(int t) { return t == T_F32 || t == T_F16 || t == T_BF16; }
+// Activation type paired with a weight type (reference csrc/ops.c:249-255).
+inline int vec_dot_type(int t) {
+    return (t == T_Q4_K || t == T_Q6_K) ? T_Q8_K : (t == T_Q8_0 || t == T_Q4_0 || t == T_Q5_0) ? T_Q8_0 : T_F32;
+}
+inline size_t row_bytes(int t, int64_t n) {
+    int be = block_elems(t);
+    return be ? (size_t)(n / be) * block_bytes(t) : 0;
+}
+
+// ------------------------------------------------------------------------------------------
+// Device weight layout ("slabs").
+//
+// Rows are taken 8 at a time (a row group, padded with zero rows at the end). For row group g
+// and block b the 8 rows' bytes of block b form one slab of 8 * block_bytes bytes, stored at
+// (g * nb + b) * SLAB. Inside a slab every field of the block is a "plane": a 16-byte-wide
+// field is cut into 16-byte chunks and chunk c of row r sits at plane + c*128 + r*16, so the 8
+// lanes that read chunk c of 8 rows touch one contiguous 128-byte segment; narrow fields
+// (2-byte d, 4-byte qh) sit at plane + r*width. Byte totals equal the raw GGUF bytes (no
+// padding inside a slab), every plane starts 16-byte aligned, and the values are the raw
+// bytes rearranged, so dequantization stays bit-exact.
+//
+//   Q4_K (1152 B): hdr [d, dmin, scales[12]] 16 B/row @0 | qs 8 chunks @128
+//   Q6_K (1680 B): ql 8 chunks @0 | qh 4 chunks @1024 | scales 16 B/row @1536 | d 2 B/row @1664
+//   Q8_0 ( 272 B): qs 2 chunks @0 | d @256
+//   Q4_0 ( 144 B): qs 1 chunk  @0 | d @128
+//   Q5_0 ( 176 B): qs 1 chunk  @0 | qh 4 B/row @128 | d @160
+// ------------------------------------------------------------------------------------------
+constexpr int GROUP_ROWS = 8;
+__host__ __device__ constexpr int slab_bytes(int t) { return GROUP_ROWS * block_bytes(t); }
+
+// Device activation layout ("XQ"), for T tokens of n_in elements quantized to Q8_0 or Q8_K:
+//   qs    int8  [T][qrow], element e at (e/256)*272 + e%256 (16 zero bytes after every 256, so
+//         lanes reading different 256-element spans from shared memory hit different banks)
+//   d     f32   [T][nbx]   per-block scale (Q8_0: the f16-rounded scale, exactly as the dot uses it)
+//   bsum  int16 [T][nbx][16] (Q8_K: sums of each 16 quants)  |  int32 [T][nbx] (Q8_0: block sums)
+constexpr int XQ_SPAN = 272;
+__host__ __device__ inline int xq_qrow(int n_in) { return ((n_in + 255) / 256) * XQ_SPAN; }
+__host__ __device__ inline int xq_pos(int e) { return (e >> 8) * XQ_SPAN + (e & 255); }
+
+struct XQ {
+    int vtype = T_Q8_K;
+    int n_in = 0, n_tok = 0, qrow = 0, nbx = 0;
+    int8_t *qs = nullptr;
+    float *d = nullptr;
+    void *sums = nullptr;  // int16 [T][nbx][16] (Q8_K) or int32 [T][nbx] (Q8_0)
+};
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+// Bytes needed for an XQ of n_tok rows, and carving it out of a buffer.
+inline size_t xq_bytes(int vtype, int n_in, int n_tok) {
+    int nbx = n_in / block_elems(vtype);
+    size_t s = align_up((size_t)n_tok * xq_qrow(n_in), 256);
+    s += align_up((size_t)n_tok * nbx * 4, 256);
+    s += align_up((size_t)n_tok * nbx * (vtype == T_Q8_K ? 32 : 4), 256);
+    return s;
+}
+inline XQ xq_carve(void *base, int vtype, int n_in, int n_tok) {
+    XQ x;
+    x.vtype = vtype; x.n_in = n_in; x.n_tok = n_tok; x.qrow = xq_qrow(n_in); x.nbx = n_in / block_elems(vtype);
+    uint8_t *p = (uint8_t *)base;
+    x.qs = (int8_t *)p;
+    p += align_up((size_t)n_tok * x.qrow, 256);
+    x.d = (float *)p;
+    p += align_up((size_t)n_tok * x.nbx * 4, 256);
+    x.sums = p;
+    return x;
+}
+
+// A quantized weight matrix resident on the device in the slab layout.
+struct QMat {
+    const uint8_t *slabs = nullptr;
+    int type = 0;
+    int n_in = 0;
+    int nb = 0;            // blocks per row
+    int64_t n_rows = 0;    // logical rows (the layout holds ceil(n_rows/8) groups)
+    int64_t n_groups() const { return (n_rows + GROUP_ROWS - 1) / GROUP_ROWS; }
+    size_t bytes() const { return (size_t)n_groups() * nb * slab_bytes(type); }
+};
+
+// ------------------------------------------------------------------------------------------ errors
+void set_error(const char *fmt, ...);
+const char *last_error();
+void clear_error();
+bool cuda_check(cudaError_t e, const char *what, const char *file, int line);
+#define SDY_CUDA(call) ::sdy::cuda_check((call), #call, __FILE__, __LINE__)
+// After every kernel launch: count it and surface launch errors.
+void note_launch();
+#define SDY_LAUNCHED()                                   \
+    do {                                                 \
+        ::sdy::note_launch();                            \
+        SDY_CUDA(cudaGetLastError());                    \
+    } while (0)
+
+// ------------------------------------------------------------------------------------------ kernels
+// Launchers (sardyne_b200/csrc/*.cu). All are asynchronous on `s` and record errors with set_error.
+void repack_to_slabs(const uint8_t *raw, int type, int64_t n_rows, int n_in, uint8_t *slabs, cudaStream_t s);
+void dequant_rows(const QMat &w, const int32_t *row_ids, int n_ids, int64_t first_row, float *out, int64_t ldo,
+                  cudaStream_t s);
+void quantize_rows(int vtype, const float *x, int64_t ldx, int n_tok, int n_in, const XQ &xq, cudaStream_t s);
+void xq_import(int vtype, const uint8_t *raw, int n_tok, int n_in, const XQ &xq, cudaStream_t s);
+void xq_export(const XQ &xq, uint8_t *raw, cudaStream_t s);
+// out[t*ldo + (r - out_row0)] = W[r] . x[t] for rows r in [row0, row1) and tokens t < xq.n_tok.
+void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
+             cudaStream_t s);
+// MoE: for each slot s < n_slots, out[s*ldo_slot + r] = E[slot_expert[s]][r] . x[s / tok_div] for
+// r < rows_per_expert. `experts` holds n_expert matrices, each padded to gpe groups. The expert ids
+// are read on the device, so no host round trip sits between the router and the experts.
+void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq, int tok_div, const int32_t *slot_expert,
+                    int n_slots, int64_t rows_per_expert, float *out, int64_t ldo_slot, cudaStream_t s);
+
+}  // namespace sdy

@@ -1,0 +1,456 @@
+// Decode / small-batch quantized matvec: y[t][r] = W[r] . x[t] for 1..8 tokens.
+//
+// Replaces the reference's per-row dot products (reference csrc/quant.c:148-235,
+// csrc/quant_avx2.c:106-385) and their row dispatch (csrc/ops.c:293-309).
+//
+// Mapping. A CTA owns a contiguous range of 8-row groups and sweeps it in batches. Every lane
+// owns one (row, superblock) pair — for the 32-element formats one (row, run of 8 blocks) — and
+// computes that pair's integer sums entirely in registers with dp4a, so no cross-lane reduction
+// happens per block. Lanes r = 0..7 of a pair column read the same 16-byte chunk of 8 rows: one
+// 128-byte segment of the slab layout per 8 lanes, 4 segments per warp instruction. The token
+// activations (int8 + scales + sums) sit in shared memory and are read as broadcasts.
+//
+// Exactness. Each pair produces the reference's per-block fp32 term (q4k_combine / q6k_combine /
+// (float)s*(dw*dx), quant.h:84-91, quant.c:160) with explicit round-to-nearest intrinsics; the
+// terms go to shared memory and one thread per (token, row) adds them in block order. The
+// result is bit-identical to the reference's scalar kernels (and, for Q4_K/Q6_K, to its AVX2
+// kernels, which share the same combine).
+#include "common.cuh"
+
+#include <algorithm>
+#include <atomic>
+
+namespace sdy {
+
+namespace {
+
+constexpr int THREADS = 256;
+constexpr int TARGET_PAIRS = 512;  // pairs per batch: 2 per thread
+
+__device__ __forceinline__ uint4 ldg16(const uint8_t *p) { return __ldg((const uint4 *)p); }
+__device__ __forceinline__ uint32_t word(const uint4 &v, int k) {
+    return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
+}
+__device__ __forceinline__ float h2f(uint32_t h) { return __half2float(__ushort_as_half((uint16_t)h)); }
+// 4 bits -> bit 4 of each of 4 bytes (Q5_0's fifth bits).
+__device__ __forceinline__ uint32_t spread4(uint32_t x) { return ((x * 0x00204081u) & 0x01010101u) << 4; }
+
+struct Args {
+    const uint8_t *slabs;
+    int nb;             // blocks per row (of the weight type)
+    int64_t g_begin;    // first group of the whole launch
+    int64_t n_groups;   // groups in the launch
+    int G;              // groups per batch
+    const int8_t *xqs;  // XQ of the first token of this chunk
+    const float *xd;
+    const void *xsums;
+    int qrow;           // XQ row stride (bytes)
+    int nbx;            // XQ blocks per token
+    float *out;
+    int64_t ldo, row0, row1, out_row0;
+    // Gathered experts (MoE): grid.y = slot; slot s multiplies expert slot_expert[s], whose
+    // groups start at expert * gpe, with the activations of token s / tok_div, into out + s*ldo_slot.
+    const int32_t *slot_expert;
+    int64_t gpe, ldo_slot;
+    int tok_div, n_expert;
+};
+
+// Shared-memory carve-up, identical on host and device.
+struct Smem {
+    int q_off, d_off, s_off, t_off, total;
+};
+__host__ __device__ inline Smem smem_plan(int type, int NT, int qrow, int nb, int G) {
+    Smem m;
+    const bool kq = (type == T_Q4_K || type == T_Q6_K);
+    m.q_off = 0;
+    m.d_off = (NT * qrow + 15) & ~15;
+    m.s_off = m.d_off + ((NT * nb * 4 + 15) & ~15);
+    m.t_off = m.s_off + ((NT * nb * (kq ? 32 : 4) + 15) & ~15);
+    m.total = m.t_off + NT * nb * G * GROUP_ROWS * 4;
+    return m;
+}
+
+// ---------------------------------------------------------------------------- per-pair kernels
+// Each writes the block term of token t to terms[(t * nb + b) * rows + rl].
+
+template <int NT>
+__device__ __forceinline__ void pair_q4k(const uint8_t *slab, int r, int b, const uint8_t *sq, int qrow,
+                                         const float *sd, const int32_t *sbs, int nb, float *terms, int rows,
+                                         int rl) {
+    const uint4 hdr = ldg16(slab + r * 16);
+    uint4 q[8];
+#pragma unroll
+    for (int c = 0; c < 8; c++) q[c] = ldg16(slab + 128 + c * 128 + r * 16);
+    const float d = h2f(hdr.x & 0xFFFF), dmin = h2f(hdr.x >> 16);
+    // 6-bit scales and mins (quant.h:72-80), four per word.
+    const uint32_t sc0 = hdr.y & 0x3F3F3F3F, m0 = hdr.z & 0x3F3F3F3F;
+    const uint32_t sc1 = (hdr.w & 0x0F0F0F0F) | ((hdr.y >> 2) & 0x30303030);
+    const uint32_t m1 = ((hdr.w >> 4) & 0x0F0F0F0F) | ((hdr.z >> 2) & 0x30303030);
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+        const int *y = (const int *)(sq + t * qrow + b * XQ_SPAN);
+        int isum = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {  // 64 elements: low nibbles -> sub-block 2j, high -> 2j+1
+            int slo = 0, shi = 0;
+#pragma unroll
+            for (int w = 0; w < 8; w++) {
+                uint32_t qw = word(q[2 * j + (w >> 2)], w & 3);
+                slo = __dp4a((int)(qw & 0x0F0F0F0F), y[16 * j + w], slo);
+                shi = __dp4a((int)((qw >> 4) & 0x0F0F0F0F), y[16 * j + 8 + w], shi);
+            }
+            const uint32_t scw = j < 2 ? sc0 : sc1;
+            const int s_lo = (scw >> (16 * (j & 1))) & 0xFF, s_hi = (scw >> (16 * (j & 1) + 8)) & 0xFF;
+            isum += s_lo * slo + s_hi * shi;
+        }
+        // Mins: msum = sum_j m_j * (bsum[2j] + bsum[2j+1]); one bsum pair per int32 word.
+        const int32_t *bw = sbs + (t * nb + b) * 8;
+        int msum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const uint32_t mw = j < 4 ? m0 : m1;
+            msum = __dp2a_lo(bw[j], (int)__byte_perm(mw, 0, (j & 3) * 0x11), msum);
+        }
+        const float yd = sd[t * nb + b];
+        const float dall = __fmul_rn(yd, d), dmn = __fmul_rn(yd, dmin);
+        terms[(t * nb + b) * rows + rl] =
+            __fsub_rn(__fmul_rn(dall, __int2float_rn(isum)), __fmul_rn(dmn, __int2float_rn(msum)));
+    }
+}
+
+template <int NT>
+__device__ __forceinline__ void pair_q6k(const uint8_t *slab, int r, int b, const uint8_t *sq, int qrow,
+                                         const float *sd, const int32_t *sbs, int nb, float *terms, int rows,
+                                         int rl) {
+    uint4 ql[8], qh[4];
+#pragma unroll
+    for (int c = 0; c < 8; c++) ql[c] = ldg16(slab + c * 128 + r * 16);
+#pragma unroll
+    for (int c = 0; c < 4; c++) qh[c] = ldg16(slab + 1024 + c * 128 + r * 16);
+    const uint4 scv = ldg16(slab + 1536 + r * 16);
+    const float d = h2f(*(const uint16_t *)(slab + 1664 + r * 2));
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+        const int *y = (const int *)(sq + t * qrow + b * XQ_SPAN);
+        int s[16];
+#pragma unroll
+        for (int g = 0; g < 16; g++) s[g] = 0;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+#pragma unroll
+            for (int w = 0; w < 8; w++) {
+                const uint32_t QL0 = word(ql[4 * h + (w >> 2)], w & 3);
+                const uint32_t QL1 = word(ql[4 * h + 2 + (w >> 2)], w & 3);
+                const uint32_t QH = word(qh[2 * h + (w >> 2)], w & 3);
+                // unsigned 6-bit values of elements 128h + 32k + 4w .. +3 (quant.c:62-74)
+                const uint32_t v0 = (QL0 & 0x0F0F0F0F) | ((QH << 4) & 0x30303030);
+                const uint32_t v1 = (QL1 & 0x0F0F0F0F) | ((QH << 2) & 0x30303030);
+                const uint32_t v2 = ((QL0 >> 4) & 0x0F0F0F0F) | (QH & 0x30303030);
+                const uint32_t v3 = ((QL1 >> 4) & 0x0F0F0F0F) | ((QH >> 2) & 0x30303030);
+                const int gw = w >> 2;
+                s[8 * h + 0 + gw] = __dp4a((int)v0, y[32 * h + 0 + w], s[8 * h + 0 + gw]);
+                s[8 * h + 2 + gw] = __dp4a((int)v1, y[32 * h + 8 + w], s[8 * h + 2 + gw]);
+                s[8 * h + 4 + gw] = __dp4a((int)v2, y[32 * h + 16 + w], s[8 * h + 4 + gw]);
+                s[8 * h + 6 + gw] = __dp4a((int)v3, y[32 * h + 24 + w], s[8 * h + 6 + gw]);
+            }
+        }
+        // isum = sum_g sc_g * (sum q*y - 32 * bsum_g): exact, as the reference's AVX2 path.
+        int isum = 0;
+#pragma unroll
+        for (int g = 0; g < 16; g++) isum += (int)(int8_t)(word(scv, g >> 2) >> (8 * (g & 3))) * s[g];
+        const int32_t *bw = sbs + (t * nb + b) * 8;
+        int corr = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            corr = (i & 1) ? __dp2a_hi(bw[i], (int)word(scv, i >> 1), corr) : __dp2a_lo(bw[i], (int)word(scv, i >> 1), corr);
+        isum -= 32 * corr;
+        const float yd = sd[t * nb + b];
+        terms[(t * nb + b) * rows + rl] = __fmul_rn(__fmul_rn(yd, d), __int2float_rn(isum));
+    }
+}
+
+// 32-element formats: one lane handles blocks b0 .. b0+7 (clipped to nb) of one row.
+template <int TYPE, int NT>
+__device__ __forceinline__ void pair_q0(const uint8_t *slabs_g, int r, int b0, const uint8_t *sq, int qrow,
+                                        const float *sd, const int32_t *ssum, int nb, float *terms, int rows,
+                                        int rl) {
+    constexpr int SB = slab_bytes(TYPE);
+    const int nblk = min(8, nb - b0);
+#pragma unroll 2
+    for (int i = 0; i < nblk; i++) {
+        const int b = b0 + i;
+        const uint8_t *slab = slabs_g + (size_t)b * SB;
+        uint4 qa, qb;
+        uint32_t qh = 0, dbits;
+        qa = ldg16(slab + r * 16);
+        if (TYPE == T_Q8_0) {
+            qb = ldg16(slab + 128 + r * 16);
+            dbits = *(const uint16_t *)(slab + 256 + r * 2);
+        } else if (TYPE == T_Q4_0) {
+            dbits = *(const uint16_t *)(slab + 128 + r * 2);
+        } else {
+            qh = __ldg((const uint32_t *)(slab + 128 + r * 4));
+            dbits = *(const uint16_t *)(slab + 160 + r * 2);
+        }
+        const float dw = h2f(dbits);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const int *y = (const int *)(sq + t * qrow + xq_pos(32 * b));
+            int s = 0;
+            if (TYPE == T_Q8_0) {
+#pragma unroll
+                for (int k = 0; k < 4; k++) s = __dp4a((int)word(qa, k), y[k], s);
+#pragma unroll
+                for (int k = 0; k < 4; k++) s = __dp4a((int)word(qb, k), y[4 + k], s);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    uint32_t lo = word(qa, k) & 0x0F0F0F0F, hi = (word(qa, k) >> 4) & 0x0F0F0F0F;
+                    if (TYPE == T_Q5_0) {
+                        lo |= spread4((qh >> (4 * k)) & 15);
+                        hi |= spread4((qh >> (16 + 4 * k)) & 15);
+                    }
+                    s = __dp4a((int)lo, y[k], s);
+                    s = __dp4a((int)hi, y[4 + k], s);
+                }
+                s -= (TYPE == T_Q4_0 ? 8 : 16) * ssum[t * nb + b];  // sum (u - bias) y
+            }
+            // (float)s * (dw * dx), quant.c:160
+            terms[(t * nb + b) * rows + rl] = __fmul_rn(__int2float_rn(s), __fmul_rn(dw, sd[t * nb + b]));
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------- the kernel
+
+template <int TYPE, int NT>
+__global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    constexpr bool KQ = (TYPE == T_Q4_K || TYPE == T_Q6_K);
+    constexpr int SB = slab_bytes(TYPE);
+    const Smem plan = smem_plan(TYPE, NT, a.qrow, a.nb, a.G);
+    uint8_t *sq = smem + plan.q_off;
+    float *sd = (float *)(smem + plan.d_off);
+    int32_t *ss = (int32_t *)(smem + plan.s_off);
+    float *terms = (float *)(smem + plan.t_off);
+    const int tid = threadIdx.x;
+    const int nb = a.nb;
+    const uint8_t *slabs = a.slabs;
+    const int8_t *xqs = a.xqs;
+    const float *xd = a.xd;
+    const int32_t *xsums = (const int32_t *)a.xsums;
+    float *out = a.out;
+    if (a.slot_expert) {
+        const int slot = blockIdx.y, e = a.slot_expert[slot];
+        if (e < 0 || e >= a.n_expert) return;
+        const int tok = slot / a.tok_div;
+        slabs += (size_t)e * a.gpe * nb * SB;
+        xqs += (size_t)tok * a.qrow;
+        xd += (size_t)tok * a.nbx;
+        xsums += (size_t)tok * a.nbx * (KQ ? 8 : 1);
+        out += (size_t)slot * a.ldo_slot;
+    }
+
+    // Stage the activations of NT tokens (broadcast operands for every pair).
+    {
+        const int qv = NT * a.qrow / 16;
+        for (int i = tid; i < qv; i += THREADS) {
+            int t = i / (a.qrow / 16), k = i % (a.qrow / 16);
+            ((uint4 *)sq)[i] = __ldg((const uint4 *)(xqs + (size_t)t * a.qrow) + k);
+        }
+        for (int i = tid; i < NT * nb; i += THREADS) {
+            int t = i / nb, b = i % nb;
+            sd[i] = xd[(size_t)t * a.nbx + b];
+        }
+        const int per = KQ ? 8 : 1;  // int32 words per block: 8 bsum pairs, or one block sum
+        for (int i = tid; i < NT * nb * per; i += THREADS) {
+            int t = i / (nb * per), k = i % (nb * per);
+            ss[i] = xsums[(size_t)t * a.nbx * per + k];
+        }
+    }
+    __syncthreads();
+
+    // This CTA's contiguous share of the launch's groups.
+    const int64_t gA = a.g_begin + a.n_groups * blockIdx.x / gridDim.x;
+    const int64_t gB = a.g_begin + a.n_groups * (blockIdx.x + 1) / gridDim.x;
+    const int units = KQ ? nb : (nb + 7) / 8;  // pair columns per row
+    for (int64_t gb = gA; gb < gB; gb += a.G) {
+        const int G = (int)((gB - gb) < a.G ? (gB - gb) : a.G);
+        const int rows = G * GROUP_ROWS;
+        const int npairs = rows * units;
+        for (int p = tid; p < npairs; p += THREADS) {
+            const int gl = p / (GROUP_ROWS * units);
+            const int rem = p - gl * GROUP_ROWS * units;
+            const int u = rem >> 3, r = rem & 7;
+            const int rl = gl * GROUP_ROWS + r;
+            const uint8_t *gslabs = slabs + (size_t)(gb + gl) * nb * SB;
+            if (TYPE == T_Q4_K)
+                pair_q4k<NT>(gslabs + (size_t)u * SB, r, u, sq, a.qrow, sd, ss, nb, terms, rows, rl);
+            else if (TYPE == T_Q6_K)
+                pair_q6k<NT>(gslabs + (size_t)u * SB, r, u, sq, a.qrow, sd, ss, nb, terms, rows, rl);
+            else
+                pair_q0<TYPE, NT>(gslabs, r, u * 8, sq, a.qrow, sd, ss, nb, terms, rows, rl);
+        }
+        __syncthreads();
+        // Ordered combine: the reference adds block terms left to right (acc = acc + term).
+        for (int i = tid; i < NT * rows; i += THREADS) {
+            const int t = i / rows, rl = i % rows;
+            const int64_t row = gb * GROUP_ROWS + rl;
+            if (row < a.row0 || row >= a.row1) continue;
+            const float *tp = terms + (size_t)t * nb * rows + rl;
+            float acc = 0.0f;
+            for (int b = 0; b < nb; b++) acc = __fadd_rn(acc, tp[(size_t)b * rows]);
+            out[(size_t)t * a.ldo + (row - a.out_row0)] = acc;
+        }
+        __syncthreads();
+    }
+}
+
+template <int TYPE, int NT>
+void launch_one(const Args &a, int smem, dim3 grid, cudaStream_t s) {
+    static std::atomic<uint64_t> configured{0};  // one attribute call per instantiation and device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(configured.load() & bit)) {
+        SDY_CUDA(cudaFuncSetAttribute(qmv_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        configured.fetch_or(bit);
+    }
+    qmv_kernel<TYPE, NT><<<grid, THREADS, smem, s>>>(a);
+}
+
+template <int TYPE>
+void launch_nt(int nt, const Args &a, int smem, dim3 grid, cudaStream_t s) {
+    switch (nt) {
+    case 1: launch_one<TYPE, 1>(a, smem, grid, s); break;
+    case 2: launch_one<TYPE, 2>(a, smem, grid, s); break;
+    case 3: launch_one<TYPE, 3>(a, smem, grid, s); break;
+    case 4: launch_one<TYPE, 4>(a, smem, grid, s); break;
+    default: launch_one<TYPE, 8>(a, smem, grid, s); break;
+    }
+}
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+void dispatch(int type, int nt, const Args &a, int smem, dim3 grid, cudaStream_t s) {
+    switch (type) {
+    case T_Q4_K: launch_nt<T_Q4_K>(nt, a, smem, grid, s); break;
+    case T_Q6_K: launch_nt<T_Q6_K>(nt, a, smem, grid, s); break;
+    case T_Q8_0: launch_nt<T_Q8_0>(nt, a, smem, grid, s); break;
+    case T_Q4_0: launch_nt<T_Q4_0>(nt, a, smem, grid, s); break;
+    case T_Q5_0: launch_nt<T_Q5_0>(nt, a, smem, grid, s); break;
+    default: set_error("qmatvec: unsupported weight type %d", type); return;
+    }
+    SDY_LAUNCHED();
+}
+
+int batch_groups(int type, int nb) {
+    const bool kq = (type == T_Q4_K || type == T_Q6_K);
+    const int per_group = GROUP_ROWS * (kq ? nb : (nb + 7) / 8);
+    return std::max(1, (TARGET_PAIRS + per_group - 1) / per_group);
+}
+
+}  // namespace
+
+void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
+             cudaStream_t s) {
+    if (row1 <= row0 || xq.n_tok <= 0) return;
+    if (xq.vtype != vec_dot_type(w.type) || xq.n_in != w.n_in) {
+        set_error("qmatvec: activation type/size does not match the weights");
+        return;
+    }
+    const bool kq = (w.type == T_Q4_K || w.type == T_Q6_K);
+    const int64_t g0 = row0 / GROUP_ROWS, g1 = (row1 + GROUP_ROWS - 1) / GROUP_ROWS;
+    const int64_t ng = g1 - g0;
+    const int limit = 200 * 1024;
+    for (int t0 = 0; t0 < xq.n_tok;) {
+        int rem = xq.n_tok - t0;
+        int nt = rem >= 8 ? 8 : rem >= 4 ? 4 : rem;
+        int G = batch_groups(w.type, w.nb);
+        // Shrink the batch, then the token chunk, until shared memory fits.
+        while (smem_plan(w.type, nt, xq.qrow, w.nb, G).total > limit && G > 1) G = (G + 1) / 2;
+        while (smem_plan(w.type, nt, xq.qrow, w.nb, G).total > limit && nt > 1) nt = nt >= 8 ? 4 : nt == 4 ? 3 : nt - 1;
+        Smem plan = smem_plan(w.type, nt, xq.qrow, w.nb, G);
+        if (plan.total > limit) {
+            set_error("qmatvec: row of %d elements too long for one CTA", w.n_in);
+            return;
+        }
+        Args a{};
+        a.slabs = w.slabs;
+        a.nb = w.nb;
+        a.g_begin = g0;
+        a.n_groups = ng;
+        a.G = G;
+        a.xqs = xq.qs + (size_t)t0 * xq.qrow;
+        a.xd = xq.d + (size_t)t0 * xq.nbx;
+        a.xsums = (const uint8_t *)xq.sums + (size_t)t0 * xq.nbx * (kq ? 32 : 4);
+        a.qrow = xq.qrow;
+        a.nbx = xq.nbx;
+        a.out = out + (size_t)t0 * ldo;
+        a.ldo = ldo;
+        a.row0 = row0;
+        a.row1 = row1;
+        a.out_row0 = out_row0;
+        // Enough CTAs for two per SM, never more than one per group.
+        int grid = (int)std::min<int64_t>(ng, (int64_t)sm_count() * 2);
+        dispatch(w.type, nt, a, plan.total, dim3(grid), s);
+        t0 += nt;
+    }
+}
+
+}  // namespace sdy
+
+namespace sdy {
+
+void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq, int tok_div, const int32_t *slot_expert,
+                    int n_slots, int64_t rows_per_expert, float *out, int64_t ldo_slot, cudaStream_t s) {
+    if (n_slots <= 0) return;
+    if (xq.vtype != vec_dot_type(experts.type) || xq.n_in != experts.n_in) {
+        set_error("qmatvec_gather: activation type/size does not match the weights");
+        return;
+    }
+    const bool kq = (experts.type == T_Q4_K || experts.type == T_Q6_K);
+    int G = batch_groups(experts.type, experts.nb);
+    const int limit = 200 * 1024;
+    while (smem_plan(experts.type, 1, xq.qrow, experts.nb, G).total > limit && G > 1) G = (G + 1) / 2;
+    Smem plan = smem_plan(experts.type, 1, xq.qrow, experts.nb, G);
+    if (plan.total > limit) {
+        set_error("qmatvec_gather: row of %d elements too long for one CTA", experts.n_in);
+        return;
+    }
+    Args a{};
+    a.slabs = experts.slabs;
+    a.nb = experts.nb;
+    a.g_begin = 0;
+    a.n_groups = gpe;
+    a.G = G;
+    a.xqs = xq.qs;
+    a.xd = xq.d;
+    a.xsums = xq.sums;
+    a.qrow = xq.qrow;
+    a.nbx = xq.nbx;
+    a.out = out;
+    a.ldo = 0;
+    a.row0 = 0;
+    a.row1 = rows_per_expert;
+    a.out_row0 = 0;
+    a.slot_expert = slot_expert;
+    a.gpe = gpe;
+    a.ldo_slot = ldo_slot;
+    a.tok_div = tok_div;
+    a.n_expert = n_expert;
+    (void)kq;
+    int per_slot = (int)std::max<int64_t>(1, std::min<int64_t>(gpe, ((int64_t)sm_count() * 2 + n_slots - 1) / n_slots));
+    dispatch(experts.type, 1, a, plan.total, dim3(per_slot, n_slots), s);
+}
+
+}  // namespace sdy

@@ -1,0 +1,112 @@
+"""Minimal GGUF v3 writer for synthetic models (metadata, float and pre-quantized tensors).
+
+Layout (GGUF v3, little-endian): "GGUF", u32 version, u64 n_tensors, u64 n_kv; the key/value
+pairs (string key, u32 value type, value); the tensor infos (string name, u32 n_dims, u64 ne[],
+u32 ggml type, u64 offset); zero padding to the alignment; then each tensor's bytes at its
+aligned offset. The file is written to a temporary name and renamed, so a reader that already
+mapped an older file keeps seeing it intact.
+"""
+import os
+import pathlib
+import struct
+
+import numpy as np
+
+# value types
+U8, I8, U16, I16, U32, I32, F32, BOOL, STRING, ARRAY, U64, I64, F64 = range(13)
+GGML_TYPES = {"F32": 0, "F16": 1, "Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q8_0": 8, "Q4_K": 12, "Q6_K": 14, "BF16": 30}
+_BLOCK = {"F32": (1, 4), "F16": (1, 2), "BF16": (1, 2), "Q4_0": (32, 18), "Q4_1": (32, 20), "Q5_0": (32, 22),
+          "Q8_0": (32, 34), "Q4_K": (256, 144), "Q6_K": (256, 210)}
+_SCALAR_FMT = {U8: "<B", I8: "<b", U16: "<H", I16: "<h", U32: "<I", I32: "<i", F32: "<f", BOOL: "<?",
+               U64: "<Q", I64: "<q", F64: "<d"}
+
+
+def _str(s) -> bytes:
+    b = s.encode() if isinstance(s, str) else bytes(s)
+    return struct.pack("<Q", len(b)) + b
+
+
+def f32_to_bf16(x: np.ndarray) -> np.ndarray:
+    """Round to nearest even bf16 bit patterns (uint16)."""
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    rounded = (b + 0x7FFF + ((b >> 16) & 1)) >> 16
+    nan = np.isnan(np.asarray(x, np.float32))
+    out = rounded.astype(np.uint16)
+    out[nan] = 0x7FC0
+    return out
+
+
+class GGUFWriter:
+    def __init__(self, path, alignment: int = 32):
+        self.path = pathlib.Path(path)
+        self.alignment = alignment
+        self.kv = []        # (key, type, payload bytes)
+        self.tensors = []   # (name, ne, type name, bytes)
+
+    def add(self, key: str, value, vtype: int | None = None, arr_type: int | None = None):
+        if vtype is None:
+            if isinstance(value, bool):
+                vtype = BOOL
+            elif isinstance(value, int):
+                vtype = U32 if 0 <= value < 2 ** 32 else I64
+            elif isinstance(value, float):
+                vtype = F32
+            elif isinstance(value, str):
+                vtype = STRING
+            elif isinstance(value, (list, tuple)):
+                vtype = ARRAY
+            else:
+                raise TypeError(f"{key}: unsupported value {type(value)}")
+        if vtype == STRING:
+            payload = _str(value)
+        elif vtype == ARRAY:
+            if arr_type is None:
+                arr_type = STRING if value and isinstance(value[0], str) else (F32 if value and isinstance(value[0], float) else I32)
+            body = b"".join(_str(v) for v in value) if arr_type == STRING else \
+                b"".join(struct.pack(_SCALAR_FMT[arr_type], v) for v in value)
+            payload = struct.pack("<IQ", arr_type, len(value)) + body
+        else:
+            payload = struct.pack(_SCALAR_FMT[vtype], value)
+        self.kv.append((key, vtype, payload))
+
+    def add_tensor(self, name: str, data: np.ndarray, kind: str = "F32"):
+        """Float tensor; data shape [..., n_in] (row-major, as PyTorch): ne = reversed shape."""
+        data = np.asarray(data)
+        if kind == "F32":
+            raw = np.ascontiguousarray(data, np.float32).tobytes()
+        elif kind == "F16":
+            raw = np.ascontiguousarray(data, np.float16).tobytes()
+        elif kind == "BF16":
+            raw = (data if data.dtype == np.uint16 else f32_to_bf16(data)).tobytes()
+        else:
+            raise ValueError(f"{kind}: use add_raw_tensor for quantized data")
+        self.tensors.append((name, tuple(reversed(data.shape)), kind, raw))
+
+    def add_raw_tensor(self, name: str, ne, kind: str, raw: bytes):
+        block, size = _BLOCK[kind]
+        n = int(np.prod(ne))
+        if ne[0] % block or len(raw) != n // block * size:
+            raise ValueError(f"{name}: {len(raw)} bytes do not match {kind} {tuple(ne)}")
+        self.tensors.append((name, tuple(int(v) for v in ne), kind, bytes(raw)))
+
+    def write(self):
+        head = b"GGUF" + struct.pack("<IQQ", 3, len(self.tensors), len(self.kv))
+        for key, vtype, payload in self.kv:
+            head += _str(key) + struct.pack("<I", vtype) + payload
+        offsets, off = [], 0
+        for _, _, _, raw in self.tensors:
+            offsets.append(off)
+            off += len(raw)
+            off += -off % self.alignment
+        for (name, ne, kind, _), o in zip(self.tensors, offsets):
+            head += _str(name) + struct.pack("<I", len(ne)) + struct.pack(f"<{len(ne)}Q", *ne)
+            head += struct.pack("<IQ", GGML_TYPES[kind], o)
+        head += b"\0" * (-len(head) % self.alignment)
+        tmp = self.path.with_name(self.path.name + ".tmp")
+        with open(tmp, "wb") as f:
+            f.write(head)
+            for (_, _, _, raw), o in zip(self.tensors, offsets):
+                f.write(raw)
+                f.write(b"\0" * (-len(raw) % self.alignment))
+        os.replace(tmp, self.path)
+        return self.path

@@ -1,0 +1,127 @@
+"""The GGUF reader (host code, no GPU) against files made by the package's writer."""
+import ctypes
+import struct
+
+import numpy as np
+import pytest
+
+from sardyne_b200 import capi
+from sardyne_b200.gguf_writer import GGUFWriter
+
+
+def open_gguf(path):
+    err = ctypes.create_string_buffer(256)
+    h = capi.lib().gguf_open(str(path).encode(), err, len(err))
+    return h, err.value.decode()
+
+
+def test_roundtrip(tmp_path):
+    w = GGUFWriter(tmp_path / "a.gguf")
+    w.add("general.architecture", "llama")
+    w.add("llama.block_count", 3)
+    w.add("llama.rope.freq_base", 10000.0)
+    w.add("tokenizer.ggml.tokens", ["a", "bé", ""])
+    x = np.arange(64, dtype=np.float32).reshape(2, 32)
+    w.add_tensor("t.weight", x)
+    w.add_raw_tensor("q.weight", (32, 2), "Q8_0", bytes(range(68)))
+    w.write()
+    lib = capi.lib()
+    h, err = open_gguf(w.path)
+    assert h, err
+    try:
+        assert lib.gguf_version(h) == 3 and lib.gguf_n_kv(h) == 4 and lib.gguf_n_tensors(h) == 2
+        i = lib.gguf_find_kv(h, b"llama.block_count")
+        v = ctypes.c_uint64()
+        assert lib.gguf_kv_get_u64(h, i, ctypes.byref(v)) == 0 and v.value == 3
+        f = ctypes.c_double()
+        assert lib.gguf_kv_get_f64(h, lib.gguf_find_kv(h, b"llama.rope.freq_base"), ctypes.byref(f)) == 0
+        assert f.value == 10000.0
+        n = ctypes.c_uint64()
+        p = lib.gguf_kv_get_str(h, lib.gguf_find_kv(h, b"general.architecture"), ctypes.byref(n))
+        assert ctypes.string_at(p, n.value) == b"llama"
+        k = lib.gguf_find_kv(h, b"tokenizer.ggml.tokens")
+        got = [ctypes.string_at(lib.gguf_kv_get_arr_str(h, k, j, ctypes.byref(n)), n.value).decode() for j in range(3)]
+        assert got == ["a", "bé", ""]
+        assert not lib.gguf_kv_get_arr_str(h, k, 3, ctypes.byref(n))
+        assert lib.gguf_kv_get_u64(h, lib.gguf_find_kv(h, b"general.architecture"), ctypes.byref(v)) != 0
+        t = lib.gguf_get_tensor(h, lib.gguf_find_tensor(h, b"t.weight")).contents
+        assert (t.n_dims, tuple(t.ne[:2]), t.type, t.nbytes) == (2, (32, 2), 0, 256)
+        assert np.array_equal(np.frombuffer(ctypes.string_at(t.data, t.nbytes), np.float32).reshape(2, 32), x)
+        t = lib.gguf_get_tensor(h, lib.gguf_find_tensor(h, b"q.weight")).contents
+        assert t.offset % 32 == 0 and ctypes.string_at(t.data, t.nbytes) == bytes(range(68))
+        assert lib.gguf_type_name(14) == b"Q6_K" and lib.gguf_type_name(4) is None
+        assert lib.gguf_find_tensor(h, b"nope") == -1
+    finally:
+        lib.gguf_close(h)
+
+
+def _raw(path, kvs=(), tensors=(), version=3):
+    def s(b):
+        return struct.pack("<Q", len(b)) + b
+    out = b"GGUF" + struct.pack("<IQQ", version, len(tensors), len(kvs))
+    for k, t, v in kvs:
+        out += s(k) + struct.pack("<I", t) + v
+    for n, ne, t, off in tensors:
+        out += s(n) + struct.pack("<I", len(ne)) + struct.pack(f"<{len(ne)}Q", *ne) + struct.pack("<IQ", t, off)
+    out += b"\0" * (-len(out) % 32)
+    path.write_bytes(out + b"\0" * 64 * max(1, len(tensors)))
+    return path
+
+
+@pytest.mark.parametrize("case,msg", [
+    ("valid", None), ("nul_key", "UTF-8"), ("dup_key", "duplicato"), ("bad_utf8", "UTF-8"),
+    ("overlong", "UTF-8"), ("surrogate", "UTF-8"), ("dup_tensor", "duplicato"), ("nul_name", "UTF-8"),
+    ("zero_dim", "nulla"), ("big_endian", "big-endian"), ("bad_type", "sconosciuto"), ("bad_align", "alignment"),
+    ("past_end", "oltre la fine"), ("unaligned", "allineato"), ("bad_block", "multiplo")])
+def test_rejections(tmp_path, case, msg):
+    U32 = 4
+    kv = [(b"general.architecture", 8, struct.pack("<Q", 4) + b"test")]
+    t = [(b"a", (4,), 0, 0)]
+    if case == "nul_key":
+        kv.append((b"k\0x", U32, struct.pack("<I", 1)))
+    elif case == "dup_key":
+        kv += [(b"k", U32, struct.pack("<I", 1)), (b"k", U32, struct.pack("<I", 2))]
+    elif case == "bad_utf8":
+        kv.append((b"caf\xe9", U32, struct.pack("<I", 1)))
+    elif case == "overlong":
+        kv.append((b"\xc0\xaf", U32, struct.pack("<I", 1)))
+    elif case == "surrogate":
+        kv.append((b"\xed\xa0\x80", U32, struct.pack("<I", 1)))
+    elif case == "dup_tensor":
+        t.append((b"a", (4,), 0, 32))
+    elif case == "nul_name":
+        t = [(b"a\0b", (4,), 0, 0)]
+    elif case == "zero_dim":
+        t = [(b"a", (4, 0), 0, 0)]
+    elif case == "bad_type":
+        t = [(b"a", (4,), 4, 0)]
+    elif case == "bad_align":
+        kv.append((b"general.alignment", U32, struct.pack("<I", 48)))
+    elif case == "past_end":
+        t = [(b"a", (4096,), 0, 0)]
+    elif case == "unaligned":
+        t = [(b"a", (4,), 0, 8)]
+    elif case == "bad_block":
+        t = [(b"a", (16,), 8, 0)]
+    path = _raw(tmp_path / f"{case}.gguf", kv, t, version=0x03000000 if case == "big_endian" else 3)
+    h, err = open_gguf(path)
+    if msg is None:
+        assert h, err
+        capi.lib().gguf_close(h)
+    else:
+        assert not h and msg in err
+
+
+def test_missing_and_truncated(tmp_path):
+    h, err = open_gguf(tmp_path / "missing.gguf")
+    assert not h and "impossibile aprire" in err
+    w = GGUFWriter(tmp_path / "a.gguf")
+    w.add("general.architecture", "llama")
+    w.add_tensor("t.weight", np.ones((4, 32), np.float32))
+    w.write()
+    data = w.path.read_bytes()
+    for cut in (3, 20, 60, len(data) - 8):
+        p = tmp_path / f"cut{cut}.gguf"
+        p.write_bytes(data[:cut])
+        h, err = open_gguf(p)
+        assert not h and err
