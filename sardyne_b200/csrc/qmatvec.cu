@@ -25,7 +25,9 @@ namespace sdy {
 namespace {
 
 constexpr int THREADS = 256;
-constexpr int TARGET_PAIRS = 512;  // pairs per batch: 2 per thread
+constexpr int CTAS_PER_SM = 4;
+constexpr int SMEM_BUDGET = 48 * 1024;  // keeps CTAS_PER_SM resident for one token
+constexpr int SMEM_LIMIT = 200 * 1024;
 
 __device__ __forceinline__ uint4 ldg16(const uint8_t *p) { return __ldg((const uint4 *)p); }
 __device__ __forceinline__ uint32_t word(const uint4 &v, int k) {
@@ -313,7 +315,7 @@ void launch_one(const Args &a, int smem, dim3 grid, cudaStream_t s) {
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
     if (!(configured.load() & bit)) {
-        SDY_CUDA(cudaFuncSetAttribute(qmv_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        SDY_CUDA(cudaFuncSetAttribute(qmv_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT));
         configured.fetch_or(bit);
     }
     qmv_kernel<TYPE, NT><<<grid, THREADS, smem, s>>>(a);
@@ -353,10 +355,31 @@ void dispatch(int type, int nt, const Args &a, int smem, dim3 grid, cudaStream_t
     SDY_LAUNCHED();
 }
 
-int batch_groups(int type, int nb) {
-    const bool kq = (type == T_Q4_K || type == T_Q6_K);
-    const int per_group = GROUP_ROWS * (kq ? nb : (nb + 7) / 8);
-    return std::max(1, (TARGET_PAIRS + per_group - 1) / per_group);
+// Launch shape: CTAS_PER_SM CTAs per SM (never more than one per group), each sweeping its
+// contiguous share of groups in batches of G groups; G is the whole share when its block terms
+// fit the shared-memory budget (one ordered combine per CTA), else as many as fit.
+
+struct Plan {
+    int grid = 0, G = 0, nt = 0, smem = 0;
+};
+
+bool plan_launch(int type, int nb, int qrow, int64_t ng, int64_t cta_cap, int nt_want, Plan *p) {
+    p->grid = (int)std::max<int64_t>(1, std::min<int64_t>(ng, cta_cap));
+    const int64_t per_cta = (ng + p->grid - 1) / p->grid;
+    int nt = nt_want;
+    for (;;) {
+        int G = (int)std::min<int64_t>(per_cta, 1 << 20);
+        while (G > 1 && smem_plan(type, nt, qrow, nb, G).total > SMEM_BUDGET) G = (G + 1) / 2;
+        int total = smem_plan(type, nt, qrow, nb, G).total;
+        if (total <= SMEM_LIMIT) {
+            p->G = G;
+            p->nt = nt;
+            p->smem = total;
+            return true;
+        }
+        if (nt == 1) return false;
+        nt = nt >= 8 ? 4 : nt == 4 ? 3 : nt - 1;
+    }
 }
 
 }  // namespace
@@ -371,25 +394,21 @@ void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0,
     const bool kq = (w.type == T_Q4_K || w.type == T_Q6_K);
     const int64_t g0 = row0 / GROUP_ROWS, g1 = (row1 + GROUP_ROWS - 1) / GROUP_ROWS;
     const int64_t ng = g1 - g0;
-    const int limit = 200 * 1024;
     for (int t0 = 0; t0 < xq.n_tok;) {
         int rem = xq.n_tok - t0;
-        int nt = rem >= 8 ? 8 : rem >= 4 ? 4 : rem;
-        int G = batch_groups(w.type, w.nb);
-        // Shrink the batch, then the token chunk, until shared memory fits.
-        while (smem_plan(w.type, nt, xq.qrow, w.nb, G).total > limit && G > 1) G = (G + 1) / 2;
-        while (smem_plan(w.type, nt, xq.qrow, w.nb, G).total > limit && nt > 1) nt = nt >= 8 ? 4 : nt == 4 ? 3 : nt - 1;
-        Smem plan = smem_plan(w.type, nt, xq.qrow, w.nb, G);
-        if (plan.total > limit) {
+        Plan plan;
+        if (!plan_launch(w.type, w.nb, xq.qrow, ng, (int64_t)sm_count() * CTAS_PER_SM, rem >= 8 ? 8 : rem >= 4 ? 4 : rem,
+                         &plan)) {
             set_error("qmatvec: row of %d elements too long for one CTA", w.n_in);
             return;
         }
+        const int nt = plan.nt;
         Args a{};
         a.slabs = w.slabs;
         a.nb = w.nb;
         a.g_begin = g0;
         a.n_groups = ng;
-        a.G = G;
+        a.G = plan.G;
         a.xqs = xq.qs + (size_t)t0 * xq.qrow;
         a.xd = xq.d + (size_t)t0 * xq.nbx;
         a.xsums = (const uint8_t *)xq.sums + (size_t)t0 * xq.nbx * (kq ? 32 : 4);
@@ -400,9 +419,7 @@ void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0,
         a.row0 = row0;
         a.row1 = row1;
         a.out_row0 = out_row0;
-        // Enough CTAs for two per SM, never more than one per group.
-        int grid = (int)std::min<int64_t>(ng, (int64_t)sm_count() * 2);
-        dispatch(w.type, nt, a, plan.total, dim3(grid), s);
+        dispatch(w.type, nt, a, plan.smem, dim3(plan.grid), s);
         t0 += nt;
     }
 }
@@ -418,12 +435,9 @@ void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq
         set_error("qmatvec_gather: activation type/size does not match the weights");
         return;
     }
-    const bool kq = (experts.type == T_Q4_K || experts.type == T_Q6_K);
-    int G = batch_groups(experts.type, experts.nb);
-    const int limit = 200 * 1024;
-    while (smem_plan(experts.type, 1, xq.qrow, experts.nb, G).total > limit && G > 1) G = (G + 1) / 2;
-    Smem plan = smem_plan(experts.type, 1, xq.qrow, experts.nb, G);
-    if (plan.total > limit) {
+    const int64_t cap = std::max<int64_t>(1, ((int64_t)sm_count() * CTAS_PER_SM + n_slots - 1) / n_slots);
+    Plan plan;
+    if (!plan_launch(experts.type, experts.nb, xq.qrow, gpe, cap, 1, &plan)) {
         set_error("qmatvec_gather: row of %d elements too long for one CTA", experts.n_in);
         return;
     }
@@ -432,7 +446,7 @@ void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq
     a.nb = experts.nb;
     a.g_begin = 0;
     a.n_groups = gpe;
-    a.G = G;
+    a.G = plan.G;
     a.xqs = xq.qs;
     a.xd = xq.d;
     a.xsums = xq.sums;
@@ -448,9 +462,7 @@ void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq
     a.ldo_slot = ldo_slot;
     a.tok_div = tok_div;
     a.n_expert = n_expert;
-    (void)kq;
-    int per_slot = (int)std::max<int64_t>(1, std::min<int64_t>(gpe, ((int64_t)sm_count() * 2 + n_slots - 1) / n_slots));
-    dispatch(experts.type, 1, a, plan.total, dim3(per_slot, n_slots), s);
+    dispatch(experts.type, 1, a, plan.smem, dim3(plan.grid, n_slots), s);
 }
 
 }  // namespace sdy
