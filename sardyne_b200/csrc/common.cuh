@@ -105,6 +105,9 @@ struct QMat {
     size_t bytes() const { return (size_t)n_groups() * nb * slab_bytes(type); }
 };
 
+// The matrix behind a handle returned by sdy_qmat_upload (nullptr for a null handle).
+const QMat *qmat_of(const void *handle);
+
 // ------------------------------------------------------------------------------------------ errors
 void set_error(const char *fmt, ...);
 const char *last_error();

@@ -507,9 +507,16 @@ void sdy_qmat_free(void *h) {
 
 size_t sdy_qmat_bytes(const void *h) { return h ? ((const sdy_qmat_s *)h)->m.bytes() : 0; }
 
+}  // extern "C"
+
+const QMat *sdy::qmat_of(const void *h) { return h ? &((const sdy_qmat_s *)h)->m : nullptr; }
+
+extern "C" {
+
 size_t sdy_xq_bytes(int vtype, int n_in, int n_tok) { return xq_bytes(vtype, n_in, n_tok); }
 
 int sdy_quantize_rows_dev(int vtype, const float *d_x, int n_tok, int n_in, void *d_xq, void *stream) {
+    clear_error();
     if ((vtype != T_Q8_0 && vtype != T_Q8_K) || n_in <= 0 || n_in % block_elems(vtype) || n_tok <= 0) {
         set_error("sdy_quantize_rows_dev: bad type %d / n_in %d / n_tok %d", vtype, n_in, n_tok);
         return -1;
@@ -521,6 +528,7 @@ int sdy_quantize_rows_dev(int vtype, const float *d_x, int n_tok, int n_in, void
 
 int sdy_qmatvec_dev(const void *h, const void *d_xq, int n_tok, float *d_out, int64_t ldo, int64_t row0,
                     int64_t row1, void *stream) {
+    clear_error();
     const sdy_qmat_s *w = (const sdy_qmat_s *)h;
     if (!w || row0 < 0 || row1 > w->m.n_rows || row1 < row0 || n_tok <= 0) {
         set_error("sdy_qmatvec_dev: bad arguments");
