@@ -395,6 +395,96 @@ def run_b200(args, rank, world, local_rank):
     return 0
 
 
+# ------------------------------------------------------------------------------ decode workload
+
+DECODE_MODELS = {  # shape, prompt length, decode steps, max context
+    "smollm2": ("SMOLLM2_135M", 128, 256, 2048),
+    "qwen25_3b": ("QWEN25_3B", 512, 512, 4096),
+    "qwen3moe": ("QWEN3_30B_A3B", 256, 256, 4096),
+}
+
+
+def decode_model_path(name, directory):
+    from sardyne_b200 import synth
+    spec_name = DECODE_MODELS[name][0]
+    path = pathlib.Path(directory) / f"{name}.gguf"
+    if not path.exists():
+        t0 = time.perf_counter()
+        synth.write_model(path, synth.Spec(**getattr(synth, spec_name), synth=True, seed=0))
+        log(f"wrote {path} ({path.stat().st_size / 1e9:.2f} GB) in {time.perf_counter() - t0:.1f} s")
+    return path
+
+
+def weight_bytes_per_token(path, info):
+    """Weight bytes one decode token reads: every matrix; of the experts only k of n; of an
+    untied embedding table only the looked-up row."""
+    from sardyne_b200 import capi
+    lib = capi.lib()
+    err = ctypes.create_string_buffer(256)
+    h = lib.gguf_open(str(path).encode(), err, len(err))
+    total = 0
+    for i in range(lib.gguf_n_tensors(h)):
+        t = lib.gguf_get_tensor(h, i).contents
+        name, nb = t.name.decode(), t.nbytes
+        if "_exps" in name:
+            nb = nb * info.n_expert_used // info.n_expert
+        if name == "token_embd.weight" and not info.tied_embeddings:
+            nb = nb // info.n_vocab
+        total += nb
+    lib.gguf_close(h)
+    return total
+
+
+def run_decode(args):
+    import torch
+    from sardyne_b200 import capi, runtime
+    spec_name, n_prompt, n_decode, ctx_len = DECODE_MODELS[args.model]
+    n_decode = args.decode_steps or n_decode
+    path = decode_model_path(args.model, args.model_dir)
+    t0 = time.perf_counter()
+    model = runtime.Model(path)
+    load_s = time.perf_counter() - t0
+    info = model.info
+    prompt = np.random.default_rng(0).integers(0, info.n_vocab, n_prompt).tolist()
+    ctx = runtime.Context(model, max_seq=ctx_len, n_batch=n_prompt)
+    ctx.eval(prompt)  # warm-up: a prefill and a few decode steps (the second one captures the graph)
+    for _ in range(max(args.warmup, 3)):
+        ctx.eval([1])
+    ctx.reset()
+    launches0 = capi.lib().sdy_kernel_launches()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        t0 = time.perf_counter()
+        logits = ctx.eval(prompt)
+        t1 = time.perf_counter()
+        tokens = []
+        for _ in range(n_decode):
+            nxt = int(np.argmax(logits))
+            tokens.append(nxt)
+            logits = ctx.eval([nxt])
+        t2 = time.perf_counter()
+    capi.check()
+    wbytes = weight_bytes_per_token(path, info)
+    peak, peak_kind = load_peaks()
+    tps = n_decode / (t2 - t1)
+    line = {"metric": f"decode tok/s {spec_name} shape (greedy, e2e through engine_eval)",
+            "value": round(tps, 2), "unit": "tok/s", "n_gpus": 1, "steps": n_decode, "warmup": args.warmup,
+            "ms_per_step": round((t2 - t1) / n_decode * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"{spec_name}: {n_prompt}-token prompt (uniform ids, seed 0), {n_decode} greedy "
+                                   f"decode steps, context {ctx_len}", "model_gb": round(path.stat().st_size / 1e9, 2),
+                       "weight_bytes_per_token": wbytes},
+            "prefill_tok_s": round(n_prompt / (t1 - t0), 1),
+            "roofline": {"bound": "hbm", "achieved": round(wbytes * tps / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(wbytes * tps / 1e9 / peak, 4), "traffic": None,
+                         "kernel": "whole decode step (weight bytes per token x tok/s)", "peak_source": peak_kind},
+            "e2e": {"value": round(tps, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4 * info.n_vocab},
+            "gpu_launches": int(capi.lib().sdy_kernel_launches() - launches0), "clocks": clk.summary(),
+            "load_s": round(load_s, 2), "first_tokens": tokens[:8]}
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -402,9 +492,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["matvec", "decode"], default="matvec")
+    ap.add_argument("--model", choices=sorted(DECODE_MODELS), default="qwen3moe")
+    ap.add_argument("--model-dir", default=os.environ.get("SARDYNE_BENCH_DIR", "/tmp"))
+    ap.add_argument("--decode-steps", type=int, default=0)
     args = ap.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.workload == "decode":
+        return run_decode(args)
     if args.impl == "reference":
         return run_reference_arm(args, rank, world)
     if world > 1:

@@ -131,8 +131,9 @@ void quantize_rows(int vtype, const float *x, int64_t ldx, int n_tok, int n_in, 
 void xq_import(int vtype, const uint8_t *raw, int n_tok, int n_in, const XQ &xq, cudaStream_t s);
 void xq_export(const XQ &xq, uint8_t *raw, cudaStream_t s);
 // out[t*ldo + (r - out_row0)] = W[r] . x[t] for rows r in [row0, row1) and tokens t < xq.n_tok.
+// With `residual`, out = residual + product (same indexing; residual may alias out).
 void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
-             cudaStream_t s);
+             cudaStream_t s, const float *residual = nullptr);
 // MoE: for each slot s < n_slots, out[s*ldo_slot + r] = E[slot_expert[s]][r] . x[s / tok_div] for
 // r < rows_per_expert. `experts` holds n_expert matrices, each padded to gpe groups. The expert ids
 // are read on the device, so no host round trip sits between the router and the experts.

@@ -2,16 +2,19 @@
 //
 // engine_model_load reads the GGUF with the gguf_* reader, checks the configuration exactly as
 // the reference does (same accepted files, same error messages), and uploads every weight
-// matrix once: quantized matrices are repacked into the slab layout (3D expert tensors one
-// expert at a time, each padded to whole 8-row groups), float matrices stay as they are, norms
-// and biases become f32. engine_ctx_new allocates the device KV cache, the RoPE tables and all
-// activation buffers in one arena. engine_eval runs the forward (model_llama.c:757-832) as a
-// sequence of CUDA kernels on the context's stream and copies only the logits back.
+// matrix once in the slab layout. Projections that share an input and a quantized type are
+// stored as one device matrix (q|k|v, gate|up; for MoE gate|up of every expert), so each runs as
+// one launch. engine_ctx_new allocates the device KV cache, the RoPE tables and all activation
+// buffers in one arena. engine_eval runs the forward (model_llama.c:757-832) as CUDA kernels on
+// the context's stream; a single-token step is captured once as a CUDA graph and replayed (the
+// token id and its position are read from device memory), and only the logits come back.
 #include "common.cuh"
 #include "fp_ops.cuh"
+#include "fused.cuh"
 #include "sardyne_b200.h"
 
 #include <stdarg.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <string>
@@ -36,18 +39,29 @@ void put_err(char *err, size_t len, const char *fmt, ...) {
 struct DMat {
     int type = -1;
     int n_in = 0;
-    int64_t n_out = 0;
-    int n_expert = 0;      // 0: a plain matrix
-    QMat q;                // quantized: slabs (each expert padded to gpe groups)
-    int64_t gpe = 0;       // groups per expert
+    int64_t n_out = 0;        // rows (per expert)
+    int n_expert = 0;         // 0: a plain matrix
+    QMat q;                   // quantized: slabs (each expert padded to gpe groups)
+    int64_t gpe = 0;          // groups per expert
     const void *f = nullptr;  // float weights, raw [n_expert][n_out][n_in]
     bool quant() const { return is_quant_weight(type); }
+};
+
+// Projections sharing one input: each part fills output columns [col, col + m.n_out).
+struct Part {
+    DMat m;
+    int col = 0;
+};
+struct Proj {
+    std::vector<Part> parts;
+    int width = 0;
 };
 
 struct DLayer {
     float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
     float *q_norm = nullptr, *k_norm = nullptr;
-    DMat wq, wk, wv, wo, gate, up, down, gate_inp;
+    Proj qkv, gateup;
+    DMat wo, down, gate_inp;
 };
 
 const char *LAYER_SUFFIXES[] = {
@@ -97,22 +111,32 @@ struct engine_model {
     size_t raw_cap = 0;
 };
 
+// Quantized activations of one buffer, reused while the buffer is unchanged (model_llama.c:590-611).
+struct ActCache {
+    const float *src = nullptr;
+    int64_t ld = 0;
+    int n = 0, n_in = 0;
+};
+
 struct engine_ctx {
     const engine_model *m = nullptr;
     int max_seq = 0, n_batch = 0, logits_all = 0, n_past = 0, n_logits = 0, n_threads = 0;
+    int qkv_ld = 0, gu_ld = 0;
     cudaStream_t st = nullptr;
     void *arena = nullptr;
     float *k_cache = nullptr, *v_cache = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
-    float *x = nullptr, *xb = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *hb = nullptr,
-          *hb2 = nullptr, *logits = nullptr, *scores = nullptr;
-    float *moe_probs = nullptr, *moe_w = nullptr, *moe_g = nullptr, *moe_u = nullptr, *moe_y = nullptr,
-          *moe_sum = nullptr;
-    int32_t *moe_top = nullptr, *tok_ids = nullptr;
+    float *x = nullptr, *xb = nullptr, *qkv = nullptr, *att = nullptr, *hgu = nullptr, *tmp = nullptr,
+          *logits = nullptr, *scores = nullptr;
+    float *moe_probs = nullptr, *moe_w = nullptr, *moe_gu = nullptr, *moe_y = nullptr;
+    int32_t *moe_top = nullptr;
+    int32_t *tokpos = nullptr;    // device: [0] position of the first token, [1..] token ids
+    int32_t *h_tokpos = nullptr;  // pinned staging of the same
     void *xq_buf[2] = {nullptr, nullptr};  // [0] Q8_0, [1] Q8_K activations
-    const float *xq_src[2] = {nullptr, nullptr};
-    int xq_n[2] = {0, 0}, xq_in[2] = {0, 0};
     XQ xq[2];
-    float *h_logits = nullptr;  // pinned host copy returned by engine_logits
+    ActCache xc[2];
+    float *h_logits = nullptr;             // pinned host copy returned by engine_logits
+    cudaGraphExec_t step_graph = nullptr;  // the single-token forward, replayed each decode step
+    int graph_state = 0;  // 0: next single-token step runs eagerly, 2: capture next, 1: captured, -1: off
     char err[256] = {0};
 };
 
@@ -281,60 +305,115 @@ uint8_t *bounce(engine_model *m, size_t bytes) {
     return m->raw;
 }
 
-// A tensor [n_expert][n_out][n_in] (n_expert 0: a matrix) of a supported type (model_llama.c:163-185).
-int get_tensor(engine_model *m, const char *name, int n_in, int64_t n_out, int n_expert, DMat *out, char *err,
-               size_t len) {
+// Checks a tensor [n_expert][n_out][n_in] (n_expert 0: a matrix) of a supported type
+// (model_llama.c:163-185).
+const gguf_tensor *check_tensor(engine_model *m, const char *name, int n_in, int64_t n_out, int n_expert, char *err,
+                                size_t len) {
     const gguf_tensor *t = find(m->gf, name);
     if (!t) {
         put_err(err, len, "tensore mancante: %s", name);
-        return -1;
+        return nullptr;
     }
     if (t->n_dims != (n_expert ? 3u : 2u) || t->ne[0] != (uint64_t)n_in || t->ne[1] != (uint64_t)n_out ||
         (n_expert && t->ne[2] != (uint64_t)n_expert)) {
         put_err(err, len, "%s: dimensioni [%llu, %llu, %llu], attese [%d, %lld, %d]", name,
                 (unsigned long long)t->ne[0], (unsigned long long)t->ne[1], (unsigned long long)t->ne[2], n_in,
                 (long long)n_out, n_expert ? n_expert : 1);
-        return -1;
+        return nullptr;
     }
     if (!type_supported(t->type)) {
         put_err(err, len,
                 "%s: tipo %s non supportato dal runtime (supportati: F32, F16, BF16, Q8_0, Q4_0, Q5_0, Q4_K, Q6_K)",
                 name, gguf_type_name(t->type));
-        return -1;
+        return nullptr;
     }
+    return t;
+}
+
+// Uploads tensors of one type that share n_in as ONE device matrix: expert e (or the single
+// matrix) holds the rows of ts[0], then ts[1], ... Quantized rows are repacked into slabs.
+int upload_group(engine_model *m, const std::vector<const gguf_tensor *> &ts, const std::vector<int64_t> &rows,
+                 int n_in, int n_expert, DMat *out, char *err, size_t len) {
     DMat d;
-    d.type = (int)t->type;
+    d.type = (int)ts[0]->type;
     d.n_in = n_in;
-    d.n_out = n_out;
     d.n_expert = n_expert;
-    int ne = n_expert ? n_expert : 1;
-    if (d.quant()) {
+    int64_t total = 0;
+    for (int64_t r : rows) total += r;
+    d.n_out = total;
+    const int ne = n_expert ? n_expert : 1;
+    const size_t rb = row_bytes(d.type, n_in);
+    uint8_t *raw = bounce(m, (size_t)ne * total * rb);
+    bool ok = raw != nullptr;
+    for (int e = 0; ok && e < ne; e++) {
+        size_t off = (size_t)e * total * rb;
+        for (size_t i = 0; ok && i < ts.size(); i++) {
+            const uint8_t *src = (const uint8_t *)ts[i]->data + (size_t)e * rows[i] * rb;
+            ok = SDY_CUDA(cudaMemcpyAsync(raw + off, src, rows[i] * rb, cudaMemcpyHostToDevice, m->st));
+            off += rows[i] * rb;
+        }
+    }
+    if (ok && d.quant()) {
         d.q.type = d.type;
         d.q.n_in = n_in;
         d.q.nb = n_in / block_elems(d.type);
-        d.q.n_rows = n_out;
+        d.q.n_rows = total;
         d.gpe = d.q.n_groups();
-        size_t per = d.q.bytes();
+        const size_t per = d.q.bytes();
         uint8_t *slabs = (uint8_t *)dalloc(m, per * ne);
-        uint8_t *raw = bounce(m, t->nbytes);
-        if (!slabs || !raw) goto oom;
-        if (!SDY_CUDA(cudaMemcpyAsync(raw, t->data, t->nbytes, cudaMemcpyHostToDevice, m->st))) goto oom;
-        size_t rb = row_bytes(d.type, n_in);
-        for (int e = 0; e < ne; e++)
-            repack_to_slabs(raw + (size_t)e * n_out * rb, d.type, n_out, n_in, slabs + per * e, m->st);
+        ok = slabs != nullptr;
+        for (int e = 0; ok && e < ne; e++)
+            repack_to_slabs(raw + (size_t)e * total * rb, d.type, total, n_in, slabs + per * e, m->st);
         d.q.slabs = slabs;
-        d.q.n_rows = n_out;
-    } else {
-        void *f = dalloc(m, t->nbytes);
-        if (!f || !SDY_CUDA(cudaMemcpyAsync(f, t->data, t->nbytes, cudaMemcpyHostToDevice, m->st))) goto oom;
+    } else if (ok) {
+        void *f = dalloc(m, (size_t)ne * total * rb);
+        ok = f && SDY_CUDA(cudaMemcpyAsync(f, raw, (size_t)ne * total * rb, cudaMemcpyDeviceToDevice, m->st));
         d.f = f;
     }
-    if (!SDY_CUDA(cudaStreamSynchronize(m->st))) goto oom;
+    ok = ok && SDY_CUDA(cudaStreamSynchronize(m->st));
+    if (!ok) {
+        put_err(err, len, "%s: caricamento sulla GPU fallito (%s)", ts[0]->name, last_error());
+        return -1;
+    }
     *out = d;
     return 0;
-oom:
-    put_err(err, len, "%s: caricamento sulla GPU fallito (%s)", name, last_error());
-    return -1;
+}
+
+int get_tensor(engine_model *m, const char *name, int n_in, int64_t n_out, int n_expert, DMat *out, char *err,
+               size_t len) {
+    const gguf_tensor *t = check_tensor(m, name, n_in, n_out, n_expert, err, len);
+    if (!t) return -1;
+    return upload_group(m, {t}, {n_out}, n_in, n_expert, out, err, len);
+}
+
+// A projection from one input: consecutive tensors of the same quantized type whose row counts
+// are whole 8-row groups share one device matrix (one launch); the others stay separate.
+int get_proj(engine_model *m, const std::vector<std::string> &names, const std::vector<int64_t> &rows, int n_in,
+             int n_expert, Proj *out, char *err, size_t len) {
+    std::vector<const gguf_tensor *> ts;
+    for (size_t i = 0; i < names.size(); i++) {
+        const gguf_tensor *t = check_tensor(m, names[i].c_str(), n_in, rows[i], n_expert, err, len);
+        if (!t) return -1;
+        ts.push_back(t);
+    }
+    Proj p;
+    int col = 0;
+    for (size_t i = 0; i < ts.size();) {
+        size_t j = i + 1;
+        const bool fusable = is_quant_weight((int)ts[i]->type) && rows[i] % GROUP_ROWS == 0;
+        while (fusable && j < ts.size() && ts[j]->type == ts[i]->type && rows[j] % GROUP_ROWS == 0) j++;
+        Part part;
+        part.col = col;
+        if (upload_group(m, std::vector<const gguf_tensor *>(ts.begin() + i, ts.begin() + j),
+                         std::vector<int64_t>(rows.begin() + i, rows.begin() + j), n_in, n_expert, &part.m, err, len))
+            return -1;
+        col += (int)part.m.n_out;
+        p.parts.push_back(part);
+        i = j;
+    }
+    p.width = col;
+    *out = p;
+    return 0;
 }
 
 // A vector of n elements converted to f32 on the device.
@@ -379,20 +458,8 @@ __global__ void embed_float_kernel(const void *table, int type, const int32_t *i
     }
 }
 
-// K and V of n tokens into the cache [n_kv_head][max_seq][hd] at positions pos0.. (model_llama.c:796-799).
-__global__ void kv_store_kernel(const float *k, const float *v, int kv_dim, int hd, int max_seq, int pos0, float *kc,
-                                float *vc) {
-    int t = blockIdx.y;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kv_dim; i += gridDim.x * blockDim.x) {
-        int h = i / hd, j = i % hd;
-        size_t dst = ((size_t)h * max_seq + pos0 + t) * hd + j;
-        kc[dst] = k[(size_t)t * kv_dim + i];
-        vc[dst] = v[(size_t)t * kv_dim + i];
-    }
-}
-
-// Router selection per token (model_llama.c:653-666): the k most probable experts, ties to the
-// lowest index, weights renormalised by their float sum.
+// Router selection per token for a quantized router (model_llama.c:653-666): the k most
+// probable experts, ties to the lowest index, weights renormalised by their float sum.
 __global__ void topk_kernel(const float *probs, int n_tok, int ne, int k, int32_t *top, float *w) {
     int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= n_tok) return;
@@ -412,29 +479,8 @@ __global__ void topk_kernel(const float *probs, int n_tok, int ne, int k, int32_
     for (int i = 0; i < k; i++) w[(size_t)t * k + i] = __fdiv_rn(p[tp[i]], sum);
 }
 
-// out[t] = sum over t's k slots, in ascending expert order (the order moe_ffn adds them,
-// model_llama.c:734-750), of w * y[slot].
-__global__ void moe_combine_kernel(const float *y, const int32_t *top, const float *w, int k, int dim, float *out) {
-    int t = blockIdx.y;
-    int order[64];
-    for (int i = 0; i < k; i++) order[i] = i;
-    for (int i = 1; i < k; i++) {  // insertion sort of the slots by expert id (k is small)
-        int s = order[i], j = i;
-        while (j > 0 && top[(size_t)t * k + order[j - 1]] > top[(size_t)t * k + s]) { order[j] = order[j - 1]; j--; }
-        order[j] = s;
-    }
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) {
-        float acc = 0.0f;
-        for (int j = 0; j < k; j++) {
-            int s = order[j];
-            acc = __fadd_rn(acc, __fmul_rn(w[(size_t)t * k + s], y[((size_t)t * k + s) * dim + i]));
-        }
-        out[(size_t)t * dim + i] = acc;
-    }
-}
-
-// Float-weight experts: out[s][r] = E[top[s]][r] . x[s / tok_div], one thread per row, in the
-// reference's scalar dot order (four accumulators, csrc/ops.c:155-167).
+// Float-weight experts: out[s*ldo + r] = E[top[s]][r] . x[s / tok_div], one thread per row, in
+// the reference's scalar dot order (four accumulators, csrc/ops.c:155-167).
 __global__ void fmatmul_gather_kernel(const void *w, int type, int n_in, int64_t rows, const int32_t *top,
                                       const float *x, int64_t ldx, int tok_div, float *out, int64_t ldo) {
     int s = blockIdx.y;
@@ -461,121 +507,221 @@ __global__ void fmatmul_gather_kernel(const void *w, int type, int n_in, int64_t
 
 // ------------------------------------------------------------------------------ forward
 
-// Quantized activations of x for weight type wtype, reused while the input is unchanged
-// (model_llama.c:590-611).
-const XQ &activations(engine_ctx *c, const float *x, int n, int n_in, int wtype) {
-    int vt = vec_dot_type(wtype), s = vt == T_Q8_K ? 1 : 0;
-    if (c->xq_src[s] != x || c->xq_n[s] != n || c->xq_in[s] != n_in) {
+int act_slot(int vt) { return vt == T_Q8_K ? 1 : 0; }
+
+// Quantized activations of x (n rows of n_in, row stride ldx) for weights of type wtype.
+const XQ &activations(engine_ctx *c, const float *x, int64_t ldx, int n, int n_in, int wtype) {
+    const int vt = vec_dot_type(wtype), s = act_slot(vt);
+    ActCache &k = c->xc[s];
+    if (k.src != x || k.ld != ldx || k.n != n || k.n_in != n_in) {
         c->xq[s] = xq_carve(c->xq_buf[s], vt, n_in, n);
-        quantize_rows(vt, x, n_in, n, n_in, c->xq[s], c->st);
-        c->xq_src[s] = x;
-        c->xq_n[s] = n;
-        c->xq_in[s] = n_in;
+        quantize_rows(vt, x, ldx, n, n_in, c->xq[s], c->st);
+        k = ActCache{x, ldx, n, n_in};
     }
     return c->xq[s];
 }
 
-// out = x . W^T for n tokens (model_llama.c:592-611). new_input: x changed since the last call.
-void matmul(engine_ctx *c, float *out, const float *x, const DMat &w, int n, bool new_input) {
-    if (new_input) c->xq_src[0] = c->xq_src[1] = nullptr;
-    if (!w.quant()) {
-        fmatmul(x, w.n_in, w.f, w.type, n, w.n_in, 0, w.n_out, out, w.n_out, 0, c->st);
-        return;
+void forget_activations(engine_ctx *c) { c->xc[0] = c->xc[1] = ActCache(); }
+
+// Reserves the XQ slots a producer kernel (norm or SiLU fused with quantization) fills for
+// (x, n, n_in), for the activation types the given matrices consume.
+void want_activations(engine_ctx *c, const std::vector<const DMat *> &mats, const float *x, int64_t ldx, int n,
+                      int n_in, const XQ **q8k, const XQ **q80) {
+    forget_activations(c);
+    *q8k = *q80 = nullptr;
+    for (const DMat *d : mats) {
+        if (!d->quant()) continue;
+        const int vt = vec_dot_type(d->type), s = act_slot(vt);
+        if (c->xc[s].src) continue;
+        c->xq[s] = xq_carve(c->xq_buf[s], vt, n_in, n);
+        c->xc[s] = ActCache{x, ldx, n, n_in};
+        (vt == T_Q8_K ? *q8k : *q80) = &c->xq[s];
     }
-    const XQ &xq = activations(c, x, n, w.n_in, w.type);
-    qmatvec(w.q, xq, out, w.n_out, 0, w.n_out, 0, c->st);
 }
 
-// Gathered experts: out[s] = E[top[s]] . x[s / tok_div] for n_slots slots.
-void matmul_experts(engine_ctx *c, float *out, const float *x, int n_x, const DMat &w, int n_slots, int tok_div,
-                    bool new_input) {
-    if (new_input) c->xq_src[0] = c->xq_src[1] = nullptr;
+// out[t*ldo + j] = x[t] . W[j] (+ residual), W a plain matrix.
+void matmul(engine_ctx *c, float *out, int64_t ldo, const float *x, int64_t ldx, const DMat &w, int n,
+            const float *residual = nullptr) {
     if (!w.quant()) {
-        dim3 grid((unsigned)((w.n_out + 255) / 256), n_slots);
-        fmatmul_gather_kernel<<<grid, 256, 0, c->st>>>(w.f, w.type, w.n_in, w.n_out, c->moe_top, x, w.n_in, tok_div,
-                                                        out, w.n_out);
-        SDY_LAUNCHED();
+        float *dst = residual ? c->tmp : out;
+        const int64_t ld = residual ? w.n_out : ldo;
+        fmatmul(x, ldx, w.f, w.type, n, w.n_in, 0, w.n_out, dst, ld, 0, c->st);
+        if (residual)  // x + W.a as the reference's `x[i] += xb[i]`
+            for (int t = 0; t < n; t++)
+                add(out + (size_t)t * ldo, residual + (size_t)t * ldo, c->tmp + (size_t)t * ld, w.n_out, c->st);
         return;
     }
-    const XQ &xq = activations(c, x, n_x, w.n_in, w.type);
-    qmatvec_gather(w.q, w.gpe, w.n_expert, xq, tok_div, c->moe_top, n_slots, w.n_out, out, w.n_out, c->st);
+    const XQ &xq = activations(c, x, ldx, n, w.n_in, w.type);
+    qmatvec(w.q, xq, out, ldo, 0, w.n_out, 0, c->st, residual);
+}
+
+void project(engine_ctx *c, const Proj &p, float *out, int64_t ldo, const float *x, int64_t ldx, int n) {
+    for (const Part &part : p.parts) matmul(c, out + part.col, ldo, x, ldx, part.m, n);
+}
+
+// Experts: out[s*ldo + part.col + r] = E[top[s]][r] . x[s / tok_div] for every part.
+void project_experts(engine_ctx *c, const Proj &p, float *out, int64_t ldo, const float *x, int64_t ldx, int n_x,
+                     int n_slots, int tok_div) {
+    for (const Part &part : p.parts) {
+        const DMat &w = part.m;
+        if (!w.quant()) {
+            dim3 grid((unsigned)((w.n_out + 255) / 256), n_slots);
+            fmatmul_gather_kernel<<<grid, 256, 0, c->st>>>(w.f, w.type, w.n_in, w.n_out, c->moe_top, x, ldx, tok_div,
+                                                            out + part.col, ldo);
+            SDY_LAUNCHED();
+            continue;
+        }
+        const XQ &xq = activations(c, x, ldx, n_x, w.n_in, w.type);
+        qmatvec_gather(w.q, w.gpe, w.n_expert, xq, tok_div, c->moe_top, n_slots, w.n_out, out + part.col, ldo, c->st);
+    }
 }
 
 void moe_ffn(engine_ctx *c, const DLayer &L, int n) {
     const engine_model_info &in = c->m->info;
     const int dim = in.dim, fe = in.ffn_exp_dim, ne = in.n_expert, k = in.n_expert_used;
-    matmul(c, c->moe_probs, c->xb, L.gate_inp, n, true);
-    softmax(c->moe_probs, ne, ne, n, c->st);
-    topk_kernel<<<(n + 127) / 128, 128, 0, c->st>>>(c->moe_probs, n, ne, k, c->moe_top, c->moe_w);
-    SDY_LAUNCHED();
-    matmul_experts(c, c->moe_g, c->xb, n, L.gate, n * k, k, true);
-    matmul_experts(c, c->moe_u, c->xb, n, L.up, n * k, k, false);
-    silu_mul(c->moe_g, c->moe_u, (int64_t)n * k * fe, c->st);
-    matmul_experts(c, c->moe_y, c->moe_g, n * k, L.down, n * k, 1, true);
-    moe_combine_kernel<<<dim3((dim + 255) / 256, n), 256, 0, c->st>>>(c->moe_y, c->moe_top, c->moe_w, k, dim,
-                                                                     c->moe_sum);
-    SDY_LAUNCHED();
+    const DMat &r = L.gate_inp;
+    if (!r.quant()) {
+        router_topk(c->xb, dim, r.f, r.type, dim, ne, k, n, c->moe_top, c->moe_w, nullptr, c->st);
+    } else {
+        matmul(c, c->moe_probs, ne, c->xb, dim, r, n);
+        softmax(c->moe_probs, ne, ne, n, c->st);
+        topk_kernel<<<(n + 127) / 128, 128, 0, c->st>>>(c->moe_probs, n, ne, k, c->moe_top, c->moe_w);
+        SDY_LAUNCHED();
+    }
+    const int slots = n * k, gu = 2 * fe;
+    project_experts(c, L.gateup, c->moe_gu, gu, c->xb, dim, n, slots, k);
+    const XQ *q8k, *q80;
+    want_activations(c, {&L.down}, c->moe_gu, gu, slots, fe, &q8k, &q80);
+    silu_quant(c->moe_gu, gu, c->moe_gu + fe, gu, fe, slots, q8k, q80, c->st);
+    Proj down;
+    down.parts.push_back(Part{L.down, 0});
+    project_experts(c, down, c->moe_y, dim, c->moe_gu, gu, slots, slots, 1);
+    moe_combine(c->moe_y, dim, c->moe_top, c->moe_w, k, dim, n, c->x, dim, c->st);
 }
 
 void embed(engine_ctx *c, int n) {
     const engine_model *m = c->m;
     const DMat &e = m->tok_embd;
-    if (e.quant()) dequant_rows(e.q, c->tok_ids, n, 0, c->x, m->info.dim, c->st);
+    const int32_t *ids = c->tokpos + 1;
+    if (e.quant()) dequant_rows(e.q, ids, n, 0, c->x, m->info.dim, c->st);
     else {
-        embed_float_kernel<<<n, 256, 0, c->st>>>(e.f, e.type, c->tok_ids, m->info.dim, c->x);
+        embed_float_kernel<<<n, 256, 0, c->st>>>(e.f, e.type, ids, m->info.dim, c->x);
         SDY_LAUNCHED();
     }
 }
 
-// n <= n_batch tokens at n_past; logits of the last out_rows tokens (model_llama.c:757-832).
+std::vector<const DMat *> mats_of(const Proj &p) {
+    std::vector<const DMat *> v;
+    for (const Part &q : p.parts) v.push_back(&q.m);
+    return v;
+}
+
+// n <= n_batch tokens at the position stored in tokpos[0]; logits of the last out_rows tokens
+// (model_llama.c:757-832).
 void forward(engine_ctx *c, int n, int out_rows) {
     const engine_model *m = c->m;
     const engine_model_info &in = m->info;
     const int dim = in.dim, hd = in.head_dim, q_dim = in.n_head * hd, kv_dim = in.n_kv_head * hd;
-    const int pos0 = c->n_past;
     const size_t layer_stride = (size_t)in.n_kv_head * c->max_seq * hd;
+    const int64_t QL = c->qkv_ld;
+    const XQ *q8k, *q80;
     embed(c, n);
     for (int l = 0; l < in.n_layer; l++) {
         const DLayer &L = m->layers[l];
         float *kc = c->k_cache + l * layer_stride, *vc = c->v_cache + l * layer_stride;
-        rmsnorm(c->xb, dim, c->x, dim, L.attn_norm, dim, n, in.norm_eps, c->st);
-        matmul(c, c->q, c->xb, L.wq, n, true);
-        matmul(c, c->k, c->xb, L.wk, n, false);
-        matmul(c, c->v, c->xb, L.wv, n, false);
-        if (L.bq) {
-            add_bias(c->q, q_dim, L.bq, q_dim, n, c->st);
-            add_bias(c->k, kv_dim, L.bk, kv_dim, n, c->st);
-            add_bias(c->v, kv_dim, L.bv, kv_dim, n, c->st);
-        }
-        if (L.q_norm) {
-            rmsnorm(c->q, hd, c->q, hd, L.q_norm, hd, n * in.n_head, in.norm_eps, c->st);
-            rmsnorm(c->k, hd, c->k, hd, L.k_norm, hd, n * in.n_kv_head, in.norm_eps, c->st);
-        }
-        rope(c->q, q_dim, n, in.n_head, hd, c->rope_cos, c->rope_sin, pos0, nullptr, in.rope_interleaved, c->st);
-        rope(c->k, kv_dim, n, in.n_kv_head, hd, c->rope_cos, c->rope_sin, pos0, nullptr, in.rope_interleaved, c->st);
-        kv_store_kernel<<<dim3((kv_dim + 255) / 256, n), 256, 0, c->st>>>(c->k, c->v, kv_dim, hd, c->max_seq, pos0, kc,
-                                                                         vc);
-        SDY_LAUNCHED();
-        attention(c->att, c->q, kc, vc, n, in.n_head, in.n_kv_head, hd, pos0, c->max_seq, c->scores, 0, c->st);
-        matmul(c, c->xb, c->att, L.wo, n, true);
-        add(c->x, c->x, c->xb, (int64_t)n * dim, c->st);
-        rmsnorm(c->xb, dim, c->x, dim, L.ffn_norm, dim, n, in.norm_eps, c->st);
-        const float *ffn_out = c->xb;
+        // attention: x = x + Wo . Attn(RoPE(Wq.norm(x)), RoPE(Wk.norm(x)), Wv.norm(x))
+        want_activations(c, mats_of(L.qkv), c->xb, dim, n, dim, &q8k, &q80);
+        rmsnorm_quant(c->x, dim, L.attn_norm, dim, n, in.norm_eps, c->xb, dim, q8k, q80, c->st);
+        project(c, L.qkv, c->qkv, QL, c->xb, dim, n);
+        PostQKV p{};
+        p.q = c->qkv;
+        p.k = c->qkv + q_dim;
+        p.v = c->qkv + q_dim + kv_dim;
+        p.ldq = p.ldk = p.ldv = QL;
+        p.bq = L.bq;
+        p.bk = L.bk;
+        p.bv = L.bv;
+        p.q_norm = L.q_norm;
+        p.k_norm = L.k_norm;
+        p.n_head = in.n_head;
+        p.n_kv_head = in.n_kv_head;
+        p.hd = hd;
+        p.eps = in.norm_eps;
+        p.cos = c->rope_cos;
+        p.sin = c->rope_sin;
+        p.pos_dev = c->tokpos;
+        p.interleaved = in.rope_interleaved;
+        p.kc = kc;
+        p.vc = vc;
+        p.max_seq = c->max_seq;
+        post_qkv(p, n, c->st);
+        attention(c->att, c->qkv, QL, kc, vc, n, in.n_head, in.n_kv_head, hd, 0, c->tokpos, c->max_seq, c->scores, 0,
+                  c->st);
+        forget_activations(c);
+        matmul(c, c->x, dim, c->att, q_dim, L.wo, n, c->x);
+        // MLP: x = x + down(silu(gate.norm(x)) * up.norm(x)), or its MoE
         if (in.n_expert) {
+            std::vector<const DMat *> need = mats_of(L.gateup);
+            if (L.gate_inp.quant()) need.push_back(&L.gate_inp);
+            want_activations(c, need, c->xb, dim, n, dim, &q8k, &q80);
+            rmsnorm_quant(c->x, dim, L.ffn_norm, dim, n, in.norm_eps, c->xb, dim, q8k, q80, c->st);
             moe_ffn(c, L, n);
-            ffn_out = c->moe_sum;
         } else {
-            matmul(c, c->hb, c->xb, L.gate, n, true);
-            matmul(c, c->hb2, c->xb, L.up, n, false);
-            silu_mul(c->hb, c->hb2, (int64_t)n * in.ffn_dim, c->st);
-            matmul(c, c->xb, c->hb, L.down, n, true);
+            const int F = in.ffn_dim, GU = c->gu_ld;
+            want_activations(c, mats_of(L.gateup), c->xb, dim, n, dim, &q8k, &q80);
+            rmsnorm_quant(c->x, dim, L.ffn_norm, dim, n, in.norm_eps, c->xb, dim, q8k, q80, c->st);
+            project(c, L.gateup, c->hgu, GU, c->xb, dim, n);
+            want_activations(c, {&L.down}, c->hgu, GU, n, F, &q8k, &q80);
+            silu_quant(c->hgu, GU, c->hgu + F, GU, F, n, q8k, q80, c->st);
+            matmul(c, c->x, dim, c->hgu, GU, L.down, n, c->x);
         }
-        add(c->x, c->x, ffn_out, (int64_t)n * dim, c->st);
     }
     if (out_rows > 0) {
-        rmsnorm(c->xb, dim, c->x + (size_t)(n - out_rows) * dim, dim, m->output_norm, dim, out_rows, in.norm_eps,
-                c->st);
-        matmul(c, c->logits, c->xb, m->output, out_rows, true);
+        // final norm and vocabulary projection for the requested rows only
+        const float *xs = c->x + (size_t)(n - out_rows) * dim;
+        want_activations(c, {&m->output}, c->xb, dim, out_rows, dim, &q8k, &q80);
+        rmsnorm_quant(xs, dim, m->output_norm, dim, out_rows, in.norm_eps, c->xb, dim, q8k, q80, c->st);
+        matmul(c, c->logits, in.n_vocab, c->xb, dim, m->output, out_rows);
+    }
+    forget_activations(c);
+}
+
+// One engine step of `chunk` tokens: staged token ids and position, then the forward. The
+// single-token forward runs eagerly once, is captured as a CUDA graph on the next single-token
+// step, and is replayed from then on (positions and ids are read from device memory).
+void step(engine_ctx *c, const int32_t *tokens, int chunk, int out_rows) {
+    c->h_tokpos[0] = c->n_past;
+    memcpy(c->h_tokpos + 1, tokens, (size_t)chunk * 4);
+    SDY_CUDA(cudaMemcpyAsync(c->tokpos, c->h_tokpos, (size_t)(chunk + 1) * 4, cudaMemcpyHostToDevice, c->st));
+    if (chunk != 1 || out_rows != 1 || c->graph_state < 0) {
+        forward(c, chunk, out_rows);
+        return;
+    }
+    if (c->graph_state == 1) {
+        SDY_CUDA(cudaGraphLaunch(c->step_graph, c->st));
+        return;
+    }
+    if (c->graph_state == 0) {
+        forward(c, 1, 1);
+        c->graph_state = 2;
+        return;
+    }
+    cudaGraph_t g = nullptr;
+    bool ok = SDY_CUDA(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
+    if (ok) {
+        forward(c, 1, 1);
+        ok = SDY_CUDA(cudaStreamEndCapture(c->st, &g)) && g;
+    }
+    ok = ok && SDY_CUDA(cudaGraphInstantiate(&c->step_graph, g, 0));
+    if (g) cudaGraphDestroy(g);
+    if (ok) {
+        c->graph_state = 1;
+        SDY_CUDA(cudaGraphLaunch(c->step_graph, c->st));
+    } else {  // capture unavailable: stay eager for this context
+        clear_error();
+        cudaGetLastError();
+        c->graph_state = -1;
+        forward(c, 1, 1);
     }
 }
 
@@ -626,36 +772,31 @@ engine_model *engine_model_load(const char *path, char *err, size_t err_len) {
     }
     for (int l = 0; ok && l < in.n_layer; l++) {
         DLayer &L = m->layers[l];
-        auto nm = [&](const char *suffix) {
-            static thread_local char buf[96];
-            snprintf(buf, sizeof buf, "blk.%d.%s", l, suffix);
-            return buf;
-        };
-        ok = !get_vector(m, nm("attn_norm.weight"), dim, &L.attn_norm, err, err_len) &&
-             !get_vector(m, nm("ffn_norm.weight"), dim, &L.ffn_norm, err, err_len) &&
-             !get_tensor(m, nm("attn_q.weight"), dim, q_dim, 0, &L.wq, err, err_len) &&
-             !get_tensor(m, nm("attn_k.weight"), dim, kv_dim, 0, &L.wk, err, err_len) &&
-             !get_tensor(m, nm("attn_v.weight"), dim, kv_dim, 0, &L.wv, err, err_len) &&
-             !get_tensor(m, nm("attn_output.weight"), q_dim, dim, 0, &L.wo, err, err_len);
+        auto nm = [&](const char *suffix) { return "blk." + std::to_string(l) + "." + suffix; };
+        ok = !get_vector(m, nm("attn_norm.weight").c_str(), dim, &L.attn_norm, err, err_len) &&
+             !get_vector(m, nm("ffn_norm.weight").c_str(), dim, &L.ffn_norm, err, err_len) &&
+             !get_proj(m, {nm("attn_q.weight"), nm("attn_k.weight"), nm("attn_v.weight")}, {q_dim, kv_dim, kv_dim},
+                       dim, 0, &L.qkv, err, err_len) &&
+             !get_tensor(m, nm("attn_output.weight").c_str(), q_dim, dim, 0, &L.wo, err, err_len);
         if (!ok) break;
         if (in.n_expert) {
             int ne = in.n_expert, fe = in.ffn_exp_dim;
-            ok = !get_tensor(m, nm("ffn_gate_inp.weight"), dim, ne, 0, &L.gate_inp, err, err_len) &&
-                 !get_tensor(m, nm("ffn_gate_exps.weight"), dim, fe, ne, &L.gate, err, err_len) &&
-                 !get_tensor(m, nm("ffn_up_exps.weight"), dim, fe, ne, &L.up, err, err_len) &&
-                 !get_tensor(m, nm("ffn_down_exps.weight"), fe, dim, ne, &L.down, err, err_len);
+            ok = !get_tensor(m, nm("ffn_gate_inp.weight").c_str(), dim, ne, 0, &L.gate_inp, err, err_len) &&
+                 !get_proj(m, {nm("ffn_gate_exps.weight"), nm("ffn_up_exps.weight")}, {fe, fe}, dim, ne, &L.gateup, err,
+                           err_len) &&
+                 !get_tensor(m, nm("ffn_down_exps.weight").c_str(), fe, dim, ne, &L.down, err, err_len);
         } else {
-            ok = !get_tensor(m, nm("ffn_gate.weight"), dim, in.ffn_dim, 0, &L.gate, err, err_len) &&
-                 !get_tensor(m, nm("ffn_up.weight"), dim, in.ffn_dim, 0, &L.up, err, err_len) &&
-                 !get_tensor(m, nm("ffn_down.weight"), in.ffn_dim, dim, 0, &L.down, err, err_len);
+            ok = !get_proj(m, {nm("ffn_gate.weight"), nm("ffn_up.weight")}, {in.ffn_dim, in.ffn_dim}, dim, 0,
+                           &L.gateup, err, err_len) &&
+                 !get_tensor(m, nm("ffn_down.weight").c_str(), in.ffn_dim, dim, 0, &L.down, err, err_len);
         }
         if (ok && in.qkv_bias)
-            ok = !get_vector(m, nm("attn_q.bias"), q_dim, &L.bq, err, err_len) &&
-                 !get_vector(m, nm("attn_k.bias"), kv_dim, &L.bk, err, err_len) &&
-                 !get_vector(m, nm("attn_v.bias"), kv_dim, &L.bv, err, err_len);
+            ok = !get_vector(m, nm("attn_q.bias").c_str(), q_dim, &L.bq, err, err_len) &&
+                 !get_vector(m, nm("attn_k.bias").c_str(), kv_dim, &L.bk, err, err_len) &&
+                 !get_vector(m, nm("attn_v.bias").c_str(), kv_dim, &L.bv, err, err_len);
         if (ok && in.qk_norm)
-            ok = !get_vector(m, nm("attn_q_norm.weight"), in.head_dim, &L.q_norm, err, err_len) &&
-                 !get_vector(m, nm("attn_k_norm.weight"), in.head_dim, &L.k_norm, err, err_len);
+            ok = !get_vector(m, nm("attn_q_norm.weight").c_str(), in.head_dim, &L.q_norm, err, err_len) &&
+                 !get_vector(m, nm("attn_k_norm.weight").c_str(), in.head_dim, &L.k_norm, err, err_len);
     }
     if (m->raw) {
         cudaFree(m->raw);
@@ -696,33 +837,36 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
     c->n_batch = n_batch;
     c->logits_all = logits_all != 0;
     c->n_threads = n_threads;
+    if (getenv("SARDYNE_NO_GRAPH")) c->graph_state = -1;
     const engine_model_info &in = m->info;
     const size_t B = n_batch, S = max_seq, hd = in.head_dim;
     const size_t q_dim = (size_t)in.n_head * hd, kv_dim = (size_t)in.n_kv_head * hd;
     const size_t kv = (size_t)in.n_layer * in.n_kv_head * S * hd;
     const size_t ffn = in.n_expert ? in.ffn_exp_dim : in.ffn_dim;
     const size_t K = in.n_expert ? in.n_expert_used : 0, slots = B * K;
-    size_t max_in = std::max<size_t>(std::max<size_t>(in.dim, q_dim), ffn);
-    // Arena layout: one pass to size, one to assign.
-    struct Item { void **dst; size_t bytes; };
+    c->qkv_ld = (int)(q_dim + 2 * kv_dim);
+    c->gu_ld = (int)(2 * ffn);
+    const size_t tmp_n = std::max<size_t>((size_t)in.dim, (size_t)in.n_vocab) * B;
+    struct Item {
+        void **dst;
+        size_t bytes;
+    };
     std::vector<Item> items = {
         {(void **)&c->k_cache, kv * 4}, {(void **)&c->v_cache, kv * 4},
         {(void **)&c->rope_cos, S * hd / 2 * 4}, {(void **)&c->rope_sin, S * hd / 2 * 4},
-        {(void **)&c->x, B * in.dim * 4}, {(void **)&c->xb, B * in.dim * 4}, {(void **)&c->q, B * q_dim * 4},
-        {(void **)&c->k, B * kv_dim * 4}, {(void **)&c->v, B * kv_dim * 4}, {(void **)&c->att, B * q_dim * 4},
-        {(void **)&c->hb, B * ffn * 4}, {(void **)&c->hb2, B * ffn * 4},
+        {(void **)&c->x, B * in.dim * 4}, {(void **)&c->xb, B * in.dim * 4},
+        {(void **)&c->qkv, B * c->qkv_ld * 4}, {(void **)&c->att, B * q_dim * 4},
+        {(void **)&c->hgu, B * c->gu_ld * 4}, {(void **)&c->tmp, tmp_n * 4},
         {(void **)&c->scores, B * in.n_head * S * 4},
         {(void **)&c->logits, (c->logits_all ? B : 1) * in.n_vocab * 4},
-        {(void **)&c->tok_ids, B * 4},
+        {(void **)&c->tokpos, (B + 1) * 4},
     };
     if (in.n_expert) {
         items.push_back({(void **)&c->moe_probs, B * in.n_expert * 4});
         items.push_back({(void **)&c->moe_w, slots * 4});
         items.push_back({(void **)&c->moe_top, slots * 4});
-        items.push_back({(void **)&c->moe_g, slots * ffn * 4});
-        items.push_back({(void **)&c->moe_u, slots * ffn * 4});
+        items.push_back({(void **)&c->moe_gu, slots * 2 * ffn * 4});
         items.push_back({(void **)&c->moe_y, slots * in.dim * 4});
-        items.push_back({(void **)&c->moe_sum, B * in.dim * 4});
     }
     size_t xq_cap = 0;
     for (int vt : {T_Q8_0, T_Q8_K}) {
@@ -731,7 +875,6 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
             if (nin % be == 0) xq_cap = std::max(xq_cap, xq_bytes(vt, (int)nin, (int)B));
         if (in.n_expert && ffn % be == 0) xq_cap = std::max(xq_cap, xq_bytes(vt, (int)ffn, (int)slots));
     }
-    (void)max_in;
     items.push_back({&c->xq_buf[0], xq_cap});
     items.push_back({&c->xq_buf[1], xq_cap});
     size_t total = 0;
@@ -748,7 +891,7 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
     }
     size_t lbytes = (c->logits_all ? B : 1) * in.n_vocab * 4;
     if (!SDY_CUDA(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking)) ||
-        !SDY_CUDA(cudaMallocHost(&c->h_logits, lbytes))) {
+        !SDY_CUDA(cudaMallocHost(&c->h_logits, lbytes)) || !SDY_CUDA(cudaMallocHost(&c->h_tokpos, (B + 1) * 4))) {
         put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
         engine_ctx_free(c);
         return nullptr;
@@ -766,9 +909,11 @@ int32_t engine_ctx_n_threads(const engine_ctx *c) { return c ? c->n_threads : 0;
 
 void engine_ctx_free(engine_ctx *c) {
     if (!c) return;
+    if (c->step_graph) cudaGraphExecDestroy(c->step_graph);
     if (c->st) cudaStreamDestroy(c->st);
     if (c->arena) cudaFree(c->arena);
     if (c->h_logits) cudaFreeHost(c->h_logits);
+    if (c->h_tokpos) cudaFreeHost(c->h_tokpos);
     delete c;
 }
 
@@ -801,8 +946,8 @@ int engine_eval(engine_ctx *c, const int32_t *tokens, int32_t n) {
         int chunk = std::min(n - done, c->n_batch);
         bool last = done + chunk == n;
         out_rows = last ? (c->logits_all ? chunk : 1) : 0;
-        SDY_CUDA(cudaMemcpyAsync(c->tok_ids, tokens + done, (size_t)chunk * 4, cudaMemcpyHostToDevice, c->st));
-        forward(c, chunk, out_rows);
+        step(c, tokens + done, chunk, out_rows);
+        if (!last) SDY_CUDA(cudaStreamSynchronize(c->st));  // the staging buffer is reused by the next chunk
         c->n_past += chunk;
         done += chunk;
     }

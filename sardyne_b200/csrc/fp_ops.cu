@@ -197,14 +197,16 @@ void rope(float *x, int64_t ldx, int n_tok, int n_heads, int head_dim, const flo
 
 // One (head, token) per block (ops.c:405-423): scores over n_kv = pos0 + t + 1 positions (the
 // causal mask), one thread per key; softmax; then out[i] = sum_j p_j v_j[i] in key order, one
-// thread per output element. q: [n_tok][n_head*hd]; k/v cache: [n_kv_head][stride][hd];
+// thread per output element. q: token t at q + t*ldq, heads of hd; k/v cache:
+// [n_kv_head][stride][hd]; the first token's position is *pos_dev when given, else pos0;
 // scratch: n_tok*n_head*stride floats.
-__global__ void attention_kernel(float *out, const float *q, const float *kc, const float *vc, int n_head,
-                                 int n_kv_head, int hd, int pos0, int stride, float *scratch, int fixed_nkv) {
+__global__ void attention_kernel(float *out, const float *q, int64_t ldq, const float *kc, const float *vc, int n_head,
+                                 int n_kv_head, int hd, int pos0, const int32_t *pos_dev, int stride, float *scratch,
+                                 int fixed_nkv) {
     int t = blockIdx.y, h = blockIdx.x;
-    int n_kv = fixed_nkv > 0 ? fixed_nkv : pos0 + t + 1;
+    int n_kv = fixed_nkv > 0 ? fixed_nkv : (pos_dev ? *pos_dev : pos0) + t + 1;
     int n_rep = n_head / n_kv_head;
-    const float *qv = q + ((size_t)t * n_head + h) * hd;
+    const float *qv = q + (size_t)t * ldq + (size_t)h * hd;
     const float *kh = kc + (size_t)(h / n_rep) * stride * hd;
     const float *vh = vc + (size_t)(h / n_rep) * stride * hd;
     float *sc = scratch + ((size_t)t * n_head + h) * stride;
@@ -224,11 +226,12 @@ __global__ void attention_kernel(float *out, const float *q, const float *kc, co
     }
 }
 
-void attention(float *out, const float *q, const float *kc, const float *vc, int n_tok, int n_head, int n_kv_head,
-               int hd, int pos0, int stride, float *scratch, int fixed_nkv, cudaStream_t s) {
+void attention(float *out, const float *q, int64_t ldq, const float *kc, const float *vc, int n_tok, int n_head,
+               int n_kv_head, int hd, int pos0, const int32_t *pos_dev, int stride, float *scratch, int fixed_nkv,
+               cudaStream_t s) {
     if (n_tok <= 0) return;
-    attention_kernel<<<dim3(n_head, n_tok), 128, 0, s>>>(out, q, kc, vc, n_head, n_kv_head, hd, pos0, stride, scratch,
-                                                         fixed_nkv);
+    attention_kernel<<<dim3(n_head, n_tok), 128, 0, s>>>(out, q, ldq, kc, vc, n_head, n_kv_head, hd, pos0, pos_dev,
+                                                         stride, scratch, fixed_nkv);
     SDY_LAUNCHED();
 }
 

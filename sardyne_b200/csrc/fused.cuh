@@ -1,0 +1,38 @@
+// Launchers of the fused per-token kernels (fused.cu). All asynchronous on stream s.
+#pragma once
+#include "common.cuh"
+
+namespace sdy {
+
+// xb = RMSNorm(x) * w (optional f32 copy) and its quantization into q8k and/or q80 (either may be null).
+void rmsnorm_quant(const float *x, int64_t ldx, const float *w, int n, int rows, float eps, float *xb, int64_t ldb,
+                   const XQ *q8k, const XQ *q80, cudaStream_t s);
+// g = silu(g) * u in place, then quantized into q8k and/or q80.
+void silu_quant(float *g, int64_t ldg, const float *u, int64_t ldu, int n, int rows, const XQ *q8k, const XQ *q80,
+                cudaStream_t s);
+
+struct PostQKV {
+    float *q, *k;
+    const float *v;
+    int64_t ldq, ldk, ldv;          // token strides
+    const float *bq, *bk, *bv;      // biases or null
+    const float *q_norm, *k_norm;   // qk-norm weights or null
+    int n_head, n_kv_head, hd;
+    float eps;
+    const float *cos, *sin;         // RoPE tables [max_seq][hd/2]
+    const int32_t *pos_dev;         // position of token 0 read on the device, or null: pos0
+    int pos0, interleaved;
+    float *kc, *vc;                 // this layer's cache [n_kv_head][max_seq][hd]
+    int max_seq;
+};
+// Bias, qk-norm, RoPE on q and k, then k and v into the KV cache.
+void post_qkv(const PostQKV &p, int n_tok, cudaStream_t s);
+
+// Float router: top [n_tok][k] expert ids and renormalised weights (probs_out optional).
+void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, int n_tok,
+                 int32_t *top, float *wout, float *probs_out, cudaStream_t s);
+// x[t] += sum over t's k slots in ascending expert id of w * y[slot].
+void moe_combine(const float *y, int64_t ldy, const int32_t *top, const float *w, int k, int dim, int n_tok, float *x,
+                 int64_t ldx, cudaStream_t s);
+
+}  // namespace sdy

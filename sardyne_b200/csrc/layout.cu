@@ -3,6 +3,7 @@
 // (reference csrc/quant.c:13-144); every fp32 step uses an explicit round-to-nearest intrinsic
 // so nothing is contracted into an FMA (the reference builds with -ffp-contract=off).
 #include "common.cuh"
+#include "quant_device.cuh"
 
 namespace sdy {
 
@@ -113,80 +114,6 @@ void dequant_rows(const QMat &w, const int32_t *row_ids, int n_ids, int64_t firs
 }
 
 // ------------------------------------------------------------------------------ activation quantization
-
-// Q8_K (quant.c:118-144): one warp per 256-element block, 8 consecutive elements per lane.
-// The scale comes from the FIRST element of largest magnitude, with its sign.
-__device__ void quant_q8k_block(const float *x, int t, int blk, const XQ &xq) {
-    const int lane = threadIdx.x & 31;
-    float4 a = *(const float4 *)(x + blk * 256 + lane * 8);
-    float4 c = *(const float4 *)(x + blk * 256 + lane * 8 + 4);
-    float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-    float amax = 0.0f;
-    int idx = 0x7FFFFFFF;
-    for (int i = 0; i < 8; i++)
-        if (fabsf(v[i]) > amax) { amax = fabsf(v[i]); idx = lane * 8 + i; }
-    for (int o = 16; o; o >>= 1) {
-        float a2 = __shfl_xor_sync(0xffffffffu, amax, o);
-        int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (a2 > amax || (a2 == amax && i2 < idx)) { amax = a2; idx = i2; }
-    }
-    int8_t *qs = xq.qs + (size_t)t * xq.qrow + blk * XQ_SPAN + lane * 8;
-    int16_t *bs = (int16_t *)xq.sums + ((size_t)t * xq.nbx + blk) * 16;
-    float *dd = xq.d + (size_t)t * xq.nbx + blk;
-    if (amax == 0.0f) {
-        *(uint2 *)qs = make_uint2(0, 0);
-        if ((lane & 1) == 0) bs[lane >> 1] = 0;
-        if (lane == 0) *dd = 0.0f;
-        return;
-    }
-    float vmax = __shfl_sync(0xffffffffu, v[idx & 7], (idx >> 3) & 31);
-    float iscale = __fdiv_rn(-127.0f, vmax);
-    int q[8], sum = 0;
-    for (int i = 0; i < 8; i++) {
-        int r = __float2int_rn(__fmul_rn(iscale, v[i]));  // round half to even (quant.c:111-116)
-        q[i] = r < 127 ? r : 127;
-        sum += q[i];
-    }
-    uint32_t lo = (q[0] & 255) | ((q[1] & 255) << 8) | ((q[2] & 255) << 16) | ((uint32_t)(q[3] & 255) << 24);
-    uint32_t hi = (q[4] & 255) | ((q[5] & 255) << 8) | ((q[6] & 255) << 16) | ((uint32_t)(q[7] & 255) << 24);
-    *(uint2 *)qs = make_uint2(lo, hi);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // 16 elements = 2 lanes
-    if ((lane & 1) == 0) bs[lane >> 1] = (int16_t)sum;
-    if (lane == 0) *dd = __fdiv_rn(1.0f, iscale);
-}
-
-// Q8_0 (quant.c:98-108): 4 lanes per 32-element block, 8 elements per lane.
-__device__ void quant_q80_span(const float *x, int t, int span, int n_in, const XQ &xq) {
-    const int lane = threadIdx.x & 31;
-    const int e0 = span * 256 + lane * 8;
-    const bool live = e0 < n_in;  // n_in is a multiple of 32: a 4-lane group is all live or all dead
-    float v[8];
-    if (live) {
-        float4 a = *(const float4 *)(x + e0), c = *(const float4 *)(x + e0 + 4);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
-    } else {
-        for (int i = 0; i < 8; i++) v[i] = 0.0f;
-    }
-    float amax = 0.0f;
-    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    float d = __fdiv_rn(amax, 127.0f);
-    float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    int q[8], sum = 0;
-    for (int i = 0; i < 8; i++) { q[i] = (int)roundf(__fmul_rn(v[i], id)); sum += q[i]; }
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    if (!live) return;
-    uint32_t lo = (q[0] & 255) | ((q[1] & 255) << 8) | ((q[2] & 255) << 16) | ((uint32_t)(q[3] & 255) << 24);
-    uint32_t hi = (q[4] & 255) | ((q[5] & 255) << 8) | ((q[6] & 255) << 16) | ((uint32_t)(q[7] & 255) << 24);
-    *(uint2 *)(xq.qs + (size_t)t * xq.qrow + span * XQ_SPAN + lane * 8) = make_uint2(lo, hi);
-    if ((lane & 3) == 0) {
-        int blk = e0 >> 5;
-        xq.d[(size_t)t * xq.nbx + blk] = __half2float(__float2half_rn(d));
-        ((int32_t *)xq.sums)[(size_t)t * xq.nbx + blk] = sum;
-    }
-}
 
 __global__ void quantize_kernel(int vtype, const float *__restrict__ x, int64_t ldx, int n_in, XQ xq) {
     const int t = blockIdx.y;

@@ -460,7 +460,7 @@ void op_attention(float *out, const float *q, const float *k_cache, const float 
     float *dq = upload(s, 0, q, qn), *dk = upload(s, 1, k_cache, cn), *dv = upload(s, 2, v_cache, cn);
     float *dout = upload(s, 3, nullptr, qn), *dsc = upload(s, 4, nullptr, (size_t)n_head * stride);
     if (!dq || !dk || !dv || !dout || !dsc) return;
-    attention(dout, dq, dk, dv, 1, n_head, n_kv_head, head_dim, 0, stride, dsc, n_kv, s->st);
+    attention(dout, dq, (int64_t)qn, dk, dv, 1, n_head, n_kv_head, head_dim, 0, nullptr, stride, dsc, n_kv, s->st);
     download(s, out, dout, qn);
 }
 

@@ -50,6 +50,7 @@ struct Args {
     int nbx;            // XQ blocks per token
     float *out;
     int64_t ldo, row0, row1, out_row0;
+    const float *residual;  // when set: out = residual + product (same indexing as out)
     // Gathered experts (MoE): grid.y = slot; slot s multiplies expert slot_expert[s], whose
     // groups start at expert * gpe, with the activations of token s / tok_div, into out + s*ldo_slot.
     const int32_t *slot_expert;
@@ -302,7 +303,9 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
             const float *tp = terms + (size_t)t * nb * rows + rl;
             float acc = 0.0f;
             for (int b = 0; b < nb; b++) acc = __fadd_rn(acc, tp[(size_t)b * rows]);
-            out[(size_t)t * a.ldo + (row - a.out_row0)] = acc;
+            const size_t o = (size_t)t * a.ldo + (row - a.out_row0);
+            // residual stream: x = x + W.a, the reference's `x[i] += xb[i]` (model_llama.c:804,820)
+            out[o] = a.residual ? __fadd_rn(a.residual[o], acc) : acc;
         }
         __syncthreads();
     }
@@ -385,7 +388,7 @@ bool plan_launch(int type, int nb, int qrow, int64_t ng, int64_t cta_cap, int nt
 }  // namespace
 
 void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
-             cudaStream_t s) {
+             cudaStream_t s, const float *residual) {
     if (row1 <= row0 || xq.n_tok <= 0) return;
     if (xq.vtype != vec_dot_type(w.type) || xq.n_in != w.n_in) {
         set_error("qmatvec: activation type/size does not match the weights");
@@ -415,6 +418,7 @@ void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0,
         a.qrow = xq.qrow;
         a.nbx = xq.nbx;
         a.out = out + (size_t)t0 * ldo;
+        a.residual = residual ? residual + (size_t)t0 * ldo : nullptr;
         a.ldo = ldo;
         a.row0 = row0;
         a.row1 = row1;
