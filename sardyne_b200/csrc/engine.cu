@@ -581,7 +581,7 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n) {
     const int dim = in.dim, fe = in.ffn_exp_dim, ne = in.n_expert, k = in.n_expert_used;
     const DMat &r = L.gate_inp;
     if (!r.quant()) {
-        router_topk(c->xb, dim, r.f, r.type, dim, ne, k, n, c->moe_top, c->moe_w, nullptr, c->st);
+        router_topk(c->xb, dim, r.f, r.type, dim, ne, k, n, c->moe_top, c->moe_w, c->moe_probs, c->st);
     } else {
         matmul(c, c->moe_probs, ne, c->xb, dim, r, n);
         softmax(c->moe_probs, ne, ne, n, c->st);

@@ -195,43 +195,87 @@ void rope(float *x, int64_t ldx, int n_tok, int n_heads, int head_dim, const flo
     SDY_LAUNCHED();
 }
 
-// One (head, token) per block (ops.c:405-423): scores over n_kv = pos0 + t + 1 positions (the
-// causal mask), one thread per key; softmax; then out[i] = sum_j p_j v_j[i] in key order, one
-// thread per output element. q: token t at q + t*ldq, heads of hd; k/v cache:
-// [n_kv_head][stride][hd]; the first token's position is *pos_dev when given, else pos0;
-// scratch: n_tok*n_head*stride floats.
+// One (head, token) per block of ATT_THREADS (ops.c:405-423): scores over n_kv = pos0 + t + 1
+// positions (the causal mask); softmax; then out[i] = sum_j p_j v_j[i] in key order.
+// K and V are staged through shared memory in tiles read with coalesced 16-byte loads: a K tile
+// holds one key per thread (rows padded to hd+1 floats, so the threads' dot products, each over
+// its own row, hit distinct banks); a V tile holds as many keys as fit the same space, and thread
+// i adds p_j * v_j[i] for the tile's keys in order. q: token t at q + t*ldq, heads of hd (a
+// multiple of 4, at most 2*ATT_THREADS); k/v cache [n_kv_head][stride][hd]; the first token's
+// position is *pos_dev when given, else pos0; scratch: n_tok*n_head*stride floats (scores).
+constexpr int ATT_THREADS = 128;
+__host__ __device__ inline int att_smem_floats(int hd) { return hd + ATT_THREADS * (hd + 1) + 2 * ATT_THREADS + 8; }
+
 __global__ void attention_kernel(float *out, const float *q, int64_t ldq, const float *kc, const float *vc, int n_head,
                                  int n_kv_head, int hd, int pos0, const int32_t *pos_dev, int stride, float *scratch,
                                  int fixed_nkv) {
-    int t = blockIdx.y, h = blockIdx.x;
-    int n_kv = fixed_nkv > 0 ? fixed_nkv : (pos_dev ? *pos_dev : pos0) + t + 1;
-    int n_rep = n_head / n_kv_head;
+    extern __shared__ __align__(16) float sm[];
+    const int t = blockIdx.y, h = blockIdx.x, tid = threadIdx.x;
+    const int n_kv = fixed_nkv > 0 ? fixed_nkv : (pos_dev ? *pos_dev : pos0) + t + 1;
+    const int n_rep = n_head / n_kv_head, ldt = hd + 1, hd4 = hd / 4;
     const float *qv = q + (size_t)t * ldq + (size_t)h * hd;
     const float *kh = kc + (size_t)(h / n_rep) * stride * hd;
     const float *vh = vc + (size_t)(h / n_rep) * stride * hd;
     float *sc = scratch + ((size_t)t * n_head + h) * stride;
+    float *qs = sm, *tile = sm + ((hd + 3) & ~3), *ps = tile + ATT_THREADS * ldt;
     const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
-    for (int j = threadIdx.x; j < n_kv; j += blockDim.x) {
-        const float *kj = kh + (size_t)j * hd;
-        sc[j] = __fmul_rn(dot4(qv, [&](int i) { return kj[i]; }, hd), scale);
+    for (int i = tid; i < hd; i += ATT_THREADS) qs[i] = qv[i];
+    for (int j0 = 0; j0 < n_kv; j0 += ATT_THREADS) {
+        const int nk = min(ATT_THREADS, n_kv - j0);
+        __syncthreads();
+        for (int idx = tid; idx < nk * hd4; idx += ATT_THREADS) {
+            const int j = idx / hd4, i = (idx - j * hd4) * 4;
+            const float4 v = *(const float4 *)(kh + (size_t)(j0 + j) * hd + i);
+            float *d = tile + j * ldt + i;
+            d[0] = v.x; d[1] = v.y; d[2] = v.z; d[3] = v.w;
+        }
+        __syncthreads();
+        if (tid < nk) {
+            const float *row = tile + tid * ldt;
+            sc[j0 + tid] = __fmul_rn(dot4(qs, [&](int i) { return row[i]; }, hd), scale);
+        }
     }
     __syncthreads();
     softmax_block(sc, n_kv);
     __syncthreads();
-    float *ov = out + ((size_t)t * n_head + h) * hd;
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-        float acc = 0.0f;
-        for (int j = 0; j < n_kv; j++) acc = __fadd_rn(acc, __fmul_rn(sc[j], vh[(size_t)j * hd + i]));
-        ov[i] = acc;
+    const int tv = (ATT_THREADS * ldt) / hd;  // keys per V tile
+    float acc0 = 0.0f, acc1 = 0.0f;
+    const int i0 = tid, i1 = tid + ATT_THREADS;
+    for (int j0 = 0; j0 < n_kv; j0 += tv) {
+        const int nv = min(tv, n_kv - j0);
+        __syncthreads();
+        for (int idx = tid; idx < nv * hd4; idx += ATT_THREADS)
+            *(float4 *)(tile + idx * 4) = *(const float4 *)(vh + (size_t)j0 * hd + idx * 4);
+        for (int j = tid; j < nv; j += ATT_THREADS) ps[j] = sc[j0 + j];
+        __syncthreads();
+        for (int j = 0; j < nv; j++) {
+            const float p = ps[j];
+            if (i0 < hd) acc0 = __fadd_rn(acc0, __fmul_rn(p, tile[j * hd + i0]));
+            if (i1 < hd) acc1 = __fadd_rn(acc1, __fmul_rn(p, tile[j * hd + i1]));
+        }
     }
+    float *ov = out + ((size_t)t * n_head + h) * hd;
+    if (i0 < hd) ov[i0] = acc0;
+    if (i1 < hd) ov[i1] = acc1;
 }
 
 void attention(float *out, const float *q, int64_t ldq, const float *kc, const float *vc, int n_tok, int n_head,
                int n_kv_head, int hd, int pos0, const int32_t *pos_dev, int stride, float *scratch, int fixed_nkv,
                cudaStream_t s) {
     if (n_tok <= 0) return;
-    attention_kernel<<<dim3(n_head, n_tok), 128, 0, s>>>(out, q, ldq, kc, vc, n_head, n_kv_head, hd, pos0, pos_dev,
-                                                         stride, scratch, fixed_nkv);
+    if (hd % 4 || hd > 2 * ATT_THREADS) {
+        set_error("attention: head_dim %d not supported (multiple of 4, at most %d)", hd, 2 * ATT_THREADS);
+        return;
+    }
+    const size_t smem = (size_t)att_smem_floats(hd) * 4;
+    static bool configured = false;
+    if (!configured) {
+        SDY_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      att_smem_floats(2 * ATT_THREADS) * 4));
+        configured = true;
+    }
+    attention_kernel<<<dim3(n_head, n_tok), ATT_THREADS, smem, s>>>(out, q, ldq, kc, vc, n_head, n_kv_head, hd, pos0,
+                                                                    pos_dev, stride, scratch, fixed_nkv);
     SDY_LAUNCHED();
 }
 

@@ -6,6 +6,8 @@
 //   silu_quant     op_silu_mul (ops.c:366-371) + op_quantize_rows
 //   router_topk    F32 router matvec + op_softmax + moe_select (model_llama.c:653-684)
 //   moe_combine    sum over a token's experts in ascending id + residual add (model_llama.c:734-750, 820)
+// In the norm and SiLU kernels lane l of warp w owns elements 256w + 8l .. +7 in registers, so
+// each warp quantizes its own 256-element span without staging through shared memory.
 #include "fused.cuh"
 #include "quant_device.cuh"
 
@@ -35,47 +37,51 @@ __device__ float bmax_f(float v, float *part) {
     return v;
 }
 
-// Quantize the row in shared memory into the requested activation types (warps take 256-spans).
-__device__ void quantize_smem_row(const float *row, int n, int t, const XQ &q8k, const XQ &q80) {
-    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, spans = (n + 255) / 256;
-    for (int sp = warp; sp < spans; sp += nw) {
-        if (q8k.qs) quant_q8k_block(row, t, sp, q8k);
-        if (q80.qs) quant_q80_span(row, t, sp, n, q80);
-    }
+// Quantize the warp's span (values in registers) into the requested activation types.
+__device__ __forceinline__ void quantize_span(const float v[8], int e0, int n, int t, int span, const XQ &q8k,
+                                              const XQ &q80) {
+    if (q8k.qs) quant_q8k_vals(v, t, span, q8k);  // only requested when n is a multiple of 256
+    if (q80.qs) quant_q80_vals(v, e0 < n, t, span, q80);
 }
 
+// One block per row, thread i owning elements 8i..8i+7 (blockDim = n/8 rounded up to a warp).
 __global__ void rmsnorm_quant_kernel(const float *x, int64_t ldx, const float *w, int n, float eps, float *xb,
                                      int64_t ldb, XQ q8k, XQ q80) {
-    extern __shared__ __align__(16) float row[];
     __shared__ double part[32];
-    const int t = blockIdx.x;
+    const int t = blockIdx.x, e0 = threadIdx.x * 8;
     const float *xv = x + (size_t)t * ldx;
+    float v[8];
     double ss = 0.0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += (double)xv[i] * xv[i];
+    for (int j = 0; j < 8; j++) {
+        v[j] = e0 + j < n ? xv[e0 + j] : 0.0f;
+        ss += (double)v[j] * v[j];
+    }
     ss = bsum_d(ss, part);
     const float scale = (float)(1.0 / sqrt(ss / n + (double)eps));
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float v = __fmul_rn(__fmul_rn(xv[i], scale), w[i]);
-        row[i] = v;
-        if (xb) xb[(size_t)t * ldb + i] = v;
+    for (int j = 0; j < 8; j++) {
+        v[j] = e0 + j < n ? __fmul_rn(__fmul_rn(v[j], scale), w[e0 + j]) : 0.0f;
+        if (xb && e0 + j < n) xb[(size_t)t * ldb + e0 + j] = v[j];
     }
-    __syncthreads();
-    quantize_smem_row(row, n, t, q8k, q80);
+    quantize_span(v, e0, n, t, threadIdx.x >> 5, q8k, q80);
 }
 
+// grid (ceil(n/2048), rows), 256 threads: warp w of block b owns span 8b + w.
 __global__ void silu_quant_kernel(float *g, int64_t ldg, const float *u, int64_t ldu, int n, XQ q8k, XQ q80) {
-    extern __shared__ __align__(16) float row[];
-    const int t = blockIdx.x;
+    const int t = blockIdx.y, span = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (span * 256 >= n) return;  // whole warps leave together
+    const int e0 = span * 256 + (threadIdx.x & 31) * 8;
     float *gv = g + (size_t)t * ldg;
     const float *uv = u + (size_t)t * ldu;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float a = gv[i];
-        float h = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, exp_cr(-a))), uv[i]);
-        row[i] = h;
-        gv[i] = h;
+    float v[8];
+    for (int j = 0; j < 8; j++) {
+        v[j] = 0.0f;
+        if (e0 + j < n) {
+            float a = gv[e0 + j];
+            v[j] = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, exp_cr(-a))), uv[e0 + j]);
+            gv[e0 + j] = v[j];
+        }
     }
-    __syncthreads();
-    quantize_smem_row(row, n, t, q8k, q80);
+    quantize_span(v, e0, n, t, span, q8k, q80);
 }
 
 // One block per (head, token). Heads [0, n_head) are q heads; [n_head, n_head + n_kv_head) are
@@ -124,33 +130,51 @@ __global__ void post_qkv_kernel(PostQKV p) {
     }
 }
 
-// Router for float weights, one block per token: logits (the reference's scalar dot order),
-// softmax, stable top-k with ties to the lowest index, weights renormalised by their sum.
-__global__ void router_topk_kernel(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k,
-                                   int32_t *top, float *wout, float *probs_out) {
+// Router logits for float weights: one warp per expert row. The warp copies x and its row into
+// shared memory with coalesced loads; lanes 0..3 then run the reference's four accumulator
+// chains (ops.c:155-167: s_k over i = 4g + k, the tail into s0) and combine (s0+s1)+(s2+s3).
+constexpr int ROUTER_WARPS = 4;
+__global__ void router_logits_kernel(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne,
+                                     float *logits) {
+    extern __shared__ __align__(16) float sm[];
+    float *xs = sm, *rows = sm + dim;
+    const int t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e = blockIdx.x * ROUTER_WARPS + warp;
+    const float *xv = x + (size_t)t * ldx;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) xs[i] = xv[i];
+    float *row = rows + (size_t)warp * dim;
+    if (e < ne) {
+        const size_t base = (size_t)e * dim;
+        for (int i = lane; i < dim; i += 32) {
+            float v;
+            if (wtype == T_F32) v = ((const float *)w)[base + i];
+            else if (wtype == T_F16) v = __half2float(((const __half *)w)[base + i]);
+            else v = __uint_as_float((uint32_t)((const uint16_t *)w)[base + i] << 16);
+            row[i] = v;
+        }
+    }
+    __syncthreads();
+    if (e >= ne) return;
+    float s = 0.0f;
+    if (lane < 4) {
+        const int groups = dim / 4;
+        for (int g = 0; g < groups; g++) s = __fadd_rn(s, __fmul_rn(xs[4 * g + lane], row[4 * g + lane]));
+        if (lane == 0)
+            for (int i = groups * 4; i < dim; i++) s = __fadd_rn(s, __fmul_rn(xs[i], row[i]));
+    }
+    const float s1 = __shfl_sync(0xffffffffu, s, 1), s2 = __shfl_sync(0xffffffffu, s, 2),
+                s3 = __shfl_sync(0xffffffffu, s, 3);
+    if (lane == 0) logits[(size_t)t * ne + e] = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
+}
+
+// Softmax (ops.c:353-364) and stable top-k with ties to the lowest index, weights renormalised
+// by their float sum (model_llama.c:653-666), one block per token.
+__global__ void softmax_topk_kernel(const float *logits, int ne, int k, int32_t *top, float *wout) {
     extern __shared__ __align__(16) float prob[];
     __shared__ double dpart[32];
     __shared__ float fpart[32];
     const int t = blockIdx.x;
-    const float *xv = x + (size_t)t * ldx;
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) {
-        size_t base = (size_t)e * dim;
-        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-        auto wv = [&](int i) -> float {
-            if (wtype == T_F32) return ((const float *)w)[base + i];
-            if (wtype == T_F16) return __half2float(((const __half *)w)[base + i]);
-            return __uint_as_float((uint32_t)((const uint16_t *)w)[base + i] << 16);
-        };
-        int i = 0;
-        for (; i + 4 <= dim; i += 4) {
-            s0 = __fadd_rn(s0, __fmul_rn(xv[i], wv(i)));
-            s1 = __fadd_rn(s1, __fmul_rn(xv[i + 1], wv(i + 1)));
-            s2 = __fadd_rn(s2, __fmul_rn(xv[i + 2], wv(i + 2)));
-            s3 = __fadd_rn(s3, __fmul_rn(xv[i + 3], wv(i + 3)));
-        }
-        for (; i < dim; i++) s0 = __fadd_rn(s0, __fmul_rn(xv[i], wv(i)));
-        prob[e] = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
-    }
+    for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = logits[(size_t)t * ne + e];
     __syncthreads();
     float m = -INFINITY;
     for (int e = threadIdx.x; e < ne; e += blockDim.x) m = fmaxf(m, prob[e]);
@@ -165,8 +189,6 @@ __global__ void router_topk_kernel(const float *x, int64_t ldx, const void *w, i
     const float inv = (float)(1.0 / sum);
     for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = __fmul_rn(prob[e], inv);
     __syncthreads();
-    if (probs_out)
-        for (int e = threadIdx.x; e < ne; e += blockDim.x) probs_out[(size_t)t * ne + e] = prob[e];
     if (threadIdx.x != 0) return;
     int32_t *tp = top + (size_t)t * k;
     int n = 0;
@@ -205,27 +227,30 @@ __global__ void moe_combine_kernel(const float *y, int64_t ldy, const int32_t *t
     }
 }
 
-int row_threads(int n) { return n >= 1024 ? 512 : n >= 256 ? 256 : 128; }
+XQ pick(const XQ *q) {
+    XQ a = q ? *q : XQ();
+    if (!q) a.qs = nullptr;
+    return a;
+}
 
 }  // namespace
 
 void rmsnorm_quant(const float *x, int64_t ldx, const float *w, int n, int rows, float eps, float *xb, int64_t ldb,
                    const XQ *q8k, const XQ *q80, cudaStream_t s) {
     if (rows <= 0) return;
-    XQ a = q8k ? *q8k : XQ(), b = q80 ? *q80 : XQ();
-    if (!q8k) a.qs = nullptr;
-    if (!q80) b.qs = nullptr;
-    rmsnorm_quant_kernel<<<rows, row_threads(n), (size_t)n * 4, s>>>(x, ldx, w, n, eps, xb, ldb, a, b);
+    if (n > 8192) {
+        set_error("rmsnorm_quant: rows of %d elements exceed 8192", n);
+        return;
+    }
+    const int threads = ((n + 7) / 8 + 31) / 32 * 32;
+    rmsnorm_quant_kernel<<<rows, threads, 0, s>>>(x, ldx, w, n, eps, xb, ldb, pick(q8k), pick(q80));
     SDY_LAUNCHED();
 }
 
 void silu_quant(float *g, int64_t ldg, const float *u, int64_t ldu, int n, int rows, const XQ *q8k, const XQ *q80,
                 cudaStream_t s) {
     if (rows <= 0) return;
-    XQ a = q8k ? *q8k : XQ(), b = q80 ? *q80 : XQ();
-    if (!q8k) a.qs = nullptr;
-    if (!q80) b.qs = nullptr;
-    silu_quant_kernel<<<rows, row_threads(n), (size_t)n * 4, s>>>(g, ldg, u, ldu, n, a, b);
+    silu_quant_kernel<<<dim3((n + 2047) / 2048, rows), 256, 0, s>>>(g, ldg, u, ldu, n, pick(q8k), pick(q80));
     SDY_LAUNCHED();
 }
 
@@ -236,9 +261,22 @@ void post_qkv(const PostQKV &p, int n_tok, cudaStream_t s) {
 }
 
 void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, int n_tok,
-                 int32_t *top, float *wout, float *probs_out, cudaStream_t s) {
+                 int32_t *top, float *wout, float *logits, cudaStream_t s) {
     if (n_tok <= 0) return;
-    router_topk_kernel<<<n_tok, 128, (size_t)ne * 4, s>>>(x, ldx, w, wtype, dim, ne, k, top, wout, probs_out);
+    const size_t smem = (size_t)(ROUTER_WARPS + 1) * dim * 4;
+    if (smem > 200 * 1024) {
+        set_error("router_topk: hidden size %d too large", dim);
+        return;
+    }
+    static bool configured = false;
+    if (!configured) {
+        SDY_CUDA(cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        configured = true;
+    }
+    router_logits_kernel<<<dim3((ne + ROUTER_WARPS - 1) / ROUTER_WARPS, n_tok), 32 * ROUTER_WARPS, smem, s>>>(
+        x, ldx, w, wtype, dim, ne, logits);
+    SDY_LAUNCHED();
+    softmax_topk_kernel<<<n_tok, 128, (size_t)ne * 4, s>>>(logits, ne, k, top, wout);
     SDY_LAUNCHED();
 }
 

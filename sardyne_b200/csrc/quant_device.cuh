@@ -1,17 +1,16 @@
 // Warp-level activation quantizers shared by the standalone quantize kernel and the fused
 // norm/activation kernels: byte-exact Q8_K and Q8_0 (reference csrc/quant.c:98-144).
+//
+// Every function is warp-collective: lane l holds elements span*256 + 8l .. +7 of token t.
 #pragma once
 #include "common.cuh"
 
 namespace sdy {
 
-// Q8_K (quant.c:118-144): one warp per 256-element block, 8 consecutive elements per lane.
-// The scale comes from the FIRST element of largest magnitude, with its sign.
-__device__ __forceinline__ void quant_q8k_block(const float *x, int t, int blk, const XQ &xq) {
+// Q8_K (quant.c:118-144) of one 256-element block whose 8 values per lane are in v. The scale
+// comes from the FIRST element of largest magnitude, with its sign.
+__device__ __forceinline__ void quant_q8k_vals(const float v[8], int t, int blk, const XQ &xq) {
     const int lane = threadIdx.x & 31;
-    float4 a = *(const float4 *)(x + blk * 256 + lane * 8);
-    float4 c = *(const float4 *)(x + blk * 256 + lane * 8 + 4);
-    float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
     float amax = 0.0f;
     int idx = 0x7FFFFFFF;
     for (int i = 0; i < 8; i++)
@@ -30,8 +29,11 @@ __device__ __forceinline__ void quant_q8k_block(const float *x, int t, int blk, 
         if (lane == 0) *dd = 0.0f;
         return;
     }
-    float vmax = __shfl_sync(0xffffffffu, v[idx & 7], (idx >> 3) & 31);
-    float iscale = __fdiv_rn(-127.0f, vmax);
+    float mine = 0.0f;
+    for (int i = 0; i < 8; i++)
+        if (i == (idx & 7)) mine = v[i];
+    const float vmax = __shfl_sync(0xffffffffu, mine, (idx >> 3) & 31);
+    const float iscale = __fdiv_rn(-127.0f, vmax);
     int q[8], sum = 0;
     for (int i = 0; i < 8; i++) {
         int r = __float2int_rn(__fmul_rn(iscale, v[i]));  // round half to even (quant.c:111-116)
@@ -46,26 +48,20 @@ __device__ __forceinline__ void quant_q8k_block(const float *x, int t, int blk, 
     if (lane == 0) *dd = __fdiv_rn(1.0f, iscale);
 }
 
-// Q8_0 (quant.c:98-108): 4 lanes per 32-element block, 8 elements per lane.
-__device__ __forceinline__ void quant_q80_span(const float *x, int t, int span, int n_in, const XQ &xq) {
+// Q8_0 (quant.c:98-108) of span `span`: 4 lanes per 32-element block. Lanes whose elements lie
+// past the row (live = false; n_in is a multiple of 32, so a 4-lane group is all live or dead)
+// take part in the shuffles and write nothing.
+__device__ __forceinline__ void quant_q80_vals(const float v[8], bool live, int t, int span, const XQ &xq) {
     const int lane = threadIdx.x & 31;
     const int e0 = span * 256 + lane * 8;
-    const bool live = e0 < n_in;  // n_in is a multiple of 32: a 4-lane group is all live or all dead
-    float v[8];
-    if (live) {
-        float4 a = *(const float4 *)(x + e0), c = *(const float4 *)(x + e0 + 4);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
-    } else {
-        for (int i = 0; i < 8; i++) v[i] = 0.0f;
-    }
     float amax = 0.0f;
-    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
+    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(live ? v[i] : 0.0f));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     float d = __fdiv_rn(amax, 127.0f);
     float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     int q[8], sum = 0;
-    for (int i = 0; i < 8; i++) { q[i] = (int)roundf(__fmul_rn(v[i], id)); sum += q[i]; }
+    for (int i = 0; i < 8; i++) { q[i] = live ? (int)roundf(__fmul_rn(v[i], id)) : 0; sum += q[i]; }
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     if (!live) return;
@@ -77,6 +73,29 @@ __device__ __forceinline__ void quant_q80_span(const float *x, int t, int span, 
         xq.d[(size_t)t * xq.nbx + blk] = __half2float(__float2half_rn(d));
         ((int32_t *)xq.sums)[(size_t)t * xq.nbx + blk] = sum;
     }
+}
+
+// The same, reading the lane's 8 values from x (row of token t).
+__device__ __forceinline__ void load8(const float *x, int e0, bool live, float v[8]) {
+    if (live) {
+        float4 a = *(const float4 *)(x + e0), c = *(const float4 *)(x + e0 + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+    } else {
+        for (int i = 0; i < 8; i++) v[i] = 0.0f;
+    }
+}
+
+__device__ __forceinline__ void quant_q8k_block(const float *x, int t, int blk, const XQ &xq) {
+    float v[8];
+    load8(x, blk * 256 + (threadIdx.x & 31) * 8, true, v);
+    quant_q8k_vals(v, t, blk, xq);
+}
+
+__device__ __forceinline__ void quant_q80_span(const float *x, int t, int span, int n_in, const XQ &xq) {
+    const int e0 = span * 256 + (threadIdx.x & 31) * 8;
+    float v[8];
+    load8(x, e0, e0 < n_in, v);
+    quant_q80_vals(v, e0 < n_in, t, span, xq);
 }
 
 }  // namespace sdy
