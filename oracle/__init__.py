@@ -143,6 +143,7 @@ def ref() -> ctypes.CDLL:
             "op_vec_dot_q": (ctypes.c_float, [_i, _vp, _vp, _i]),
             "op_matmul": (None, [_vp, _vp, _vp, _i, _i, _i, _i]),
             "op_f32_to_f16": (ctypes.c_uint16, [ctypes.c_float]),
+            "op_attention": (None, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
             "engine_model_load": (_vp, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]),
             "engine_model_free": (None, [_vp]),
             "engine_ctx_new": (_vp, [_vp, _i32, _i32, _i32, _i32, ctypes.c_char_p, ctypes.c_size_t]),

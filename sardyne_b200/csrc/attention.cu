@@ -1,0 +1,328 @@
+// Causal attention over the KV cache (reference csrc/ops.c:405-423, called per token from
+// model_llama.c:803-806): for each query head, scores = q.k_j * (1/sqrt(hd)) over the n_kv
+// cached positions, softmax, then out[i] = sum over j IN KEY ORDER of p_j * v_j[i].
+//
+// The reference's result is a sequential rounding chain per output element (axpy into out, one
+// key at a time, no fused multiply-add), so the only parallelism that keeps it exact is across
+// heads and elements, never across keys of one element. The main kernel is built around that:
+//
+//   one cluster of AC = 8 CTAs per (KV head, token), serving the n_rep query heads that share
+//   the KV head (GQA), so each K/V row is read from HBM once for all of them;
+//   phase A  CTA c scores keys [c*L, (c+1)*L): K tiles staged with cp.async, one key per thread,
+//            dot products in the reference's four-accumulator order (ops.c:155-167), scores to
+//            the scratch rows in global memory;
+//   phase B  max and double sum of exp(s - max) per head reduced across the cluster through
+//            distributed shared memory (two cluster barriers);
+//   phase C  CTA c owns elements [c*S, (c+1)*S) of every head: n_rep*S exact chains, fed by
+//            double-buffered cp.async chunks of probabilities and of the V columns it needs.
+//
+// A per-head kernel (one CTA per (head, token)) covers the shapes the cluster kernel does not
+// (head_dim not a multiple of 32, more than 32 query heads per KV head, unaligned buffers).
+#include "fp_device.cuh"
+#include "fp_ops.cuh"
+
+#include <cooperative_groups.h>
+
+namespace sdy {
+namespace cg = cooperative_groups;
+namespace {
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory"); }
+
+constexpr int AC = 8;             // CTAs per cluster
+constexpr int AC_THREADS = 256;
+constexpr int AC_KT = 64;         // keys per K tile (phase A)
+constexpr int AC_HG = AC_THREADS / AC_KT;  // head groups in phase A
+constexpr int AC_KC = 256;        // keys per chunk (phase C)
+constexpr int AC_PLD = AC_KC + 4; // probability row stride in shared memory (rows on distinct banks)
+constexpr int AC_MAX_REP = 32;    // query heads per KV head
+constexpr int AC_MAX_GROUP = AC * AC_THREADS;  // n_rep * hd: one chain per thread in phase C
+
+__host__ __device__ inline int ac_smem_floats(int n_rep, int hd) {
+    const int a = 2 * AC_KT * (hd + 4), c = 2 * (n_rep * AC_PLD + AC_KC * (hd / AC));
+    return n_rep * hd + (a > c ? a : c);
+}
+
+// q: token t at q + t*ldq, heads of hd; k/v cache [n_kv_head][stride][hd]; scratch rows of
+// stride floats per (token, head); the first token's position is *pos_dev when given, else pos0;
+// fixed_nkv > 0 overrides the causal count. hd % (4*AC) == 0, stride % 4 == 0, n_rep <= 32.
+__global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
+    attention_cluster_kernel(float *__restrict__ out, const float *__restrict__ q, int64_t ldq,
+                             const float *__restrict__ kc, const float *__restrict__ vc, int n_head, int n_kv_head,
+                             int hd, int pos0, const int32_t *pos_dev, int stride, float *scratch, int fixed_nkv) {
+    pdl_trigger();
+    extern __shared__ __align__(16) float sm[];
+    __shared__ float cmax[AC_MAX_REP], gmax[AC_MAX_REP], ginv[AC_MAX_REP];
+    __shared__ double csum[AC_MAX_REP];
+    cg::cluster_group cl = cg::this_cluster();
+    const int c = (int)cl.block_rank();
+    const int g = blockIdx.y, t = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n_kv = fixed_nkv > 0 ? fixed_nkv : (pos_dev ? *pos_dev : pos0) + t + 1;
+    const int n_rep = n_head / n_kv_head, h0 = g * n_rep;
+    const float *kh = kc + (size_t)g * stride * hd, *vh = vc + (size_t)g * stride * hd;
+    float *sc0 = scratch + ((size_t)t * n_head + h0) * stride;  // head r's row at sc0 + r*stride
+    float *qs = sm, *buf = sm + n_rep * hd;
+    const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
+    const int L = (n_kv + AC - 1) / AC;
+    const int jb = min(n_kv, c * L), je = min(n_kv, jb + L);
+    // The positions are host-written before the step's first kernel, so n_kv is known here. While
+    // the previous kernel (which stores the newest K/V rows) finishes, pull this CTA's K rows and
+    // the same V rows into L2: a cache hint only, the reads below still follow pdl_wait.
+    if (tid == 0 && je > jb) {
+        const uint32_t bytes = (uint32_t)((size_t)(je - jb) * hd * 4);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(kh + (size_t)jb * hd), "r"(bytes) : "memory");
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(vh + (size_t)jb * hd), "r"(bytes) : "memory");
+    }
+    pdl_wait();
+    for (int i = tid; i < n_rep * hd; i += AC_THREADS) qs[i] = q[(size_t)t * ldq + (size_t)h0 * hd + i];
+
+    // ---- phase A: scores of this CTA's keys
+    const int ldk = hd + 4, hd4 = hd / 4;  // padded rows: a quarter-warp's 16-byte reads hit all banks once
+    const int kk = tid % AC_KT, hg = tid / AC_KT;
+    const int ntile = (je - jb + AC_KT - 1) / AC_KT;
+    auto load_k = [&](int it) {
+        const int j0 = jb + it * AC_KT, nk = min(AC_KT, je - j0);
+        float *dst = buf + (it & 1) * AC_KT * ldk;
+        for (int idx = tid; idx < nk * hd4; idx += AC_THREADS) {
+            const int j = idx / hd4, i = (idx - j * hd4) * 4;
+            cp_async16(dst + j * ldk + i, kh + (size_t)(j0 + j) * hd + i);
+        }
+        cp_async_commit();
+    };
+    if (ntile > 0) load_k(0);
+    __syncthreads();  // qs
+    for (int it = 0; it < ntile; it++) {
+        if (it + 1 < ntile) {
+            load_k(it + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const int j = jb + it * AC_KT + kk;
+        if (j < je) {
+            const float *row = buf + (it & 1) * AC_KT * ldk + kk * ldk;
+            for (int r0 = hg; r0 < n_rep; r0 += 2 * AC_HG) {
+                const int r1 = r0 + AC_HG;
+                const bool two = r1 < n_rep;
+                const float *x0 = qs + r0 * hd, *x1 = qs + (two ? r1 : r0) * hd;
+                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f, b0 = 0.0f, b1 = 0.0f, b2 = 0.0f, b3 = 0.0f;
+                for (int i = 0; i < hd; i += 4) {
+                    const float4 k4 = *(const float4 *)(row + i);
+                    const float4 u = *(const float4 *)(x0 + i), w = *(const float4 *)(x1 + i);
+                    a0 = __fadd_rn(a0, __fmul_rn(u.x, k4.x));
+                    a1 = __fadd_rn(a1, __fmul_rn(u.y, k4.y));
+                    a2 = __fadd_rn(a2, __fmul_rn(u.z, k4.z));
+                    a3 = __fadd_rn(a3, __fmul_rn(u.w, k4.w));
+                    b0 = __fadd_rn(b0, __fmul_rn(w.x, k4.x));
+                    b1 = __fadd_rn(b1, __fmul_rn(w.y, k4.y));
+                    b2 = __fadd_rn(b2, __fmul_rn(w.z, k4.z));
+                    b3 = __fadd_rn(b3, __fmul_rn(w.w, k4.w));
+                }
+                sc0[(size_t)r0 * stride + j] = __fmul_rn(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)), scale);
+                if (two)
+                    sc0[(size_t)r1 * stride + j] = __fmul_rn(__fadd_rn(__fadd_rn(b0, b1), __fadd_rn(b2, b3)), scale);
+            }
+        }
+        __syncthreads();
+    }
+
+    // ---- phase B: cluster-wide max and sum of exponentials per head
+    for (int r = warp; r < n_rep; r += AC_THREADS / 32) {
+        const float *row = sc0 + (size_t)r * stride;
+        float m = -INFINITY;
+        for (int j = jb + lane; j < je; j += 32) m = fmaxf(m, row[j]);
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) cmax[r] = m;
+    }
+    cl.sync();
+    if (tid < n_rep) {
+        float m = -INFINITY;
+        for (int p = 0; p < AC; p++) m = fmaxf(m, *cl.map_shared_rank(cmax + tid, p));
+        gmax[tid] = m;
+    }
+    __syncthreads();
+    for (int r = warp; r < n_rep; r += AC_THREADS / 32) {
+        float *row = sc0 + (size_t)r * stride;
+        const float m = gmax[r];
+        double s = 0.0;
+        for (int j = jb + lane; j < je; j += 32) {
+            const float e = exp_cr(__fsub_rn(row[j], m));
+            row[j] = e;
+            s += e;
+        }
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) csum[r] = s;
+    }
+    cl.sync();  // also publishes every CTA's exponentials in the scratch rows
+    if (tid < n_rep) {
+        double s = 0.0;
+        for (int p = 0; p < AC; p++) s += *cl.map_shared_rank(csum + tid, p);
+        ginv[tid] = (float)(1.0 / s);
+    }
+    cluster_arrive();  // done with the other CTAs' shared memory; the matching wait is at the end
+    __syncthreads();
+
+    // ---- phase C: out[e] = sum_j (e_j * inv) * v_j[e] in key order, e in this CTA's slice
+    const int S = hd / AC, S4 = S / 4, e0 = c * S;
+    const int ch_r = tid / S, ch_e = tid - ch_r * S;
+    const bool chain = tid < n_rep * S;
+    const float inv = chain ? ginv[ch_r] : 0.0f;
+    float *pbuf = buf, *vbuf = buf + 2 * n_rep * AC_PLD;
+    const int nchunk = (n_kv + AC_KC - 1) / AC_KC;
+    auto load_c = [&](int ic) {
+        const int j0 = ic * AC_KC, nk = min(AC_KC, n_kv - j0), nk4 = (nk + 3) / 4;
+        float *pb = pbuf + (ic & 1) * n_rep * AC_PLD, *vb = vbuf + (ic & 1) * AC_KC * S;
+        for (int idx = tid; idx < n_rep * nk4; idx += AC_THREADS) {
+            const int r = idx / nk4, j = (idx - r * nk4) * 4;
+            cp_async16(pb + r * AC_PLD + j, sc0 + (size_t)r * stride + j0 + j);
+        }
+        for (int idx = tid; idx < nk * S4; idx += AC_THREADS) {
+            const int j = idx / S4, i = (idx - j * S4) * 4;
+            cp_async16(vb + j * S + i, vh + (size_t)(j0 + j) * hd + e0 + i);
+        }
+        cp_async_commit();
+    };
+    float acc = 0.0f;
+    if (nchunk > 0) load_c(0);
+    for (int ic = 0; ic < nchunk; ic++) {
+        if (ic + 1 < nchunk) {
+            load_c(ic + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        if (chain) {
+            const float *pr = pbuf + (ic & 1) * n_rep * AC_PLD + ch_r * AC_PLD;
+            const float *vr = vbuf + (ic & 1) * AC_KC * S + ch_e;
+            const int nk = min(AC_KC, n_kv - ic * AC_KC);
+#pragma unroll 8
+            for (int j = 0; j < nk; j++) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(pr[j], inv), vr[j * S]));
+        }
+        __syncthreads();
+    }
+    if (chain) out[((size_t)t * n_head + h0 + ch_r) * hd + e0 + ch_e] = acc;
+    cluster_wait();
+}
+
+// General per-(head, token) kernel, one CTA of ATT_THREADS each: K and V staged through shared
+// memory in coalesced tiles (K rows padded to hd+1 floats), scores in the scratch rows, block
+// softmax, then thread i adds p_j * v_j[i] for the keys in order. hd a multiple of 4, at most
+// 2*ATT_THREADS.
+constexpr int ATT_THREADS = 128;
+__host__ __device__ inline int att_smem_floats(int hd) { return hd + ATT_THREADS * (hd + 1) + 2 * ATT_THREADS + 8; }
+
+__global__ void attention_head_kernel(float *out, const float *q, int64_t ldq, const float *kc, const float *vc,
+                                      int n_head, int n_kv_head, int hd, int pos0, const int32_t *pos_dev, int stride,
+                                      float *scratch, int fixed_nkv) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ __align__(16) float sm[];
+    const int t = blockIdx.y, h = blockIdx.x, tid = threadIdx.x;
+    const int n_kv = fixed_nkv > 0 ? fixed_nkv : (pos_dev ? *pos_dev : pos0) + t + 1;
+    const int n_rep = n_head / n_kv_head, ldt = hd + 1, hd4 = hd / 4;
+    const float *qv = q + (size_t)t * ldq + (size_t)h * hd;
+    const float *kh = kc + (size_t)(h / n_rep) * stride * hd;
+    const float *vh = vc + (size_t)(h / n_rep) * stride * hd;
+    float *sc = scratch + ((size_t)t * n_head + h) * stride;
+    float *qs = sm, *tile = sm + ((hd + 3) & ~3), *ps = tile + ATT_THREADS * ldt;
+    const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
+    for (int i = tid; i < hd; i += ATT_THREADS) qs[i] = qv[i];
+    for (int j0 = 0; j0 < n_kv; j0 += ATT_THREADS) {
+        const int nk = min(ATT_THREADS, n_kv - j0);
+        __syncthreads();
+        for (int idx = tid; idx < nk * hd4; idx += ATT_THREADS) {
+            const int j = idx / hd4, i = (idx - j * hd4) * 4;
+            const float4 v = *(const float4 *)(kh + (size_t)(j0 + j) * hd + i);
+            float *d = tile + j * ldt + i;
+            d[0] = v.x;
+            d[1] = v.y;
+            d[2] = v.z;
+            d[3] = v.w;
+        }
+        __syncthreads();
+        if (tid < nk) {
+            const float *row = tile + tid * ldt;
+            sc[j0 + tid] = __fmul_rn(dot4(qs, [&](int i) { return row[i]; }, hd), scale);
+        }
+    }
+    __syncthreads();
+    softmax_block(sc, n_kv);
+    __syncthreads();
+    const int tv = (ATT_THREADS * ldt) / hd;  // keys per V tile
+    float acc0 = 0.0f, acc1 = 0.0f;
+    const int i0 = tid, i1 = tid + ATT_THREADS;
+    for (int j0 = 0; j0 < n_kv; j0 += tv) {
+        const int nv = min(tv, n_kv - j0);
+        __syncthreads();
+        for (int idx = tid; idx < nv * hd4; idx += ATT_THREADS)
+            *(float4 *)(tile + idx * 4) = *(const float4 *)(vh + (size_t)j0 * hd + idx * 4);
+        for (int j = tid; j < nv; j += ATT_THREADS) ps[j] = sc[j0 + j];
+        __syncthreads();
+        for (int j = 0; j < nv; j++) {
+            const float p = ps[j];
+            if (i0 < hd) acc0 = __fadd_rn(acc0, __fmul_rn(p, tile[j * hd + i0]));
+            if (i1 < hd) acc1 = __fadd_rn(acc1, __fmul_rn(p, tile[j * hd + i1]));
+        }
+    }
+    float *ov = out + ((size_t)t * n_head + h) * hd;
+    if (i0 < hd) ov[i0] = acc0;
+    if (i1 < hd) ov[i1] = acc1;
+}
+
+bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace
+
+void attention(float *out, const float *q, int64_t ldq, const float *kc, const float *vc, int n_tok, int n_head,
+               int n_kv_head, int hd, int pos0, const int32_t *pos_dev, int stride, float *scratch, int fixed_nkv,
+               cudaStream_t s) {
+    if (n_tok <= 0) return;
+    if (hd % 4 || n_kv_head <= 0 || n_head % n_kv_head) {
+        set_error("attention: head_dim %d / heads %d/%d not supported", hd, n_head, n_kv_head);
+        return;
+    }
+    const int n_rep = n_head / n_kv_head;
+    const bool cluster = hd % (4 * AC) == 0 && stride % 4 == 0 && n_rep <= AC_MAX_REP &&
+                         n_rep * hd <= AC_MAX_GROUP && aligned16(kc) && aligned16(vc) && aligned16(scratch) &&
+                         ac_smem_floats(n_rep, hd) * 4 <= 200 * 1024 && n_kv_head <= 65535 && n_tok <= 65535;
+    if (cluster) {
+        const size_t smem = (size_t)ac_smem_floats(n_rep, hd) * 4;
+        static bool configured = false;
+        if (!configured) {
+            SDY_CUDA(cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          200 * 1024));
+            configured = true;
+        }
+        launch(attention_cluster_kernel, dim3(AC, n_kv_head, n_tok), AC_THREADS, smem, s, out, q, ldq, kc, vc, n_head, n_kv_head, hd, pos0, pos_dev, stride, scratch, fixed_nkv);
+        SDY_LAUNCHED();
+        return;
+    }
+    if (hd > 2 * ATT_THREADS) {
+        set_error("attention: head_dim %d not supported (multiple of 4, at most %d)", hd, 2 * ATT_THREADS);
+        return;
+    }
+    const size_t smem = (size_t)att_smem_floats(hd) * 4;
+    static bool configured = false;
+    if (!configured) {
+        SDY_CUDA(cudaFuncSetAttribute(attention_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      att_smem_floats(2 * ATT_THREADS) * 4));
+        configured = true;
+    }
+    launch(attention_head_kernel, dim3(n_head, n_tok), ATT_THREADS, smem, s, out, q, ldq, kc, vc, n_head, n_kv_head, hd,
+                                                                         pos0, pos_dev, stride, scratch, fixed_nkv);
+    SDY_LAUNCHED();
+}
+
+}  // namespace sdy

@@ -8,6 +8,7 @@
 #include <stdio.h>
 
 #include <string>
+#include <utility>
 
 namespace sdy {
 
@@ -121,6 +122,35 @@ void note_launch();
         ::sdy::note_launch();                            \
         SDY_CUDA(cudaGetLastError());                    \
     } while (0)
+
+// ------------------------------------------------------------------------------ dependent launch
+// Kernels are launched with programmatic dependent launch: the next kernel's CTAs are placed on
+// the SMs while the current kernel runs and block in pdl_wait() until it has completed and its
+// writes are visible, which takes launch latency (and, in the quantized matvec, the first weight
+// loads) off the critical path. So every kernel begins with pdl_trigger() and reads or writes no
+// activation before pdl_wait(); only weights may be read before it. Kernels that write weights
+// (repacking, format conversion) do not call pdl_trigger(): the kernel after them then starts
+// only once they have completed, so no later kernel's early weight reads can overlap them.
+// Launched without the attribute (SARDYNE_NO_PDL set), both instructions are no-ops.
+#ifdef __CUDACC__
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+#endif
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args &&...args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    SDY_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 // ------------------------------------------------------------------------------------------ kernels
 // Launchers (sardyne_b200/csrc/*.cu). All are asynchronous on `s` and record errors with set_error.

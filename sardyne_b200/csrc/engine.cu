@@ -447,6 +447,8 @@ int get_vector(engine_model *m, const char *name, int n, float **out, char *err,
 
 // x[t] = row tok[t] of a float table (F32/F16/BF16).
 __global__ void embed_float_kernel(const void *table, int type, const int32_t *ids, int dim, float *x) {
+    pdl_trigger();
+    pdl_wait();
     int t = blockIdx.x;
     size_t base = (size_t)ids[t] * dim;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) {
@@ -461,6 +463,8 @@ __global__ void embed_float_kernel(const void *table, int type, const int32_t *i
 // Router selection per token for a quantized router (model_llama.c:653-666): the k most
 // probable experts, ties to the lowest index, weights renormalised by their float sum.
 __global__ void topk_kernel(const float *probs, int n_tok, int ne, int k, int32_t *top, float *w) {
+    pdl_trigger();
+    pdl_wait();
     int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= n_tok) return;
     const float *p = probs + (size_t)t * ne;
@@ -483,6 +487,8 @@ __global__ void topk_kernel(const float *probs, int n_tok, int ne, int k, int32_
 // the reference's scalar dot order (four accumulators, csrc/ops.c:155-167).
 __global__ void fmatmul_gather_kernel(const void *w, int type, int n_in, int64_t rows, const int32_t *top,
                                       const float *x, int64_t ldx, int tok_div, float *out, int64_t ldo) {
+    pdl_trigger();
+    pdl_wait();
     int s = blockIdx.y;
     int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (r >= rows) return;
@@ -566,7 +572,7 @@ void project_experts(engine_ctx *c, const Proj &p, float *out, int64_t ldo, cons
         const DMat &w = part.m;
         if (!w.quant()) {
             dim3 grid((unsigned)((w.n_out + 255) / 256), n_slots);
-            fmatmul_gather_kernel<<<grid, 256, 0, c->st>>>(w.f, w.type, w.n_in, w.n_out, c->moe_top, x, ldx, tok_div,
+            launch(fmatmul_gather_kernel, grid, 256, 0, c->st, w.f, w.type, w.n_in, w.n_out, c->moe_top, x, ldx, tok_div,
                                                             out + part.col, ldo);
             SDY_LAUNCHED();
             continue;
@@ -585,7 +591,7 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n) {
     } else {
         matmul(c, c->moe_probs, ne, c->xb, dim, r, n);
         softmax(c->moe_probs, ne, ne, n, c->st);
-        topk_kernel<<<(n + 127) / 128, 128, 0, c->st>>>(c->moe_probs, n, ne, k, c->moe_top, c->moe_w);
+        launch(topk_kernel, (n + 127) / 128, 128, 0, c->st, c->moe_probs, n, ne, k, c->moe_top, c->moe_w);
         SDY_LAUNCHED();
     }
     const int slots = n * k, gu = 2 * fe;
@@ -605,7 +611,7 @@ void embed(engine_ctx *c, int n) {
     const int32_t *ids = c->tokpos + 1;
     if (e.quant()) dequant_rows(e.q, ids, n, 0, c->x, m->info.dim, c->st);
     else {
-        embed_float_kernel<<<n, 256, 0, c->st>>>(e.f, e.type, ids, m->info.dim, c->x);
+        launch(embed_float_kernel, n, 256, 0, c->st, e.f, e.type, ids, m->info.dim, c->x);
         SDY_LAUNCHED();
     }
 }

@@ -1,0 +1,81 @@
+// Device helpers shared by the fp32 kernels (fp_ops.cu, attention.cu, fused.cu): the
+// reference's scalar dot product, the correctly rounded exp, and block reductions.
+#pragma once
+#include "common.cuh"
+
+#include <cuda_bf16.h>
+
+namespace sdy {
+
+// The correctly rounded expf: exp() in double rounded once to float. The reference calls libm's
+// expf, whose glibc version (error < 0.502 ulp) differs from this in the last bit on ~0.06% of
+// inputs; softmax and SiLU results can differ from the reference's by that much.
+__device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
+
+__device__ __forceinline__ float load_w(const void *w, int type, size_t i) {
+    if (type == T_F32) return ((const float *)w)[i];
+    if (type == T_F16) return __half2float(((const __half *)w)[i]);
+    return __bfloat162float(((const __nv_bfloat16 *)w)[i]);
+}
+
+// The reference's scalar dot (ops.c:155-167): four accumulators, tail into the first.
+template <class Load>
+__device__ __forceinline__ float dot4(const float *x, Load w, int n) {
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    int i = 0;
+    for (; i + 4 <= n; i += 4) {
+        s0 = __fadd_rn(s0, __fmul_rn(x[i], w(i)));
+        s1 = __fadd_rn(s1, __fmul_rn(x[i + 1], w(i + 1)));
+        s2 = __fadd_rn(s2, __fmul_rn(x[i + 2], w(i + 2)));
+        s3 = __fadd_rn(s3, __fmul_rn(x[i + 3], w(i + 3)));
+    }
+    for (; i < n; i++) s0 = __fadd_rn(s0, __fmul_rn(x[i], w(i)));
+    return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
+// Block-wide sum of doubles (blockDim.x a multiple of 32, at most 1024).
+__device__ inline double block_sum_d(double v) {
+    __shared__ double part[32];
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) part[w] = v;
+    __syncthreads();
+    int nw = blockDim.x >> 5;
+    v = lane < nw ? part[lane] : 0.0;
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ inline float block_max_f(float v) {
+    __shared__ float part[32];
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) part[w] = v;
+    __syncthreads();
+    int nw = blockDim.x >> 5;
+    v = lane < nw ? part[lane] : -INFINITY;
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Softmax in place by the whole block (ops.c:353-364): exp(x - max), double sum, scaled by
+// (float)(1/sum). The double sum is taken in a different order than the reference's sequential
+// one; the two agree to ~1e-16 relative before the final rounding to float.
+__device__ inline void softmax_block(float *v, int n) {
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, v[i]);
+    m = block_max_f(m);
+    double sum = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float e = exp_cr(__fsub_rn(v[i], m));
+        v[i] = e;
+        sum += e;
+    }
+    sum = block_sum_d(sum);
+    float inv = (float)(1.0 / sum);
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) v[i] = __fmul_rn(v[i], inv);
+}
+
+}  // namespace sdy

@@ -8,13 +8,13 @@
 //   moe_combine    sum over a token's experts in ascending id + residual add (model_llama.c:734-750, 820)
 // In the norm and SiLU kernels lane l of warp w owns elements 256w + 8l .. +7 in registers, so
 // each warp quantizes its own 256-element span without staging through shared memory.
+#include "fp_device.cuh"
 #include "fused.cuh"
 #include "quant_device.cuh"
 
 namespace sdy {
 namespace {
 
-__device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
 
 __device__ double bsum_d(double v, double *part) {
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -47,6 +47,8 @@ __device__ __forceinline__ void quantize_span(const float v[8], int e0, int n, i
 // One block per row, thread i owning elements 8i..8i+7 (blockDim = n/8 rounded up to a warp).
 __global__ void rmsnorm_quant_kernel(const float *x, int64_t ldx, const float *w, int n, float eps, float *xb,
                                      int64_t ldb, XQ q8k, XQ q80) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ double part[32];
     const int t = blockIdx.x, e0 = threadIdx.x * 8;
     const float *xv = x + (size_t)t * ldx;
@@ -67,6 +69,8 @@ __global__ void rmsnorm_quant_kernel(const float *x, int64_t ldx, const float *w
 
 // grid (ceil(n/2048), rows), 256 threads: warp w of block b owns span 8b + w.
 __global__ void silu_quant_kernel(float *g, int64_t ldg, const float *u, int64_t ldu, int n, XQ q8k, XQ q80) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y, span = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (span * 256 >= n) return;  // whole warps leave together
     const int e0 = span * 256 + (threadIdx.x & 31) * 8;
@@ -87,6 +91,8 @@ __global__ void silu_quant_kernel(float *g, int64_t ldg, const float *u, int64_t
 // One block per (head, token). Heads [0, n_head) are q heads; [n_head, n_head + n_kv_head) are
 // k heads, whose block also handles the v head with the same index.
 __global__ void post_qkv_kernel(PostQKV p) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) float vec[];
     __shared__ double part[32];
     const int t = blockIdx.y, hh = blockIdx.x, hd = p.hd, half = hd / 2;
@@ -133,32 +139,56 @@ __global__ void post_qkv_kernel(PostQKV p) {
 // Router logits for float weights: one warp per expert row. The warp copies x and its row into
 // shared memory with coalesced loads; lanes 0..3 then run the reference's four accumulator
 // chains (ops.c:155-167: s_k over i = 4g + k, the tail into s0) and combine (s0+s1)+(s2+s3).
-constexpr int ROUTER_WARPS = 4;
+constexpr int ROUTER_WARPS = 2;  // experts per CTA: one warp each
+
+__device__ __forceinline__ float4 load4_w(const void *w, int wtype, size_t i) {  // i a multiple of 4
+    if (wtype == T_F32) return *(const float4 *)((const float *)w + i);
+    const uint2 u = *(const uint2 *)((const uint16_t *)w + i);
+    if (wtype == T_F16) {
+        const float2 a = __half22float2(*(const __half2 *)&u.x), b = __half22float2(*(const __half2 *)&u.y);
+        return make_float4(a.x, a.y, b.x, b.y);
+    }
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xFFFF0000u));
+}
+
+// logits[t][e] = x[t] . w[e] with the reference's four-accumulator dot (ops.c:155-167): the row
+// and x are staged in shared memory with 16-byte loads, then lanes 0-3 of the expert's warp each
+// run one accumulator's chain (unrolled, so the shared-memory reads run ahead of the adds).
+// vec: dim % 4 == 0 and x rows 16-byte aligned.
 __global__ void router_logits_kernel(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne,
-                                     float *logits) {
+                                     float *logits, int vec) {
+    pdl_trigger();
     extern __shared__ __align__(16) float sm[];
-    float *xs = sm, *rows = sm + dim;
+    float *xs = sm, *rows = sm + ((dim + 3) & ~3);
     const int t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.x * ROUTER_WARPS + warp;
     const float *xv = x + (size_t)t * ldx;
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) xs[i] = xv[i];
-    float *row = rows + (size_t)warp * dim;
+    float *row = rows + (size_t)warp * ((dim + 3) & ~3);
+    const size_t base = (size_t)e * dim;
+    // The router row is a constant weight: staged before waiting for the previous kernel.
     if (e < ne) {
-        const size_t base = (size_t)e * dim;
-        for (int i = lane; i < dim; i += 32) {
-            float v;
-            if (wtype == T_F32) v = ((const float *)w)[base + i];
-            else if (wtype == T_F16) v = __half2float(((const __half *)w)[base + i]);
-            else v = __uint_as_float((uint32_t)((const uint16_t *)w)[base + i] << 16);
-            row[i] = v;
+        if (vec) {
+#pragma unroll 4
+            for (int i = lane * 4; i < dim; i += 128) *(float4 *)(row + i) = load4_w(w, wtype, base + i);
+        } else {
+            for (int i = lane; i < dim; i += 32) row[i] = load_w(w, wtype, base + i);
         }
+    }
+    pdl_wait();
+    if (vec) {
+        for (int i = threadIdx.x * 4; i < dim; i += blockDim.x * 4) *(float4 *)(xs + i) = *(const float4 *)(xv + i);
+    } else {
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) xs[i] = xv[i];
     }
     __syncthreads();
     if (e >= ne) return;
     float s = 0.0f;
     if (lane < 4) {
         const int groups = dim / 4;
-        for (int g = 0; g < groups; g++) s = __fadd_rn(s, __fmul_rn(xs[4 * g + lane], row[4 * g + lane]));
+        const float *xa = xs + lane, *ra = row + lane;
+#pragma unroll 8
+        for (int g = 0; g < groups; g++) s = __fadd_rn(s, __fmul_rn(xa[4 * g], ra[4 * g]));
         if (lane == 0)
             for (int i = groups * 4; i < dim; i++) s = __fadd_rn(s, __fmul_rn(xs[i], row[i]));
     }
@@ -167,12 +197,17 @@ __global__ void router_logits_kernel(const float *x, int64_t ldx, const void *w,
     if (lane == 0) logits[(size_t)t * ne + e] = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
 }
 
-// Softmax (ops.c:353-364) and stable top-k with ties to the lowest index, weights renormalised
-// by their float sum (model_llama.c:653-666), one block per token.
+// Softmax (ops.c:353-364) and top-k (model_llama.c:653-666), one CTA per token. The reference's
+// insertion keeps the k largest probabilities in descending order, equal values in ascending
+// expert id; here warp 0 takes k rounds of a warp-wide argmax under that same order. Weights are
+// renormalised by their float sum taken in the selected order.
 __global__ void softmax_topk_kernel(const float *logits, int ne, int k, int32_t *top, float *wout) {
-    extern __shared__ __align__(16) float prob[];
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ __align__(16) float prob[];  // [ne] probabilities, [ne] selection keys
     __shared__ double dpart[32];
     __shared__ float fpart[32];
+    float *key = prob + ne;
     const int t = blockIdx.x;
     for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = logits[(size_t)t * ne + e];
     __syncthreads();
@@ -187,27 +222,41 @@ __global__ void softmax_topk_kernel(const float *logits, int ne, int k, int32_t 
     }
     sum = bsum_d(sum, dpart);
     const float inv = (float)(1.0 / sum);
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = __fmul_rn(prob[e], inv);
+    for (int e = threadIdx.x; e < ne; e += blockDim.x) key[e] = prob[e] = __fmul_rn(prob[e], inv);
     __syncthreads();
-    if (threadIdx.x != 0) return;
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
     int32_t *tp = top + (size_t)t * k;
-    int n = 0;
-    for (int e = 0; e < ne; e++) {
-        int pos = n;
-        while (pos > 0 && prob[e] > prob[tp[pos - 1]]) pos--;
-        if (pos == k) continue;
-        for (int j = n < k ? n : k - 1; j > pos; j--) tp[j] = tp[j - 1];
-        tp[pos] = e;
-        if (n < k) n++;
-    }
     float s = 0.0f;
-    for (int i = 0; i < k; i++) s = __fadd_rn(s, prob[tp[i]]);
-    for (int i = 0; i < k; i++) wout[(size_t)t * k + i] = __fdiv_rn(prob[tp[i]], s);
+    for (int r = 0; r < k; r++) {
+        float bv = -1.0f;  // probabilities are >= 0; taken entries hold -1
+        int bi = 0x7FFFFFFF;
+        for (int e = lane; e < ne; e += 32) {
+            const float v = key[e];
+            if (v > bv) { bv = v; bi = e; }  // ascending e: the first of equal values stays
+        }
+        for (int o = 16; o; o >>= 1) {
+            const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (v2 > bv || (v2 == bv && i2 < bi)) { bv = v2; bi = i2; }
+        }
+        if (lane == 0) {
+            if (bi >= ne) bi = 0;  // only reachable with NaN probabilities; keeps the index in range
+            tp[r] = bi;
+            key[bi] = -1.0f;
+            s = __fadd_rn(s, prob[bi]);
+        }
+        __syncwarp();
+    }
+    if (lane == 0)
+        for (int i = 0; i < k; i++) wout[(size_t)t * k + i] = __fdiv_rn(prob[tp[i]], s);
 }
 
 // x[t] += sum over t's k slots, in ascending expert id, of w * y[slot].
 __global__ void moe_combine_kernel(const float *y, int64_t ldy, const int32_t *top, const float *w, int k, int dim,
                                    float *x, int64_t ldx) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y;
     int order[64];
     for (int i = 0; i < k; i++) order[i] = i;
@@ -243,27 +292,27 @@ void rmsnorm_quant(const float *x, int64_t ldx, const float *w, int n, int rows,
         return;
     }
     const int threads = ((n + 7) / 8 + 31) / 32 * 32;
-    rmsnorm_quant_kernel<<<rows, threads, 0, s>>>(x, ldx, w, n, eps, xb, ldb, pick(q8k), pick(q80));
+    launch(rmsnorm_quant_kernel, rows, threads, 0, s, x, ldx, w, n, eps, xb, ldb, pick(q8k), pick(q80));
     SDY_LAUNCHED();
 }
 
 void silu_quant(float *g, int64_t ldg, const float *u, int64_t ldu, int n, int rows, const XQ *q8k, const XQ *q80,
                 cudaStream_t s) {
     if (rows <= 0) return;
-    silu_quant_kernel<<<dim3((n + 2047) / 2048, rows), 256, 0, s>>>(g, ldg, u, ldu, n, pick(q8k), pick(q80));
+    launch(silu_quant_kernel, dim3((n + 2047) / 2048, rows), 256, 0, s, g, ldg, u, ldu, n, pick(q8k), pick(q80));
     SDY_LAUNCHED();
 }
 
 void post_qkv(const PostQKV &p, int n_tok, cudaStream_t s) {
     if (n_tok <= 0) return;
-    post_qkv_kernel<<<dim3(p.n_head + p.n_kv_head, n_tok), 64, (size_t)p.hd * 4, s>>>(p);
+    launch(post_qkv_kernel, dim3(p.n_head + p.n_kv_head, n_tok), 64, (size_t)p.hd * 4, s, p);
     SDY_LAUNCHED();
 }
 
 void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, int n_tok,
                  int32_t *top, float *wout, float *logits, cudaStream_t s) {
     if (n_tok <= 0) return;
-    const size_t smem = (size_t)(ROUTER_WARPS + 1) * dim * 4;
+    const size_t smem = (size_t)(ROUTER_WARPS + 1) * ((dim + 3) & ~3) * 4;
     if (smem > 200 * 1024) {
         set_error("router_topk: hidden size %d too large", dim);
         return;
@@ -273,17 +322,18 @@ void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim,
         SDY_CUDA(cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         configured = true;
     }
-    router_logits_kernel<<<dim3((ne + ROUTER_WARPS - 1) / ROUTER_WARPS, n_tok), 32 * ROUTER_WARPS, smem, s>>>(
-        x, ldx, w, wtype, dim, ne, logits);
+    const bool w_aligned = wtype == T_F32 ? ((uintptr_t)w & 15) == 0 : ((uintptr_t)w & 7) == 0;
+    const int vec = dim % 4 == 0 && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0 && w_aligned;
+    launch(router_logits_kernel, dim3((ne + ROUTER_WARPS - 1) / ROUTER_WARPS, n_tok), 32 * ROUTER_WARPS, smem, s, x, ldx, w, wtype, dim, ne, logits, vec);
     SDY_LAUNCHED();
-    softmax_topk_kernel<<<n_tok, 128, (size_t)ne * 4, s>>>(logits, ne, k, top, wout);
+    launch(softmax_topk_kernel, n_tok, 128, (size_t)ne * 8, s, logits, ne, k, top, wout);
     SDY_LAUNCHED();
 }
 
 void moe_combine(const float *y, int64_t ldy, const int32_t *top, const float *w, int k, int dim, int n_tok, float *x,
                  int64_t ldx, cudaStream_t s) {
     if (n_tok <= 0) return;
-    moe_combine_kernel<<<dim3((dim + 255) / 256, n_tok), 256, 0, s>>>(y, ldy, top, w, k, dim, x, ldx);
+    launch(moe_combine_kernel, dim3((dim + 255) / 256, n_tok), 256, 0, s, y, ldy, top, w, k, dim, x, ldx);
     SDY_LAUNCHED();
 }
 

@@ -29,6 +29,7 @@ __device__ __forceinline__ int slab_off(int type, int r, int k) {
 
 __global__ void repack_kernel(const uint8_t *__restrict__ raw, int type, int64_t n_rows, int nb,
                               uint8_t *__restrict__ slabs) {
+    pdl_wait();
     const int bb = block_bytes(type), sb = slab_bytes(type);
     int64_t n_groups = (n_rows + GROUP_ROWS - 1) / GROUP_ROWS;
     int64_t total = n_groups * GROUP_ROWS * nb;
@@ -48,7 +49,7 @@ void repack_to_slabs(const uint8_t *raw, int type, int64_t n_rows, int n_in, uin
     int nb = n_in / block_elems(type);
     int64_t total = ((n_rows + 7) / 8) * 8 * nb;
     int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
-    repack_kernel<<<blocks, 256, 0, s>>>(raw, type, n_rows, nb, slabs);
+    launch(repack_kernel, blocks, 256, 0, s, raw, type, n_rows, nb, slabs);
     SDY_LAUNCHED();
 }
 
@@ -101,6 +102,8 @@ __device__ float dequant_elem(const QMat &w, int64_t row, int e) {
 
 __global__ void dequant_kernel(QMat w, const int32_t *__restrict__ ids, int64_t first_row, float *__restrict__ out,
                                int64_t ldo) {
+    pdl_trigger();
+    pdl_wait();
     int64_t row = ids ? (int64_t)ids[blockIdx.x] : first_row + blockIdx.x;
     float *o = out + (int64_t)blockIdx.x * ldo;
     for (int e = threadIdx.x; e < w.n_in; e += blockDim.x) o[e] = dequant_elem(w, row, e);
@@ -109,13 +112,15 @@ __global__ void dequant_kernel(QMat w, const int32_t *__restrict__ ids, int64_t 
 void dequant_rows(const QMat &w, const int32_t *row_ids, int n_ids, int64_t first_row, float *out, int64_t ldo,
                   cudaStream_t s) {
     if (n_ids <= 0) return;
-    dequant_kernel<<<n_ids, 256, 0, s>>>(w, row_ids, first_row, out, ldo);
+    launch(dequant_kernel, n_ids, 256, 0, s, w, row_ids, first_row, out, ldo);
     SDY_LAUNCHED();
 }
 
 // ------------------------------------------------------------------------------ activation quantization
 
 __global__ void quantize_kernel(int vtype, const float *__restrict__ x, int64_t ldx, int n_in, XQ xq) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y;
     const int span = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (span * 256 >= n_in) return;
@@ -128,12 +133,14 @@ void quantize_rows(int vtype, const float *x, int64_t ldx, int n_tok, int n_in, 
     if (n_tok <= 0) return;
     int spans = (n_in + 255) / 256;
     dim3 grid((spans + 7) / 8, n_tok);
-    quantize_kernel<<<grid, 256, 0, s>>>(vtype, x, ldx, n_in, xq);
+    launch(quantize_kernel, grid, 256, 0, s, vtype, x, ldx, n_in, xq);
     SDY_LAUNCHED();
 }
 
 // Reference-format activation bytes (Q8_K 292 B / Q8_0 34 B blocks) <-> XQ.
 __global__ void xq_import_kernel(int vtype, const uint8_t *__restrict__ raw, int n_tok, XQ xq) {
+    pdl_trigger();
+    pdl_wait();
     const int QB = block_elems(vtype), BB = block_bytes(vtype);
     int64_t total = (int64_t)n_tok * xq.nbx;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -161,6 +168,8 @@ __global__ void xq_import_kernel(int vtype, const uint8_t *__restrict__ raw, int
 }
 
 __global__ void xq_export_kernel(XQ xq, uint8_t *__restrict__ raw) {
+    pdl_trigger();
+    pdl_wait();
     const int vtype = xq.vtype, QB = block_elems(vtype), BB = block_bytes(vtype);
     int64_t total = (int64_t)xq.n_tok * xq.nbx;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -184,14 +193,14 @@ void xq_import(int vtype, const uint8_t *raw, int n_tok, int n_in, const XQ &xq,
     (void)n_in;
     int64_t total = (int64_t)n_tok * xq.nbx;
     if (total <= 0) return;
-    xq_import_kernel<<<(int)std::min<int64_t>((total + 127) / 128, 4096), 128, 0, s>>>(vtype, raw, n_tok, xq);
+    launch(xq_import_kernel, (int)std::min<int64_t>((total + 127) / 128, 4096), 128, 0, s, vtype, raw, n_tok, xq);
     SDY_LAUNCHED();
 }
 
 void xq_export(const XQ &xq, uint8_t *raw, cudaStream_t s) {
     int64_t total = (int64_t)xq.n_tok * xq.nbx;
     if (total <= 0) return;
-    xq_export_kernel<<<(int)std::min<int64_t>((total + 127) / 128, 4096), 128, 0, s>>>(xq, raw);
+    launch(xq_export_kernel, (int)std::min<int64_t>((total + 127) / 128, 4096), 128, 0, s, xq, raw);
     SDY_LAUNCHED();
 }
 

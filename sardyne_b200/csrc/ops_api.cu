@@ -39,6 +39,10 @@ bool cuda_check(cudaError_t e, const char *what, const char *file, int line) {
     return false;
 }
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+bool pdl_enabled() {
+    static const bool on = getenv("SARDYNE_NO_PDL") == nullptr;
+    return on;
+}
 
 // ------------------------------------------------------------------------------ staging
 

@@ -26,7 +26,7 @@ namespace {
 
 constexpr int THREADS = 256;
 constexpr int CTAS_PER_SM = 4;
-constexpr int SMEM_BUDGET = 48 * 1024;  // keeps CTAS_PER_SM resident for one token
+constexpr int SMEM_BUDGET = 48 * 1024;  // keeps up to CTAS_PER_SM resident for one token
 constexpr int SMEM_LIMIT = 200 * 1024;
 
 __device__ __forceinline__ uint4 ldg16(const uint8_t *p) { return __ldg((const uint4 *)p); }
@@ -73,17 +73,75 @@ __host__ __device__ inline Smem smem_plan(int type, int NT, int qrow, int nb, in
     return m;
 }
 
-// ---------------------------------------------------------------------------- per-pair kernels
-// Each writes the block term of token t to terms[(t * nb + b) * rows + rl].
+// ---------------------------------------------------------------------------- per-pair work
+// A pair's weight bytes are first loaded into registers (Raw), then combined with the staged
+// activations. Splitting the two lets each thread load its first pair before pdl_wait, so the
+// DRAM latency of the weights overlaps the kernel that produces the activations.
 
-template <int NT>
-__device__ __forceinline__ void pair_q4k(const uint8_t *slab, int r, int b, const uint8_t *sq, int qrow,
-                                         const float *sd, const int32_t *sbs, int nb, float *terms, int rows,
-                                         int rl) {
-    const uint4 hdr = ldg16(slab + r * 16);
-    uint4 q[8];
+template <int TYPE> struct Raw;
+template <> struct Raw<T_Q4_K> { uint4 hdr, q[8]; };
+template <> struct Raw<T_Q6_K> { uint4 ql[8], qh[4], sc; uint32_t d; };
+template <> struct Raw<T_Q8_0> { uint4 qa[8], qb[8]; uint32_t d[8]; };
+template <> struct Raw<T_Q4_0> { uint4 qa[8]; uint32_t d[8]; };
+template <> struct Raw<T_Q5_0> { uint4 qa[8]; uint32_t qh[8], d[8]; };
+
+__device__ __forceinline__ uint32_t ldg_u16(const uint8_t *p) { return __ldg((const unsigned short *)p); }
+
+// gslabs: the group's first slab; u: pair column (superblock, or run of 8 blocks); r: row.
+__device__ __forceinline__ void load_pair(Raw<T_Q4_K> &w, const uint8_t *gslabs, int u, int r, int) {
+    const uint8_t *slab = gslabs + (size_t)u * slab_bytes(T_Q4_K);
+    w.hdr = ldg16(slab + r * 16);
 #pragma unroll
-    for (int c = 0; c < 8; c++) q[c] = ldg16(slab + 128 + c * 128 + r * 16);
+    for (int c = 0; c < 8; c++) w.q[c] = ldg16(slab + 128 + c * 128 + r * 16);
+}
+__device__ __forceinline__ void load_pair(Raw<T_Q6_K> &w, const uint8_t *gslabs, int u, int r, int) {
+    const uint8_t *slab = gslabs + (size_t)u * slab_bytes(T_Q6_K);
+#pragma unroll
+    for (int c = 0; c < 8; c++) w.ql[c] = ldg16(slab + c * 128 + r * 16);
+#pragma unroll
+    for (int c = 0; c < 4; c++) w.qh[c] = ldg16(slab + 1024 + c * 128 + r * 16);
+    w.sc = ldg16(slab + 1536 + r * 16);
+    w.d = ldg_u16(slab + 1664 + r * 2);
+}
+__device__ __forceinline__ void load_pair(Raw<T_Q8_0> &w, const uint8_t *gslabs, int u, int r, int nb) {
+    const int nblk = min(8, nb - u * 8);
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+        if (i < nblk) {
+            const uint8_t *slab = gslabs + (size_t)(u * 8 + i) * slab_bytes(T_Q8_0);
+            w.qa[i] = ldg16(slab + r * 16);
+            w.qb[i] = ldg16(slab + 128 + r * 16);
+            w.d[i] = ldg_u16(slab + 256 + r * 2);
+        }
+}
+__device__ __forceinline__ void load_pair(Raw<T_Q4_0> &w, const uint8_t *gslabs, int u, int r, int nb) {
+    const int nblk = min(8, nb - u * 8);
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+        if (i < nblk) {
+            const uint8_t *slab = gslabs + (size_t)(u * 8 + i) * slab_bytes(T_Q4_0);
+            w.qa[i] = ldg16(slab + r * 16);
+            w.d[i] = ldg_u16(slab + 128 + r * 2);
+        }
+}
+__device__ __forceinline__ void load_pair(Raw<T_Q5_0> &w, const uint8_t *gslabs, int u, int r, int nb) {
+    const int nblk = min(8, nb - u * 8);
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+        if (i < nblk) {
+            const uint8_t *slab = gslabs + (size_t)(u * 8 + i) * slab_bytes(T_Q5_0);
+            w.qa[i] = ldg16(slab + r * 16);
+            w.qh[i] = __ldg((const uint32_t *)(slab + 128 + r * 4));
+            w.d[i] = ldg_u16(slab + 160 + r * 2);
+        }
+}
+
+// Each writes the block term of token t to terms[(t * nb + b) * rows + rl].
+template <int NT>
+__device__ __forceinline__ void pair_terms(const Raw<T_Q4_K> &w, int b, const uint8_t *sq, int qrow,
+                                           const float *sd, const int32_t *sbs, int nb, float *terms, int rows,
+                                           int rl) {
+    const uint4 hdr = w.hdr;
     const float d = h2f(hdr.x & 0xFFFF), dmin = h2f(hdr.x >> 16);
     // 6-bit scales and mins (quant.h:72-80), four per word.
     const uint32_t sc0 = hdr.y & 0x3F3F3F3F, m0 = hdr.z & 0x3F3F3F3F;
@@ -97,10 +155,10 @@ __device__ __forceinline__ void pair_q4k(const uint8_t *slab, int r, int b, cons
         for (int j = 0; j < 4; j++) {  // 64 elements: low nibbles -> sub-block 2j, high -> 2j+1
             int slo = 0, shi = 0;
 #pragma unroll
-            for (int w = 0; w < 8; w++) {
-                uint32_t qw = word(q[2 * j + (w >> 2)], w & 3);
-                slo = __dp4a((int)(qw & 0x0F0F0F0F), y[16 * j + w], slo);
-                shi = __dp4a((int)((qw >> 4) & 0x0F0F0F0F), y[16 * j + 8 + w], shi);
+            for (int k = 0; k < 8; k++) {
+                uint32_t qw = word(w.q[2 * j + (k >> 2)], k & 3);
+                slo = __dp4a((int)(qw & 0x0F0F0F0F), y[16 * j + k], slo);
+                shi = __dp4a((int)((qw >> 4) & 0x0F0F0F0F), y[16 * j + 8 + k], shi);
             }
             const uint32_t scw = j < 2 ? sc0 : sc1;
             const int s_lo = (scw >> (16 * (j & 1))) & 0xFF, s_hi = (scw >> (16 * (j & 1) + 8)) & 0xFF;
@@ -122,16 +180,10 @@ __device__ __forceinline__ void pair_q4k(const uint8_t *slab, int r, int b, cons
 }
 
 template <int NT>
-__device__ __forceinline__ void pair_q6k(const uint8_t *slab, int r, int b, const uint8_t *sq, int qrow,
-                                         const float *sd, const int32_t *sbs, int nb, float *terms, int rows,
-                                         int rl) {
-    uint4 ql[8], qh[4];
-#pragma unroll
-    for (int c = 0; c < 8; c++) ql[c] = ldg16(slab + c * 128 + r * 16);
-#pragma unroll
-    for (int c = 0; c < 4; c++) qh[c] = ldg16(slab + 1024 + c * 128 + r * 16);
-    const uint4 scv = ldg16(slab + 1536 + r * 16);
-    const float d = h2f(*(const uint16_t *)(slab + 1664 + r * 2));
+__device__ __forceinline__ void pair_terms(const Raw<T_Q6_K> &w, int b, const uint8_t *sq, int qrow,
+                                           const float *sd, const int32_t *sbs, int nb, float *terms, int rows,
+                                           int rl) {
+    const float d = h2f(w.d);
 #pragma unroll
     for (int t = 0; t < NT; t++) {
         const int *y = (const int *)(sq + t * qrow + b * XQ_SPAN);
@@ -141,77 +193,64 @@ __device__ __forceinline__ void pair_q6k(const uint8_t *slab, int r, int b, cons
 #pragma unroll
         for (int h = 0; h < 2; h++) {
 #pragma unroll
-            for (int w = 0; w < 8; w++) {
-                const uint32_t QL0 = word(ql[4 * h + (w >> 2)], w & 3);
-                const uint32_t QL1 = word(ql[4 * h + 2 + (w >> 2)], w & 3);
-                const uint32_t QH = word(qh[2 * h + (w >> 2)], w & 3);
+            for (int k = 0; k < 8; k++) {
+                const uint32_t QL0 = word(w.ql[4 * h + (k >> 2)], k & 3);
+                const uint32_t QL1 = word(w.ql[4 * h + 2 + (k >> 2)], k & 3);
+                const uint32_t QH = word(w.qh[2 * h + (k >> 2)], k & 3);
                 // unsigned 6-bit values of elements 128h + 32k + 4w .. +3 (quant.c:62-74)
                 const uint32_t v0 = (QL0 & 0x0F0F0F0F) | ((QH << 4) & 0x30303030);
                 const uint32_t v1 = (QL1 & 0x0F0F0F0F) | ((QH << 2) & 0x30303030);
                 const uint32_t v2 = ((QL0 >> 4) & 0x0F0F0F0F) | (QH & 0x30303030);
                 const uint32_t v3 = ((QL1 >> 4) & 0x0F0F0F0F) | ((QH >> 2) & 0x30303030);
-                const int gw = w >> 2;
-                s[8 * h + 0 + gw] = __dp4a((int)v0, y[32 * h + 0 + w], s[8 * h + 0 + gw]);
-                s[8 * h + 2 + gw] = __dp4a((int)v1, y[32 * h + 8 + w], s[8 * h + 2 + gw]);
-                s[8 * h + 4 + gw] = __dp4a((int)v2, y[32 * h + 16 + w], s[8 * h + 4 + gw]);
-                s[8 * h + 6 + gw] = __dp4a((int)v3, y[32 * h + 24 + w], s[8 * h + 6 + gw]);
+                const int gw = k >> 2;
+                s[8 * h + 0 + gw] = __dp4a((int)v0, y[32 * h + 0 + k], s[8 * h + 0 + gw]);
+                s[8 * h + 2 + gw] = __dp4a((int)v1, y[32 * h + 8 + k], s[8 * h + 2 + gw]);
+                s[8 * h + 4 + gw] = __dp4a((int)v2, y[32 * h + 16 + k], s[8 * h + 4 + gw]);
+                s[8 * h + 6 + gw] = __dp4a((int)v3, y[32 * h + 24 + k], s[8 * h + 6 + gw]);
             }
         }
         // isum = sum_g sc_g * (sum q*y - 32 * bsum_g): exact, as the reference's AVX2 path.
         int isum = 0;
 #pragma unroll
-        for (int g = 0; g < 16; g++) isum += (int)(int8_t)(word(scv, g >> 2) >> (8 * (g & 3))) * s[g];
+        for (int g = 0; g < 16; g++) isum += (int)(int8_t)(word(w.sc, g >> 2) >> (8 * (g & 3))) * s[g];
         const int32_t *bw = sbs + (t * nb + b) * 8;
         int corr = 0;
 #pragma unroll
         for (int i = 0; i < 8; i++)
-            corr = (i & 1) ? __dp2a_hi(bw[i], (int)word(scv, i >> 1), corr) : __dp2a_lo(bw[i], (int)word(scv, i >> 1), corr);
+            corr = (i & 1) ? __dp2a_hi(bw[i], (int)word(w.sc, i >> 1), corr)
+                           : __dp2a_lo(bw[i], (int)word(w.sc, i >> 1), corr);
         isum -= 32 * corr;
         const float yd = sd[t * nb + b];
         terms[(t * nb + b) * rows + rl] = __fmul_rn(__fmul_rn(yd, d), __int2float_rn(isum));
     }
 }
 
-// 32-element formats: one lane handles blocks b0 .. b0+7 (clipped to nb) of one row.
-template <int TYPE, int NT>
-__device__ __forceinline__ void pair_q0(const uint8_t *slabs_g, int r, int b0, const uint8_t *sq, int qrow,
-                                        const float *sd, const int32_t *ssum, int nb, float *terms, int rows,
-                                        int rl) {
-    constexpr int SB = slab_bytes(TYPE);
-    const int nblk = min(8, nb - b0);
-#pragma unroll 2
-    for (int i = 0; i < nblk; i++) {
-        const int b = b0 + i;
-        const uint8_t *slab = slabs_g + (size_t)b * SB;
-        uint4 qa, qb;
-        uint32_t qh = 0, dbits;
-        qa = ldg16(slab + r * 16);
-        if (TYPE == T_Q8_0) {
-            qb = ldg16(slab + 128 + r * 16);
-            dbits = *(const uint16_t *)(slab + 256 + r * 2);
-        } else if (TYPE == T_Q4_0) {
-            dbits = *(const uint16_t *)(slab + 128 + r * 2);
-        } else {
-            qh = __ldg((const uint32_t *)(slab + 128 + r * 4));
-            dbits = *(const uint16_t *)(slab + 160 + r * 2);
-        }
-        const float dw = h2f(dbits);
+// 32-element formats: the pair is blocks 8u .. 8u+7 (clipped to nb) of one row.
+template <int TYPE, int NT, class R>
+__device__ __forceinline__ void pair_terms_q0(const R &w, int u, const uint8_t *sq, int qrow, const float *sd,
+                                              const int32_t *ssum, int nb, float *terms, int rows, int rl) {
+    const int nblk = min(8, nb - u * 8);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        if (i >= nblk) break;
+        const int b = u * 8 + i;
+        const float dw = h2f(w.d[i]);
 #pragma unroll
         for (int t = 0; t < NT; t++) {
             const int *y = (const int *)(sq + t * qrow + xq_pos(32 * b));
             int s = 0;
-            if (TYPE == T_Q8_0) {
+            if constexpr (TYPE == T_Q8_0) {
 #pragma unroll
-                for (int k = 0; k < 4; k++) s = __dp4a((int)word(qa, k), y[k], s);
+                for (int k = 0; k < 4; k++) s = __dp4a((int)word(w.qa[i], k), y[k], s);
 #pragma unroll
-                for (int k = 0; k < 4; k++) s = __dp4a((int)word(qb, k), y[4 + k], s);
+                for (int k = 0; k < 4; k++) s = __dp4a((int)word(w.qb[i], k), y[4 + k], s);
             } else {
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
-                    uint32_t lo = word(qa, k) & 0x0F0F0F0F, hi = (word(qa, k) >> 4) & 0x0F0F0F0F;
-                    if (TYPE == T_Q5_0) {
-                        lo |= spread4((qh >> (4 * k)) & 15);
-                        hi |= spread4((qh >> (16 + 4 * k)) & 15);
+                    uint32_t lo = word(w.qa[i], k) & 0x0F0F0F0F, hi = (word(w.qa[i], k) >> 4) & 0x0F0F0F0F;
+                    if constexpr (TYPE == T_Q5_0) {
+                        lo |= spread4((w.qh[i] >> (4 * k)) & 15);
+                        hi |= spread4((w.qh[i] >> (16 + 4 * k)) & 15);
                     }
                     s = __dp4a((int)lo, y[k], s);
                     s = __dp4a((int)hi, y[4 + k], s);
@@ -222,6 +261,15 @@ __device__ __forceinline__ void pair_q0(const uint8_t *slabs_g, int r, int b0, c
             terms[(t * nb + b) * rows + rl] = __fmul_rn(__int2float_rn(s), __fmul_rn(dw, sd[t * nb + b]));
         }
     }
+}
+
+template <int TYPE, int NT>
+__device__ __forceinline__ void pair_compute(const Raw<TYPE> &w, int u, const uint8_t *sq, int qrow, const float *sd,
+                                             const int32_t *ss, int nb, float *terms, int rows, int rl) {
+    if constexpr (TYPE == T_Q4_K || TYPE == T_Q6_K)
+        pair_terms<NT>(w, u, sq, qrow, sd, ss, nb, terms, rows, rl);
+    else
+        pair_terms_q0<TYPE, NT>(w, u, sq, qrow, sd, ss, nb, terms, rows, rl);
 }
 
 // ---------------------------------------------------------------------------- the kernel
@@ -243,6 +291,22 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
     const float *xd = a.xd;
     const int32_t *xsums = (const int32_t *)a.xsums;
     float *out = a.out;
+    // This CTA's contiguous share of the launch's groups, swept in batches of a.G groups.
+    const int64_t gA = a.g_begin + a.n_groups * blockIdx.x / gridDim.x;
+    const int64_t gB = a.g_begin + a.n_groups * (blockIdx.x + 1) / gridDim.x;
+    const int units = KQ ? nb : (nb + 7) / 8;  // pair columns per row
+    const int ppg = GROUP_ROWS * units;        // pairs per group
+    pdl_trigger();
+    // The thread's first pair (pair tid of the first batch): loaded before waiting on the
+    // activations' producer. For gathered experts the expert id is itself produced upstream.
+    Raw<TYPE> w;
+    const int G0 = (int)((gB - gA) < a.G ? (gB - gA) : a.G);
+    const bool pre = !a.slot_expert && tid < G0 * ppg;
+    if (pre) {
+        const int gl = tid / ppg, rem = tid - gl * ppg;
+        load_pair(w, slabs + (size_t)(gA + gl) * nb * SB, rem >> 3, rem & 7, nb);
+    }
+    pdl_wait();
     if (a.slot_expert) {
         const int slot = blockIdx.y, e = a.slot_expert[slot];
         if (e < 0 || e >= a.n_expert) return;
@@ -273,26 +337,16 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
     }
     __syncthreads();
 
-    // This CTA's contiguous share of the launch's groups.
-    const int64_t gA = a.g_begin + a.n_groups * blockIdx.x / gridDim.x;
-    const int64_t gB = a.g_begin + a.n_groups * (blockIdx.x + 1) / gridDim.x;
-    const int units = KQ ? nb : (nb + 7) / 8;  // pair columns per row
     for (int64_t gb = gA; gb < gB; gb += a.G) {
         const int G = (int)((gB - gb) < a.G ? (gB - gb) : a.G);
         const int rows = G * GROUP_ROWS;
         const int npairs = rows * units;
         for (int p = tid; p < npairs; p += THREADS) {
-            const int gl = p / (GROUP_ROWS * units);
-            const int rem = p - gl * GROUP_ROWS * units;
+            const int gl = p / ppg;
+            const int rem = p - gl * ppg;
             const int u = rem >> 3, r = rem & 7;
-            const int rl = gl * GROUP_ROWS + r;
-            const uint8_t *gslabs = slabs + (size_t)(gb + gl) * nb * SB;
-            if (TYPE == T_Q4_K)
-                pair_q4k<NT>(gslabs + (size_t)u * SB, r, u, sq, a.qrow, sd, ss, nb, terms, rows, rl);
-            else if (TYPE == T_Q6_K)
-                pair_q6k<NT>(gslabs + (size_t)u * SB, r, u, sq, a.qrow, sd, ss, nb, terms, rows, rl);
-            else
-                pair_q0<TYPE, NT>(gslabs, r, u * 8, sq, a.qrow, sd, ss, nb, terms, rows, rl);
+            if (!(pre && gb == gA && p == tid)) load_pair(w, slabs + (size_t)(gb + gl) * nb * SB, u, r, nb);
+            pair_compute<TYPE, NT>(w, u, sq, a.qrow, sd, ss, nb, terms, rows, gl * GROUP_ROWS + r);
         }
         __syncthreads();
         // Ordered combine: the reference adds block terms left to right (acc = acc + term).
@@ -321,7 +375,7 @@ void launch_one(const Args &a, int smem, dim3 grid, cudaStream_t s) {
         SDY_CUDA(cudaFuncSetAttribute(qmv_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT));
         configured.fetch_or(bit);
     }
-    qmv_kernel<TYPE, NT><<<grid, THREADS, smem, s>>>(a);
+    launch(qmv_kernel<TYPE, NT>, grid, THREADS, smem, s, a);
 }
 
 template <int TYPE>
@@ -346,6 +400,42 @@ int sm_count() {
     return n;
 }
 
+// Resident CTAs per SM of one instantiation at the shared-memory budget (register use differs
+// by format and token count), at most CTAS_PER_SM; cached per (type, nt).
+template <int TYPE, int NT>
+int occupancy_one() {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qmv_kernel<TYPE, NT>, THREADS, SMEM_BUDGET) != cudaSuccess)
+        n = 1;
+    return std::max(1, std::min(n, CTAS_PER_SM));
+}
+template <int TYPE>
+int occupancy_nt(int nt) {
+    switch (nt) {
+    case 1: return occupancy_one<TYPE, 1>();
+    case 2: return occupancy_one<TYPE, 2>();
+    case 3: return occupancy_one<TYPE, 3>();
+    case 4: return occupancy_one<TYPE, 4>();
+    default: return occupancy_one<TYPE, 8>();
+    }
+}
+int ctas_per_sm(int type, int nt) {
+    static std::atomic<int> cache[5][9];  // 0 = not yet queried
+    const int ti = type == T_Q4_K ? 0 : type == T_Q6_K ? 1 : type == T_Q8_0 ? 2 : type == T_Q4_0 ? 3 : 4;
+    const int ni = nt >= 8 ? 8 : nt;
+    int v = cache[ti][ni].load();
+    if (v) return v;
+    switch (type) {
+    case T_Q4_K: v = occupancy_nt<T_Q4_K>(nt); break;
+    case T_Q6_K: v = occupancy_nt<T_Q6_K>(nt); break;
+    case T_Q8_0: v = occupancy_nt<T_Q8_0>(nt); break;
+    case T_Q4_0: v = occupancy_nt<T_Q4_0>(nt); break;
+    default: v = occupancy_nt<T_Q5_0>(nt); break;
+    }
+    cache[ti][ni].store(v);
+    return v;
+}
+
 void dispatch(int type, int nt, const Args &a, int smem, dim3 grid, cudaStream_t s) {
     switch (type) {
     case T_Q4_K: launch_nt<T_Q4_K>(nt, a, smem, grid, s); break;
@@ -358,16 +448,21 @@ void dispatch(int type, int nt, const Args &a, int smem, dim3 grid, cudaStream_t
     SDY_LAUNCHED();
 }
 
-// Launch shape: CTAS_PER_SM CTAs per SM (never more than one per group), each sweeping its
-// contiguous share of groups in batches of G groups; G is the whole share when its block terms
-// fit the shared-memory budget (one ordered combine per CTA), else as many as fit.
+// Launch shape: at most CTAS_PER_SM CTAs per SM and at least THREADS pairs per CTA where the
+// matrix has them, each CTA sweeping its contiguous share of groups in batches of G groups; G is
+// the whole share when its block terms fit the shared-memory budget (one ordered combine per
+// CTA), else as many as fit.
 
 struct Plan {
     int grid = 0, G = 0, nt = 0, smem = 0;
 };
 
 bool plan_launch(int type, int nb, int qrow, int64_t ng, int64_t cta_cap, int nt_want, Plan *p) {
-    p->grid = (int)std::max<int64_t>(1, std::min<int64_t>(ng, cta_cap));
+    // Enough groups per CTA that every thread has a pair: small matrices then take about one CTA
+    // per SM, which leaves room on the SMs for the next kernel's CTAs to be placed early.
+    const int units = (type == T_Q4_K || type == T_Q6_K) ? nb : (nb + 7) / 8;
+    const int64_t gmin = std::max(1, THREADS / (GROUP_ROWS * units));
+    p->grid = (int)std::max<int64_t>(1, std::min<int64_t>((ng + gmin - 1) / gmin, cta_cap));
     const int64_t per_cta = (ng + p->grid - 1) / p->grid;
     int nt = nt_want;
     for (;;) {
@@ -400,7 +495,8 @@ void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0,
     for (int t0 = 0; t0 < xq.n_tok;) {
         int rem = xq.n_tok - t0;
         Plan plan;
-        if (!plan_launch(w.type, w.nb, xq.qrow, ng, (int64_t)sm_count() * CTAS_PER_SM, rem >= 8 ? 8 : rem >= 4 ? 4 : rem,
+        const int nt_want = rem >= 8 ? 8 : rem >= 4 ? 4 : rem;
+        if (!plan_launch(w.type, w.nb, xq.qrow, ng, (int64_t)sm_count() * ctas_per_sm(w.type, nt_want), nt_want,
                          &plan)) {
             set_error("qmatvec: row of %d elements too long for one CTA", w.n_in);
             return;
@@ -439,7 +535,8 @@ void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq
         set_error("qmatvec_gather: activation type/size does not match the weights");
         return;
     }
-    const int64_t cap = std::max<int64_t>(1, ((int64_t)sm_count() * CTAS_PER_SM + n_slots - 1) / n_slots);
+    const int64_t cap =
+        std::max<int64_t>(1, ((int64_t)sm_count() * ctas_per_sm(experts.type, 1) + n_slots - 1) / n_slots);
     Plan plan;
     if (!plan_launch(experts.type, experts.nb, xq.qrow, gpe, cap, 1, &plan)) {
         set_error("qmatvec_gather: row of %d elements too long for one CTA", experts.n_in);
