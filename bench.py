@@ -60,12 +60,15 @@ def alg_bytes(fmt, n_out, n_in):
     return weight_bytes(fmt, n_out, n_in) + 4 * n_in + 4 * n_out
 
 
-def make_inputs(seed=0):
+def make_inputs(seed=0, only=None):
+    """The sweep's matrices; `only` ("Q6_K:151936") keeps one format/row count (profiling runs)."""
     from sardyne_b200 import kquant
     rng = np.random.default_rng(seed)
     mats = []
     for fmt in FORMATS:
         for n_out, n_in in SHAPES:
+            if only and only != f"{fmt}:{n_out}":
+                continue
             if n_out * n_in <= 32 * 1024 * 1024:
                 w = (rng.standard_normal((n_out, n_in)) * 0.02).astype(np.float32)
                 raw = kquant.quantize(w, fmt)
@@ -246,7 +249,9 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     lib = capi.lib()
-    mats, xs = make_inputs()
+    mats, xs = make_inputs(only=args.only)
+    if not mats:
+        raise SystemExit(f"--only {args.only}: no such matrix in the sweep")
     stream = torch.cuda.Stream(device=dev)
     sp = ctypes.c_void_p(stream.cuda_stream)
 
@@ -463,6 +468,13 @@ def run_decode(args):
             logits = ctx.eval([nxt])
         t2 = time.perf_counter()
     capi.check()
+    if args.profile_step:  # one more decode step between profiler start/stop, after the timed region
+        import torch.cuda.profiler as prof
+        torch.cuda.synchronize()
+        prof.start()
+        ctx.eval([int(np.argmax(logits))])
+        torch.cuda.synchronize()
+        prof.stop()
     wbytes = weight_bytes_per_token(path, info)
     peak, peak_kind = load_peaks()
     tps = n_decode / (t2 - t1)
@@ -496,6 +508,9 @@ def main():
     ap.add_argument("--model", choices=sorted(DECODE_MODELS), default="qwen3moe")
     ap.add_argument("--model-dir", default=os.environ.get("SARDYNE_BENCH_DIR", "/tmp"))
     ap.add_argument("--decode-steps", type=int, default=0)
+    ap.add_argument("--profile-step", action="store_true",
+                    help="decode: run one extra step between cudaProfilerStart/Stop (ncu --profile-from-start off)")
+    ap.add_argument("--only", default=None, help="matvec: keep one matrix, e.g. Q6_K:151936 (for ncu captures)")
     args = ap.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

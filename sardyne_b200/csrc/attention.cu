@@ -9,15 +9,17 @@
 //   one cluster of AC = 8 CTAs per (KV head, token), serving the n_rep query heads that share
 //   the KV head (GQA), so each K/V row is read from HBM once for all of them;
 //   phase A  CTA c scores keys [c*L, (c+1)*L): K tiles staged with cp.async, one key per thread,
-//            dot products in the reference's four-accumulator order (ops.c:155-167), scores to
-//            the scratch rows in global memory;
+//            dot products in the reference's four-accumulator order (ops.c:155-167), scores kept
+//            in the CTA's shared memory;
 //   phase B  max and double sum of exp(s - max) per head reduced across the cluster through
 //            distributed shared memory (two cluster barriers);
 //   phase C  CTA c owns elements [c*S, (c+1)*S) of every head: n_rep*S exact chains, fed by
-//            double-buffered cp.async chunks of probabilities and of the V columns it needs.
+//            chunks of exponentials read from their owners' shared memory and double-buffered
+//            cp.async chunks of the V columns it needs (the first chunk requested in phase A).
 //
 // A per-head kernel (one CTA per (head, token)) covers the shapes the cluster kernel does not
-// (head_dim not a multiple of 32, more than 32 query heads per KV head, unaligned buffers).
+// (head_dim not a multiple of 32, more than 32 query heads per KV head, unaligned buffers, a
+// context too long for the scores to stay in shared memory).
 #include "fp_device.cuh"
 #include "fp_ops.cuh"
 
@@ -47,19 +49,37 @@ constexpr int AC_KC = 256;        // keys per chunk (phase C)
 constexpr int AC_PLD = AC_KC + 4; // probability row stride in shared memory (rows on distinct banks)
 constexpr int AC_MAX_REP = 32;    // query heads per KV head
 constexpr int AC_MAX_GROUP = AC * AC_THREADS;  // n_rep * hd: one chain per thread in phase C
+constexpr int AC_SMEM_LIMIT = 200 * 1024;
 
-__host__ __device__ inline int ac_smem_floats(int n_rep, int hd) {
-    const int a = 2 * AC_KT * (hd + 4), c = 2 * (n_rep * AC_PLD + AC_KC * (hd / AC));
-    return n_rep * hd + (a > c ? a : c);
+// Scores row length per head: this CTA's share of the keys, at most ceil(stride / AC).
+__host__ __device__ inline int ac_lmax(int stride) { return ((stride + AC - 1) / AC + 3) & ~3; }
+struct AcSmem {
+    int qs, scl, vb, work, total;  // float offsets
+};
+__host__ __device__ inline AcSmem ac_smem(int n_rep, int hd, int stride) {
+    AcSmem m;
+    const int S = hd / AC;
+    m.qs = 0;
+    m.scl = n_rep * hd;
+    m.vb = m.scl + n_rep * ac_lmax(stride);
+    m.work = m.vb + 2 * AC_KC * S;
+    const int a = 2 * AC_KT * (hd + 4), c = 2 * n_rep * AC_PLD;
+    m.total = m.work + (a > c ? a : c);
+    return m;
 }
 
-// q: token t at q + t*ldq, heads of hd; k/v cache [n_kv_head][stride][hd]; scratch rows of
-// stride floats per (token, head); the first token's position is *pos_dev when given, else pos0;
-// fixed_nkv > 0 overrides the causal count. hd % (4*AC) == 0, stride % 4 == 0, n_rep <= 32.
+// q: token t at q + t*ldq, heads of hd; k/v cache [n_kv_head][stride][hd]; the first token's
+// position is *pos_dev when given, else pos0; fixed_nkv > 0 overrides the causal count.
+// hd % (4*AC) == 0, stride % 4 == 0, n_rep <= 32, n_rep*hd <= AC*AC_THREADS.
+//
+// Shared memory: q of the n_rep heads; this CTA's scores (then exponentials) per head, which the
+// other CTAs of the cluster read in phase C through distributed shared memory; two V chunks of
+// this CTA's column slice (the first one requested together with the first K tile); and a work
+// area holding the K tiles in phase A and the probability chunks in phase C.
 __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
     attention_cluster_kernel(float *__restrict__ out, const float *__restrict__ q, int64_t ldq,
                              const float *__restrict__ kc, const float *__restrict__ vc, int n_head, int n_kv_head,
-                             int hd, int pos0, const int32_t *pos_dev, int stride, float *scratch, int fixed_nkv) {
+                             int hd, int pos0, const int32_t *pos_dev, int stride, int fixed_nkv) {
     pdl_trigger();
     extern __shared__ __align__(16) float sm[];
     __shared__ float cmax[AC_MAX_REP], gmax[AC_MAX_REP], ginv[AC_MAX_REP];
@@ -70,11 +90,13 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
     const int n_kv = fixed_nkv > 0 ? fixed_nkv : (pos_dev ? *pos_dev : pos0) + t + 1;
     const int n_rep = n_head / n_kv_head, h0 = g * n_rep;
     const float *kh = kc + (size_t)g * stride * hd, *vh = vc + (size_t)g * stride * hd;
-    float *sc0 = scratch + ((size_t)t * n_head + h0) * stride;  // head r's row at sc0 + r*stride
-    float *qs = sm, *buf = sm + n_rep * hd;
+    const AcSmem lay = ac_smem(n_rep, hd, stride);
+    const int lmax = ac_lmax(stride);
+    float *qs = sm + lay.qs, *scl = sm + lay.scl, *vb = sm + lay.vb, *work = sm + lay.work;
     const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
     const int L = (n_kv + AC - 1) / AC;
     const int jb = min(n_kv, c * L), je = min(n_kv, jb + L);
+    const int S = hd / AC, S4 = S / 4, e0 = c * S;
     // The positions are host-written before the step's first kernel, so n_kv is known here. While
     // the previous kernel (which stores the newest K/V rows) finishes, pull this CTA's K rows and
     // the same V rows into L2: a cache hint only, the reads below still follow pdl_wait.
@@ -84,64 +106,84 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(vh + (size_t)jb * hd), "r"(bytes) : "memory");
     }
     pdl_wait();
-    for (int i = tid; i < n_rep * hd; i += AC_THREADS) qs[i] = q[(size_t)t * ldq + (size_t)h0 * hd + i];
 
-    // ---- phase A: scores of this CTA's keys
+    // ---- phase A: scores of this CTA's keys into scl
     const int ldk = hd + 4, hd4 = hd / 4;  // padded rows: a quarter-warp's 16-byte reads hit all banks once
     const int kk = tid % AC_KT, hg = tid / AC_KT;
     const int ntile = (je - jb + AC_KT - 1) / AC_KT;
     auto load_k = [&](int it) {
         const int j0 = jb + it * AC_KT, nk = min(AC_KT, je - j0);
-        float *dst = buf + (it & 1) * AC_KT * ldk;
+        float *dst = work + (it & 1) * AC_KT * ldk;
         for (int idx = tid; idx < nk * hd4; idx += AC_THREADS) {
             const int j = idx / hd4, i = (idx - j * hd4) * 4;
             cp_async16(dst + j * ldk + i, kh + (size_t)(j0 + j) * hd + i);
         }
-        cp_async_commit();
+    };
+    auto load_v = [&](int ic) {  // V columns [e0, e0+S) of chunk ic's keys into vb[ic & 1]
+        const int j0 = ic * AC_KC, nk = min(AC_KC, n_kv - j0);
+        float *dst = vb + (ic & 1) * AC_KC * S;
+        for (int idx = tid; idx < nk * S4; idx += AC_THREADS) {
+            const int j = idx / S4, i = (idx - j * S4) * 4;
+            cp_async16(dst + j * S + i, vh + (size_t)(j0 + j) * hd + e0 + i);
+        }
     };
     if (ntile > 0) load_k(0);
-    __syncthreads();  // qs
+    load_v(0);  // phase C's first chunk travels with the first K tile
+    cp_async_commit();
+    for (int i = tid; i < n_rep * hd; i += AC_THREADS) qs[i] = q[(size_t)t * ldq + (size_t)h0 * hd + i];
     for (int it = 0; it < ntile; it++) {
         if (it + 1 < ntile) {
             load_k(it + 1);
+            cp_async_commit();
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
         }
         __syncthreads();
-        const int j = jb + it * AC_KT + kk;
-        if (j < je) {
-            const float *row = buf + (it & 1) * AC_KT * ldk + kk * ldk;
+        const int jl = it * AC_KT + kk;  // index within this CTA's keys
+        if (jb + jl < je) {
+            const float *row = work + (it & 1) * AC_KT * ldk + kk * ldk;
             for (int r0 = hg; r0 < n_rep; r0 += 2 * AC_HG) {
                 const int r1 = r0 + AC_HG;
                 const bool two = r1 < n_rep;
                 const float *x0 = qs + r0 * hd, *x1 = qs + (two ? r1 : r0) * hd;
                 float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f, b0 = 0.0f, b1 = 0.0f, b2 = 0.0f, b3 = 0.0f;
-                for (int i = 0; i < hd; i += 4) {
-                    const float4 k4 = *(const float4 *)(row + i);
-                    const float4 u = *(const float4 *)(x0 + i), w = *(const float4 *)(x1 + i);
-                    a0 = __fadd_rn(a0, __fmul_rn(u.x, k4.x));
-                    a1 = __fadd_rn(a1, __fmul_rn(u.y, k4.y));
-                    a2 = __fadd_rn(a2, __fmul_rn(u.z, k4.z));
-                    a3 = __fadd_rn(a3, __fmul_rn(u.w, k4.w));
-                    b0 = __fadd_rn(b0, __fmul_rn(w.x, k4.x));
-                    b1 = __fadd_rn(b1, __fmul_rn(w.y, k4.y));
-                    b2 = __fadd_rn(b2, __fmul_rn(w.z, k4.z));
-                    b3 = __fadd_rn(b3, __fmul_rn(w.w, k4.w));
+                for (int i0 = 0; i0 < hd; i0 += 16) {  // loads of 16 elements issued ahead of their adds
+                    float4 k4[4], u[4], w[4];
+#pragma unroll
+                    for (int v = 0; v < 4; v++) {
+                        k4[v] = *(const float4 *)(row + i0 + 4 * v);
+                        u[v] = *(const float4 *)(x0 + i0 + 4 * v);
+                        w[v] = *(const float4 *)(x1 + i0 + 4 * v);
+                    }
+#pragma unroll
+                    for (int v = 0; v < 4; v++) {
+                        a0 = __fadd_rn(a0, __fmul_rn(u[v].x, k4[v].x));
+                        a1 = __fadd_rn(a1, __fmul_rn(u[v].y, k4[v].y));
+                        a2 = __fadd_rn(a2, __fmul_rn(u[v].z, k4[v].z));
+                        a3 = __fadd_rn(a3, __fmul_rn(u[v].w, k4[v].w));
+                        b0 = __fadd_rn(b0, __fmul_rn(w[v].x, k4[v].x));
+                        b1 = __fadd_rn(b1, __fmul_rn(w[v].y, k4[v].y));
+                        b2 = __fadd_rn(b2, __fmul_rn(w[v].z, k4[v].z));
+                        b3 = __fadd_rn(b3, __fmul_rn(w[v].w, k4[v].w));
+                    }
                 }
-                sc0[(size_t)r0 * stride + j] = __fmul_rn(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)), scale);
-                if (two)
-                    sc0[(size_t)r1 * stride + j] = __fmul_rn(__fadd_rn(__fadd_rn(b0, b1), __fadd_rn(b2, b3)), scale);
+                scl[r0 * lmax + jl] = __fmul_rn(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)), scale);
+                if (two) scl[r1 * lmax + jl] = __fmul_rn(__fadd_rn(__fadd_rn(b0, b1), __fadd_rn(b2, b3)), scale);
             }
         }
         __syncthreads();
     }
+    if (ntile == 0) {
+        cp_async_wait<0>();
+        __syncthreads();
+    }
 
     // ---- phase B: cluster-wide max and sum of exponentials per head
+    const int nl = je - jb;
     for (int r = warp; r < n_rep; r += AC_THREADS / 32) {
-        const float *row = sc0 + (size_t)r * stride;
         float m = -INFINITY;
-        for (int j = jb + lane; j < je; j += 32) m = fmaxf(m, row[j]);
+        for (int j = lane; j < nl; j += 32) m = fmaxf(m, scl[r * lmax + j]);
         for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (lane == 0) cmax[r] = m;
     }
@@ -153,65 +195,56 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
     }
     __syncthreads();
     for (int r = warp; r < n_rep; r += AC_THREADS / 32) {
-        float *row = sc0 + (size_t)r * stride;
         const float m = gmax[r];
-        double s = 0.0;
-        for (int j = jb + lane; j < je; j += 32) {
-            const float e = exp_cr(__fsub_rn(row[j], m));
-            row[j] = e;
-            s += e;
+        double sacc = 0.0;
+        for (int j = lane; j < nl; j += 32) {
+            const float e = exp_cr(__fsub_rn(scl[r * lmax + j], m));
+            scl[r * lmax + j] = e;
+            sacc += e;
         }
-        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) csum[r] = s;
+        for (int o = 16; o; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
+        if (lane == 0) csum[r] = sacc;
     }
-    cl.sync();  // also publishes every CTA's exponentials in the scratch rows
+    cl.sync();  // also publishes every CTA's exponentials for phase C
     if (tid < n_rep) {
-        double s = 0.0;
-        for (int p = 0; p < AC; p++) s += *cl.map_shared_rank(csum + tid, p);
-        ginv[tid] = (float)(1.0 / s);
+        double sacc = 0.0;
+        for (int p = 0; p < AC; p++) sacc += *cl.map_shared_rank(csum + tid, p);
+        ginv[tid] = (float)(1.0 / sacc);
     }
-    cluster_arrive();  // done with the other CTAs' shared memory; the matching wait is at the end
     __syncthreads();
 
     // ---- phase C: out[e] = sum_j (e_j * inv) * v_j[e] in key order, e in this CTA's slice
-    const int S = hd / AC, S4 = S / 4, e0 = c * S;
     const int ch_r = tid / S, ch_e = tid - ch_r * S;
     const bool chain = tid < n_rep * S;
     const float inv = chain ? ginv[ch_r] : 0.0f;
-    float *pbuf = buf, *vbuf = buf + 2 * n_rep * AC_PLD;
     const int nchunk = (n_kv + AC_KC - 1) / AC_KC;
-    auto load_c = [&](int ic) {
-        const int j0 = ic * AC_KC, nk = min(AC_KC, n_kv - j0), nk4 = (nk + 3) / 4;
-        float *pb = pbuf + (ic & 1) * n_rep * AC_PLD, *vb = vbuf + (ic & 1) * AC_KC * S;
-        for (int idx = tid; idx < n_rep * nk4; idx += AC_THREADS) {
-            const int r = idx / nk4, j = (idx - r * nk4) * 4;
-            cp_async16(pb + r * AC_PLD + j, sc0 + (size_t)r * stride + j0 + j);
+    auto load_p = [&](int ic) {  // exponentials of chunk ic's keys, from their owners' shared memory
+        const int j0 = ic * AC_KC, nk = min(AC_KC, n_kv - j0);
+        float *pb = work + (ic & 1) * n_rep * AC_PLD;
+        for (int idx = tid; idx < n_rep * nk; idx += AC_THREADS) {
+            const int r = idx / nk, jj = idx - r * nk, j = j0 + jj, owner = j / L;
+            pb[r * AC_PLD + jj] = *cl.map_shared_rank(scl + r * lmax + (j - owner * L), owner);
         }
-        for (int idx = tid; idx < nk * S4; idx += AC_THREADS) {
-            const int j = idx / S4, i = (idx - j * S4) * 4;
-            cp_async16(vb + j * S + i, vh + (size_t)(j0 + j) * hd + e0 + i);
-        }
-        cp_async_commit();
     };
     float acc = 0.0f;
-    if (nchunk > 0) load_c(0);
+    load_p(0);
     for (int ic = 0; ic < nchunk; ic++) {
         if (ic + 1 < nchunk) {
-            load_c(ic + 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
+            load_v(ic + 1);
+            cp_async_commit();
         }
         __syncthreads();
         if (chain) {
-            const float *pr = pbuf + (ic & 1) * n_rep * AC_PLD + ch_r * AC_PLD;
-            const float *vr = vbuf + (ic & 1) * AC_KC * S + ch_e;
+            const float *pr = work + (ic & 1) * n_rep * AC_PLD + ch_r * AC_PLD;
+            const float *vr = vb + (ic & 1) * AC_KC * S + ch_e;
             const int nk = min(AC_KC, n_kv - ic * AC_KC);
-#pragma unroll 8
-            for (int j = 0; j < nk; j++) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(pr[j], inv), vr[j * S]));
+            acc = ordered_sum<16>(acc, nk, [&](int j) { return __fmul_rn(__fmul_rn(pr[j], inv), vr[j * S]); });
         }
+        if (ic + 1 < nchunk) load_p(ic + 1);
+        cp_async_wait<0>();
         __syncthreads();
     }
+    cluster_arrive();  // done reading the other CTAs' shared memory; the matching wait is at the end
     if (chain) out[((size_t)t * n_head + h0 + ch_r) * hd + e0 + ch_e] = acc;
     cluster_wait();
 }
@@ -295,17 +328,19 @@ void attention(float *out, const float *q, int64_t ldq, const float *kc, const f
     }
     const int n_rep = n_head / n_kv_head;
     const bool cluster = hd % (4 * AC) == 0 && stride % 4 == 0 && n_rep <= AC_MAX_REP &&
-                         n_rep * hd <= AC_MAX_GROUP && aligned16(kc) && aligned16(vc) && aligned16(scratch) &&
-                         ac_smem_floats(n_rep, hd) * 4 <= 200 * 1024 && n_kv_head <= 65535 && n_tok <= 65535;
+                         n_rep * hd <= AC_MAX_GROUP && aligned16(kc) && aligned16(vc) &&
+                         (size_t)ac_smem(n_rep, hd, stride).total * 4 <= AC_SMEM_LIMIT && n_kv_head <= 65535 &&
+                         n_tok <= 65535;
     if (cluster) {
-        const size_t smem = (size_t)ac_smem_floats(n_rep, hd) * 4;
+        const size_t smem = (size_t)ac_smem(n_rep, hd, stride).total * 4;
         static bool configured = false;
         if (!configured) {
             SDY_CUDA(cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          200 * 1024));
+                                          AC_SMEM_LIMIT));
             configured = true;
         }
-        launch(attention_cluster_kernel, dim3(AC, n_kv_head, n_tok), AC_THREADS, smem, s, out, q, ldq, kc, vc, n_head, n_kv_head, hd, pos0, pos_dev, stride, scratch, fixed_nkv);
+        launch(attention_cluster_kernel, dim3(AC, n_kv_head, n_tok), AC_THREADS, smem, s, out, q, ldq, kc, vc, n_head,
+               n_kv_head, hd, pos0, pos_dev, stride, fixed_nkv);
         SDY_LAUNCHED();
         return;
     }

@@ -133,6 +133,22 @@ void note_launch();
 // only once they have completed, so no later kernel's early weight reads can overlap them.
 // Launched without the attribute (SARDYNE_NO_PDL set), both instructions are no-ops.
 #ifdef __CUDACC__
+// acc + term(0) + term(1) + ... + term(n-1), added left to right with every sum rounded (the
+// reference's sequential loops). The terms of a batch of B are evaluated (their loads issued)
+// before the batch's dependent adds, so load latency is paid once per batch, not once per term.
+template <int B, class Term>
+__device__ __forceinline__ float ordered_sum(float acc, int n, Term term) {
+    int j = 0;
+    for (; j + B <= n; j += B) {
+        float v[B];
+#pragma unroll
+        for (int u = 0; u < B; u++) v[u] = term(j + u);
+#pragma unroll
+        for (int u = 0; u < B; u++) acc = __fadd_rn(acc, v[u]);
+    }
+    for (; j < n; j++) acc = __fadd_rn(acc, term(j));
+    return acc;
+}
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 #endif

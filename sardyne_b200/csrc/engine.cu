@@ -128,6 +128,7 @@ struct engine_ctx {
     float *x = nullptr, *xb = nullptr, *qkv = nullptr, *att = nullptr, *hgu = nullptr, *tmp = nullptr,
           *logits = nullptr, *scores = nullptr;
     float *moe_probs = nullptr, *moe_w = nullptr, *moe_gu = nullptr, *moe_y = nullptr;
+    int32_t *moe_count = nullptr;  // per-token router counters (router_topk)
     int32_t *moe_top = nullptr;
     int32_t *tokpos = nullptr;    // device: [0] position of the first token, [1..] token ids
     int32_t *h_tokpos = nullptr;  // pinned staging of the same
@@ -135,8 +136,13 @@ struct engine_ctx {
     XQ xq[2];
     ActCache xc[2];
     float *h_logits = nullptr;             // pinned host copy returned by engine_logits
-    cudaGraphExec_t step_graph = nullptr;  // the single-token forward, replayed each decode step
+    // The single-token forward as a chain of graphs of a few layers each, replayed each decode step:
+    // launching a graph costs host time per node, so the GPU starts on the first segment while
+    // the host still launches the later ones.
+    std::vector<cudaGraphExec_t> step_graphs;
     int graph_state = 0;  // 0: next single-token step runs eagerly, 2: capture next, 1: captured, -1: off
+    bool capturing = false;
+    bool capture_ok = true;
     char err[256] = {0};
 };
 
@@ -587,7 +593,8 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n) {
     const int dim = in.dim, fe = in.ffn_exp_dim, ne = in.n_expert, k = in.n_expert_used;
     const DMat &r = L.gate_inp;
     if (!r.quant()) {
-        router_topk(c->xb, dim, r.f, r.type, dim, ne, k, n, c->moe_top, c->moe_w, c->moe_probs, c->st);
+        router_topk(c->xb, dim, r.f, r.type, dim, ne, k, n, c->moe_top, c->moe_w, c->moe_probs, c->moe_count,
+                    c->st);
     } else {
         matmul(c, c->moe_probs, ne, c->xb, dim, r, n);
         softmax(c->moe_probs, ne, ne, n, c->st);
@@ -624,6 +631,8 @@ std::vector<const DMat *> mats_of(const Proj &p) {
 
 // n <= n_batch tokens at the position stored in tokpos[0]; logits of the last out_rows tokens
 // (model_llama.c:757-832).
+void maybe_segment(engine_ctx *c, int layer);
+
 void forward(engine_ctx *c, int n, int out_rows) {
     const engine_model *m = c->m;
     const engine_model_info &in = m->info;
@@ -633,6 +642,7 @@ void forward(engine_ctx *c, int n, int out_rows) {
     const XQ *q8k, *q80;
     embed(c, n);
     for (int l = 0; l < in.n_layer; l++) {
+        maybe_segment(c, l);
         const DLayer &L = m->layers[l];
         float *kc = c->k_cache + l * layer_stride, *vc = c->v_cache + l * layer_stride;
         // attention: x = x + Wo . Attn(RoPE(Wq.norm(x)), RoPE(Wk.norm(x)), Wv.norm(x))
@@ -695,6 +705,34 @@ void forward(engine_ctx *c, int n, int out_rows) {
 // One engine step of `chunk` tokens: staged token ids and position, then the forward. The
 // single-token forward runs eagerly once, is captured as a CUDA graph on the next single-token
 // step, and is replayed from then on (positions and ids are read from device memory).
+void drop_graphs(engine_ctx *c) {
+    for (cudaGraphExec_t e : c->step_graphs) cudaGraphExecDestroy(e);
+    c->step_graphs.clear();
+}
+
+// Ends the capture in progress, instantiates it as the next segment and, unless `last`, opens the
+// next capture. Failures are recorded in c->capture_ok.
+void capture_segment(engine_ctx *c, bool last) {
+    cudaGraph_t g = nullptr;
+    bool ok = SDY_CUDA(cudaStreamEndCapture(c->st, &g)) && g;
+    cudaGraphExec_t e = nullptr;
+    ok = ok && SDY_CUDA(cudaGraphInstantiate(&e, g, 0));
+    if (g) cudaGraphDestroy(g);
+    if (ok) c->step_graphs.push_back(e);
+    c->capture_ok = c->capture_ok && ok;
+    if (!last && c->capture_ok)
+        c->capture_ok = SDY_CUDA(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
+}
+
+// Segment boundary inside forward(): every GRAPH_LAYERS layers while capturing.
+constexpr int GRAPH_LAYERS = 4;
+void maybe_segment(engine_ctx *c, int layer) {
+    if (c->capturing && c->capture_ok && layer > 0 && layer % GRAPH_LAYERS == 0) capture_segment(c, false);
+}
+
+// One engine step of `chunk` tokens: staged token ids and position, then the forward. The
+// single-token forward runs eagerly once, is captured as CUDA graphs on the next single-token
+// step, and is replayed from then on (positions and ids are read from device memory).
 void step(engine_ctx *c, const int32_t *tokens, int chunk, int out_rows) {
     c->h_tokpos[0] = c->n_past;
     memcpy(c->h_tokpos + 1, tokens, (size_t)chunk * 4);
@@ -704,7 +742,7 @@ void step(engine_ctx *c, const int32_t *tokens, int chunk, int out_rows) {
         return;
     }
     if (c->graph_state == 1) {
-        SDY_CUDA(cudaGraphLaunch(c->step_graph, c->st));
+        for (cudaGraphExec_t e : c->step_graphs) SDY_CUDA(cudaGraphLaunch(e, c->st));
         return;
     }
     if (c->graph_state == 0) {
@@ -712,18 +750,24 @@ void step(engine_ctx *c, const int32_t *tokens, int chunk, int out_rows) {
         c->graph_state = 2;
         return;
     }
-    cudaGraph_t g = nullptr;
-    bool ok = SDY_CUDA(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
-    if (ok) {
+    c->capture_ok = SDY_CUDA(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
+    if (c->capture_ok) {
+        c->capturing = true;
         forward(c, 1, 1);
-        ok = SDY_CUDA(cudaStreamEndCapture(c->st, &g)) && g;
+        c->capturing = false;
+        if (c->capture_ok) capture_segment(c, true);
     }
-    ok = ok && SDY_CUDA(cudaGraphInstantiate(&c->step_graph, g, 0));
-    if (g) cudaGraphDestroy(g);
-    if (ok) {
+    if (c->capture_ok) {
         c->graph_state = 1;
-        SDY_CUDA(cudaGraphLaunch(c->step_graph, c->st));
+        for (cudaGraphExec_t e : c->step_graphs) SDY_CUDA(cudaGraphLaunch(e, c->st));
     } else {  // capture unavailable: stay eager for this context
+        cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(c->st, &st) == cudaSuccess && st != cudaStreamCaptureStatusNone) {
+            cudaGraph_t g = nullptr;
+            cudaStreamEndCapture(c->st, &g);
+            if (g) cudaGraphDestroy(g);
+        }
+        drop_graphs(c);
         clear_error();
         cudaGetLastError();
         c->graph_state = -1;
@@ -869,6 +913,7 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
     };
     if (in.n_expert) {
         items.push_back({(void **)&c->moe_probs, B * in.n_expert * 4});
+        items.push_back({(void **)&c->moe_count, B * 4});
         items.push_back({(void **)&c->moe_w, slots * 4});
         items.push_back({(void **)&c->moe_top, slots * 4});
         items.push_back({(void **)&c->moe_gu, slots * 2 * ffn * 4});
@@ -895,6 +940,11 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
         *it.dst = p;
         p += align_up(it.bytes, 256);
     }
+    if (c->moe_count && !SDY_CUDA(cudaMemset(c->moe_count, 0, B * 4))) {  // router counters start at zero
+        put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
+        engine_ctx_free(c);
+        return nullptr;
+    }
     size_t lbytes = (c->logits_all ? B : 1) * in.n_vocab * 4;
     if (!SDY_CUDA(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking)) ||
         !SDY_CUDA(cudaMallocHost(&c->h_logits, lbytes)) || !SDY_CUDA(cudaMallocHost(&c->h_tokpos, (B + 1) * 4))) {
@@ -915,7 +965,7 @@ int32_t engine_ctx_n_threads(const engine_ctx *c) { return c ? c->n_threads : 0;
 
 void engine_ctx_free(engine_ctx *c) {
     if (!c) return;
-    if (c->step_graph) cudaGraphExecDestroy(c->step_graph);
+    drop_graphs(c);
     if (c->st) cudaStreamDestroy(c->st);
     if (c->arena) cudaFree(c->arena);
     if (c->h_logits) cudaFreeHost(c->h_logits);

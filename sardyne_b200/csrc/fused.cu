@@ -9,6 +9,8 @@
 // In the norm and SiLU kernels lane l of warp w owns elements 256w + 8l .. +7 in registers, so
 // each warp quantizes its own 256-element span without staging through shared memory.
 #include "fp_device.cuh"
+
+#include <algorithm>
 #include "fused.cuh"
 #include "quant_device.cuh"
 
@@ -139,7 +141,7 @@ __global__ void post_qkv_kernel(PostQKV p) {
 // Router logits for float weights: one warp per expert row. The warp copies x and its row into
 // shared memory with coalesced loads; lanes 0..3 then run the reference's four accumulator
 // chains (ops.c:155-167: s_k over i = 4g + k, the tail into s0) and combine (s0+s1)+(s2+s3).
-constexpr int ROUTER_WARPS = 2;  // experts per CTA: one warp each
+constexpr int ROUTER_THREADS = 128;
 
 __device__ __forceinline__ float4 load4_w(const void *w, int wtype, size_t i) {  // i a multiple of 4
     if (wtype == T_F32) return *(const float4 *)((const float *)w + i);
@@ -152,64 +154,14 @@ __device__ __forceinline__ float4 load4_w(const void *w, int wtype, size_t i) { 
                        __uint_as_float(u.y & 0xFFFF0000u));
 }
 
-// logits[t][e] = x[t] . w[e] with the reference's four-accumulator dot (ops.c:155-167): the row
-// and x are staged in shared memory with 16-byte loads, then lanes 0-3 of the expert's warp each
-// run one accumulator's chain (unrolled, so the shared-memory reads run ahead of the adds).
-// vec: dim % 4 == 0 and x rows 16-byte aligned.
-__global__ void router_logits_kernel(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne,
-                                     float *logits, int vec) {
-    pdl_trigger();
-    extern __shared__ __align__(16) float sm[];
-    float *xs = sm, *rows = sm + ((dim + 3) & ~3);
-    const int t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e = blockIdx.x * ROUTER_WARPS + warp;
-    const float *xv = x + (size_t)t * ldx;
-    float *row = rows + (size_t)warp * ((dim + 3) & ~3);
-    const size_t base = (size_t)e * dim;
-    // The router row is a constant weight: staged before waiting for the previous kernel.
-    if (e < ne) {
-        if (vec) {
-#pragma unroll 4
-            for (int i = lane * 4; i < dim; i += 128) *(float4 *)(row + i) = load4_w(w, wtype, base + i);
-        } else {
-            for (int i = lane; i < dim; i += 32) row[i] = load_w(w, wtype, base + i);
-        }
-    }
-    pdl_wait();
-    if (vec) {
-        for (int i = threadIdx.x * 4; i < dim; i += blockDim.x * 4) *(float4 *)(xs + i) = *(const float4 *)(xv + i);
-    } else {
-        for (int i = threadIdx.x; i < dim; i += blockDim.x) xs[i] = xv[i];
-    }
-    __syncthreads();
-    if (e >= ne) return;
-    float s = 0.0f;
-    if (lane < 4) {
-        const int groups = dim / 4;
-        const float *xa = xs + lane, *ra = row + lane;
-#pragma unroll 8
-        for (int g = 0; g < groups; g++) s = __fadd_rn(s, __fmul_rn(xa[4 * g], ra[4 * g]));
-        if (lane == 0)
-            for (int i = groups * 4; i < dim; i++) s = __fadd_rn(s, __fmul_rn(xs[i], row[i]));
-    }
-    const float s1 = __shfl_sync(0xffffffffu, s, 1), s2 = __shfl_sync(0xffffffffu, s, 2),
-                s3 = __shfl_sync(0xffffffffu, s, 3);
-    if (lane == 0) logits[(size_t)t * ne + e] = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
-}
-
-// Softmax (ops.c:353-364) and top-k (model_llama.c:653-666), one CTA per token. The reference's
-// insertion keeps the k largest probabilities in descending order, equal values in ascending
-// expert id; here warp 0 takes k rounds of a warp-wide argmax under that same order. Weights are
-// renormalised by their float sum taken in the selected order.
-__global__ void softmax_topk_kernel(const float *logits, int ne, int k, int32_t *top, float *wout) {
-    pdl_trigger();
-    pdl_wait();
-    extern __shared__ __align__(16) float prob[];  // [ne] probabilities, [ne] selection keys
-    __shared__ double dpart[32];
-    __shared__ float fpart[32];
-    float *key = prob + ne;
-    const int t = blockIdx.x;
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = logits[(size_t)t * ne + e];
+// Softmax (ops.c:353-364) and top-k (model_llama.c:653-666) of one token's ne logits by the whole
+// block. The reference's insertion keeps the k largest probabilities in descending order, equal
+// values in ascending expert id; here warp 0 takes k rounds of a warp-wide argmax under that
+// same order. Weights are renormalised by their float sum taken in the selected order.
+// prob, key: shared arrays of ne floats.
+__device__ void softmax_topk_block(const float *logits, float *prob, float *key, int ne, int k, int32_t *tp,
+                                   float *wout, double *dpart, float *fpart) {
+    for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = __ldcg(logits + e);
     __syncthreads();
     float m = -INFINITY;
     for (int e = threadIdx.x; e < ne; e += blockDim.x) m = fmaxf(m, prob[e]);
@@ -226,7 +178,6 @@ __global__ void softmax_topk_kernel(const float *logits, int ne, int k, int32_t 
     __syncthreads();
     if (threadIdx.x >= 32) return;
     const int lane = threadIdx.x;
-    int32_t *tp = top + (size_t)t * k;
     float s = 0.0f;
     for (int r = 0; r < k; r++) {
         float bv = -1.0f;  // probabilities are >= 0; taken entries hold -1
@@ -249,28 +200,92 @@ __global__ void softmax_topk_kernel(const float *logits, int ne, int k, int32_t 
         __syncwarp();
     }
     if (lane == 0)
-        for (int i = 0; i < k; i++) wout[(size_t)t * k + i] = __fdiv_rn(prob[tp[i]], s);
+        for (int i = 0; i < k; i++) wout[i] = __fdiv_rn(prob[tp[i]], s);
 }
 
-// x[t] += sum over t's k slots, in ascending expert id, of w * y[slot].
+// Float router, one CTA per (expert, token): logits[t][e] = x[t] . w[e] with the reference's
+// four-accumulator dot (ops.c:155-167) — the row (a constant weight, staged before pdl_wait) and
+// x go through shared memory with 16-byte loads, then lanes 0-3 run one accumulator chain each.
+// The last CTA of a token to finish (a counter per token, left at zero again) runs the softmax
+// and top-k over the token's logits. vec: dim % 4 == 0 and 16-byte aligned x rows / weights.
+__global__ void __launch_bounds__(ROUTER_THREADS)
+    router_topk_kernel(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, float *logits,
+                       int32_t *counters, int32_t *top, float *wout, int vec) {
+    pdl_trigger();
+    extern __shared__ __align__(16) float sm[];
+    __shared__ double dpart[32];
+    __shared__ float fpart[32];
+    __shared__ int last;
+    const int dp = (dim + 3) & ~3;
+    float *xs = sm, *row = sm + dp;
+    const int e = blockIdx.x, t = blockIdx.y, tid = threadIdx.x;
+    const size_t base = (size_t)e * dim;
+    if (vec) {
+#pragma unroll 4
+        for (int i = tid * 4; i < dim; i += ROUTER_THREADS * 4) *(float4 *)(row + i) = load4_w(w, wtype, base + i);
+    } else {
+        for (int i = tid; i < dim; i += ROUTER_THREADS) row[i] = load_w(w, wtype, base + i);
+    }
+    pdl_wait();
+    const float *xv = x + (size_t)t * ldx;
+    if (vec) {
+        for (int i = tid * 4; i < dim; i += ROUTER_THREADS * 4) *(float4 *)(xs + i) = *(const float4 *)(xv + i);
+    } else {
+        for (int i = tid; i < dim; i += ROUTER_THREADS) xs[i] = xv[i];
+    }
+    __syncthreads();
+    if (tid < 32) {
+        float s = 0.0f;
+        if (tid < 4) {
+            const int groups = dim / 4;
+            const float *xa = xs + tid, *ra = row + tid;
+            s = ordered_sum<16>(s, groups, [&](int g) { return __fmul_rn(xa[4 * g], ra[4 * g]); });
+            if (tid == 0)
+                for (int i = groups * 4; i < dim; i++) s = __fadd_rn(s, __fmul_rn(xs[i], row[i]));
+        }
+        const float s1 = __shfl_sync(0xffffffffu, s, 1), s2 = __shfl_sync(0xffffffffu, s, 2),
+                    s3 = __shfl_sync(0xffffffffu, s, 3);
+        if (tid == 0) {
+            logits[(size_t)t * ne + e] = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
+            __threadfence();
+            last = atomicAdd(counters + t, 1) == ne - 1;
+        }
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (tid == 0) counters[t] = 0;
+    softmax_topk_block(logits + (size_t)t * ne, sm, sm + ne, ne, k, top + (size_t)t * k, wout + (size_t)t * k, dpart,
+                       fpart);
+}
+
+// x[t] += sum over t's k slots, in ascending expert id, of w * y[slot]. The slots are ranked once
+// per CTA in shared memory (ties keep slot order); each element then adds its k terms in that
+// order with the loads issued ahead of the adds.
 __global__ void moe_combine_kernel(const float *y, int64_t ldy, const int32_t *top, const float *w, int k, int dim,
                                    float *x, int64_t ldx) {
     pdl_trigger();
     pdl_wait();
+    __shared__ int order[64];
+    __shared__ float ws[64];
     const int t = blockIdx.y;
-    int order[64];
-    for (int i = 0; i < k; i++) order[i] = i;
-    for (int i = 1; i < k; i++) {
-        int s = order[i], j = i;
-        while (j > 0 && top[(size_t)t * k + order[j - 1]] > top[(size_t)t * k + s]) { order[j] = order[j - 1]; j--; }
-        order[j] = s;
-    }
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) {
-        float acc = 0.0f;
+    const int32_t *tt = top + (size_t)t * k;
+    if ((int)threadIdx.x < k) {
+        const int i = threadIdx.x, ei = tt[i];
+        int rank = 0;
         for (int j = 0; j < k; j++) {
-            int s = order[j];
-            acc = __fadd_rn(acc, __fmul_rn(w[(size_t)t * k + s], y[((size_t)t * k + s) * ldy + i]));
+            const int ej = tt[j];
+            rank += (ej < ei || (ej == ei && j < i));
         }
+        order[rank] = i;
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < k) ws[threadIdx.x] = w[(size_t)t * k + order[threadIdx.x]];
+    __syncthreads();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) {
+        const float acc = ordered_sum<8>(0.0f, k, [&](int j) {
+            return __fmul_rn(ws[j], y[((size_t)t * k + order[j]) * ldy + i]);
+        });
         float *xp = x + (size_t)t * ldx + i;
         *xp = __fadd_rn(*xp, acc);
     }
@@ -310,23 +325,22 @@ void post_qkv(const PostQKV &p, int n_tok, cudaStream_t s) {
 }
 
 void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, int n_tok,
-                 int32_t *top, float *wout, float *logits, cudaStream_t s) {
+                 int32_t *top, float *wout, float *logits, int32_t *counters, cudaStream_t s) {
     if (n_tok <= 0) return;
-    const size_t smem = (size_t)(ROUTER_WARPS + 1) * ((dim + 3) & ~3) * 4;
-    if (smem > 200 * 1024) {
-        set_error("router_topk: hidden size %d too large", dim);
+    const size_t smem = (size_t)2 * std::max((dim + 3) & ~3, ne) * 4;
+    if (smem > 200 * 1024 || n_tok > 65535) {
+        set_error("router_topk: hidden size %d / %d tokens too large", dim, n_tok);
         return;
     }
     static bool configured = false;
     if (!configured) {
-        SDY_CUDA(cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        SDY_CUDA(cudaFuncSetAttribute(router_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         configured = true;
     }
     const bool w_aligned = wtype == T_F32 ? ((uintptr_t)w & 15) == 0 : ((uintptr_t)w & 7) == 0;
     const int vec = dim % 4 == 0 && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0 && w_aligned;
-    launch(router_logits_kernel, dim3((ne + ROUTER_WARPS - 1) / ROUTER_WARPS, n_tok), 32 * ROUTER_WARPS, smem, s, x, ldx, w, wtype, dim, ne, logits, vec);
-    SDY_LAUNCHED();
-    launch(softmax_topk_kernel, n_tok, 128, (size_t)ne * 8, s, logits, ne, k, top, wout);
+    launch(router_topk_kernel, dim3(ne, n_tok), ROUTER_THREADS, smem, s, x, ldx, w, wtype, dim, ne, k, logits,
+           counters, top, wout, vec);
     SDY_LAUNCHED();
 }
 

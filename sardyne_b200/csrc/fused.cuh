@@ -28,9 +28,10 @@ struct PostQKV {
 // Bias, qk-norm, RoPE on q and k, then k and v into the KV cache.
 void post_qkv(const PostQKV &p, int n_tok, cudaStream_t s);
 
-// Float router: top [n_tok][k] expert ids and renormalised weights; logits is scratch [n_tok][ne].
+// Float router: top [n_tok][k] expert ids and renormalised weights; logits is scratch [n_tok][ne];
+// counters: n_tok int32 that start at zero (the kernel leaves them at zero).
 void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, int n_tok,
-                 int32_t *top, float *wout, float *logits, cudaStream_t s);
+                 int32_t *top, float *wout, float *logits, int32_t *counters, cudaStream_t s);
 // x[t] += sum over t's k slots in ascending expert id of w * y[slot].
 void moe_combine(const float *y, int64_t ldy, const int32_t *top, const float *w, int k, int dim, int n_tok, float *x,
                  int64_t ldx, cudaStream_t s);

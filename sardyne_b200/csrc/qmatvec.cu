@@ -355,8 +355,7 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
             const int64_t row = gb * GROUP_ROWS + rl;
             if (row < a.row0 || row >= a.row1) continue;
             const float *tp = terms + (size_t)t * nb * rows + rl;
-            float acc = 0.0f;
-            for (int b = 0; b < nb; b++) acc = __fadd_rn(acc, tp[(size_t)b * rows]);
+            const float acc = ordered_sum<8>(0.0f, nb, [&](int b) { return tp[(size_t)b * rows]; });
             const size_t o = (size_t)t * a.ldo + (row - a.out_row0);
             // residual stream: x = x + W.a, the reference's `x[i] += xb[i]` (model_llama.c:804,820)
             out[o] = a.residual ? __fadd_rn(a.residual[o], acc) : acc;
