@@ -133,6 +133,9 @@ const char *sdy_last_error(void);
 void sdy_clear_error(void);
 /* Number of GPU kernels this process has launched through the library (for launch counting). */
 uint64_t sdy_kernel_launches(void);
+/* Nonzero when a kernel's bounded wait on its tensor-core completion barrier ran out (the kernel
+ * then skipped its output and freed its tensor memory); synchronises the device. */
+uint32_t sdy_kernel_status(void);
 
 /* Device-pointer API (current device; `stream` is a cudaStream_t, NULL = legacy default stream).
  * A quantized matrix uploaded once in the device layout, activations quantized on the device,

@@ -101,6 +101,7 @@ EXTENSIONS = {
     "sdy_last_error": (ctypes.c_char_p, []),
     "sdy_clear_error": (None, []),
     "sdy_kernel_launches": (_u64, []),
+    "sdy_kernel_status": (ctypes.c_uint32, []),
     "sdy_qmat_upload": (_vp, [_vp, _i, ctypes.c_int64, _i32]),
     "sdy_qmat_free": (None, [_vp]),
     "sdy_qmat_bytes": (_sz, [_vp]),

@@ -178,6 +178,11 @@ void xq_import(int vtype, const uint8_t *raw, int n_tok, int n_in, const XQ &xq,
 void xq_export(const XQ &xq, uint8_t *raw, cudaStream_t s);
 // out[t*ldo + (r - out_row0)] = W[r] . x[t] for rows r in [row0, row1) and tokens t < xq.n_tok.
 // With `residual`, out = residual + product (same indexing; residual may alias out).
+// Many-token product on the tensor cores (qgemm.cu), same contract as qmatvec; Q4_K/Q6_K only.
+bool qgemm_supported(int type, int n_in);
+void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
+           cudaStream_t s, const float *residual = nullptr);
+unsigned qgemm_status();  // nonzero when a qgemm completion wait timed out
 void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
              cudaStream_t s, const float *residual = nullptr);
 // MoE: for each slot s < n_slots, out[s*ldo_slot + r] = E[slot_expert[s]][r] . x[s / tok_div] for

@@ -157,6 +157,7 @@ const char *engine_version(void) { return "0.0.1"; }
 const char *sdy_last_error(void) { return last_error(); }
 void sdy_clear_error(void) { clear_error(); }
 uint64_t sdy_kernel_launches(void) { return g_launches.load(); }
+uint32_t sdy_kernel_status(void) { return qgemm_status(); }
 
 static int g_simd = 1;
 int op_simd(void) { return g_simd; }

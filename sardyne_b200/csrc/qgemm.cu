@@ -1,0 +1,378 @@
+// Prefill GEMM for Q4_K / Q6_K weights on the 5th-generation tensor cores: y[t][r] = W[r] . x[t]
+// for many tokens, bit-identical to the reference's per-block integer dot products (reference
+// csrc/quant.c:176-235 and the combine of quant.h:84-91), which the matvec reproduces too.
+//
+// Exactness. Per 256-element superblock b the reference forms integer sums and rounds one float
+// term per (row, token, b), added to the row's total in block order. The integer sums become
+// int8 MMAs (tcgen05.mma kind::i8, int32 accumulators in TMEM):
+//   Q4_K  isum = sum_e sc(e) q(e) y(e) with sc*q <= 945 split as 32*hi + lo (hi <= 29, lo <= 31),
+//         msum = sum_e m(e) y(e) with the 6-bit min of e's sub-block repeated over its 32 lanes;
+//   Q6_K  isum = sum_e sc(e) (q(e) - 32) y(e), the product in [-4064, 4096] split as 64*hi + lo
+//         (hi in [-64, 64], lo in [0, 63]).
+// So the A operand of a tile is the expanded weight products (two or three int8 planes), B the
+// Q8_K activations; every K step of 32 is one MMA per plane into that plane's accumulator. After a
+// superblock's 8 K steps the epilogue reads the accumulators (tcgen05.ld), rebuilds isum/msum and
+// applies the reference's float combine, keeping each (row, token) total in registers.
+//
+// Tile: 128 weight rows (MMA M) x 128 tokens (MMA N), 256 threads. Operands sit in shared memory
+// in the no-swizzle K-major core-matrix layout: byte (row, k) of a plane at
+// (k / 16) * (rows * 16) + row * 16 + k % 16, i.e. 8-row x 16-byte core matrices, 128 B apart
+// along M and rows*16 B apart along K. This first version runs the stages of a superblock one
+// after another (expand A and load B, MMA, epilogue).
+#include "common.cuh"
+
+namespace sdy {
+namespace {
+
+constexpr int GM = 128;           // weight rows per tile
+constexpr int GN = 128;           // tokens per tile
+constexpr int G_THREADS = 256;
+constexpr int PLANE = GM * 256;   // bytes of one expanded A plane (one superblock)
+constexpr int BTILE = GN * 256;   // bytes of the B tile
+constexpr uint32_t TMEM_COLS = 512;
+constexpr long long WAIT_LIMIT = 1ll << 22;  // mbarrier polls before giving up (about a second)
+
+__device__ unsigned int g_qgemm_status;  // nonzero: an MMA completion wait timed out
+
+template <int TYPE> struct GemmPlanes { static constexpr int n = TYPE == T_Q4_K ? 3 : 2; };
+
+__host__ __device__ constexpr int g_smem_bytes(int planes) {
+    return planes * PLANE + BTILE + GN * 4 /* yd */ + 2 * GM * 4 /* d, dmin */ + 16 /* mbarrier, tmem */;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// No-swizzle K-major matrix descriptor (version 1): start, LBO = distance of the two 16-byte K
+// halves of a 32-byte K step, SBO = distance of consecutive 8-row core matrices.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
+}
+
+// kind::i8 instruction descriptor: s32 accumulator, s8 A and B, both K-major, M = GM, N = GN.
+constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(GN >> 3) << 17) | ((uint32_t)(GM >> 4) << 24);
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+// Bounded wait for phase `parity` of the mbarrier; false when the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity) {
+    for (long long it = 0; it < WAIT_LIMIT; it++) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(done)
+            : "r"(mbar), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// Byte k of a plane row in the core-matrix layout.
+__device__ __forceinline__ int plane_off(int rows, int row, int k) { return (k >> 4) * (rows * 16) + row * 16 + (k & 15); }
+
+// 4 nibbles (one per byte of L, each 0..15) times the scale s (0..63): products split as
+// 32*hi + lo, returned as 4 hi bytes and 4 lo bytes.
+__device__ __forceinline__ void mul_split32(uint32_t L, uint32_t s, uint32_t &hi, uint32_t &lo) {
+    const uint32_t p0 = (L & 0x00FF00FFu) * s, p1 = ((L >> 8) & 0x00FF00FFu) * s;  // 16-bit lanes, <= 945
+    hi = ((p0 >> 5) & 0x001F001Fu) | (((p1 >> 5) & 0x001F001Fu) << 8);
+    lo = (p0 & 0x001F001Fu) | ((p1 & 0x001F001Fu) << 8);
+}
+
+// Expand one (row, superblock) half of the A tile. Q4_K: part p covers the slab's chunks 4p..4p+3
+// (elements 128p .. 128p+127), Q6_K: half p of the superblock.
+template <int TYPE>
+__device__ __forceinline__ void expand_half(const uint8_t *slab, int r8, int row, int part, uint8_t *sa, float *dr,
+                                            float *dmr) {
+    if constexpr (TYPE == T_Q4_K) {
+        const uint4 hdr = __ldg((const uint4 *)(slab + r8 * 16));
+        const uint32_t sc0 = hdr.y & 0x3F3F3F3F, m0 = hdr.z & 0x3F3F3F3F;
+        const uint32_t sc1 = (hdr.w & 0x0F0F0F0F) | ((hdr.y >> 2) & 0x30303030);
+        const uint32_t m1 = ((hdr.w >> 4) & 0x0F0F0F0F) | ((hdr.z >> 2) & 0x30303030);
+        if (part == 0) {
+            dr[row] = __half2float(__ushort_as_half((uint16_t)(hdr.x & 0xFFFF)));
+            dmr[row] = __half2float(__ushort_as_half((uint16_t)(hdr.x >> 16)));
+        }
+        uint4 q[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) q[i] = __ldg((const uint4 *)(slab + 128 + (4 * part + i) * 128 + r8 * 16));
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int c = 4 * part + i, j = c >> 1, h = c & 1;  // chunk c: bytes 16h.. of 64-element chunk j
+            const uint32_t scw = j < 2 ? sc0 : sc1, mw = j < 2 ? m0 : m1;
+            const uint32_t s_lo = (scw >> (16 * (j & 1))) & 0xFF, s_hi = (scw >> (16 * (j & 1) + 8)) & 0xFF;
+            const uint32_t m_lo = (mw >> (16 * (j & 1))) & 0xFF, m_hi = (mw >> (16 * (j & 1) + 8)) & 0xFF;
+            uint32_t hl[4], ll[4], hh[4], lh[4];
+            const uint32_t w[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                mul_split32(w[k] & 0x0F0F0F0F, s_lo, hl[k], ll[k]);
+                mul_split32((w[k] >> 4) & 0x0F0F0F0F, s_hi, hh[k], lh[k]);
+            }
+            // low nibbles: elements 64j + 16h + 0..15 (sub-block 2j) -> plane 4j + h
+            // high nibbles: elements 64j + 32 + 16h + 0..15 (sub-block 2j+1) -> plane 4j + 2 + h
+            const int off_l = plane_off(GM, row, 64 * j + 16 * h), off_h = plane_off(GM, row, 64 * j + 32 + 16 * h);
+            *(uint4 *)(sa + off_l) = make_uint4(hl[0], hl[1], hl[2], hl[3]);
+            *(uint4 *)(sa + PLANE + off_l) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+            *(uint4 *)(sa + off_h) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+            *(uint4 *)(sa + PLANE + off_h) = make_uint4(lh[0], lh[1], lh[2], lh[3]);
+            const uint32_t ml = m_lo * 0x01010101u, mh = m_hi * 0x01010101u;
+            *(uint4 *)(sa + 2 * PLANE + off_l) = make_uint4(ml, ml, ml, ml);
+            *(uint4 *)(sa + 2 * PLANE + off_h) = make_uint4(mh, mh, mh, mh);
+        }
+    } else {  // Q6_K half `part`: elements 128p .. 128p+127
+        const uint4 scv = __ldg((const uint4 *)(slab + 1536 + r8 * 16));
+        if (part == 0) dr[row] = __half2float(__ushort_as_half(__ldg((const unsigned short *)(slab + 1664 + r8 * 2))));
+        uint4 ql[4], qh[2];
+#pragma unroll
+        for (int c = 0; c < 4; c++) ql[c] = __ldg((const uint4 *)(slab + (4 * part + c) * 128 + r8 * 16));
+#pragma unroll
+        for (int c = 0; c < 2; c++) qh[c] = __ldg((const uint4 *)(slab + 1024 + (2 * part + c) * 128 + r8 * 16));
+        const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+#pragma unroll
+        for (int k = 0; k < 8; k++) {  // the reference's 4-element groups (quant.c:62-74)
+            const uint32_t wql[4] = {ql[k >> 2].x, ql[k >> 2].y, ql[k >> 2].z, ql[k >> 2].w};
+            const uint32_t wql2[4] = {ql[2 + (k >> 2)].x, ql[2 + (k >> 2)].y, ql[2 + (k >> 2)].z, ql[2 + (k >> 2)].w};
+            const uint32_t wqh[4] = {qh[k >> 2].x, qh[k >> 2].y, qh[k >> 2].z, qh[k >> 2].w};
+            const uint32_t QL0 = wql[k & 3], QL1 = wql2[k & 3], QH = wqh[k & 3];
+            const uint32_t v[4] = {(QL0 & 0x0F0F0F0F) | ((QH << 4) & 0x30303030),
+                                   (QL1 & 0x0F0F0F0F) | ((QH << 2) & 0x30303030),
+                                   ((QL0 >> 4) & 0x0F0F0F0F) | (QH & 0x30303030),
+                                   ((QL1 >> 4) & 0x0F0F0F0F) | ((QH >> 2) & 0x30303030)};
+#pragma unroll
+            for (int g = 0; g < 4; g++) {  // elements 128p + 32g + 4k + 0..3
+                const int e0 = 128 * part + 32 * g + 4 * k;
+                const int sc = (int)(int8_t)(scw[e0 >> 6] >> (8 * ((e0 >> 4) & 3)));
+                uint32_t hw = 0, lw = 0;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int prod = sc * ((int)((v[g] >> (8 * i)) & 0xFF) - 32);
+                    hw |= (uint32_t)(prod >> 6 & 0xFF) << (8 * i);
+                    lw |= (uint32_t)(prod & 63) << (8 * i);
+                }
+                const int off = plane_off(GM, row, e0);
+                *(uint32_t *)(sa + off) = hw;
+                *(uint32_t *)(sa + PLANE + off) = lw;
+            }
+        }
+    }
+}
+
+struct GemmArgs {
+    const uint8_t *slabs;
+    int nb;                      // superblocks per row
+    int64_t g_begin, g_end;      // weight row groups of the launch
+    const int8_t *xqs;           // Q8_K activations of token 0
+    const float *xd;
+    int qrow, nbx, n_tok;
+    float *out;
+    int64_t ldo, row0, row1, out_row0;
+    const float *residual;
+};
+
+template <int TYPE>
+__global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
+    constexpr int NP = GemmPlanes<TYPE>::n;
+    constexpr int SB = slab_bytes(TYPE);
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t *sa = smem, *sb = smem + NP * PLANE;
+    float *yd = (float *)(sb + BTILE), *dr = yd + GN, *dmr = dr + GM;
+    uint64_t *mbar = (uint64_t *)(dmr + GM);
+    uint32_t *tmem_slot = (uint32_t *)(mbar + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t gt0 = a.g_begin + (int64_t)blockIdx.x * (GM / GROUP_ROWS);  // first group of the tile
+    const int tok0 = blockIdx.y * GN, nv = min(GN, a.n_tok - tok0);
+    pdl_trigger();
+    pdl_wait();
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+    }
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_u32(mbar)));
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    // Padded tokens keep zero activations for the whole kernel.
+    for (int i = tid; i < BTILE / 16; i += G_THREADS)  // chunk-plane layout: i = plane * GN + t
+        if (i % GN >= nv) ((uint4 *)sb)[i] = make_uint4(0, 0, 0, 0);
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t mbar_a = smem_u32(mbar);
+    const int row = tid & (GM - 1), part = tid >> 7;  // expansion: two threads per weight row
+    const int64_t grow = gt0 * GROUP_ROWS + row;        // this thread's weight row
+    const bool row_ok = grow < a.g_end * GROUP_ROWS;
+    const int erow = (warp & 3) * 32 + lane, ehalf = warp >> 2;  // epilogue: TMEM lane = row, 64 tokens
+    float acc[64];
+#pragma unroll
+    for (int i = 0; i < 64; i++) acc[i] = 0.0f;
+    bool ok = true;
+
+    for (int b = 0; b < a.nb && ok; b++) {
+        // B tile: chunk c of token t at c * GN * 16 + t * 16 (the XQ span keeps 16-byte alignment)
+        for (int i = tid; i < nv * 16; i += G_THREADS) {
+            const int t = i >> 4, c = i & 15;
+            const uint4 v = __ldg((const uint4 *)(a.xqs + (size_t)(tok0 + t) * a.qrow + b * XQ_SPAN + c * 16));
+            *(uint4 *)(sb + c * (GN * 16) + t * 16) = v;
+        }
+        for (int t = tid; t < GN; t += G_THREADS) yd[t] = t < nv ? a.xd[(size_t)(tok0 + t) * a.nbx + b] : 0.0f;
+        if (row_ok) {
+            const uint8_t *slab = a.slabs + ((size_t)(grow / GROUP_ROWS) * a.nb + b) * SB;
+            expand_half<TYPE>(slab, (int)(grow % GROUP_ROWS), row, part, sa, dr, dmr);
+        } else {
+            for (int k = 128 * part; k < 128 * part + 128; k += 16)
+                for (int p = 0; p < NP; p++) *(uint4 *)(sa + p * PLANE + plane_off(GM, row, k)) = make_uint4(0, 0, 0, 0);
+            if (part == 0) dr[row] = dmr[row] = 0.0f;
+        }
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        __syncthreads();
+        if (tid == 0) {
+            fence_after_sync();
+#pragma unroll
+            for (int s = 0; s < 8; s++) {  // K step s: bytes 32s..32s+31 = chunk planes 2s, 2s+1
+                const uint64_t bd = kmajor_desc(smem_u32(sb + 2 * s * GN * 16), GN * 16, 128);
+#pragma unroll
+                for (int p = 0; p < NP; p++)
+                    mma_i8(tmem + p * GN, kmajor_desc(smem_u32(sa + p * PLANE + 2 * s * GM * 16), GM * 16, 128), bd,
+                           s > 0);
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar_a)
+                         : "memory");
+        }
+        if (!mbar_wait(mbar_a, b & 1)) {
+            atomicOr(&g_qgemm_status, 1u);
+            ok = false;
+        }
+        fence_after_sync();
+        if (ok) {
+            const float d = dr[erow], dm = dmr[erow];
+#pragma unroll
+            for (int cc = 0; cc < 2; cc++) {
+                const uint32_t col = ehalf * 64 + cc * 32;
+                const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
+                int32_t h[32], l[32], m[32];
+                tmem_ld32(tmem + lanes + col, h);
+                tmem_ld32(tmem + lanes + GN + col, l);
+                if constexpr (NP == 3) tmem_ld32(tmem + lanes + 2 * GN + col, m);
+                asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const float y = yd[col + i];
+                    float term;
+                    if constexpr (TYPE == T_Q4_K) {
+                        const int isum = 32 * h[i] + l[i];
+                        const float dall = __fmul_rn(y, d), dmn = __fmul_rn(y, dm);
+                        term = __fsub_rn(__fmul_rn(dall, __int2float_rn(isum)), __fmul_rn(dmn, __int2float_rn(m[i])));
+                    } else {
+                        const int isum = 64 * h[i] + l[i];
+                        term = __fmul_rn(__fmul_rn(y, d), __int2float_rn(isum));
+                    }
+                    acc[cc * 32 + i] = __fadd_rn(acc[cc * 32 + i], term);
+                }
+            }
+        }
+        fence_before_sync();
+        __syncthreads();
+    }
+
+    // outputs (rows of this tile within [row0, row1), valid tokens)
+    const int64_t orow = gt0 * GROUP_ROWS + erow;
+    if (ok && orow >= a.row0 && orow < a.row1) {
+#pragma unroll
+        for (int i = 0; i < 64; i++) {
+            const int t = ehalf * 64 + i;
+            if (t < nv) {
+                const size_t o = (size_t)(tok0 + t) * a.ldo + (orow - a.out_row0);
+                a.out[o] = a.residual ? __fadd_rn(a.residual[o], acc[i]) : acc[i];
+            }
+        }
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        fence_after_sync();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TMEM_COLS));
+    }
+}
+
+}  // namespace
+
+bool qgemm_supported(int type, int n_in) { return (type == T_Q4_K || type == T_Q6_K) && n_in % 256 == 0; }
+
+void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
+           cudaStream_t s, const float *residual) {
+    if (row1 <= row0 || xq.n_tok <= 0) return;
+    if (!qgemm_supported(w.type, w.n_in) || xq.vtype != T_Q8_K || xq.n_in != w.n_in) {
+        set_error("qgemm: unsupported weight type %d / activation layout", w.type);
+        return;
+    }
+    GemmArgs a{};
+    a.slabs = w.slabs;
+    a.nb = w.nb;
+    a.g_begin = row0 / GROUP_ROWS;
+    a.g_end = (row1 + GROUP_ROWS - 1) / GROUP_ROWS;
+    a.xqs = xq.qs;
+    a.xd = xq.d;
+    a.qrow = xq.qrow;
+    a.nbx = xq.nbx;
+    a.n_tok = xq.n_tok;
+    a.out = out;
+    a.ldo = ldo;
+    a.row0 = row0;
+    a.row1 = row1;
+    a.out_row0 = out_row0;
+    a.residual = residual;
+    const int64_t tiles_m = (a.g_end - a.g_begin + GM / GROUP_ROWS - 1) / (GM / GROUP_ROWS);
+    const dim3 grid((unsigned)tiles_m, (unsigned)((xq.n_tok + GN - 1) / GN));
+    if (w.type == T_Q4_K) {
+        static bool configured = false;
+        const int smem = g_smem_bytes(3);
+        if (!configured) {
+            SDY_CUDA(cudaFuncSetAttribute(qgemm_kernel<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            configured = true;
+        }
+        launch(qgemm_kernel<T_Q4_K>, grid, G_THREADS, smem, s, a);
+    } else {
+        static bool configured = false;
+        const int smem = g_smem_bytes(2);
+        if (!configured) {
+            SDY_CUDA(cudaFuncSetAttribute(qgemm_kernel<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            configured = true;
+        }
+        launch(qgemm_kernel<T_Q6_K>, grid, G_THREADS, smem, s, a);
+    }
+    SDY_LAUNCHED();
+}
+
+unsigned qgemm_status() {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_qgemm_status, sizeof v) != cudaSuccess) return ~0u;
+    return v;
+}
+
+}  // namespace sdy

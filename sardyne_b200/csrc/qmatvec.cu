@@ -18,6 +18,7 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <atomic>
 
 namespace sdy {
@@ -481,9 +482,24 @@ bool plan_launch(int type, int nb, int qrow, int64_t ng, int64_t cta_cap, int nt
 
 }  // namespace
 
+// Token count from which a product goes to the tensor-core GEMM (SARDYNE_GEMM_MIN_TOKENS; 0 = never).
+int gemm_min_tokens() {
+    static const int v = [] {
+        const char *e = getenv("SARDYNE_GEMM_MIN_TOKENS");
+        return e ? atoi(e) : 32;
+    }();
+    return v;
+}
+
 void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
              cudaStream_t s, const float *residual) {
     if (row1 <= row0 || xq.n_tok <= 0) return;
+    const int gmin = gemm_min_tokens();
+    if (gmin > 0 && xq.n_tok >= gmin && qgemm_supported(w.type, w.n_in) && xq.vtype == T_Q8_K &&
+        xq.n_in == w.n_in) {
+        qgemm(w, xq, out, ldo, row0, row1, out_row0, s, residual);
+        return;
+    }
     if (xq.vtype != vec_dot_type(w.type) || xq.n_in != w.n_in) {
         set_error("qmatvec: activation type/size does not match the weights");
         return;
