@@ -137,6 +137,18 @@ uint64_t sdy_kernel_launches(void);
  * then skipped its output and freed its tensor memory); synchronises the device. */
 uint32_t sdy_kernel_status(void);
 
+/* Sharding across processes, one GPU each (no counterpart in the reference, which runs on one
+ * host). sdy_nccl_unique_id writes the 128-byte NCCL id rank 0 creates and shares with the other
+ * ranks; sdy_engine_set_shard(rank, world, id) configures the next engine_model_load of this
+ * process: world 1 (the default) is the unsharded engine. A sharded model keeps attention and
+ * the router on every rank and splits the FFN rows, the experts and the vocabulary; logits are
+ * gathered on every rank and equal the one-GPU logits bit for bit. */
+int sdy_nccl_unique_id(void *out);
+int sdy_engine_set_shard(int32_t rank, int32_t world, const void *nccl_id);
+void sdy_engine_get_shard(int32_t *rank, int32_t *world);
+/* Rows [*begin, *end) of n that `rank` of `world` holds, in whole units of `align` rows. */
+void sdy_shard_range(int64_t n, int32_t world, int32_t rank, int64_t align, int64_t *begin, int64_t *end);
+
 /* Device-pointer API (current device; `stream` is a cudaStream_t, NULL = legacy default stream).
  * A quantized matrix uploaded once in the device layout, activations quantized on the device,
  * and the matvec on device buffers, for callers that keep everything in HBM. */

@@ -102,6 +102,11 @@ EXTENSIONS = {
     "sdy_clear_error": (None, []),
     "sdy_kernel_launches": (_u64, []),
     "sdy_kernel_status": (ctypes.c_uint32, []),
+    "sdy_nccl_unique_id": (_i, [_vp]),
+    "sdy_engine_set_shard": (_i, [ctypes.c_int32, ctypes.c_int32, _vp]),
+    "sdy_engine_get_shard": (None, [ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]),
+    "sdy_shard_range": (None, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
+                               ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]),
     "sdy_qmat_upload": (_vp, [_vp, _i, ctypes.c_int64, _i32]),
     "sdy_qmat_free": (None, [_vp]),
     "sdy_qmat_bytes": (_sz, [_vp]),

@@ -186,9 +186,11 @@ unsigned qgemm_status();  // nonzero when a qgemm completion wait timed out
 void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
              cudaStream_t s, const float *residual = nullptr);
 // MoE: for each slot s < n_slots, out[s*ldo_slot + r] = E[slot_expert[s]][r] . x[s / tok_div] for
-// r < rows_per_expert. `experts` holds n_expert matrices, each padded to gpe groups. The expert ids
-// are read on the device, so no host round trip sits between the router and the experts.
+// r < rows_per_expert. `experts` holds n_expert matrices (global experts expert0 .. expert0 +
+// n_expert - 1), each padded to gpe groups; slots naming other experts are left untouched. The
+// expert ids are read on the device, so no host round trip sits between the router and the experts.
 void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq, int tok_div, const int32_t *slot_expert,
-                    int n_slots, int64_t rows_per_expert, float *out, int64_t ldo_slot, cudaStream_t s);
+                    int n_slots, int64_t rows_per_expert, float *out, int64_t ldo_slot, cudaStream_t s,
+                    int expert0 = 0);
 
 }  // namespace sdy

@@ -13,10 +13,13 @@
 #include "fused.cuh"
 #include "sardyne_b200.h"
 
+#include <dlfcn.h>
+#include <nccl.h>
 #include <stdarg.h>
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -33,6 +36,47 @@ void put_err(char *err, size_t len, const char *fmt, ...) {
     va_start(ap, fmt);
     vsnprintf(err, len, fmt, ap);
     va_end(ap);
+}
+
+// NCCL, opened on first use (only sharded models need it): the process's already loaded
+// libnccl.so.2 when there is one (e.g. torch's), else the system's.
+struct Nccl {
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    const char *(*error_string)(ncclResult_t) = nullptr;
+};
+const Nccl *nccl() {
+    static Nccl n;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (h) {
+            n.get_unique_id = (decltype(n.get_unique_id))dlsym(h, "ncclGetUniqueId");
+            n.comm_init_rank = (decltype(n.comm_init_rank))dlsym(h, "ncclCommInitRank");
+            n.all_reduce = (decltype(n.all_reduce))dlsym(h, "ncclAllReduce");
+            n.comm_destroy = (decltype(n.comm_destroy))dlsym(h, "ncclCommDestroy");
+            n.error_string = (decltype(n.error_string))dlsym(h, "ncclGetErrorString");
+        }
+    }
+    return n.get_unique_id && n.comm_init_rank && n.all_reduce && n.comm_destroy && n.error_string ? &n : nullptr;
+}
+
+// Process-wide shard configuration for the next engine_model_load (sdy_engine_set_shard).
+struct ShardCfg {
+    int rank = 0, world = 1;
+    ncclUniqueId id{};
+};
+ShardCfg g_shard;
+
+// Rows [b, e) of n for `rank` of `world`, in whole units of `align` rows.
+void shard_range(int64_t n, int world, int rank, int64_t align, int64_t *b, int64_t *e) {
+    const int64_t units = (n + align - 1) / align;
+    *b = std::min<int64_t>(n, units * rank / world * align);
+    *e = std::min<int64_t>(n, units * (rank + 1) / world * align);
 }
 
 // A weight tensor on the device: [n_expert or 1][n_out][n_in].
@@ -102,6 +146,14 @@ struct engine_model {
     gguf_file *gf = nullptr;
     engine_model_info info{};
     int dev = 0;
+    // Sharding across `world` processes, one GPU each (sdy_engine_set_shard before loading):
+    // attention and the router are replicated; this rank holds dense FFN rows [f0, f1) of gate
+    // and up, output rows [d0, d1) of down, experts [e0, e1) and vocabulary rows [v0, v1) of the
+    // output matrix. Every cross-rank exchange is an all-reduce of buffers in which each element
+    // has one nonzero contributor, so results equal the one-GPU forward bit for bit.
+    int rank = 0, world = 1;
+    ncclComm_t comm = nullptr;
+    int64_t f0 = 0, f1 = 0, d0 = 0, d1 = 0, e0 = 0, e1 = 0, v0 = 0, v1 = 0;
     DMat tok_embd, output;
     float *output_norm = nullptr;
     std::vector<DLayer> layers;
@@ -129,6 +181,9 @@ struct engine_ctx {
           *logits = nullptr, *scores = nullptr;
     float *moe_probs = nullptr, *moe_w = nullptr, *moe_gu = nullptr, *moe_y = nullptr;
     int32_t *moe_count = nullptr;  // per-token router counters (router_topk)
+    // Sharded models: all-reduce sources, zero outside this rank's columns (hsend: FFN activations
+    // [B][ffn_dim], xsend: residual [B][dim], lsend: logits), and the gathered FFN activations.
+    float *hsend = nullptr, *hfull = nullptr, *xsend = nullptr, *lsend = nullptr;
     int32_t *moe_top = nullptr;
     int32_t *tokpos = nullptr;    // device: [0] position of the first token, [1..] token ids
     int32_t *h_tokpos = nullptr;  // pinned staging of the same
@@ -337,9 +392,12 @@ const gguf_tensor *check_tensor(engine_model *m, const char *name, int n_in, int
 }
 
 // Uploads tensors of one type that share n_in as ONE device matrix: expert e (or the single
-// matrix) holds the rows of ts[0], then ts[1], ... Quantized rows are repacked into slabs.
+// matrix) holds rows [starts[0], starts[0] + rows[0]) of ts[0], then those of ts[1], ... Of a
+// tensor with experts, experts e_begin .. e_begin + n_expert - 1 are taken (n_expert 0: a plain
+// matrix). Quantized rows are repacked into slabs.
 int upload_group(engine_model *m, const std::vector<const gguf_tensor *> &ts, const std::vector<int64_t> &rows,
-                 int n_in, int n_expert, DMat *out, char *err, size_t len) {
+                 const std::vector<int64_t> &starts, int n_in, int64_t e_begin, int n_expert, DMat *out, char *err,
+                 size_t len) {
     DMat d;
     d.type = (int)ts[0]->type;
     d.n_in = n_in;
@@ -354,7 +412,8 @@ int upload_group(engine_model *m, const std::vector<const gguf_tensor *> &ts, co
     for (int e = 0; ok && e < ne; e++) {
         size_t off = (size_t)e * total * rb;
         for (size_t i = 0; ok && i < ts.size(); i++) {
-            const uint8_t *src = (const uint8_t *)ts[i]->data + (size_t)e * rows[i] * rb;
+            const size_t full = (size_t)ts[i]->ne[1];
+            const uint8_t *src = (const uint8_t *)ts[i]->data + ((size_t)(e_begin + e) * full + starts[i]) * rb;
             ok = SDY_CUDA(cudaMemcpyAsync(raw + off, src, rows[i] * rb, cudaMemcpyHostToDevice, m->st));
             off += rows[i] * rb;
         }
@@ -385,33 +444,44 @@ int upload_group(engine_model *m, const std::vector<const gguf_tensor *> &ts, co
     return 0;
 }
 
+// Rows [r0, r1) (r1 < 0: all) of experts [e_begin, e_end) (e_end < 0: all) of a checked tensor.
 int get_tensor(engine_model *m, const char *name, int n_in, int64_t n_out, int n_expert, DMat *out, char *err,
-               size_t len) {
+               size_t len, int64_t r0 = 0, int64_t r1 = -1, int64_t e_begin = 0, int64_t e_end = -1) {
     const gguf_tensor *t = check_tensor(m, name, n_in, n_out, n_expert, err, len);
     if (!t) return -1;
-    return upload_group(m, {t}, {n_out}, n_in, n_expert, out, err, len);
+    if (r1 < 0) r1 = n_out;
+    if (e_end < 0) e_end = n_expert;
+    return upload_group(m, {t}, {r1 - r0}, {r0}, n_in, e_begin, n_expert ? (int)(e_end - e_begin) : 0, out, err, len);
 }
 
 // A projection from one input: consecutive tensors of the same quantized type whose row counts
-// are whole 8-row groups share one device matrix (one launch); the others stay separate.
+// are whole 8-row groups share one device matrix (one launch); the others stay separate. Rows
+// [r0, r1) of every tensor (r1 < 0: all), experts [e_begin, e_end) (e_end < 0: all).
 int get_proj(engine_model *m, const std::vector<std::string> &names, const std::vector<int64_t> &rows, int n_in,
-             int n_expert, Proj *out, char *err, size_t len) {
+             int n_expert, Proj *out, char *err, size_t len, int64_t r0 = 0, int64_t r1 = -1, int64_t e_begin = 0,
+             int64_t e_end = -1) {
     std::vector<const gguf_tensor *> ts;
+    std::vector<int64_t> cnt, st;
     for (size_t i = 0; i < names.size(); i++) {
         const gguf_tensor *t = check_tensor(m, names[i].c_str(), n_in, rows[i], n_expert, err, len);
         if (!t) return -1;
         ts.push_back(t);
+        cnt.push_back(r1 < 0 ? rows[i] : r1 - r0);
+        st.push_back(r1 < 0 ? 0 : r0);
     }
+    if (e_end < 0) e_end = n_expert;
+    const int ne = n_expert ? (int)(e_end - e_begin) : 0;
     Proj p;
     int col = 0;
     for (size_t i = 0; i < ts.size();) {
         size_t j = i + 1;
-        const bool fusable = is_quant_weight((int)ts[i]->type) && rows[i] % GROUP_ROWS == 0;
-        while (fusable && j < ts.size() && ts[j]->type == ts[i]->type && rows[j] % GROUP_ROWS == 0) j++;
+        const bool fusable = is_quant_weight((int)ts[i]->type) && cnt[i] % GROUP_ROWS == 0;
+        while (fusable && j < ts.size() && ts[j]->type == ts[i]->type && cnt[j] % GROUP_ROWS == 0) j++;
         Part part;
         part.col = col;
         if (upload_group(m, std::vector<const gguf_tensor *>(ts.begin() + i, ts.begin() + j),
-                         std::vector<int64_t>(rows.begin() + i, rows.begin() + j), n_in, n_expert, &part.m, err, len))
+                         std::vector<int64_t>(cnt.begin() + i, cnt.begin() + j),
+                         std::vector<int64_t>(st.begin() + i, st.begin() + j), n_in, e_begin, ne, &part.m, err, len))
             return -1;
         col += (int)part.m.n_out;
         p.parts.push_back(part);
@@ -492,13 +562,15 @@ __global__ void topk_kernel(const float *probs, int n_tok, int ne, int k, int32_
 // Float-weight experts: out[s*ldo + r] = E[top[s]][r] . x[s / tok_div], one thread per row, in
 // the reference's scalar dot order (four accumulators, csrc/ops.c:155-167).
 __global__ void fmatmul_gather_kernel(const void *w, int type, int n_in, int64_t rows, const int32_t *top,
-                                      const float *x, int64_t ldx, int tok_div, float *out, int64_t ldo) {
+                                      int expert0, int n_expert, const float *x, int64_t ldx, int tok_div, float *out,
+                                      int64_t ldo) {
     pdl_trigger();
     pdl_wait();
     int s = blockIdx.y;
     int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (r >= rows) return;
-    size_t base = ((size_t)top[s] * rows + r) * n_in;
+    const int e = top[s] - expert0;  // this matrix holds experts expert0 .. expert0 + n_expert - 1
+    if (r >= rows || e < 0 || e >= n_expert) return;
+    size_t base = ((size_t)e * rows + r) * n_in;
     const float *xv = x + (size_t)(s / tok_div) * ldx;
     auto wv = [&](int i) -> float {
         if (type == T_F32) return ((const float *)w)[base + i];
@@ -578,14 +650,22 @@ void project_experts(engine_ctx *c, const Proj &p, float *out, int64_t ldo, cons
         const DMat &w = part.m;
         if (!w.quant()) {
             dim3 grid((unsigned)((w.n_out + 255) / 256), n_slots);
-            launch(fmatmul_gather_kernel, grid, 256, 0, c->st, w.f, w.type, w.n_in, w.n_out, c->moe_top, x, ldx, tok_div,
-                                                            out + part.col, ldo);
+            launch(fmatmul_gather_kernel, grid, 256, 0, c->st, w.f, w.type, w.n_in, w.n_out, c->moe_top,
+                   (int)c->m->e0, w.n_expert, x, ldx, tok_div, out + part.col, ldo);
             SDY_LAUNCHED();
             continue;
         }
         const XQ &xq = activations(c, x, ldx, n_x, w.n_in, w.type);
-        qmatvec_gather(w.q, w.gpe, w.n_expert, xq, tok_div, c->moe_top, n_slots, w.n_out, out + part.col, ldo, c->st);
+        qmatvec_gather(w.q, w.gpe, w.n_expert, xq, tok_div, c->moe_top, n_slots, w.n_out, out + part.col, ldo, c->st,
+                       (int)c->m->e0);
     }
+}
+
+// recv = sum over ranks of send (count floats). Every element has one nonzero contributor, so
+// the sum is that value exactly, whatever order NCCL adds in.
+void all_reduce(engine_ctx *c, const float *send, float *recv, size_t count) {
+    const ncclResult_t r = nccl()->all_reduce(send, recv, count, ncclFloat32, ncclSum, c->m->comm, c->st);
+    if (r != ncclSuccess) set_error("ncclAllReduce: %s", nccl()->error_string(r));
 }
 
 void moe_ffn(engine_ctx *c, const DLayer &L, int n) {
@@ -608,7 +688,10 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n) {
     silu_quant(c->moe_gu, gu, c->moe_gu + fe, gu, fe, slots, q8k, q80, c->st);
     Proj down;
     down.parts.push_back(Part{L.down, 0});
+    const bool sharded = c->m->world > 1;
+    if (sharded) SDY_CUDA(cudaMemsetAsync(c->moe_y, 0, (size_t)slots * dim * 4, c->st));  // other ranks' slots
     project_experts(c, down, c->moe_y, dim, c->moe_gu, gu, slots, slots, 1);
+    if (sharded) all_reduce(c, c->moe_y, c->moe_y, (size_t)slots * dim);  // every slot from its expert's rank
     moe_combine(c->moe_y, dim, c->moe_top, c->moe_w, k, dim, n, c->x, dim, c->st);
 }
 
@@ -687,9 +770,20 @@ void forward(engine_ctx *c, int n, int out_rows) {
             want_activations(c, mats_of(L.gateup), c->xb, dim, n, dim, &q8k, &q80);
             rmsnorm_quant(c->x, dim, L.ffn_norm, dim, n, in.norm_eps, c->xb, dim, q8k, q80, c->st);
             project(c, L.gateup, c->hgu, GU, c->xb, dim, n);
-            want_activations(c, {&L.down}, c->hgu, GU, n, F, &q8k, &q80);
-            silu_quant(c->hgu, GU, c->hgu + F, GU, F, n, q8k, q80, c->st);
-            matmul(c, c->x, dim, c->hgu, GU, L.down, n, c->x);
+            if (m->world > 1) {
+                // this rank's gate/up rows [f0, f1) -> its columns of the SiLU product, gathered to
+                // every rank; its rows [d0, d1) of down -> its columns of x, gathered likewise
+                const int nf = (int)(m->f1 - m->f0);
+                silu_scatter(c->hgu, GU, c->hgu + nf, GU, nf, n, c->hsend + m->f0, F, c->st);
+                all_reduce(c, c->hsend, c->hfull, (size_t)n * F);
+                forget_activations(c);
+                matmul(c, c->xsend + m->d0, dim, c->hfull, F, L.down, n, c->x + m->d0);
+                all_reduce(c, c->xsend, c->x, (size_t)n * dim);
+            } else {
+                want_activations(c, {&L.down}, c->hgu, GU, n, F, &q8k, &q80);
+                silu_quant(c->hgu, GU, c->hgu + F, GU, F, n, q8k, q80, c->st);
+                matmul(c, c->x, dim, c->hgu, GU, L.down, n, c->x);
+            }
         }
     }
     if (out_rows > 0) {
@@ -697,7 +791,12 @@ void forward(engine_ctx *c, int n, int out_rows) {
         const float *xs = c->x + (size_t)(n - out_rows) * dim;
         want_activations(c, {&m->output}, c->xb, dim, out_rows, dim, &q8k, &q80);
         rmsnorm_quant(xs, dim, m->output_norm, dim, out_rows, in.norm_eps, c->xb, dim, q8k, q80, c->st);
-        matmul(c, c->logits, in.n_vocab, c->xb, dim, m->output, out_rows);
+        if (m->world > 1) {  // this rank's vocabulary rows, gathered
+            matmul(c, c->lsend + m->v0, in.n_vocab, c->xb, dim, m->output, out_rows);
+            all_reduce(c, c->lsend, c->logits, (size_t)out_rows * in.n_vocab);
+        } else {
+            matmul(c, c->logits, in.n_vocab, c->xb, dim, m->output, out_rows);
+        }
     }
     forget_activations(c);
 }
@@ -787,6 +886,7 @@ extern "C" {
 void engine_model_free(engine_model *m) {
     if (!m) return;
     cudaSetDevice(m->dev);
+    if (m->comm) nccl()->comm_destroy(m->comm);
     for (void *p : m->allocs) cudaFree(p);
     if (m->raw) cudaFree(m->raw);
     if (m->st) cudaStreamDestroy(m->st);
@@ -813,12 +913,31 @@ engine_model *engine_model_load(const char *path, char *err, size_t err_len) {
     }
     const engine_model_info &in = m->info;
     const int dim = in.dim, q_dim = in.n_head * in.head_dim, kv_dim = in.n_kv_head * in.head_dim;
+    m->rank = g_shard.rank;
+    m->world = g_shard.world;
+    shard_range(in.ffn_dim, m->world, m->rank, GROUP_ROWS, &m->f0, &m->f1);
+    shard_range(dim, m->world, m->rank, GROUP_ROWS, &m->d0, &m->d1);
+    shard_range(in.n_expert, m->world, m->rank, 1, &m->e0, &m->e1);
+    shard_range(in.n_vocab, m->world, m->rank, GROUP_ROWS, &m->v0, &m->v1);
+    if (m->world > 1) {
+        const Nccl *nc = nccl();
+        ncclResult_t r = nc ? nc->comm_init_rank(&m->comm, m->world, g_shard.id, m->rank) : ncclSystemError;
+        if (r != ncclSuccess) {
+            put_err(err, err_len, "NCCL non disponibile per il rank %d di %d: %s", m->rank, m->world,
+                    nc ? nc->error_string(r) : "libnccl.so.2 mancante");
+            m->comm = nullptr;
+            engine_model_free(m);
+            return nullptr;
+        }
+    }
     m->layers.resize(in.n_layer);
     bool ok = !get_tensor(m, "token_embd.weight", dim, in.n_vocab, 0, &m->tok_embd, err, err_len) &&
               !get_vector(m, "output_norm.weight", dim, &m->output_norm, err, err_len);
     if (ok) {
-        if (in.tied_embeddings) m->output = m->tok_embd;
-        else ok = !get_tensor(m, "output.weight", dim, in.n_vocab, 0, &m->output, err, err_len);
+        const char *oname = in.tied_embeddings ? "token_embd.weight" : "output.weight";
+        if (m->world > 1) ok = !get_tensor(m, oname, dim, in.n_vocab, 0, &m->output, err, err_len, m->v0, m->v1);
+        else if (in.tied_embeddings) m->output = m->tok_embd;
+        else ok = !get_tensor(m, oname, dim, in.n_vocab, 0, &m->output, err, err_len);
     }
     for (int l = 0; ok && l < in.n_layer; l++) {
         DLayer &L = m->layers[l];
@@ -833,12 +952,14 @@ engine_model *engine_model_load(const char *path, char *err, size_t err_len) {
             int ne = in.n_expert, fe = in.ffn_exp_dim;
             ok = !get_tensor(m, nm("ffn_gate_inp.weight").c_str(), dim, ne, 0, &L.gate_inp, err, err_len) &&
                  !get_proj(m, {nm("ffn_gate_exps.weight"), nm("ffn_up_exps.weight")}, {fe, fe}, dim, ne, &L.gateup, err,
-                           err_len) &&
-                 !get_tensor(m, nm("ffn_down_exps.weight").c_str(), fe, dim, ne, &L.down, err, err_len);
+                           err_len, 0, -1, m->e0, m->e1) &&
+                 !get_tensor(m, nm("ffn_down_exps.weight").c_str(), fe, dim, ne, &L.down, err, err_len, 0, -1, m->e0,
+                             m->e1);
         } else {
             ok = !get_proj(m, {nm("ffn_gate.weight"), nm("ffn_up.weight")}, {in.ffn_dim, in.ffn_dim}, dim, 0,
-                           &L.gateup, err, err_len) &&
-                 !get_tensor(m, nm("ffn_down.weight").c_str(), in.ffn_dim, dim, 0, &L.down, err, err_len);
+                           &L.gateup, err, err_len, m->f0, m->f1) &&
+                 !get_tensor(m, nm("ffn_down.weight").c_str(), in.ffn_dim, dim, 0, &L.down, err, err_len, m->d0,
+                             m->d1);
         }
         if (ok && in.qkv_bias)
             ok = !get_vector(m, nm("attn_q.bias").c_str(), q_dim, &L.bq, err, err_len) &&
@@ -895,7 +1016,7 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
     const size_t ffn = in.n_expert ? in.ffn_exp_dim : in.ffn_dim;
     const size_t K = in.n_expert ? in.n_expert_used : 0, slots = B * K;
     c->qkv_ld = (int)(q_dim + 2 * kv_dim);
-    c->gu_ld = (int)(2 * ffn);
+    c->gu_ld = (int)(2 * (in.n_expert ? ffn : (size_t)(m->f1 - m->f0)));
     const size_t tmp_n = std::max<size_t>((size_t)in.dim, (size_t)in.n_vocab) * B;
     struct Item {
         void **dst;
@@ -919,6 +1040,15 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
         items.push_back({(void **)&c->moe_gu, slots * 2 * ffn * 4});
         items.push_back({(void **)&c->moe_y, slots * in.dim * 4});
     }
+    const size_t logit_rows = c->logits_all ? B : 1;
+    if (m->world > 1) {
+        if (!in.n_expert) {
+            items.push_back({(void **)&c->hsend, B * ffn * 4});
+            items.push_back({(void **)&c->hfull, B * ffn * 4});
+            items.push_back({(void **)&c->xsend, B * in.dim * 4});
+        }
+        items.push_back({(void **)&c->lsend, logit_rows * in.n_vocab * 4});
+    }
     size_t xq_cap = 0;
     for (int vt : {T_Q8_0, T_Q8_K}) {
         int be = block_elems(vt);
@@ -940,7 +1070,10 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
         *it.dst = p;
         p += align_up(it.bytes, 256);
     }
-    if (c->moe_count && !SDY_CUDA(cudaMemset(c->moe_count, 0, B * 4))) {  // router counters start at zero
+    bool zeroed = true;  // all-reduce sources start (and outside this rank's columns stay) zero
+    if (c->hsend) zeroed = SDY_CUDA(cudaMemset(c->hsend, 0, B * ffn * 4)) && SDY_CUDA(cudaMemset(c->xsend, 0, B * in.dim * 4));
+    if (c->lsend) zeroed = zeroed && SDY_CUDA(cudaMemset(c->lsend, 0, logit_rows * in.n_vocab * 4));
+    if (!zeroed || (c->moe_count && !SDY_CUDA(cudaMemset(c->moe_count, 0, B * 4)))) {  // router counters start at zero
         put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
         engine_ctx_free(c);
         return nullptr;
@@ -1039,6 +1172,40 @@ int engine_truncate(engine_ctx *c, int32_t n) {
     c->n_past = n;
     c->n_logits = 0;
     return 0;
+}
+
+int sdy_nccl_unique_id(void *out) {
+    const Nccl *nc = nccl();
+    ncclUniqueId id;
+    if (!out || !nc || nc->get_unique_id(&id) != ncclSuccess) {
+        set_error("sdy_nccl_unique_id: %s", nc ? "ncclGetUniqueId failed" : "libnccl.so.2 missing");
+        return -1;
+    }
+    memcpy(out, &id, sizeof id);
+    return 0;
+}
+
+int sdy_engine_set_shard(int32_t rank, int32_t world, const void *nccl_id) {
+    if (world < 1 || rank < 0 || rank >= world || (world > 1 && !nccl_id)) {
+        set_error("sdy_engine_set_shard: rank %d of %d invalid", rank, world);
+        return -1;
+    }
+    g_shard.rank = rank;
+    g_shard.world = world;
+    if (world > 1) memcpy(&g_shard.id, nccl_id, sizeof g_shard.id);
+    return 0;
+}
+
+void sdy_engine_get_shard(int32_t *rank, int32_t *world) {
+    if (rank) *rank = g_shard.rank;
+    if (world) *world = g_shard.world;
+}
+
+void sdy_shard_range(int64_t n, int32_t world, int32_t rank, int64_t align, int64_t *begin, int64_t *end) {
+    int64_t b = 0, e = n;
+    if (world >= 1 && rank >= 0 && rank < world && align >= 1 && n >= 0) shard_range(n, world, rank, align, &b, &e);
+    if (begin) *begin = b;
+    if (end) *end = e;
 }
 
 }  // extern "C"

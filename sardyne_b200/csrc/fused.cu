@@ -291,6 +291,19 @@ __global__ void moe_combine_kernel(const float *y, int64_t ldy, const int32_t *t
     }
 }
 
+// dst[t][i] = silu(g[t][i]) * u[t][i] (ops.c:366-371): the SiLU product of one rank's rows of a
+// sharded FFN, written into its columns of the buffer the ranks all-reduce.
+__global__ void silu_scatter_kernel(const float *g, int64_t ldg, const float *u, int64_t ldu, int n, float *dst,
+                                    int64_t ldd) {
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.y;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float a = g[(size_t)t * ldg + i];
+        dst[(size_t)t * ldd + i] = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, exp_cr(-a))), u[(size_t)t * ldu + i]);
+    }
+}
+
 XQ pick(const XQ *q) {
     XQ a = q ? *q : XQ();
     if (!q) a.qs = nullptr;
@@ -348,6 +361,13 @@ void moe_combine(const float *y, int64_t ldy, const int32_t *top, const float *w
                  int64_t ldx, cudaStream_t s) {
     if (n_tok <= 0) return;
     launch(moe_combine_kernel, dim3((dim + 255) / 256, n_tok), 256, 0, s, y, ldy, top, w, k, dim, x, ldx);
+    SDY_LAUNCHED();
+}
+
+void silu_scatter(const float *g, int64_t ldg, const float *u, int64_t ldu, int n, int rows, float *dst, int64_t ldd,
+                  cudaStream_t s) {
+    if (rows <= 0 || n <= 0) return;
+    launch(silu_scatter_kernel, dim3((n + 255) / 256, rows), 256, 0, s, g, ldg, u, ldu, n, dst, ldd);
     SDY_LAUNCHED();
 }
 

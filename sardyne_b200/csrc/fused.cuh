@@ -11,6 +11,10 @@ void rmsnorm_quant(const float *x, int64_t ldx, const float *w, int n, int rows,
 void silu_quant(float *g, int64_t ldg, const float *u, int64_t ldu, int n, int rows, const XQ *q8k, const XQ *q80,
                 cudaStream_t s);
 
+// dst[t*ldd + i] = silu(g) * u for i < n (no quantization): sharded FFN rows.
+void silu_scatter(const float *g, int64_t ldg, const float *u, int64_t ldu, int n, int rows, float *dst, int64_t ldd,
+                  cudaStream_t s);
+
 struct PostQKV {
     float *q, *k;
     const float *v;

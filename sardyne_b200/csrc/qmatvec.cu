@@ -56,7 +56,7 @@ struct Args {
     // groups start at expert * gpe, with the activations of token s / tok_div, into out + s*ldo_slot.
     const int32_t *slot_expert;
     int64_t gpe, ldo_slot;
-    int tok_div, n_expert;
+    int tok_div, n_expert, expert0;  // slot_expert ids are global; this matrix holds experts expert0..
 };
 
 // Shared-memory carve-up, identical on host and device.
@@ -309,8 +309,8 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
     }
     pdl_wait();
     if (a.slot_expert) {
-        const int slot = blockIdx.y, e = a.slot_expert[slot];
-        if (e < 0 || e >= a.n_expert) return;
+        const int slot = blockIdx.y, e = a.slot_expert[slot] - a.expert0;
+        if (e < 0 || e >= a.n_expert) return;  // another rank's expert (or an invalid id)
         const int tok = slot / a.tok_div;
         slabs += (size_t)e * a.gpe * nb * SB;
         xqs += (size_t)tok * a.qrow;
@@ -544,7 +544,7 @@ void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0,
 namespace sdy {
 
 void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq, int tok_div, const int32_t *slot_expert,
-                    int n_slots, int64_t rows_per_expert, float *out, int64_t ldo_slot, cudaStream_t s) {
+                    int n_slots, int64_t rows_per_expert, float *out, int64_t ldo_slot, cudaStream_t s, int expert0) {
     if (n_slots <= 0) return;
     if (xq.vtype != vec_dot_type(experts.type) || xq.n_in != experts.n_in) {
         set_error("qmatvec_gather: activation type/size does not match the weights");
@@ -578,6 +578,7 @@ void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq
     a.ldo_slot = ldo_slot;
     a.tok_div = tok_div;
     a.n_expert = n_expert;
+    a.expert0 = expert0;
     dispatch(experts.type, 1, a, plan.smem, dim3(plan.grid, n_slots), s);
 }
 

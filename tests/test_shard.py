@@ -1,0 +1,80 @@
+"""Host side of the sharded engine (no GPU): the row/expert ranges each rank holds, and the NCCL
+id exchange over a world-size-2 gloo process group."""
+import ctypes
+import os
+
+import pytest
+
+from sardyne_b200 import capi
+
+
+def shard_range(n, world, rank, align):
+    b, e = ctypes.c_int64(), ctypes.c_int64()
+    capi.lib().sdy_shard_range(n, world, rank, align, ctypes.byref(b), ctypes.byref(e))
+    return b.value, e.value
+
+
+@pytest.mark.parametrize("n,align", [(11008, 8), (2048, 8), (151936, 8), (49152, 8), (1536, 8), (128, 1), (576, 8),
+                                     (13, 8), (7, 1)])
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_ranges_partition(n, align, world):
+    """Consecutive ranks hold consecutive, aligned, non-overlapping ranges covering [0, n)."""
+    end = 0
+    for r in range(world):
+        b, e = shard_range(n, world, r, align)
+        assert b == end and b <= e <= n
+        assert b % align == 0
+        end = e
+    assert end == n
+
+
+def test_expert_split_qwen3():
+    assert [shard_range(128, 8, r, 1) for r in range(8)] == [(16 * r, 16 * r + 16) for r in range(8)]
+
+
+def test_set_shard_validation():
+    lib = capi.lib()
+    lib.sdy_clear_error()
+    assert lib.sdy_engine_set_shard(2, 2, None) == -1 and "invalid" in capi.last_error()
+    assert lib.sdy_engine_set_shard(0, 2, None) == -1  # a sharded world needs the NCCL id
+    assert lib.sdy_engine_set_shard(0, 1, None) == 0
+    r, w = ctypes.c_int32(), ctypes.c_int32()
+    lib.sdy_engine_get_shard(ctypes.byref(r), ctypes.byref(w))
+    assert (r.value, w.value) == (0, 1)
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+    from sardyne_b200 import runtime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        obj = [runtime.new_nccl_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        runtime.set_shard(rank, world, obj[0])
+        r, w = ctypes.c_int32(), ctypes.c_int32()
+        capi.lib().sdy_engine_get_shard(ctypes.byref(r), ctypes.byref(w))
+        q.put((rank, r.value, w.value, obj[0]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nccl_id_exchange_gloo():
+    """Two ranks agree on one 128-byte id and record their own rank (gloo, CPU only)."""
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    assert [g[:3] for g in got] == [(0, 0, 2), (1, 1, 2)]
+    assert got[0][3] == got[1][3] and len(got[0][3]) == 128
