@@ -13,9 +13,11 @@
 //            in the CTA's shared memory;
 //   phase B  max and double sum of exp(s - max) per head reduced across the cluster through
 //            distributed shared memory (two cluster barriers);
-//   phase C  CTA c owns elements [c*S, (c+1)*S) of every head: n_rep*S exact chains, fed by
-//            chunks of exponentials read from their owners' shared memory and double-buffered
-//            cp.async chunks of the V columns it needs (the first chunk requested in phase A).
+//   phase C  CTA c owns elements [c*S, (c+1)*S) of every head: n_rep*S exact chains, fed by the
+//            probabilities (each CTA pushes its keys' exponentials into every CTA's shared memory
+//            during phase B when all keys fit; otherwise chunks are read from their owners) and
+//            double-buffered cp.async chunks of the V columns it needs (the first chunk requested
+//            in phase A).
 //
 // A per-head kernel (one CTA per (head, token)) covers the shapes the cluster kernel does not
 // (head_dim not a multiple of 32, more than 32 query heads per KV head, unaligned buffers, a
@@ -56,14 +58,17 @@ __host__ __device__ inline int ac_lmax(int stride) { return ((stride + AC - 1) /
 struct AcSmem {
     int qs, scl, vb, work, total;  // float offsets
 };
-__host__ __device__ inline AcSmem ac_smem(int n_rep, int hd, int stride) {
+// Probability row stride when every CTA holds all keys' exponentials (push mode).
+__host__ __device__ inline int ac_ldp(int stride) { return ((stride + 3) & ~3) + 4; }
+// push: the work area also holds n_rep rows of ac_ldp(stride) exponentials (all keys) for phase C.
+__host__ __device__ inline AcSmem ac_smem(int n_rep, int hd, int stride, bool push) {
     AcSmem m;
     const int S = hd / AC;
     m.qs = 0;
     m.scl = n_rep * hd;
     m.vb = m.scl + n_rep * ac_lmax(stride);
     m.work = m.vb + 2 * AC_KC * S;
-    const int a = 2 * AC_KT * (hd + 4), c = 2 * n_rep * AC_PLD;
+    const int a = 2 * AC_KT * (hd + 4), c = push ? n_rep * ac_ldp(stride) : 2 * n_rep * AC_PLD;
     m.total = m.work + (a > c ? a : c);
     return m;
 }
@@ -79,8 +84,7 @@ __host__ __device__ inline AcSmem ac_smem(int n_rep, int hd, int stride) {
 __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
     attention_cluster_kernel(float *__restrict__ out, const float *__restrict__ q, int64_t ldq,
                              const float *__restrict__ kc, const float *__restrict__ vc, int n_head, int n_kv_head,
-                             int hd, int pos0, const int32_t *pos_dev, int stride, int fixed_nkv) {
-    pdl_trigger();
+                             int hd, int pos0, const int32_t *pos_dev, int stride, int fixed_nkv, int push) {
     extern __shared__ __align__(16) float sm[];
     __shared__ float cmax[AC_MAX_REP], gmax[AC_MAX_REP], ginv[AC_MAX_REP];
     __shared__ double csum[AC_MAX_REP];
@@ -90,7 +94,8 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
     const int n_kv = fixed_nkv > 0 ? fixed_nkv : (pos_dev ? *pos_dev : pos0) + t + 1;
     const int n_rep = n_head / n_kv_head, h0 = g * n_rep;
     const float *kh = kc + (size_t)g * stride * hd, *vh = vc + (size_t)g * stride * hd;
-    const AcSmem lay = ac_smem(n_rep, hd, stride);
+    const AcSmem lay = ac_smem(n_rep, hd, stride, push);
+    const int ldp = ac_ldp(stride);
     const int lmax = ac_lmax(stride);
     float *qs = sm + lay.qs, *scl = sm + lay.scl, *vb = sm + lay.vb, *work = sm + lay.work;
     const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
@@ -130,7 +135,23 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
     if (ntile > 0) load_k(0);
     load_v(0);  // phase C's first chunk travels with the first K tile
     cp_async_commit();
-    for (int i = tid; i < n_rep * hd; i += AC_THREADS) qs[i] = q[(size_t)t * ldq + (size_t)h0 * hd + i];
+    {  // the n_rep query heads: n_rep*hd/4 16-byte loads, all issued before any store
+        const float4 *q4 = (const float4 *)(q + (size_t)t * ldq + (size_t)h0 * hd);
+        const int n4 = n_rep * hd / 4;
+        for (int i0 = 0; i0 < n4; i0 += 4 * AC_THREADS) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = i0 + u * AC_THREADS + tid;
+                if (i < n4) v[u] = q4[i];
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = i0 + u * AC_THREADS + tid;
+                if (i < n4) ((float4 *)qs)[i] = v[u];
+            }
+        }
+    }
     for (int it = 0; it < ntile; it++) {
         if (it + 1 < ntile) {
             load_k(it + 1);
@@ -194,6 +215,9 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
         gmax[tid] = m;
     }
     __syncthreads();
+    // After the first cluster barrier every CTA is past phase A, so the work areas (K tiles until
+    // then) can receive the exponentials: in push mode each CTA stores its keys' values into the
+    // probability rows of all 8 CTAs (remote stores, made visible by the next cluster barrier).
     for (int r = warp; r < n_rep; r += AC_THREADS / 32) {
         const float m = gmax[r];
         double sacc = 0.0;
@@ -201,6 +225,9 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
             const float e = exp_cr(__fsub_rn(scl[r * lmax + j], m));
             scl[r * lmax + j] = e;
             sacc += e;
+            if (push)
+#pragma unroll
+                for (int p = 0; p < AC; p++) *cl.map_shared_rank(work + r * ldp + jb + j, p) = e;
         }
         for (int o = 16; o; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
         if (lane == 0) csum[r] = sacc;
@@ -216,18 +243,41 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
     // ---- phase C: out[e] = sum_j (e_j * inv) * v_j[e] in key order, e in this CTA's slice
     const int ch_r = tid / S, ch_e = tid - ch_r * S;
     const bool chain = tid < n_rep * S;
-    const float inv = chain ? ginv[ch_r] : 0.0f;
     const int nchunk = (n_kv + AC_KC - 1) / AC_KC;
-    auto load_p = [&](int ic) {  // exponentials of chunk ic's keys, from their owners' shared memory
-        const int j0 = ic * AC_KC, nk = min(AC_KC, n_kv - j0);
+    // Probabilities p_j = e_j * inv (ops.c:363) of chunk ic's keys: the exponentials read from their
+    // owners' shared memory, 8 remote loads in flight per thread before the stores.
+    auto load_p = [&](int ic) {
+        const int j0 = ic * AC_KC, nk = min(AC_KC, n_kv - j0), tot = n_rep * nk;
         float *pb = work + (ic & 1) * n_rep * AC_PLD;
-        for (int idx = tid; idx < n_rep * nk; idx += AC_THREADS) {
-            const int r = idx / nk, jj = idx - r * nk, j = j0 + jj, owner = j / L;
-            pb[r * AC_PLD + jj] = *cl.map_shared_rank(scl + r * lmax + (j - owner * L), owner);
+        for (int i0 = 0; i0 < tot; i0 += 8 * AC_THREADS) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int idx = i0 + u * AC_THREADS + tid;
+                if (idx < tot) {
+                    const int r = idx / nk, j = j0 + idx - r * nk, owner = j / L;
+                    v[u] = *cl.map_shared_rank(scl + r * lmax + (j - owner * L), owner);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int idx = i0 + u * AC_THREADS + tid;
+                if (idx < tot) {
+                    const int r = idx / nk, jj = idx - r * nk;
+                    pb[r * AC_PLD + jj] = __fmul_rn(v[u], ginv[r]);
+                }
+            }
         }
     };
     float acc = 0.0f;
-    load_p(0);
+    if (push) {  // p_j = e_j * inv in place, every key of every head
+        for (int idx = tid; idx < n_rep * n_kv; idx += AC_THREADS) {
+            const int r = idx / n_kv, j = idx - r * n_kv;
+            work[r * ldp + j] = __fmul_rn(work[r * ldp + j], ginv[r]);
+        }
+    } else {
+        load_p(0);
+    }
     for (int ic = 0; ic < nchunk; ic++) {
         if (ic + 1 < nchunk) {
             load_v(ic + 1);
@@ -235,12 +285,24 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
         }
         __syncthreads();
         if (chain) {
-            const float *pr = work + (ic & 1) * n_rep * AC_PLD + ch_r * AC_PLD;
+            const float *pr = push ? work + ch_r * ldp + ic * AC_KC
+                                   : work + (ic & 1) * n_rep * AC_PLD + ch_r * AC_PLD;
             const float *vr = vb + (ic & 1) * AC_KC * S + ch_e;
             const int nk = min(AC_KC, n_kv - ic * AC_KC);
-            acc = ordered_sum<16>(acc, nk, [&](int j) { return __fmul_rn(__fmul_rn(pr[j], inv), vr[j * S]); });
+            const float4 *p4 = (const float4 *)pr;  // 4 keys' probabilities per 16-byte load
+#pragma unroll 4
+            for (int q = 0; q < (nk >> 2); q++) {
+                const float4 p = p4[q];
+                const float *v = vr + 4 * q * S;
+                const float v0 = v[0], v1 = v[S], v2 = v[2 * S], v3 = v[3 * S];
+                acc = __fadd_rn(acc, __fmul_rn(p.x, v0));
+                acc = __fadd_rn(acc, __fmul_rn(p.y, v1));
+                acc = __fadd_rn(acc, __fmul_rn(p.z, v2));
+                acc = __fadd_rn(acc, __fmul_rn(p.w, v3));
+            }
+            for (int j = nk & ~3; j < nk; j++) acc = __fadd_rn(acc, __fmul_rn(pr[j], vr[j * S]));
         }
-        if (ic + 1 < nchunk) load_p(ic + 1);
+        if (!push && ic + 1 < nchunk) load_p(ic + 1);
         cp_async_wait<0>();
         __syncthreads();
     }
@@ -259,7 +321,6 @@ __host__ __device__ inline int att_smem_floats(int hd) { return hd + ATT_THREADS
 __global__ void attention_head_kernel(float *out, const float *q, int64_t ldq, const float *kc, const float *vc,
                                       int n_head, int n_kv_head, int hd, int pos0, const int32_t *pos_dev, int stride,
                                       float *scratch, int fixed_nkv) {
-    pdl_trigger();
     pdl_wait();
     extern __shared__ __align__(16) float sm[];
     const int t = blockIdx.y, h = blockIdx.x, tid = threadIdx.x;
@@ -327,12 +388,14 @@ void attention(float *out, const float *q, int64_t ldq, const float *kc, const f
         return;
     }
     const int n_rep = n_head / n_kv_head;
+    const int push = (size_t)ac_smem(n_rep, hd, stride, true).total * 4 <= AC_SMEM_LIMIT;
     const bool cluster = hd % (4 * AC) == 0 && stride % 4 == 0 && n_rep <= AC_MAX_REP &&
-                         n_rep * hd <= AC_MAX_GROUP && aligned16(kc) && aligned16(vc) &&
-                         (size_t)ac_smem(n_rep, hd, stride).total * 4 <= AC_SMEM_LIMIT && n_kv_head <= 65535 &&
+                         n_rep * hd <= AC_MAX_GROUP && aligned16(kc) && aligned16(vc) && aligned16(q) &&
+                         ldq % 4 == 0 &&
+                         (size_t)ac_smem(n_rep, hd, stride, push).total * 4 <= AC_SMEM_LIMIT && n_kv_head <= 65535 &&
                          n_tok <= 65535;
     if (cluster) {
-        const size_t smem = (size_t)ac_smem(n_rep, hd, stride).total * 4;
+        const size_t smem = (size_t)ac_smem(n_rep, hd, stride, push).total * 4;
         static bool configured = false;
         if (!configured) {
             SDY_CUDA(cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -340,7 +403,7 @@ void attention(float *out, const float *q, int64_t ldq, const float *kc, const f
             configured = true;
         }
         launch(attention_cluster_kernel, dim3(AC, n_kv_head, n_tok), AC_THREADS, smem, s, out, q, ldq, kc, vc, n_head,
-               n_kv_head, hd, pos0, pos_dev, stride, fixed_nkv);
+               n_kv_head, hd, pos0, pos_dev, stride, fixed_nkv, push);
         SDY_LAUNCHED();
         return;
     }

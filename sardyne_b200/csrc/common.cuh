@@ -124,33 +124,43 @@ void note_launch();
     } while (0)
 
 // ------------------------------------------------------------------------------ dependent launch
-// Kernels are launched with programmatic dependent launch: the next kernel's CTAs are placed on
-// the SMs while the current kernel runs and block in pdl_wait() until it has completed and its
-// writes are visible, which takes launch latency (and, in the quantized matvec, the first weight
-// loads) off the critical path. So every kernel begins with pdl_trigger() and reads or writes no
-// activation before pdl_wait(); only weights may be read before it. Kernels that write weights
-// (repacking, format conversion) do not call pdl_trigger(): the kernel after them then starts
-// only once they have completed, so no later kernel's early weight reads can overlap them.
-// Launched without the attribute (SARDYNE_NO_PDL set), both instructions are no-ops.
+// Kernels are launched with programmatic dependent launch: a kernel's CTAs are set up while the
+// previous kernel's last CTAs retire and block in pdl_wait() until it has completed and its writes
+// are visible, which takes launch latency off the critical path. Kernels do not signal their
+// dependents early (griddepcontrol.launch_dependents): the next kernel's CTAs would then be placed
+// while this one still occupies the SMs, packed onto the few with room, which measured slower than
+// launching without PDL. So every kernel reads or writes no activation before pdl_wait(); only
+// weights may be read before it (the matvec loads its first weight pair there). Kernels that write
+// weights (repacking, format conversion) complete before any later kernel starts. Launched without
+// the attribute (SARDYNE_NO_PDL set), pdl_wait() is a no-op.
 #ifdef __CUDACC__
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
 // acc + term(0) + term(1) + ... + term(n-1), added left to right with every sum rounded (the
-// reference's sequential loops). The terms of a batch of B are evaluated (their loads issued)
-// before the batch's dependent adds, so load latency is paid once per batch, not once per term.
+// reference's sequential loops). Software-pipelined: the terms of batch k+1 (their loads) are
+// requested before batch k's dependent adds run.
 template <int B, class Term>
 __device__ __forceinline__ float ordered_sum(float acc, int n, Term term) {
-    int j = 0;
-    for (; j + B <= n; j += B) {
-        float v[B];
+    const int full = n / B;
+    if (full > 0) {
+        float cur[B];
 #pragma unroll
-        for (int u = 0; u < B; u++) v[u] = term(j + u);
+        for (int u = 0; u < B; u++) cur[u] = term(u);
+        for (int k = 1; k < full; k++) {
+            float nxt[B];
 #pragma unroll
-        for (int u = 0; u < B; u++) acc = __fadd_rn(acc, v[u]);
+            for (int u = 0; u < B; u++) nxt[u] = term(k * B + u);
+#pragma unroll
+            for (int u = 0; u < B; u++) acc = __fadd_rn(acc, cur[u]);
+#pragma unroll
+            for (int u = 0; u < B; u++) cur[u] = nxt[u];
+        }
+#pragma unroll
+        for (int u = 0; u < B; u++) acc = __fadd_rn(acc, cur[u]);
     }
-    for (; j < n; j++) acc = __fadd_rn(acc, term(j));
+    for (int j = full * B; j < n; j++) acc = __fadd_rn(acc, term(j));
     return acc;
 }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 #endif
 bool pdl_enabled();
 template <typename... KArgs, typename... Args>

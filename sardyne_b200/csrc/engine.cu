@@ -523,7 +523,6 @@ int get_vector(engine_model *m, const char *name, int n, float **out, char *err,
 
 // x[t] = row tok[t] of a float table (F32/F16/BF16).
 __global__ void embed_float_kernel(const void *table, int type, const int32_t *ids, int dim, float *x) {
-    pdl_trigger();
     pdl_wait();
     int t = blockIdx.x;
     size_t base = (size_t)ids[t] * dim;
@@ -539,7 +538,6 @@ __global__ void embed_float_kernel(const void *table, int type, const int32_t *i
 // Router selection per token for a quantized router (model_llama.c:653-666): the k most
 // probable experts, ties to the lowest index, weights renormalised by their float sum.
 __global__ void topk_kernel(const float *probs, int n_tok, int ne, int k, int32_t *top, float *w) {
-    pdl_trigger();
     pdl_wait();
     int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= n_tok) return;
@@ -564,7 +562,6 @@ __global__ void topk_kernel(const float *probs, int n_tok, int ne, int k, int32_
 __global__ void fmatmul_gather_kernel(const void *w, int type, int n_in, int64_t rows, const int32_t *top,
                                       int expert0, int n_expert, const float *x, int64_t ldx, int tok_div, float *out,
                                       int64_t ldo) {
-    pdl_trigger();
     pdl_wait();
     int s = blockIdx.y;
     int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;

@@ -21,7 +21,6 @@ namespace sdy {
 __global__ void fmatmul_kernel(const float *__restrict__ x, int64_t ldx, const void *__restrict__ w, int type,
                                int n_tok, int n_in, int64_t row0, int64_t row1, float *__restrict__ out,
                                int64_t ldo, int64_t out_row0) {
-    pdl_trigger();
     pdl_wait();
     int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     int64_t rows = row1 - row0;
@@ -44,7 +43,6 @@ void fmatmul(const float *x, int64_t ldx, const void *w, int type, int n_tok, in
 
 // RMSNorm of `rows` vectors of n (ops.c:346-351): out = x * (float)(1/sqrt(mean(x^2)+eps)) * w.
 __global__ void rmsnorm_kernel(float *out, int64_t ldo, const float *x, int64_t ldx, const float *w, int n, float eps) {
-    pdl_trigger();
     pdl_wait();
     const float *xv = x + blockIdx.x * ldx;
     float *ov = out + blockIdx.x * ldo;
@@ -62,7 +60,7 @@ void rmsnorm(float *out, int64_t ldo, const float *x, int64_t ldx, const float *
     SDY_LAUNCHED();
 }
 
-__global__ void softmax_kernel(float *x, int64_t ldx, int n) { pdl_trigger(); pdl_wait(); softmax_block(x + blockIdx.x * ldx, n); }
+__global__ void softmax_kernel(float *x, int64_t ldx, int n) { pdl_wait(); softmax_block(x + blockIdx.x * ldx, n); }
 
 void softmax(float *x, int64_t ldx, int n, int rows, cudaStream_t s) {
     if (rows <= 0) return;
@@ -72,7 +70,6 @@ void softmax(float *x, int64_t ldx, int n, int rows, cudaStream_t s) {
 
 // gate = gate / (1 + exp(-gate)) * up  (ops.c:366-371)
 __global__ void silu_mul_kernel(float *gate, const float *up, int64_t n) {
-    pdl_trigger();
     pdl_wait();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         float g = gate[i];
@@ -88,7 +85,6 @@ void silu_mul(float *gate, const float *up, int64_t n, cudaStream_t s) {
 
 // cos/sin tables in double (ops.c:375-386): angle = pos * theta^(-2i/head_dim).
 __global__ void rope_table_kernel(float *c, float *sn, int n_pos, int head_dim, float theta) {
-    pdl_trigger();
     pdl_wait();
     int half = head_dim / 2;
     int64_t total = (int64_t)n_pos * half;
@@ -122,7 +118,6 @@ __device__ __forceinline__ void rope_one(float *v, int head_dim, const float *c,
 // x: [n_tok][ldx] with n_heads vectors of head_dim each; token t uses table row pos[t] (or pos0+t).
 __global__ void rope_kernel(float *x, int64_t ldx, int n_heads, int head_dim, const float *c, const float *sn,
                             int pos0, const int32_t *pos, int interleaved) {
-    pdl_trigger();
     pdl_wait();
     int t = blockIdx.y, h = blockIdx.x;
     int p = pos ? pos[t] : pos0 + t;
@@ -140,7 +135,6 @@ void rope(float *x, int64_t ldx, int n_tok, int n_heads, int head_dim, const flo
 }
 
 __global__ void axpy_kernel(float *y, float a, const float *x, int64_t n) {
-    pdl_trigger();
     pdl_wait();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         y[i] = __fadd_rn(y[i], __fmul_rn(a, x[i]));
@@ -152,7 +146,6 @@ void axpy(float *y, float a, const float *x, int64_t n, cudaStream_t s) {
 }
 
 __global__ void add_kernel(float *out, const float *a, const float *b, int64_t n) {
-    pdl_trigger();
     pdl_wait();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         out[i] = __fadd_rn(a[i], b[i]);
@@ -165,7 +158,6 @@ void add(float *out, const float *a, const float *b, int64_t n, cudaStream_t s) 
 
 // x[t][i] += b[i]
 __global__ void add_bias_kernel(float *x, int64_t ldx, const float *b, int n, int n_tok) {
-    pdl_trigger();
     pdl_wait();
     int64_t total = (int64_t)n * n_tok;
     for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < total; k += (int64_t)gridDim.x * blockDim.x) {
@@ -182,7 +174,6 @@ void add_bias(float *x, int64_t ldx, const float *b, int n, int n_tok, cudaStrea
 
 // The reference's scalar dot on one thread (op_dot_f32 is a test hook, not a hot path).
 __global__ void dot_kernel(const float *a, const float *b, int n, float *out) {
-    pdl_trigger();
     pdl_wait();
     if (threadIdx.x == 0 && blockIdx.x == 0) *out = dot4(a, [&](int i) { return b[i]; }, n);
 }

@@ -49,7 +49,6 @@ __device__ __forceinline__ void quantize_span(const float v[8], int e0, int n, i
 // One block per row, thread i owning elements 8i..8i+7 (blockDim = n/8 rounded up to a warp).
 __global__ void rmsnorm_quant_kernel(const float *x, int64_t ldx, const float *w, int n, float eps, float *xb,
                                      int64_t ldb, XQ q8k, XQ q80) {
-    pdl_trigger();
     pdl_wait();
     __shared__ double part[32];
     const int t = blockIdx.x, e0 = threadIdx.x * 8;
@@ -71,7 +70,6 @@ __global__ void rmsnorm_quant_kernel(const float *x, int64_t ldx, const float *w
 
 // grid (ceil(n/2048), rows), 256 threads: warp w of block b owns span 8b + w.
 __global__ void silu_quant_kernel(float *g, int64_t ldg, const float *u, int64_t ldu, int n, XQ q8k, XQ q80) {
-    pdl_trigger();
     pdl_wait();
     const int t = blockIdx.y, span = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (span * 256 >= n) return;  // whole warps leave together
@@ -93,7 +91,6 @@ __global__ void silu_quant_kernel(float *g, int64_t ldg, const float *u, int64_t
 // One block per (head, token). Heads [0, n_head) are q heads; [n_head, n_head + n_kv_head) are
 // k heads, whose block also handles the v head with the same index.
 __global__ void post_qkv_kernel(PostQKV p) {
-    pdl_trigger();
     pdl_wait();
     extern __shared__ __align__(16) float vec[];
     __shared__ double part[32];
@@ -141,7 +138,8 @@ __global__ void post_qkv_kernel(PostQKV p) {
 // Router logits for float weights: one warp per expert row. The warp copies x and its row into
 // shared memory with coalesced loads; lanes 0..3 then run the reference's four accumulator
 // chains (ops.c:155-167: s_k over i = 4g + k, the tail into s0) and combine (s0+s1)+(s2+s3).
-constexpr int ROUTER_THREADS = 128;
+constexpr int ROUTER_EPC = 2;  // experts per CTA: one warp each (chains of few warps share an SM's shared-memory pipe)
+constexpr int ROUTER_THREADS = 32 * ROUTER_EPC;
 
 __device__ __forceinline__ float4 load4_w(const void *w, int wtype, size_t i) {  // i a multiple of 4
     if (wtype == T_F32) return *(const float4 *)((const float *)w + i);
@@ -155,11 +153,11 @@ __device__ __forceinline__ float4 load4_w(const void *w, int wtype, size_t i) { 
 }
 
 // Softmax (ops.c:353-364) and top-k (model_llama.c:653-666) of one token's ne logits by the whole
-// block. The reference's insertion keeps the k largest probabilities in descending order, equal
-// values in ascending expert id; here warp 0 takes k rounds of a warp-wide argmax under that
-// same order. Weights are renormalised by their float sum taken in the selected order.
-// prob, key: shared arrays of ne floats.
-__device__ void softmax_topk_block(const float *logits, float *prob, float *key, int ne, int k, int32_t *tp,
+// block; prob: shared array of ne floats, pv: k floats. The reference's insertion keeps the k
+// largest probabilities in descending order, equal values in ascending expert id: expert e is at
+// position rank(e) = #{j : p_j > p_e} + #{j < e : p_j == p_e}, computed for every expert in
+// parallel. Weights are renormalised by their float sum taken in that order.
+__device__ void softmax_topk_block(const float *logits, float *prob, float *pv, int ne, int k, int32_t *tp,
                                    float *wout, double *dpart, float *fpart) {
     for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = __ldcg(logits + e);
     __syncthreads();
@@ -168,94 +166,135 @@ __device__ void softmax_topk_block(const float *logits, float *prob, float *key,
     m = bmax_f(m, fpart);
     double sum = 0.0;
     for (int e = threadIdx.x; e < ne; e += blockDim.x) {
-        float v = exp_cr(__fsub_rn(prob[e], m));
+        const float v = exp_cr(__fsub_rn(prob[e], m));
         prob[e] = v;
         sum += v;
     }
     sum = bsum_d(sum, dpart);
     const float inv = (float)(1.0 / sum);
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) key[e] = prob[e] = __fmul_rn(prob[e], inv);
+    for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = __fmul_rn(prob[e], inv);
     __syncthreads();
-    if (threadIdx.x >= 32) return;
-    const int lane = threadIdx.x;
-    float s = 0.0f;
-    for (int r = 0; r < k; r++) {
-        float bv = -1.0f;  // probabilities are >= 0; taken entries hold -1
-        int bi = 0x7FFFFFFF;
-        for (int e = lane; e < ne; e += 32) {
-            const float v = key[e];
-            if (v > bv) { bv = v; bi = e; }  // ascending e: the first of equal values stays
+    for (int e = threadIdx.x; e < ne; e += blockDim.x) {
+        const float pe = prob[e];
+        int rank = 0;
+        for (int j = 0; j < ne; j++) {
+            const float pj = prob[j];
+            rank += (pj > pe) | ((pj == pe) & (j < e));
         }
-        for (int o = 16; o; o >>= 1) {
-            const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (v2 > bv || (v2 == bv && i2 < bi)) { bv = v2; bi = i2; }
+        if (rank < k) {
+            tp[rank] = e;
+            pv[rank] = pe;
         }
-        if (lane == 0) {
-            if (bi >= ne) bi = 0;  // only reachable with NaN probabilities; keeps the index in range
-            tp[r] = bi;
-            key[bi] = -1.0f;
-            s = __fadd_rn(s, prob[bi]);
-        }
-        __syncwarp();
     }
-    if (lane == 0)
-        for (int i = 0; i < k; i++) wout[i] = __fdiv_rn(prob[tp[i]], s);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int i = 0; i < k; i++) s = __fadd_rn(s, pv[i]);
+        fpart[0] = s;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < k; i += blockDim.x) wout[i] = __fdiv_rn(pv[i], fpart[0]);
 }
 
-// Float router, one CTA per (expert, token): logits[t][e] = x[t] . w[e] with the reference's
-// four-accumulator dot (ops.c:155-167) — the row (a constant weight, staged before pdl_wait) and
-// x go through shared memory with 16-byte loads, then lanes 0-3 run one accumulator chain each.
-// The last CTA of a token to finish (a counter per token, left at zero again) runs the softmax
-// and top-k over the token's logits. vec: dim % 4 == 0 and 16-byte aligned x rows / weights.
+// Float router, one warp per (expert, token), ROUTER_EPC experts per CTA: logits[t][e] = x[t].w[e]
+// with the reference's four-accumulator dot (ops.c:155-167) — the row (a constant weight, staged
+// before pdl_wait) and x go through shared memory with 16-byte loads, then lanes 0-3 of the warp
+// run one accumulator chain each. The last CTA of a token to finish (a counter per token, left at
+// zero again) runs the softmax and top-k. vec: dim % 4 == 0 and 16-byte aligned x rows / weights.
 __global__ void __launch_bounds__(ROUTER_THREADS)
     router_topk_kernel(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, float *logits,
                        int32_t *counters, int32_t *top, float *wout, int vec) {
-    pdl_trigger();
     extern __shared__ __align__(16) float sm[];
     __shared__ double dpart[32];
     __shared__ float fpart[32];
+    __shared__ float pv[64];
     __shared__ int last;
     const int dp = (dim + 3) & ~3;
-    float *xs = sm, *row = sm + dp;
-    const int e = blockIdx.x, t = blockIdx.y, tid = threadIdx.x;
-    const size_t base = (size_t)e * dim;
-    if (vec) {
-#pragma unroll 4
-        for (int i = tid * 4; i < dim; i += ROUTER_THREADS * 4) *(float4 *)(row + i) = load4_w(w, wtype, base + i);
-    } else {
-        for (int i = tid; i < dim; i += ROUTER_THREADS) row[i] = load_w(w, wtype, base + i);
+    const int t = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int e = blockIdx.x * ROUTER_EPC + warp;
+    float *xs = sm, *row = sm + (size_t)(1 + warp) * dp;
+    // vec: x and the row are stored de-interleaved, element 4g + a at [a * G + g], so accumulator a's
+    // chain reads 4 consecutive terms with one 16-byte load per operand.
+    const int G = dim / 4;
+    if (e < ne) {
+        const size_t base = (size_t)e * dim;
+        if (vec) {
+            for (int g0 = lane; g0 < G; g0 += 32 * 16) {  // 16 loads in flight per lane before the stores
+                float4 v[16];
+#pragma unroll
+                for (int u = 0; u < 16; u++)
+                    if (g0 + 32 * u < G) v[u] = load4_w(w, wtype, base + 4 * (size_t)(g0 + 32 * u));
+#pragma unroll
+                for (int u = 0; u < 16; u++) {
+                    const int g = g0 + 32 * u;
+                    if (g < G) {
+                        row[g] = v[u].x;
+                        row[G + g] = v[u].y;
+                        row[2 * G + g] = v[u].z;
+                        row[3 * G + g] = v[u].w;
+                    }
+                }
+            }
+        } else {
+            for (int i = lane; i < dim; i += 32) row[i] = load_w(w, wtype, base + i);
+        }
     }
     pdl_wait();
     const float *xv = x + (size_t)t * ldx;
     if (vec) {
-        for (int i = tid * 4; i < dim; i += ROUTER_THREADS * 4) *(float4 *)(xs + i) = *(const float4 *)(xv + i);
+        for (int g0 = tid; g0 < G; g0 += ROUTER_THREADS * 8) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (g0 + ROUTER_THREADS * u < G) v[u] = *(const float4 *)(xv + 4 * (g0 + ROUTER_THREADS * u));
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int g = g0 + ROUTER_THREADS * u;
+                if (g < G) {
+                    xs[g] = v[u].x;
+                    xs[G + g] = v[u].y;
+                    xs[2 * G + g] = v[u].z;
+                    xs[3 * G + g] = v[u].w;
+                }
+            }
+        }
     } else {
         for (int i = tid; i < dim; i += ROUTER_THREADS) xs[i] = xv[i];
     }
     __syncthreads();
-    if (tid < 32) {
+    if (e < ne) {
         float s = 0.0f;
-        if (tid < 4) {
+        if (lane < 4 && vec) {  // G % 4 == 0: one 16-byte load per operand per 4 terms
+            const float4 *xa = (const float4 *)(xs + lane * G), *ra = (const float4 *)(row + lane * G);
+#pragma unroll 4
+            for (int q = 0; q < G / 4; q++) {
+                const float4 a = xa[q], b = ra[q];
+                s = __fadd_rn(s, __fmul_rn(a.x, b.x));
+                s = __fadd_rn(s, __fmul_rn(a.y, b.y));
+                s = __fadd_rn(s, __fmul_rn(a.z, b.z));
+                s = __fadd_rn(s, __fmul_rn(a.w, b.w));
+            }
+        } else if (lane < 4) {
             const int groups = dim / 4;
-            const float *xa = xs + tid, *ra = row + tid;
+            const float *xa = xs + lane, *ra = row + lane;
             s = ordered_sum<16>(s, groups, [&](int g) { return __fmul_rn(xa[4 * g], ra[4 * g]); });
-            if (tid == 0)
+            if (lane == 0)
                 for (int i = groups * 4; i < dim; i++) s = __fadd_rn(s, __fmul_rn(xs[i], row[i]));
         }
         const float s1 = __shfl_sync(0xffffffffu, s, 1), s2 = __shfl_sync(0xffffffffu, s, 2),
                     s3 = __shfl_sync(0xffffffffu, s, 3);
-        if (tid == 0) {
-            logits[(size_t)t * ne + e] = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
-            __threadfence();
-            last = atomicAdd(counters + t, 1) == ne - 1;
-        }
+        if (lane == 0) logits[(size_t)t * ne + e] = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        last = atomicAdd(counters + t, 1) == (int)gridDim.x - 1;
     }
     __syncthreads();
     if (!last) return;
     __threadfence();
     if (tid == 0) counters[t] = 0;
-    softmax_topk_block(logits + (size_t)t * ne, sm, sm + ne, ne, k, top + (size_t)t * k, wout + (size_t)t * k, dpart,
+    softmax_topk_block(logits + (size_t)t * ne, sm, pv, ne, k, top + (size_t)t * k, wout + (size_t)t * k, dpart,
                        fpart);
 }
 
@@ -264,7 +303,6 @@ __global__ void __launch_bounds__(ROUTER_THREADS)
 // order with the loads issued ahead of the adds.
 __global__ void moe_combine_kernel(const float *y, int64_t ldy, const int32_t *top, const float *w, int k, int dim,
                                    float *x, int64_t ldx) {
-    pdl_trigger();
     pdl_wait();
     __shared__ int order[64];
     __shared__ float ws[64];
@@ -295,7 +333,6 @@ __global__ void moe_combine_kernel(const float *y, int64_t ldy, const int32_t *t
 // sharded FFN, written into its columns of the buffer the ranks all-reduce.
 __global__ void silu_scatter_kernel(const float *g, int64_t ldg, const float *u, int64_t ldu, int n, float *dst,
                                     int64_t ldd) {
-    pdl_trigger();
     pdl_wait();
     const int t = blockIdx.y;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -340,9 +377,10 @@ void post_qkv(const PostQKV &p, int n_tok, cudaStream_t s) {
 void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, int n_tok,
                  int32_t *top, float *wout, float *logits, int32_t *counters, cudaStream_t s) {
     if (n_tok <= 0) return;
-    const size_t smem = (size_t)2 * std::max((dim + 3) & ~3, ne) * 4;
-    if (smem > 200 * 1024 || n_tok > 65535) {
-        set_error("router_topk: hidden size %d / %d tokens too large", dim, n_tok);
+    const size_t dp = (size_t)((dim + 3) & ~3);
+    const size_t smem = std::max((size_t)(1 + ROUTER_EPC) * dp, (size_t)2 * ne) * 4;
+    if (smem > 200 * 1024 || n_tok > 65535 || k > ne) {
+        set_error("router_topk: hidden size %d / %d tokens / top-%d of %d not supported", dim, n_tok, k, ne);
         return;
     }
     static bool configured = false;
@@ -351,9 +389,9 @@ void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim,
         configured = true;
     }
     const bool w_aligned = wtype == T_F32 ? ((uintptr_t)w & 15) == 0 : ((uintptr_t)w & 7) == 0;
-    const int vec = dim % 4 == 0 && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0 && w_aligned;
-    launch(router_topk_kernel, dim3(ne, n_tok), ROUTER_THREADS, smem, s, x, ldx, w, wtype, dim, ne, k, logits,
-           counters, top, wout, vec);
+    const int vec = dim % 16 == 0 && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0 && w_aligned;
+    launch(router_topk_kernel, dim3((ne + ROUTER_EPC - 1) / ROUTER_EPC, n_tok), ROUTER_THREADS, smem, s, x, ldx, w,
+           wtype, dim, ne, k, logits, counters, top, wout, vec);
     SDY_LAUNCHED();
 }
 

@@ -102,7 +102,6 @@ __device__ float dequant_elem(const QMat &w, int64_t row, int e) {
 
 __global__ void dequant_kernel(QMat w, const int32_t *__restrict__ ids, int64_t first_row, float *__restrict__ out,
                                int64_t ldo) {
-    pdl_trigger();
     pdl_wait();
     int64_t row = ids ? (int64_t)ids[blockIdx.x] : first_row + blockIdx.x;
     float *o = out + (int64_t)blockIdx.x * ldo;
@@ -119,7 +118,6 @@ void dequant_rows(const QMat &w, const int32_t *row_ids, int n_ids, int64_t firs
 // ------------------------------------------------------------------------------ activation quantization
 
 __global__ void quantize_kernel(int vtype, const float *__restrict__ x, int64_t ldx, int n_in, XQ xq) {
-    pdl_trigger();
     pdl_wait();
     const int t = blockIdx.y;
     const int span = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -139,7 +137,6 @@ void quantize_rows(int vtype, const float *x, int64_t ldx, int n_tok, int n_in, 
 
 // Reference-format activation bytes (Q8_K 292 B / Q8_0 34 B blocks) <-> XQ.
 __global__ void xq_import_kernel(int vtype, const uint8_t *__restrict__ raw, int n_tok, XQ xq) {
-    pdl_trigger();
     pdl_wait();
     const int QB = block_elems(vtype), BB = block_bytes(vtype);
     int64_t total = (int64_t)n_tok * xq.nbx;
@@ -168,7 +165,6 @@ __global__ void xq_import_kernel(int vtype, const uint8_t *__restrict__ raw, int
 }
 
 __global__ void xq_export_kernel(XQ xq, uint8_t *__restrict__ raw) {
-    pdl_trigger();
     pdl_wait();
     const int vtype = xq.vtype, QB = block_elems(vtype), BB = block_bytes(vtype);
     int64_t total = (int64_t)xq.n_tok * xq.nbx;

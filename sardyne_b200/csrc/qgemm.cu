@@ -204,7 +204,6 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t gt0 = a.g_begin + (int64_t)blockIdx.x * (GM / GROUP_ROWS);  // first group of the tile
     const int tok0 = blockIdx.y * GN, nv = min(GN, a.n_tok - tok0);
-    pdl_trigger();
     pdl_wait();
 
     if (warp == 0) {

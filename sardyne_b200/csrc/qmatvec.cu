@@ -297,7 +297,6 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
     const int64_t gB = a.g_begin + a.n_groups * (blockIdx.x + 1) / gridDim.x;
     const int units = KQ ? nb : (nb + 7) / 8;  // pair columns per row
     const int ppg = GROUP_ROWS * units;        // pairs per group
-    pdl_trigger();
     // The thread's first pair (pair tid of the first batch): loaded before waiting on the
     // activations' producer. For gathered experts the expert id is itself produced upstream.
     Raw<TYPE> w;

@@ -180,10 +180,11 @@ def attention_model(q, kc, vc, n_kv_head, n_kv):
 @pytest.mark.parametrize("n_head,n_kv_head,hd,stride,n_kv", [
     (16, 2, 128, 1024, 1), (16, 2, 128, 1024, 7), (16, 2, 128, 1024, 777), (32, 4, 128, 4096, 4096),
     (9, 3, 64, 2048, 300), (8, 8, 128, 516, 515), (32, 1, 64, 256, 200), (16, 2, 256, 600, 599),
-    (16, 2, 128, 1023, 500), (4, 4, 80, 64, 50)])
+    (16, 2, 128, 1023, 500), (4, 4, 80, 64, 50), (16, 2, 128, 8192, 3000)])
 def test_attention_vs_reference(n_head, n_kv_head, hd, stride, n_kv):
-    """The cluster kernel's shapes (head_dim a multiple of 32, stride a multiple of 4) and the
-    per-head fallback's: bit-exact against the operation-order model, and within 1e-6 of the
+    """The cluster kernel's shapes (head_dim a multiple of 32, stride a multiple of 4; probabilities
+    pushed to every CTA, or pulled in chunks when a long stride does not fit) and the per-head
+    fallback's: bit-exact against the operation-order model, and within 1e-6 of the
     reference's own op_attention. The reference's expf is glibc's (error < 0.502 ulp), which
     differs from the correctly rounded exp used here in the last bit on ~0.06% of inputs."""
     import oracle
