@@ -640,9 +640,32 @@ void project(engine_ctx *c, const Proj &p, float *out, int64_t ldo, const float 
     for (const Part &part : p.parts) matmul(c, out + part.col, ldo, x, ldx, part.m, n);
 }
 
+// Decode-step norm fusion: a single-token step whose norm feeds only quantized matrices (and the
+// float router) lets each consuming kernel normalise and quantize x itself (NormIn) instead of a
+// separate norm kernel writing xb and the quantized activations (SARDYNE_NO_FUSED_NORM: off).
+// Fused only where one kernel consumes the norm: each consumer pays the norm in its prologue
+// (about as long as the separate kernel on the critical path), so two consumers (q|k and v in
+// different formats, or the MoE router and its experts) are slower fused than not.
+bool fused_norm_ok(int n, const std::vector<const DMat *> &mats) {
+    static const bool off = getenv("SARDYNE_NO_FUSED_NORM") != nullptr;
+    if (off || n != 1 || mats.size() != 1) return false;
+    return mats[0]->quant();
+}
+
+// out = W . RMSNorm(x) for quantized W, the norm applied inside the matvec.
+void matmul_norm(engine_ctx *c, float *out, int64_t ldo, const DMat &w, const NormIn &nin, int n) {
+    const XQ geo = xq_carve(nullptr, vec_dot_type(w.type), w.n_in, n);  // geometry only
+    qmatvec(w.q, geo, out, ldo, 0, w.n_out, 0, c->st, nullptr, &nin);
+}
+
+void project_norm(engine_ctx *c, const Proj &p, float *out, int64_t ldo, const NormIn &nin, int n) {
+    forget_activations(c);
+    for (const Part &part : p.parts) matmul_norm(c, out + part.col, ldo, part.m, nin, n);
+}
+
 // Experts: out[s*ldo + part.col + r] = E[top[s]][r] . x[s / tok_div] for every part.
 void project_experts(engine_ctx *c, const Proj &p, float *out, int64_t ldo, const float *x, int64_t ldx, int n_x,
-                     int n_slots, int tok_div) {
+                     int n_slots, int tok_div, const NormIn *nin = nullptr) {
     for (const Part &part : p.parts) {
         const DMat &w = part.m;
         if (!w.quant()) {
@@ -650,6 +673,12 @@ void project_experts(engine_ctx *c, const Proj &p, float *out, int64_t ldo, cons
             launch(fmatmul_gather_kernel, grid, 256, 0, c->st, w.f, w.type, w.n_in, w.n_out, c->moe_top,
                    (int)c->m->e0, w.n_expert, x, ldx, tok_div, out + part.col, ldo);
             SDY_LAUNCHED();
+            continue;
+        }
+        if (nin) {
+            const XQ geo = xq_carve(nullptr, vec_dot_type(w.type), w.n_in, n_x);  // geometry only
+            qmatvec_gather(w.q, w.gpe, w.n_expert, geo, tok_div, c->moe_top, n_slots, w.n_out, out + part.col, ldo,
+                           c->st, (int)c->m->e0, nin);
             continue;
         }
         const XQ &xq = activations(c, x, ldx, n_x, w.n_in, w.type);
@@ -665,11 +694,15 @@ void all_reduce(engine_ctx *c, const float *send, float *recv, size_t count) {
     if (r != ncclSuccess) set_error("ncclAllReduce: %s", nccl()->error_string(r));
 }
 
-void moe_ffn(engine_ctx *c, const DLayer &L, int n) {
+// nin: the step's ffn norm is fused into the router and the gate|up experts (x = the residual).
+void moe_ffn(engine_ctx *c, const DLayer &L, int n, const NormIn *nin = nullptr) {
     const engine_model_info &in = c->m->info;
     const int dim = in.dim, fe = in.ffn_exp_dim, ne = in.n_expert, k = in.n_expert_used;
     const DMat &r = L.gate_inp;
-    if (!r.quant()) {
+    if (nin) {
+        router_topk(nin->x, dim, r.f, r.type, dim, ne, k, n, c->moe_top, c->moe_w, c->moe_probs, c->moe_count, c->st,
+                    nin->w, nin->eps);
+    } else if (!r.quant()) {
         router_topk(c->xb, dim, r.f, r.type, dim, ne, k, n, c->moe_top, c->moe_w, c->moe_probs, c->moe_count,
                     c->st);
     } else {
@@ -679,7 +712,7 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n) {
         SDY_LAUNCHED();
     }
     const int slots = n * k, gu = 2 * fe;
-    project_experts(c, L.gateup, c->moe_gu, gu, c->xb, dim, n, slots, k);
+    project_experts(c, L.gateup, c->moe_gu, gu, c->xb, dim, n, slots, k, nin);
     const XQ *q8k, *q80;
     want_activations(c, {&L.down}, c->moe_gu, gu, slots, fe, &q8k, &q80);
     silu_quant(c->moe_gu, gu, c->moe_gu + fe, gu, fe, slots, q8k, q80, c->st);
@@ -726,9 +759,13 @@ void forward(engine_ctx *c, int n, int out_rows) {
         const DLayer &L = m->layers[l];
         float *kc = c->k_cache + l * layer_stride, *vc = c->v_cache + l * layer_stride;
         // attention: x = x + Wo . Attn(RoPE(Wq.norm(x)), RoPE(Wk.norm(x)), Wv.norm(x))
-        want_activations(c, mats_of(L.qkv), c->xb, dim, n, dim, &q8k, &q80);
-        rmsnorm_quant(c->x, dim, L.attn_norm, dim, n, in.norm_eps, c->xb, dim, q8k, q80, c->st);
-        project(c, L.qkv, c->qkv, QL, c->xb, dim, n);
+        if (fused_norm_ok(n, mats_of(L.qkv))) {
+            project_norm(c, L.qkv, c->qkv, QL, NormIn{c->x, dim, L.attn_norm, in.norm_eps}, n);
+        } else {
+            want_activations(c, mats_of(L.qkv), c->xb, dim, n, dim, &q8k, &q80);
+            rmsnorm_quant(c->x, dim, L.attn_norm, dim, n, in.norm_eps, c->xb, dim, q8k, q80, c->st);
+            project(c, L.qkv, c->qkv, QL, c->xb, dim, n);
+        }
         PostQKV p{};
         p.q = c->qkv;
         p.k = c->qkv + q_dim;
@@ -756,6 +793,7 @@ void forward(engine_ctx *c, int n, int out_rows) {
         forget_activations(c);
         matmul(c, c->x, dim, c->att, q_dim, L.wo, n, c->x);
         // MLP: x = x + down(silu(gate.norm(x)) * up.norm(x)), or its MoE
+        const NormIn ffn_nin{c->x, dim, L.ffn_norm, in.norm_eps};
         if (in.n_expert) {
             std::vector<const DMat *> need = mats_of(L.gateup);
             if (L.gate_inp.quant()) need.push_back(&L.gate_inp);
@@ -764,9 +802,13 @@ void forward(engine_ctx *c, int n, int out_rows) {
             moe_ffn(c, L, n);
         } else {
             const int F = in.ffn_dim, GU = c->gu_ld;
-            want_activations(c, mats_of(L.gateup), c->xb, dim, n, dim, &q8k, &q80);
-            rmsnorm_quant(c->x, dim, L.ffn_norm, dim, n, in.norm_eps, c->xb, dim, q8k, q80, c->st);
-            project(c, L.gateup, c->hgu, GU, c->xb, dim, n);
+            if (fused_norm_ok(n, mats_of(L.gateup))) {
+                project_norm(c, L.gateup, c->hgu, GU, ffn_nin, n);
+            } else {
+                want_activations(c, mats_of(L.gateup), c->xb, dim, n, dim, &q8k, &q80);
+                rmsnorm_quant(c->x, dim, L.ffn_norm, dim, n, in.norm_eps, c->xb, dim, q8k, q80, c->st);
+                project(c, L.gateup, c->hgu, GU, c->xb, dim, n);
+            }
             if (m->world > 1) {
                 // this rank's gate/up rows [f0, f1) -> its columns of the SiLU product, gathered to
                 // every rank; its rows [d0, d1) of down -> its columns of x, gathered likewise
@@ -786,14 +828,16 @@ void forward(engine_ctx *c, int n, int out_rows) {
     if (out_rows > 0) {
         // final norm and vocabulary projection for the requested rows only
         const float *xs = c->x + (size_t)(n - out_rows) * dim;
-        want_activations(c, {&m->output}, c->xb, dim, out_rows, dim, &q8k, &q80);
-        rmsnorm_quant(xs, dim, m->output_norm, dim, out_rows, in.norm_eps, c->xb, dim, q8k, q80, c->st);
-        if (m->world > 1) {  // this rank's vocabulary rows, gathered
-            matmul(c, c->lsend + m->v0, in.n_vocab, c->xb, dim, m->output, out_rows);
-            all_reduce(c, c->lsend, c->logits, (size_t)out_rows * in.n_vocab);
+        float *lout = m->world > 1 ? c->lsend + m->v0 : c->logits;  // sharded: this rank's vocabulary rows
+        if (fused_norm_ok(out_rows, {&m->output})) {
+            forget_activations(c);
+            matmul_norm(c, lout, in.n_vocab, m->output, NormIn{xs, dim, m->output_norm, in.norm_eps}, out_rows);
         } else {
-            matmul(c, c->logits, in.n_vocab, c->xb, dim, m->output, out_rows);
+            want_activations(c, {&m->output}, c->xb, dim, out_rows, dim, &q8k, &q80);
+            rmsnorm_quant(xs, dim, m->output_norm, dim, out_rows, in.norm_eps, c->xb, dim, q8k, q80, c->st);
+            matmul(c, lout, in.n_vocab, c->xb, dim, m->output, out_rows);
         }
+        if (m->world > 1) all_reduce(c, c->lsend, c->logits, (size_t)out_rows * in.n_vocab);
     }
     forget_activations(c);
 }

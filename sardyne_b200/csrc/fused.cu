@@ -51,21 +51,8 @@ __global__ void rmsnorm_quant_kernel(const float *x, int64_t ldx, const float *w
                                      int64_t ldb, XQ q8k, XQ q80) {
     pdl_wait();
     __shared__ double part[32];
-    const int t = blockIdx.x, e0 = threadIdx.x * 8;
-    const float *xv = x + (size_t)t * ldx;
-    float v[8];
-    double ss = 0.0;
-    for (int j = 0; j < 8; j++) {
-        v[j] = e0 + j < n ? xv[e0 + j] : 0.0f;
-        ss += (double)v[j] * v[j];
-    }
-    ss = bsum_d(ss, part);
-    const float scale = (float)(1.0 / sqrt(ss / n + (double)eps));
-    for (int j = 0; j < 8; j++) {
-        v[j] = e0 + j < n ? __fmul_rn(__fmul_rn(v[j], scale), w[e0 + j]) : 0.0f;
-        if (xb && e0 + j < n) xb[(size_t)t * ldb + e0 + j] = v[j];
-    }
-    quantize_span(v, e0, n, t, threadIdx.x >> 5, q8k, q80);
+    const int t = blockIdx.x;
+    norm_quant_row(x + (size_t)t * ldx, w, n, eps, t, q8k, q80, xb ? xb + (size_t)t * ldb : nullptr, part);
 }
 
 // grid (ceil(n/2048), rows), 256 threads: warp w of block b owns span 8b + w.
@@ -203,7 +190,7 @@ __device__ void softmax_topk_block(const float *logits, float *prob, float *pv, 
 // zero again) runs the softmax and top-k. vec: dim % 4 == 0 and 16-byte aligned x rows / weights.
 __global__ void __launch_bounds__(ROUTER_THREADS)
     router_topk_kernel(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, float *logits,
-                       int32_t *counters, int32_t *top, float *wout, int vec) {
+                       int32_t *counters, int32_t *top, float *wout, int vec, const float *nw, float neps) {
     extern __shared__ __align__(16) float sm[];
     __shared__ double dpart[32];
     __shared__ float fpart[32];
@@ -241,6 +228,11 @@ __global__ void __launch_bounds__(ROUTER_THREADS)
     }
     pdl_wait();
     const float *xv = x + (size_t)t * ldx;
+    // nw: the router input is RMSNorm(x) * nw, computed here in the shared fixed order (the value
+    // the standalone norm kernel would have stored), instead of a normalised copy read from memory.
+    float scale = 1.0f;
+    if (nw) scale = (float)(1.0 / sqrt(span_sumsq(xv, dim, dpart) / dim + (double)neps));
+    auto nrm = [&](float v, int i) { return nw ? __fmul_rn(__fmul_rn(v, scale), nw[i]) : v; };
     if (vec) {
         for (int g0 = tid; g0 < G; g0 += ROUTER_THREADS * 8) {
             float4 v[8];
@@ -251,15 +243,15 @@ __global__ void __launch_bounds__(ROUTER_THREADS)
             for (int u = 0; u < 8; u++) {
                 const int g = g0 + ROUTER_THREADS * u;
                 if (g < G) {
-                    xs[g] = v[u].x;
-                    xs[G + g] = v[u].y;
-                    xs[2 * G + g] = v[u].z;
-                    xs[3 * G + g] = v[u].w;
+                    xs[g] = nrm(v[u].x, 4 * g);
+                    xs[G + g] = nrm(v[u].y, 4 * g + 1);
+                    xs[2 * G + g] = nrm(v[u].z, 4 * g + 2);
+                    xs[3 * G + g] = nrm(v[u].w, 4 * g + 3);
                 }
             }
         }
     } else {
-        for (int i = tid; i < dim; i += ROUTER_THREADS) xs[i] = xv[i];
+        for (int i = tid; i < dim; i += ROUTER_THREADS) xs[i] = nrm(xv[i], i);
     }
     __syncthreads();
     if (e < ne) {
@@ -375,11 +367,12 @@ void post_qkv(const PostQKV &p, int n_tok, cudaStream_t s) {
 }
 
 void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, int n_tok,
-                 int32_t *top, float *wout, float *logits, int32_t *counters, cudaStream_t s) {
+                 int32_t *top, float *wout, float *logits, int32_t *counters, cudaStream_t s, const float *norm_w,
+                 float norm_eps) {
     if (n_tok <= 0) return;
     const size_t dp = (size_t)((dim + 3) & ~3);
     const size_t smem = std::max((size_t)(1 + ROUTER_EPC) * dp, (size_t)2 * ne) * 4;
-    if (smem > 200 * 1024 || n_tok > 65535 || k > ne) {
+    if (smem > 200 * 1024 || n_tok > 65535 || k > ne || (norm_w && dim > 8192)) {
         set_error("router_topk: hidden size %d / %d tokens / top-%d of %d not supported", dim, n_tok, k, ne);
         return;
     }
@@ -391,7 +384,7 @@ void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim,
     const bool w_aligned = wtype == T_F32 ? ((uintptr_t)w & 15) == 0 : ((uintptr_t)w & 7) == 0;
     const int vec = dim % 16 == 0 && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0 && w_aligned;
     launch(router_topk_kernel, dim3((ne + ROUTER_EPC - 1) / ROUTER_EPC, n_tok), ROUTER_THREADS, smem, s, x, ldx, w,
-           wtype, dim, ne, k, logits, counters, top, wout, vec);
+           wtype, dim, ne, k, logits, counters, top, wout, vec, norm_w, norm_eps);
     SDY_LAUNCHED();
 }
 

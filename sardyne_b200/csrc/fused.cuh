@@ -34,8 +34,10 @@ void post_qkv(const PostQKV &p, int n_tok, cudaStream_t s);
 
 // Float router: top [n_tok][k] expert ids and renormalised weights; logits is scratch [n_tok][ne];
 // counters: n_tok int32 that start at zero (the kernel leaves them at zero).
+// norm_w: the router input is RMSNorm(x) * norm_w, computed inside the kernel (x the residual).
 void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, int n_tok,
-                 int32_t *top, float *wout, float *logits, int32_t *counters, cudaStream_t s);
+                 int32_t *top, float *wout, float *logits, int32_t *counters, cudaStream_t s,
+                 const float *norm_w = nullptr, float norm_eps = 0.0f);
 // x[t] += sum over t's k slots in ascending expert id of w * y[slot].
 void moe_combine(const float *y, int64_t ldy, const int32_t *top, const float *w, int k, int dim, int n_tok, float *x,
                  int64_t ldx, cudaStream_t s);

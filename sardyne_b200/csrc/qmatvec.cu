@@ -16,6 +16,7 @@
 // result is bit-identical to the reference's scalar kernels (and, for Q4_K/Q6_K, to its AVX2
 // kernels, which share the same combine).
 #include "common.cuh"
+#include "quant_device.cuh"
 
 #include <algorithm>
 #include <cstdlib>
@@ -56,6 +57,11 @@ struct Args {
     // groups start at expert * gpe, with the activations of token s / tok_div, into out + s*ldo_slot.
     const int32_t *slot_expert;
     int64_t gpe, ldo_slot;
+    // When nx is set, the activations are not read from the XQ: each CTA normalises its tokens'
+    // rows x[t] (RMSNorm with weight nw, eps neps) and quantizes them into shared memory itself.
+    const float *nx, *nw;
+    int64_t ldnx;
+    float neps;
     int tok_div, n_expert, expert0;  // slot_expert ids are global; this matrix holds experts expert0..
 };
 
@@ -307,6 +313,7 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
         load_pair(w, slabs + (size_t)(gA + gl) * nb * SB, rem >> 3, rem & 7, nb);
     }
     pdl_wait();
+    const float *nx = a.nx;
     if (a.slot_expert) {
         const int slot = blockIdx.y, e = a.slot_expert[slot] - a.expert0;
         if (e < 0 || e >= a.n_expert) return;  // another rank's expert (or an invalid id)
@@ -315,11 +322,27 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
         xqs += (size_t)tok * a.qrow;
         xd += (size_t)tok * a.nbx;
         xsums += (size_t)tok * a.nbx * (KQ ? 8 : 1);
+        if (nx) nx += (size_t)tok * a.ldnx;
         out += (size_t)slot * a.ldo_slot;
     }
 
-    // Stage the activations of NT tokens (broadcast operands for every pair).
-    {
+    if (nx) {  // normalise and quantize the NT rows into the shared-memory XQ
+        __shared__ double part[32];
+        XQ v;
+        v.vtype = KQ ? T_Q8_K : T_Q8_0;
+        v.n_in = nb * block_elems(TYPE);
+        v.n_tok = NT;
+        v.qrow = a.qrow;
+        v.nbx = nb;
+        v.qs = (int8_t *)sq;
+        v.d = sd;
+        v.sums = ss;
+        XQ none;
+        none.qs = nullptr;
+        for (int t = 0; t < NT; t++)
+            norm_quant_row(nx + (size_t)t * a.ldnx, a.nw, v.n_in, a.neps, t, KQ ? v : none, KQ ? none : v, nullptr,
+                           part);
+    } else {  // stage the activations of NT tokens (broadcast operands for every pair)
         const int qv = NT * a.qrow / 16;
         for (int i = tid; i < qv; i += THREADS) {
             int t = i / (a.qrow / 16), k = i % (a.qrow / 16);
@@ -491,10 +514,10 @@ int gemm_min_tokens() {
 }
 
 void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
-             cudaStream_t s, const float *residual) {
+             cudaStream_t s, const float *residual, const NormIn *norm) {
     if (row1 <= row0 || xq.n_tok <= 0) return;
     const int gmin = gemm_min_tokens();
-    if (gmin > 0 && xq.n_tok >= gmin && qgemm_supported(w.type, w.n_in) && xq.vtype == T_Q8_K &&
+    if (!norm && gmin > 0 && xq.n_tok >= gmin && qgemm_supported(w.type, w.n_in) && xq.vtype == T_Q8_K &&
         xq.n_in == w.n_in) {
         qgemm(w, xq, out, ldo, row0, row1, out_row0, s, residual);
         return;
@@ -529,6 +552,12 @@ void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0,
         a.nbx = xq.nbx;
         a.out = out + (size_t)t0 * ldo;
         a.residual = residual ? residual + (size_t)t0 * ldo : nullptr;
+        if (norm) {
+            a.nx = norm->x + (size_t)t0 * norm->ldx;
+            a.ldnx = norm->ldx;
+            a.nw = norm->w;
+            a.neps = norm->eps;
+        }
         a.ldo = ldo;
         a.row0 = row0;
         a.row1 = row1;
@@ -543,7 +572,8 @@ void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0,
 namespace sdy {
 
 void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq, int tok_div, const int32_t *slot_expert,
-                    int n_slots, int64_t rows_per_expert, float *out, int64_t ldo_slot, cudaStream_t s, int expert0) {
+                    int n_slots, int64_t rows_per_expert, float *out, int64_t ldo_slot, cudaStream_t s, int expert0,
+                    const NormIn *norm) {
     if (n_slots <= 0) return;
     if (xq.vtype != vec_dot_type(experts.type) || xq.n_in != experts.n_in) {
         set_error("qmatvec_gather: activation type/size does not match the weights");
@@ -578,6 +608,12 @@ void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq
     a.tok_div = tok_div;
     a.n_expert = n_expert;
     a.expert0 = expert0;
+    if (norm) {
+        a.nx = norm->x;
+        a.ldnx = norm->ldx;
+        a.nw = norm->w;
+        a.neps = norm->eps;
+    }
     dispatch(experts.type, 1, a, plan.smem, dim3(plan.grid, n_slots), s);
 }
 

@@ -98,4 +98,71 @@ __device__ __forceinline__ void quant_q80_span(const float *x, int t, int span, 
     quant_q80_vals(v, e0 < n_in, t, span, xq);
 }
 
+// ------------------------------------------------------------------------------ RMSNorm rows
+// The reference's RMSNorm (ops.c:346-351) of one row, shared by the standalone norm kernel and
+// the kernels that normalise their own input in a prologue, so that all of them produce the same
+// floats: the double sum of squares is taken in one fixed order that does not depend on the block
+// size (8 consecutive elements per lane in order, a 256-element span by a warp's shuffle tree, the
+// span partials by a second shuffle tree over part[0 .. ceil(n/256))). n <= 8192.
+
+// Every thread of the block calls it and gets the total; part: 32 shared doubles.
+__device__ inline double span_sumsq(const float *x, int n, double *part) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5, ns = (n + 255) / 256;
+    for (int s = warp; s < ns; s += nw) {
+        const int e0 = s * 256 + lane * 8;
+        double ss = 0.0;
+        for (int j = 0; j < 8; j++) {
+            const float v = e0 + j < n ? x[e0 + j] : 0.0f;
+            ss += (double)v * v;
+        }
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) part[s] = ss;
+    }
+    __syncthreads();
+    double v = lane < ns ? part[lane] : 0.0;
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();  // part may be reused
+    return v;
+}
+
+// v = x * (float)(1/sqrt(ss/n + eps)) * w for token t, quantized into q8k and/or q80 (XQ views of
+// global or shared memory; a null qs skips that type; q8k needs n % 256 == 0) and optionally
+// stored to xb. Whole block. When every warp has at most one span the row stays in registers
+// between the sum of squares and the scaling (same order and values as span_sumsq).
+__device__ inline void norm_quant_row(const float *x, const float *w, int n, float eps, int t, const XQ &q8k,
+                                      const XQ &q80, float *xb, double *part) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5, ns = (n + 255) / 256;
+    double ss;
+    float r[8];
+    const bool one = ns <= nw;
+    if (one) {
+        const int e0 = warp * 256 + lane * 8;
+        double p = 0.0;
+        for (int j = 0; j < 8; j++) {
+            r[j] = warp < ns && e0 + j < n ? x[e0 + j] : 0.0f;
+            p += (double)r[j] * r[j];
+        }
+        for (int o = 16; o; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+        if (lane == 0 && warp < ns) part[warp] = p;
+        __syncthreads();
+        ss = lane < ns ? part[lane] : 0.0;
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        __syncthreads();
+    } else {
+        ss = span_sumsq(x, n, part);
+    }
+    const float scale = (float)(1.0 / sqrt(ss / n + (double)eps));
+    for (int s = warp; s < ns; s += nw) {
+        const int e0 = s * 256 + lane * 8;
+        float v[8];
+        for (int j = 0; j < 8; j++) {
+            const float xv = one ? r[j] : (e0 + j < n ? x[e0 + j] : 0.0f);
+            v[j] = e0 + j < n ? __fmul_rn(__fmul_rn(xv, scale), w[e0 + j]) : 0.0f;
+            if (xb && e0 + j < n) xb[e0 + j] = v[j];
+        }
+        if (q8k.qs) quant_q8k_vals(v, t, s, q8k);
+        if (q80.qs) quant_q80_vals(v, e0 < n, t, s, q80);
+    }
+}
+
 }  // namespace sdy
