@@ -375,6 +375,125 @@ __global__ void attention_head_kernel(float *out, const float *q, int64_t ldq, c
     if (i1 < hd) ov[i1] = acc1;
 }
 
+// Prefill: one CTA per (head, PQ consecutive query tokens), PF_THREADS threads. The reference's
+// per-query work in the same operation order, with K and V tiles shared by the PQ queries:
+//   scores  s[q][j] = dot4(q_q, k_j) * scale for j < n_kv(q) = pos(q) + 1, into the scratch rows;
+//   softmax one warp per query (exp in double rounded once, double sum, p = e * (float)(1/sum));
+//   output  thread (element e, query half) runs PQ/2 chains acc_q += p[q][j] * v_j[e] in key order
+//           (probabilities of masked keys are 0, and adding +0 leaves a chain unchanged).
+constexpr int PQ = 16;
+constexpr int PF_THREADS = 256;
+constexpr int PF_KT = 64;  // keys per K/V tile
+__host__ __device__ inline int pf_smem_floats(int hd) {
+    return PQ * hd + PF_KT * (hd + 4) + PF_KT * hd + PF_KT * PQ;
+}
+
+__global__ void __launch_bounds__(PF_THREADS)
+    attention_prefill_kernel(float *__restrict__ out, const float *__restrict__ q, int64_t ldq,
+                             const float *__restrict__ kc, const float *__restrict__ vc, int n_tok, int n_head,
+                             int n_kv_head, int hd, int pos0, const int32_t *pos_dev, int stride, float *scratch) {
+    pdl_wait();
+    extern __shared__ __align__(16) float sm[];
+    const int h = blockIdx.x, t0 = blockIdx.y * PQ, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nq = min(PQ, n_tok - t0);
+    const int p0 = (pos_dev ? *pos_dev : pos0) + t0;  // position of query 0; query i sees p0 + i + 1 keys
+    const int kv_max = p0 + nq;
+    const int n_rep = n_head / n_kv_head;
+    const float *kh = kc + (size_t)(h / n_rep) * stride * hd, *vh = vc + (size_t)(h / n_rep) * stride * hd;
+    float *qs = sm, *kt = qs + PQ * hd, *vt = kt + PF_KT * (hd + 4), *pt = vt + PF_KT * hd;
+    const int ldk = hd + 4, hd4 = hd / 4;
+    const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
+    auto srow = [&](int i) { return scratch + ((size_t)(t0 + i) * n_head + h) * stride; };
+    for (int idx = tid; idx < PQ * hd4; idx += PF_THREADS) {
+        const int i = idx / hd4, c = idx - i * hd4;
+        const float4 v = i < nq ? *(const float4 *)(q + (size_t)(t0 + i) * ldq + (size_t)h * hd + 4 * c)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        *(float4 *)(qs + i * hd + 4 * c) = v;
+    }
+    // ---- scores
+    for (int j0 = 0; j0 < kv_max; j0 += PF_KT) {
+        const int nk = min(PF_KT, kv_max - j0);
+        __syncthreads();
+        for (int idx = tid; idx < nk * hd4; idx += PF_THREADS) {
+            const int j = idx / hd4, c = idx - j * hd4;
+            *(float4 *)(kt + j * ldk + 4 * c) = *(const float4 *)(kh + (size_t)(j0 + j) * hd + 4 * c);
+        }
+        __syncthreads();
+        for (int pr = tid; pr < PQ * PF_KT; pr += PF_THREADS) {  // (query, key) pairs, key fastest
+            const int i = pr / PF_KT, j = pr - i * PF_KT;
+            if (i >= nq || j >= nk || j0 + j >= p0 + i + 1) continue;
+            const float *x = qs + i * hd, *k = kt + j * ldk;
+            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+            for (int c = 0; c < hd; c += 4) {
+                const float4 u = *(const float4 *)(x + c), w = *(const float4 *)(k + c);
+                a0 = __fadd_rn(a0, __fmul_rn(u.x, w.x));
+                a1 = __fadd_rn(a1, __fmul_rn(u.y, w.y));
+                a2 = __fadd_rn(a2, __fmul_rn(u.z, w.z));
+                a3 = __fadd_rn(a3, __fmul_rn(u.w, w.w));
+            }
+            srow(i)[j0 + j] = __fmul_rn(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)), scale);
+        }
+    }
+    __syncthreads();
+    // ---- softmax, one warp per query
+    for (int i = warp; i < nq; i += PF_THREADS / 32) {
+        float *r = srow(i);
+        const int nk = p0 + i + 1;
+        float m = -INFINITY;
+        for (int j = lane; j < nk; j += 32) m = fmaxf(m, r[j]);
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        double sacc = 0.0;
+        for (int j = lane; j < nk; j += 32) {
+            const float e = exp_cr(__fsub_rn(r[j], m));
+            r[j] = e;
+            sacc += e;
+        }
+        for (int o = 16; o; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
+        const float inv = (float)(1.0 / sacc);
+        for (int j = lane; j < nk; j += 32) r[j] = __fmul_rn(r[j], inv);
+    }
+    __syncthreads();
+    // ---- weighted sums: thread (e, half) keeps the chains of queries half*PQ/2 .. +PQ/2-1
+    constexpr int QH = PQ / 2;
+    const int e = tid % hd, half = tid / hd;  // hd <= 128: 2*hd <= 256 threads
+    const bool active = tid < 2 * hd;
+    float acc[QH];
+#pragma unroll
+    for (int c = 0; c < QH; c++) acc[c] = 0.0f;
+    for (int j0 = 0; j0 < kv_max; j0 += PF_KT) {
+        const int nk = min(PF_KT, kv_max - j0);
+        __syncthreads();
+        for (int idx = tid; idx < nk * hd4; idx += PF_THREADS)
+            *(float4 *)(vt + idx * 4) = *(const float4 *)(vh + (size_t)j0 * hd + idx * 4);
+        for (int idx = tid; idx < PF_KT * PQ; idx += PF_THREADS) {  // pt[j][i]: 0 where masked
+            const int j = idx / PQ, i = idx - j * PQ;
+            pt[idx] = (i < nq && j < nk && j0 + j < p0 + i + 1) ? srow(i)[j0 + j] : 0.0f;
+        }
+        __syncthreads();
+        if (active) {
+            const float *pq = pt + half * QH;
+            for (int j = 0; j < nk; j++) {
+                const float v = vt[j * hd + e];
+                const float4 pa = *(const float4 *)(pq + j * PQ), pb = *(const float4 *)(pq + j * PQ + 4);
+                acc[0] = __fadd_rn(acc[0], __fmul_rn(pa.x, v));
+                acc[1] = __fadd_rn(acc[1], __fmul_rn(pa.y, v));
+                acc[2] = __fadd_rn(acc[2], __fmul_rn(pa.z, v));
+                acc[3] = __fadd_rn(acc[3], __fmul_rn(pa.w, v));
+                acc[4] = __fadd_rn(acc[4], __fmul_rn(pb.x, v));
+                acc[5] = __fadd_rn(acc[5], __fmul_rn(pb.y, v));
+                acc[6] = __fadd_rn(acc[6], __fmul_rn(pb.z, v));
+                acc[7] = __fadd_rn(acc[7], __fmul_rn(pb.w, v));
+            }
+        }
+    }
+    if (active)
+#pragma unroll
+        for (int c = 0; c < QH; c++) {
+            const int i = half * QH + c;
+            if (i < nq) out[((size_t)(t0 + i) * n_head + h) * hd + e] = acc[c];
+        }
+}
+
 bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
 }  // namespace
@@ -385,6 +504,22 @@ void attention(float *out, const float *q, int64_t ldq, const float *kc, const f
     if (n_tok <= 0) return;
     if (hd % 4 || n_kv_head <= 0 || n_head % n_kv_head) {
         set_error("attention: head_dim %d / heads %d/%d not supported", hd, n_head, n_kv_head);
+        return;
+    }
+    // Many queries (prefill): the query-tile kernel (causal counts only; fixed_nkv is op_attention's
+    // single query).
+    if (n_tok >= PQ && fixed_nkv <= 0 && hd <= 128 && aligned16(q) && ldq % 4 == 0 && aligned16(kc) &&
+        aligned16(vc) && n_tok <= 65535 * PQ) {
+        const size_t smem = (size_t)pf_smem_floats(hd) * 4;
+        static bool configured = false;
+        if (!configured) {
+            SDY_CUDA(cudaFuncSetAttribute(attention_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          pf_smem_floats(128) * 4));
+            configured = true;
+        }
+        launch(attention_prefill_kernel, dim3(n_head, (n_tok + PQ - 1) / PQ), PF_THREADS, smem, s, out, q, ldq, kc, vc,
+               n_tok, n_head, n_kv_head, hd, pos0, pos_dev, stride, scratch);
+        SDY_LAUNCHED();
         return;
     }
     const int n_rep = n_head / n_kv_head;

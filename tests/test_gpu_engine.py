@@ -69,6 +69,20 @@ def test_forward_matches_reference(model_path, ref_lib):
     assert (got.argmax(-1) == want.argmax(-1)).all()
 
 
+LONG = [(7 * i + 3) % 60 + 1 for i in range(45)]
+
+
+@pytest.mark.parametrize("n_batch", [45, 20])
+def test_long_prompt_matches_reference(model_path, ref_lib, n_batch):
+    """A 45-token prompt in one chunk or in chunks of 20 (the second and third start at positions
+    20 and 40): the tensor-core GEMM and the query-tile prefill attention."""
+    want = runtime.Context(runtime.Model(model_path, lib=ref_lib), max_seq=64, n_batch=n_batch,
+                           logits_all=True).eval(LONG)
+    got = runtime.Context(runtime.Model(model_path), max_seq=64, n_batch=n_batch, logits_all=True).eval(LONG)
+    close(got, want)
+    assert (got.argmax(-1) == want.argmax(-1)).all()
+
+
 def test_generate_matches_reference(model_path, ref_lib):
     want = runtime.generate(runtime.Context(runtime.Model(model_path, lib=ref_lib), max_seq=32), TOKENS[:4], 16)
     got = runtime.generate(runtime.Context(runtime.Model(model_path), max_seq=32), TOKENS[:4], 16)
