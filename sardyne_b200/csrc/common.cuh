@@ -198,11 +198,21 @@ struct NormIn {
     float eps = 0.0f;
 };
 
+// Token count from which products go to the tensor-core GEMM (0 = never).
+int gemm_min_tokens();
 // Many-token product on the tensor cores (qgemm.cu), same contract as qmatvec; Q4_K/Q6_K only.
 bool qgemm_supported(int type, int n_in);
 void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
            cudaStream_t s, const float *residual = nullptr);
 unsigned qgemm_status();  // nonzero when a qgemm completion wait timed out
+// Grouped experts on the tensor cores (MoE prefill): for local expert e, the slots
+// grp_slot[grp_off[e] .. grp_off[e+1]) (device arrays from moe_group with tile GEMM_TILE_TOKENS;
+// at most max_slots in all) multiply expert e with activation row slot / xdiv into
+// out + slot * ldo_slot; rows_per_expert rows each.
+constexpr int GEMM_TILE_TOKENS = 128;
+void qgemm_grouped(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq, int xdiv, const int32_t *grp_off,
+                   const int32_t *grp_slot, const int32_t *grp_tiles, int max_slots, int64_t rows_per_expert,
+                   float *out, int64_t ldo_slot, cudaStream_t s);
 // norm: x -> RMSNorm -> quantize inside the kernel (xq then only gives the activation geometry).
 void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
              cudaStream_t s, const float *residual = nullptr, const NormIn *norm = nullptr);

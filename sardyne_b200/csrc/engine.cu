@@ -181,6 +181,7 @@ struct engine_ctx {
           *logits = nullptr, *scores = nullptr;
     float *moe_probs = nullptr, *moe_w = nullptr, *moe_gu = nullptr, *moe_y = nullptr;
     int32_t *moe_count = nullptr;  // per-token router counters (router_topk)
+    int32_t *grp_off = nullptr, *grp_slot = nullptr, *grp_tiles = nullptr;  // slots by expert (prefill GEMM)
     // Sharded models: all-reduce sources, zero outside this rank's columns (hsend: FFN activations
     // [B][ffn_dim], xsend: residual [B][dim], lsend: logits), and the gathered FFN activations.
     float *hsend = nullptr, *hfull = nullptr, *xsend = nullptr, *lsend = nullptr;
@@ -712,7 +713,23 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n, const NormIn *nin = nullptr)
         SDY_LAUNCHED();
     }
     const int slots = n * k, gu = 2 * fe;
-    project_experts(c, L.gateup, c->moe_gu, gu, c->xb, dim, n, slots, k, nin);
+    // Many tokens: experts as grouped tensor-core GEMMs over the slots sorted by expert.
+    bool grouped = !nin && gemm_min_tokens() > 0 && n >= gemm_min_tokens() && L.down.quant() &&
+                   qgemm_supported(L.down.type, L.down.n_in);
+    for (const Part &part : L.gateup.parts)
+        grouped = grouped && part.m.quant() && qgemm_supported(part.m.type, part.m.n_in);
+    const int ne_local = L.down.n_expert;
+    if (grouped) {
+        moe_group(c->moe_top, slots, (int)c->m->e0, ne_local, GEMM_TILE_TOKENS, c->grp_off, c->grp_slot,
+                  c->grp_tiles, c->st);
+        for (const Part &part : L.gateup.parts) {
+            const XQ &xq = activations(c, c->xb, dim, n, dim, part.m.type);
+            qgemm_grouped(part.m.q, part.m.gpe, ne_local, xq, k, c->grp_off, c->grp_slot, c->grp_tiles, slots,
+                          part.m.n_out, c->moe_gu + part.col, gu, c->st);
+        }
+    } else {
+        project_experts(c, L.gateup, c->moe_gu, gu, c->xb, dim, n, slots, k, nin);
+    }
     const XQ *q8k, *q80;
     want_activations(c, {&L.down}, c->moe_gu, gu, slots, fe, &q8k, &q80);
     silu_quant(c->moe_gu, gu, c->moe_gu + fe, gu, fe, slots, q8k, q80, c->st);
@@ -720,7 +737,13 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n, const NormIn *nin = nullptr)
     down.parts.push_back(Part{L.down, 0});
     const bool sharded = c->m->world > 1;
     if (sharded) SDY_CUDA(cudaMemsetAsync(c->moe_y, 0, (size_t)slots * dim * 4, c->st));  // other ranks' slots
-    project_experts(c, down, c->moe_y, dim, c->moe_gu, gu, slots, slots, 1);
+    if (grouped) {
+        const XQ &xq = activations(c, c->moe_gu, gu, slots, fe, L.down.type);
+        qgemm_grouped(L.down.q, L.down.gpe, ne_local, xq, 1, c->grp_off, c->grp_slot, c->grp_tiles, slots,
+                      L.down.n_out, c->moe_y, dim, c->st);
+    } else {
+        project_experts(c, down, c->moe_y, dim, c->moe_gu, gu, slots, slots, 1);
+    }
     if (sharded) all_reduce(c, c->moe_y, c->moe_y, (size_t)slots * dim);  // every slot from its expert's rank
     moe_combine(c->moe_y, dim, c->moe_top, c->moe_w, k, dim, n, c->x, dim, c->st);
 }
@@ -1076,6 +1099,9 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
     if (in.n_expert) {
         items.push_back({(void **)&c->moe_probs, B * in.n_expert * 4});
         items.push_back({(void **)&c->moe_count, B * 4});
+        items.push_back({(void **)&c->grp_off, ((size_t)in.n_expert + 2) * 4});
+        items.push_back({(void **)&c->grp_slot, slots * 4});
+        items.push_back({(void **)&c->grp_tiles, (slots / GEMM_TILE_TOKENS + in.n_expert) * 4});
         items.push_back({(void **)&c->moe_w, slots * 4});
         items.push_back({(void **)&c->moe_top, slots * 4});
         items.push_back({(void **)&c->moe_gu, slots * 2 * ffn * 4});

@@ -333,6 +333,44 @@ __global__ void silu_scatter_kernel(const float *g, int64_t ldg, const float *u,
     }
 }
 
+// Counting sort of the slots by (local) expert: off[e] .. off[e+1] indexes slots[] for expert
+// e0 + e; slots of other ranks' experts are left out. One CTA; order within an expert follows the
+// atomics (each slot's product does not depend on its position).
+// Also the work list of the grouped GEMM: tiles[i] = (e << 16) | token tile, i < off[ne + 1].
+__global__ void moe_group_kernel(const int32_t *top, int n_slots, int e0, int ne, int tile, int32_t *off,
+                                 int32_t *slots, int32_t *tiles) {
+    pdl_wait();
+    extern __shared__ int cnt[];  // ne counts, then cursors
+    for (int i = threadIdx.x; i < ne; i += blockDim.x) cnt[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n_slots; i += blockDim.x) {
+        const int e = top[i] - e0;
+        if (e >= 0 && e < ne) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int e = 0; e < ne; e++) {
+            const int c = cnt[e];
+            cnt[e] = run;
+            off[e] = run;
+            run += c;
+        }
+        off[ne] = run;
+        int nt = 0;
+        for (int e = 0; e < ne; e++) {
+            const int c = (e + 1 < ne ? cnt[e + 1] : run) - cnt[e];
+            for (int tt = 0; tt * tile < c; tt++) tiles[nt++] = (e << 16) | tt;
+        }
+        off[ne + 1] = nt;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n_slots; i += blockDim.x) {
+        const int e = top[i] - e0;
+        if (e >= 0 && e < ne) slots[atomicAdd(&cnt[e], 1)] = i;
+    }
+}
+
 XQ pick(const XQ *q) {
     XQ a = q ? *q : XQ();
     if (!q) a.qs = nullptr;
@@ -399,6 +437,17 @@ void silu_scatter(const float *g, int64_t ldg, const float *u, int64_t ldu, int 
                   cudaStream_t s) {
     if (rows <= 0 || n <= 0) return;
     launch(silu_scatter_kernel, dim3((n + 255) / 256, rows), 256, 0, s, g, ldg, u, ldu, n, dst, ldd);
+    SDY_LAUNCHED();
+}
+
+void moe_group(const int32_t *top, int n_slots, int e0, int ne, int tile, int32_t *off, int32_t *slots,
+               int32_t *tiles, cudaStream_t s) {
+    if (ne <= 0) return;
+    if (ne >= (1 << 15) || n_slots / tile >= (1 << 16)) {
+        set_error("moe_group: %d experts / %d slots not supported", ne, n_slots);
+        return;
+    }
+    launch(moe_group_kernel, 1, 1024, (size_t)ne * 4, s, top, n_slots, e0, ne, tile, off, slots, tiles);
     SDY_LAUNCHED();
 }
 

@@ -38,6 +38,10 @@ void post_qkv(const PostQKV &p, int n_tok, cudaStream_t s);
 void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, int n_tok,
                  int32_t *top, float *wout, float *logits, int32_t *counters, cudaStream_t s,
                  const float *norm_w = nullptr, float norm_eps = 0.0f);
+// Slots grouped by expert e0 + e (e < ne): slots[off[e] .. off[e+1]); tiles[0 .. off[ne+1]) lists
+// (e << 16 | token tile) for every `tile` slots of every expert (off: ne + 2 ints).
+void moe_group(const int32_t *top, int n_slots, int e0, int ne, int tile, int32_t *off, int32_t *slots,
+               int32_t *tiles, cudaStream_t s);
 // x[t] += sum over t's k slots in ascending expert id of w * y[slot].
 void moe_combine(const float *y, int64_t ldy, const int32_t *top, const float *w, int k, int dim, int n_tok, float *x,
                  int64_t ldx, cudaStream_t s);

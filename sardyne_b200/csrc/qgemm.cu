@@ -25,7 +25,7 @@ namespace sdy {
 namespace {
 
 constexpr int GM = 128;           // weight rows per tile
-constexpr int GN = 128;           // tokens per tile
+constexpr int GN = GEMM_TILE_TOKENS;  // tokens per tile
 constexpr int G_THREADS = 256;
 constexpr int PLANE = GM * 256;   // bytes of one expanded A plane (one superblock)
 constexpr int BTILE = GN * 256;   // bytes of the B tile
@@ -190,6 +190,14 @@ struct GemmArgs {
     float *out;
     int64_t ldo, row0, row1, out_row0;
     const float *residual;
+    // Grouped experts (MoE prefill): grid.y walks the work list grp_tiles[0 .. grp_off[ne+1]) of
+    // (e << 16 | token tile); expert e's slots are grp_slot[grp_off[e] .. grp_off[e+1]); slot s
+    // reads activation row s / xdiv and writes out + s * ldo; expert e's matrix starts at group
+    // e * gpe.
+    const int32_t *grp_off, *grp_slot, *grp_tiles;
+    int n_expert;
+    int xdiv;
+    int64_t gpe;
 };
 
 template <int TYPE>
@@ -203,8 +211,23 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
     uint32_t *tmem_slot = (uint32_t *)(mbar + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t gt0 = a.g_begin + (int64_t)blockIdx.x * (GM / GROUP_ROWS);  // first group of the tile
-    const int tok0 = blockIdx.y * GN, nv = min(GN, a.n_tok - tok0);
+    int tok0 = blockIdx.y * GN;
+    int nv = min(GN, a.n_tok - tok0);
+    const uint8_t *slabs = a.slabs;
+    const int32_t *gslot = nullptr;  // grouped: the tile's slots
     pdl_wait();
+    if (a.grp_off) {
+        if ((int)blockIdx.y >= a.grp_off[a.n_expert + 1]) return;  // past the work list: leaves before any barrier
+        const int item = a.grp_tiles[blockIdx.y], e = item >> 16;
+        tok0 = (item & 0xFFFF) * GN;
+        const int g0 = a.grp_off[e];
+        nv = min(GN, a.grp_off[e + 1] - g0 - tok0);
+        gslot = a.grp_slot + g0 + tok0;
+        slabs += (size_t)e * a.gpe * a.nb * slab_bytes(TYPE);
+    }
+    // activation row and output row of the tile's token t
+    auto xrow = [&](int t) -> int64_t { return gslot ? gslot[t] / a.xdiv : tok0 + t; };
+    auto orow_of = [&](int t) -> int64_t { return gslot ? gslot[t] : tok0 + t; };
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
@@ -236,12 +259,12 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
         // B tile: chunk c of token t at c * GN * 16 + t * 16 (the XQ span keeps 16-byte alignment)
         for (int i = tid; i < nv * 16; i += G_THREADS) {
             const int t = i >> 4, c = i & 15;
-            const uint4 v = __ldg((const uint4 *)(a.xqs + (size_t)(tok0 + t) * a.qrow + b * XQ_SPAN + c * 16));
+            const uint4 v = __ldg((const uint4 *)(a.xqs + (size_t)xrow(t) * a.qrow + b * XQ_SPAN + c * 16));
             *(uint4 *)(sb + c * (GN * 16) + t * 16) = v;
         }
-        for (int t = tid; t < GN; t += G_THREADS) yd[t] = t < nv ? a.xd[(size_t)(tok0 + t) * a.nbx + b] : 0.0f;
+        for (int t = tid; t < GN; t += G_THREADS) yd[t] = t < nv ? a.xd[(size_t)xrow(t) * a.nbx + b] : 0.0f;
         if (row_ok) {
-            const uint8_t *slab = a.slabs + ((size_t)(grow / GROUP_ROWS) * a.nb + b) * SB;
+            const uint8_t *slab = slabs + ((size_t)(grow / GROUP_ROWS) * a.nb + b) * SB;
             expand_half<TYPE>(slab, (int)(grow % GROUP_ROWS), row, part, sa, dr, dmr);
         } else {
             for (int k = 128 * part; k < 128 * part + 128; k += 16)
@@ -306,7 +329,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
         for (int i = 0; i < 64; i++) {
             const int t = ehalf * 64 + i;
             if (t < nv) {
-                const size_t o = (size_t)(tok0 + t) * a.ldo + (orow - a.out_row0);
+                const size_t o = (size_t)orow_of(t) * a.ldo + (orow - a.out_row0);
                 a.out[o] = a.residual ? __fadd_rn(a.residual[o], acc[i]) : acc[i];
             }
         }
@@ -349,6 +372,58 @@ void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, i
     const int64_t tiles_m = (a.g_end - a.g_begin + GM / GROUP_ROWS - 1) / (GM / GROUP_ROWS);
     const dim3 grid((unsigned)tiles_m, (unsigned)((xq.n_tok + GN - 1) / GN));
     if (w.type == T_Q4_K) {
+        static bool configured = false;
+        const int smem = g_smem_bytes(3);
+        if (!configured) {
+            SDY_CUDA(cudaFuncSetAttribute(qgemm_kernel<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            configured = true;
+        }
+        launch(qgemm_kernel<T_Q4_K>, grid, G_THREADS, smem, s, a);
+    } else {
+        static bool configured = false;
+        const int smem = g_smem_bytes(2);
+        if (!configured) {
+            SDY_CUDA(cudaFuncSetAttribute(qgemm_kernel<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            configured = true;
+        }
+        launch(qgemm_kernel<T_Q6_K>, grid, G_THREADS, smem, s, a);
+    }
+    SDY_LAUNCHED();
+}
+
+void qgemm_grouped(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq, int xdiv, const int32_t *grp_off,
+                   const int32_t *grp_slot, const int32_t *grp_tiles, int max_slots, int64_t rows_per_expert,
+                   float *out, int64_t ldo_slot, cudaStream_t s) {
+    if (max_slots <= 0 || n_expert <= 0) return;
+    if (!qgemm_supported(experts.type, experts.n_in) || xq.vtype != T_Q8_K || xq.n_in != experts.n_in) {
+        set_error("qgemm_grouped: unsupported weight type %d / activation layout", experts.type);
+        return;
+    }
+    GemmArgs a{};
+    a.slabs = experts.slabs;
+    a.nb = experts.nb;
+    a.g_begin = 0;
+    a.g_end = (rows_per_expert + GROUP_ROWS - 1) / GROUP_ROWS;
+    a.xqs = xq.qs;
+    a.xd = xq.d;
+    a.qrow = xq.qrow;
+    a.nbx = xq.nbx;
+    a.n_tok = max_slots;
+    a.out = out;
+    a.ldo = ldo_slot;
+    a.row0 = 0;
+    a.row1 = rows_per_expert;
+    a.out_row0 = 0;
+    a.grp_off = grp_off;
+    a.grp_slot = grp_slot;
+    a.grp_tiles = grp_tiles;
+    a.n_expert = n_expert;
+    a.xdiv = xdiv;
+    a.gpe = gpe;
+    const int64_t tiles_m = (a.g_end + GM / GROUP_ROWS - 1) / (GM / GROUP_ROWS);
+    // at most ceil(count_e / GN) tiles per expert: sum <= max_slots / GN + n_expert
+    const dim3 grid((unsigned)tiles_m, (unsigned)(max_slots / GN + n_expert));
+    if (experts.type == T_Q4_K) {
         static bool configured = false;
         const int smem = g_smem_bytes(3);
         if (!configured) {
