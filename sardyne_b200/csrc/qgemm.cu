@@ -17,8 +17,10 @@
 // Tile: 128 weight rows (MMA M) x 128 tokens (MMA N), 256 threads. Operands sit in shared memory
 // in the no-swizzle K-major core-matrix layout: byte (row, k) of a plane at
 // (k / 16) * (rows * 16) + row * 16 + k % 16, i.e. 8-row x 16-byte core matrices, 128 B apart
-// along M and rows*16 B apart along K. This first version runs the stages of a superblock one
-// after another (expand A and load B, MMA, epilogue).
+// along M and rows*16 B apart along K. The next superblock's raw slabs, B tile and token scales
+// are requested with cp.async before the current superblock's MMAs are issued, so their latency
+// overlaps the MMAs and the epilogue; expansion, MMA and epilogue of one superblock still follow
+// each other.
 #include "common.cuh"
 
 namespace sdy {
@@ -36,9 +38,23 @@ __device__ unsigned int g_qgemm_status;  // nonzero: an MMA completion wait time
 
 template <int TYPE> struct GemmPlanes { static constexpr int n = TYPE == T_Q4_K ? 3 : 2; };
 
-__host__ __device__ constexpr int g_smem_bytes(int planes) {
-    return planes * PLANE + BTILE + GN * 4 /* yd */ + 2 * GM * 4 /* d, dmin */ + 16 /* mbarrier, tmem */;
+// Shared memory: the expanded A planes, two B tiles and two yd rows (superblock b+1 arrives by
+// cp.async while b is multiplied), d/dmin per row, the raw slabs of the next superblock, mbarrier.
+__host__ __device__ constexpr int g_raw_bytes(int type) { return (GM / GROUP_ROWS) * slab_bytes(type); }
+__host__ __device__ constexpr int g_smem_bytes(int planes, int type) {
+    return planes * PLANE + 2 * BTILE + 2 * GN * 4 + 2 * GM * 4 + g_raw_bytes(type) + 16;
 }
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -107,7 +123,7 @@ template <int TYPE>
 __device__ __forceinline__ void expand_half(const uint8_t *slab, int r8, int row, int part, uint8_t *sa, float *dr,
                                             float *dmr) {
     if constexpr (TYPE == T_Q4_K) {
-        const uint4 hdr = __ldg((const uint4 *)(slab + r8 * 16));
+        const uint4 hdr = *(const uint4 *)(slab + r8 * 16);
         const uint32_t sc0 = hdr.y & 0x3F3F3F3F, m0 = hdr.z & 0x3F3F3F3F;
         const uint32_t sc1 = (hdr.w & 0x0F0F0F0F) | ((hdr.y >> 2) & 0x30303030);
         const uint32_t m1 = ((hdr.w >> 4) & 0x0F0F0F0F) | ((hdr.z >> 2) & 0x30303030);
@@ -117,7 +133,7 @@ __device__ __forceinline__ void expand_half(const uint8_t *slab, int r8, int row
         }
         uint4 q[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) q[i] = __ldg((const uint4 *)(slab + 128 + (4 * part + i) * 128 + r8 * 16));
+        for (int i = 0; i < 4; i++) q[i] = *(const uint4 *)(slab + 128 + (4 * part + i) * 128 + r8 * 16);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int c = 4 * part + i, j = c >> 1, h = c & 1;  // chunk c: bytes 16h.. of 64-element chunk j
@@ -143,13 +159,13 @@ __device__ __forceinline__ void expand_half(const uint8_t *slab, int r8, int row
             *(uint4 *)(sa + 2 * PLANE + off_h) = make_uint4(mh, mh, mh, mh);
         }
     } else {  // Q6_K half `part`: elements 128p .. 128p+127
-        const uint4 scv = __ldg((const uint4 *)(slab + 1536 + r8 * 16));
-        if (part == 0) dr[row] = __half2float(__ushort_as_half(__ldg((const unsigned short *)(slab + 1664 + r8 * 2))));
+        const uint4 scv = *(const uint4 *)(slab + 1536 + r8 * 16);
+        if (part == 0) dr[row] = __half2float(__ushort_as_half(*(const unsigned short *)(slab + 1664 + r8 * 2)));
         uint4 ql[4], qh[2];
 #pragma unroll
-        for (int c = 0; c < 4; c++) ql[c] = __ldg((const uint4 *)(slab + (4 * part + c) * 128 + r8 * 16));
+        for (int c = 0; c < 4; c++) ql[c] = *(const uint4 *)(slab + (4 * part + c) * 128 + r8 * 16);
 #pragma unroll
-        for (int c = 0; c < 2; c++) qh[c] = __ldg((const uint4 *)(slab + 1024 + (2 * part + c) * 128 + r8 * 16));
+        for (int c = 0; c < 2; c++) qh[c] = *(const uint4 *)(slab + 1024 + (2 * part + c) * 128 + r8 * 16);
         const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
 #pragma unroll
         for (int k = 0; k < 8; k++) {  // the reference's 4-element groups (quant.c:62-74)
@@ -205,9 +221,10 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
     constexpr int NP = GemmPlanes<TYPE>::n;
     constexpr int SB = slab_bytes(TYPE);
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t *sa = smem, *sb = smem + NP * PLANE;
-    float *yd = (float *)(sb + BTILE), *dr = yd + GN, *dmr = dr + GM;
-    uint64_t *mbar = (uint64_t *)(dmr + GM);
+    uint8_t *sa = smem, *sb = smem + NP * PLANE;  // sb: two B tiles
+    float *yd = (float *)(sb + 2 * BTILE), *dr = yd + 2 * GN, *dmr = dr + GM;
+    uint8_t *raw = (uint8_t *)(dmr + GM);
+    uint64_t *mbar = (uint64_t *)(raw + g_raw_bytes(TYPE));
     uint32_t *tmem_slot = (uint32_t *)(mbar + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t gt0 = a.g_begin + (int64_t)blockIdx.x * (GM / GROUP_ROWS);  // first group of the tile
@@ -239,8 +256,10 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     // Padded tokens keep zero activations for the whole kernel.
-    for (int i = tid; i < BTILE / 16; i += G_THREADS)  // chunk-plane layout: i = plane * GN + t
+    for (int i = tid; i < 2 * BTILE / 16; i += G_THREADS)  // chunk-plane layout: i = buffer/plane * GN + t
         if (i % GN >= nv) ((uint4 *)sb)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < 2 * GN; i += G_THREADS)
+        if (i % GN >= nv) yd[i] = 0.0f;
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
@@ -255,29 +274,45 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
     for (int i = 0; i < 64; i++) acc[i] = 0.0f;
     bool ok = true;
 
-    for (int b = 0; b < a.nb && ok; b++) {
-        // B tile: chunk c of token t at c * GN * 16 + t * 16 (the XQ span keeps 16-byte alignment)
+    // Superblock b's raw slabs, B tile and token scales, requested with cp.async (B and yd into
+    // buffer b & 1) so that they travel while the previous superblock is multiplied.
+    const int ng_tile = (int)(a.g_end - gt0 < GM / GROUP_ROWS ? a.g_end - gt0 : GM / GROUP_ROWS);
+    auto issue = [&](int b) {
+        uint8_t *sbb = sb + (b & 1) * BTILE;
+        float *ydb = yd + (b & 1) * GN;
         for (int i = tid; i < nv * 16; i += G_THREADS) {
             const int t = i >> 4, c = i & 15;
-            const uint4 v = __ldg((const uint4 *)(a.xqs + (size_t)xrow(t) * a.qrow + b * XQ_SPAN + c * 16));
-            *(uint4 *)(sb + c * (GN * 16) + t * 16) = v;
+            cp_async16(sbb + c * (GN * 16) + t * 16, a.xqs + (size_t)xrow(t) * a.qrow + b * XQ_SPAN + c * 16);
         }
-        for (int t = tid; t < GN; t += G_THREADS) yd[t] = t < nv ? a.xd[(size_t)xrow(t) * a.nbx + b] : 0.0f;
+        for (int t = tid; t < nv; t += G_THREADS) cp_async4(ydb + t, a.xd + (size_t)xrow(t) * a.nbx + b);
+        constexpr int C16 = SB / 16;
+        for (int i = tid; i < ng_tile * C16; i += G_THREADS) {
+            const int g = i / C16, c = i - g * C16;
+            cp_async16(raw + g * SB + c * 16, slabs + ((size_t)(gt0 + g) * a.nb + b) * SB + c * 16);
+        }
+        cp_async_commit();
+    };
+    issue(0);
+    for (int b = 0; b < a.nb && ok; b++) {
+        cp_async_wait_all();
+        __syncthreads();
         if (row_ok) {
-            const uint8_t *slab = slabs + ((size_t)(grow / GROUP_ROWS) * a.nb + b) * SB;
-            expand_half<TYPE>(slab, (int)(grow % GROUP_ROWS), row, part, sa, dr, dmr);
+            expand_half<TYPE>(raw + (grow / GROUP_ROWS - gt0) * SB, (int)(grow % GROUP_ROWS), row, part, sa, dr, dmr);
         } else {
             for (int k = 128 * part; k < 128 * part + 128; k += 16)
                 for (int p = 0; p < NP; p++) *(uint4 *)(sa + p * PLANE + plane_off(GM, row, k)) = make_uint4(0, 0, 0, 0);
             if (part == 0) dr[row] = dmr[row] = 0.0f;
         }
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // B (cp.async) and A for the MMA
         __syncthreads();
+        if (b + 1 < a.nb) issue(b + 1);  // the raw buffer is free, B buffer (b+1)&1 was read by MMA b-1
+        const uint8_t *sbb = sb + (b & 1) * BTILE;
+        const float *ydb = yd + (b & 1) * GN;
         if (tid == 0) {
             fence_after_sync();
 #pragma unroll
             for (int s = 0; s < 8; s++) {  // K step s: bytes 32s..32s+31 = chunk planes 2s, 2s+1
-                const uint64_t bd = kmajor_desc(smem_u32(sb + 2 * s * GN * 16), GN * 16, 128);
+                const uint64_t bd = kmajor_desc(smem_u32(sbb + 2 * s * GN * 16), GN * 16, 128);
 #pragma unroll
                 for (int p = 0; p < NP; p++)
                     mma_i8(tmem + p * GN, kmajor_desc(smem_u32(sa + p * PLANE + 2 * s * GM * 16), GM * 16, 128), bd,
@@ -304,7 +339,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
                 asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 #pragma unroll
                 for (int i = 0; i < 32; i++) {
-                    const float y = yd[col + i];
+                    const float y = ydb[col + i];
                     float term;
                     if constexpr (TYPE == T_Q4_K) {
                         const int isum = 32 * h[i] + l[i];
@@ -322,6 +357,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
         __syncthreads();
     }
 
+    cp_async_wait_all();  // nothing in flight when the CTA leaves (only after a timed-out wait)
     // outputs (rows of this tile within [row0, row1), valid tokens)
     const int64_t orow = gt0 * GROUP_ROWS + erow;
     if (ok && orow >= a.row0 && orow < a.row1) {
@@ -373,7 +409,7 @@ void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, i
     const dim3 grid((unsigned)tiles_m, (unsigned)((xq.n_tok + GN - 1) / GN));
     if (w.type == T_Q4_K) {
         static bool configured = false;
-        const int smem = g_smem_bytes(3);
+        const int smem = g_smem_bytes(3, T_Q4_K);
         if (!configured) {
             SDY_CUDA(cudaFuncSetAttribute(qgemm_kernel<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
             configured = true;
@@ -381,7 +417,7 @@ void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, i
         launch(qgemm_kernel<T_Q4_K>, grid, G_THREADS, smem, s, a);
     } else {
         static bool configured = false;
-        const int smem = g_smem_bytes(2);
+        const int smem = g_smem_bytes(2, T_Q6_K);
         if (!configured) {
             SDY_CUDA(cudaFuncSetAttribute(qgemm_kernel<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
             configured = true;
@@ -425,7 +461,7 @@ void qgemm_grouped(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq,
     const dim3 grid((unsigned)tiles_m, (unsigned)(max_slots / GN + n_expert));
     if (experts.type == T_Q4_K) {
         static bool configured = false;
-        const int smem = g_smem_bytes(3);
+        const int smem = g_smem_bytes(3, T_Q4_K);
         if (!configured) {
             SDY_CUDA(cudaFuncSetAttribute(qgemm_kernel<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
             configured = true;
@@ -433,7 +469,7 @@ void qgemm_grouped(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq,
         launch(qgemm_kernel<T_Q4_K>, grid, G_THREADS, smem, s, a);
     } else {
         static bool configured = false;
-        const int smem = g_smem_bytes(2);
+        const int smem = g_smem_bytes(2, T_Q6_K);
         if (!configured) {
             SDY_CUDA(cudaFuncSetAttribute(qgemm_kernel<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
             configured = true;
