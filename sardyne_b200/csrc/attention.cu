@@ -24,6 +24,7 @@
 // context too long for the scores to stay in shared memory).
 #include "fp_device.cuh"
 #include "fp_ops.cuh"
+#include "fused.cuh"
 
 #include <cooperative_groups.h>
 
@@ -56,7 +57,7 @@ constexpr int AC_SMEM_LIMIT = 200 * 1024;
 // Scores row length per head: this CTA's share of the keys, at most ceil(stride / AC).
 __host__ __device__ inline int ac_lmax(int stride) { return ((stride + AC - 1) / AC + 3) & ~3; }
 struct AcSmem {
-    int qs, scl, vb, work, total;  // float offsets
+    int qs, kv, scl, vb, work, total;  // float offsets
 };
 // Probability row stride when every CTA holds all keys' exponentials (push mode).
 __host__ __device__ inline int ac_ldp(int stride) { return ((stride + 3) & ~3) + 4; }
@@ -65,12 +66,67 @@ __host__ __device__ inline AcSmem ac_smem(int n_rep, int hd, int stride, bool pu
     AcSmem m;
     const int S = hd / AC;
     m.qs = 0;
-    m.scl = n_rep * hd;
+    m.kv = n_rep * hd;            // the new token's K and V rows (fused post-QKV)
+    m.scl = m.kv + 2 * hd;
     m.vb = m.scl + n_rep * ac_lmax(stride);
     m.work = m.vb + 2 * AC_KC * S;
     const int a = 2 * AC_KT * (hd + 4), c = push ? n_rep * ac_ldp(stride) : 2 * n_rep * AC_PLD;
     m.total = m.work + (a > c ? a : c);
     return m;
+}
+
+// One head of the reference's post-projection steps (model_llama.c:781-800) by one warp: bias,
+// per-head RMSNorm (qk-norm: double sum of squares, lane-strided then a shuffle tree), RoPE
+// (ops.c:388-403) at table row `pos`; result in dst (shared, hd floats; hd % 32 == 0).
+__device__ void head_post(const float *src, const float *bias, const float *norm, float eps, const float *cs,
+                          const float *sn, int interleaved, int hd, float *dst) {
+    const int lane = threadIdx.x & 31, nu = hd / 32, half = hd / 2;
+    // every global operand requested first (one round of load latency)
+    float v[8], bv[8], nv[8], c[4], sv[4];
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+        if (u < nu) {
+            const int i = lane + 32 * u;
+            v[u] = src[i];
+            bv[u] = bias ? bias[i] : 0.0f;
+            nv[u] = norm ? norm[i] : 0.0f;
+        }
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+        if (cs && lane + 32 * u < half) {
+            c[u] = cs[lane + 32 * u];
+            sv[u] = sn[lane + 32 * u];
+        }
+    double ss = 0.0;
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+        if (u < nu) {
+            if (bias) v[u] = __fadd_rn(v[u], bv[u]);
+            ss += (double)v[u] * v[u];
+        }
+    if (norm) {
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float scale = (float)(1.0 / sqrt(ss / hd + (double)eps));
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+            if (u < nu) v[u] = __fmul_rn(__fmul_rn(v[u], scale), nv[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+        if (u < nu) dst[lane + 32 * u] = v[u];
+    __syncwarp();
+    if (cs)
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int i = lane + 32 * u;
+            if (i < half) {
+                const int ia = interleaved ? 2 * i : i, ib = interleaved ? 2 * i + 1 : i + half;
+                const float a = dst[ia], b = dst[ib];
+                dst[ia] = __fsub_rn(__fmul_rn(a, c[u]), __fmul_rn(b, sv[u]));
+                dst[ib] = __fadd_rn(__fmul_rn(a, sv[u]), __fmul_rn(b, c[u]));
+            }
+        }
+    __syncwarp();
 }
 
 // q: token t at q + t*ldq, heads of hd; k/v cache [n_kv_head][stride][hd]; the first token's
@@ -84,7 +140,8 @@ __host__ __device__ inline AcSmem ac_smem(int n_rep, int hd, int stride, bool pu
 __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
     attention_cluster_kernel(float *__restrict__ out, const float *__restrict__ q, int64_t ldq,
                              const float *__restrict__ kc, const float *__restrict__ vc, int n_head, int n_kv_head,
-                             int hd, int pos0, const int32_t *pos_dev, int stride, int fixed_nkv, int push) {
+                             int hd, int pos0, const int32_t *pos_dev, int stride, int fixed_nkv, int push,
+                             PostQKV pp) {
     extern __shared__ __align__(16) float sm[];
     __shared__ float cmax[AC_MAX_REP], gmax[AC_MAX_REP], ginv[AC_MAX_REP];
     __shared__ double csum[AC_MAX_REP];
@@ -98,6 +155,8 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
     const int ldp = ac_ldp(stride);
     const int lmax = ac_lmax(stride);
     float *qs = sm + lay.qs, *scl = sm + lay.scl, *vb = sm + lay.vb, *work = sm + lay.work;
+    float *knew = sm + lay.kv, *vnew = knew + hd;
+    const bool post = pp.kc != nullptr;  // fused post-QKV (single token): the new row is key n_kv - 1
     const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
     const int L = (n_kv + AC - 1) / AC;
     const int jb = min(n_kv, c * L), je = min(n_kv, jb + L);
@@ -135,7 +194,32 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
     if (ntile > 0) load_k(0);
     load_v(0);  // phase C's first chunk travels with the first K tile
     cp_async_commit();
-    {  // the n_rep query heads: n_rep*hd/4 16-byte loads, all issued before any store
+    if (post) {
+        // Each CTA transforms its query heads and the new K and V rows itself; rank 0 stores the
+        // rows in the cache for later steps, and every CTA patches them into its staged tiles
+        // below (its own copies of the cache rows may predate rank 0's store).
+        const int pos = n_kv - 1, half = hd / 2;
+        const float *cs = pp.cos + (size_t)pos * half, *sn = pp.sin + (size_t)pos * half;
+        for (int r = warp; r < n_rep + 2; r += AC_THREADS / 32) {
+            if (r < n_rep) {
+                const int h = h0 + r;
+                head_post(pp.q + (size_t)t * pp.ldq + (size_t)h * hd, pp.bq ? pp.bq + (size_t)h * hd : nullptr,
+                          pp.q_norm, pp.eps, cs, sn, pp.interleaved, hd, qs + r * hd);
+            } else if (r == n_rep) {
+                head_post(pp.k + (size_t)t * pp.ldk + (size_t)g * hd, pp.bk ? pp.bk + (size_t)g * hd : nullptr,
+                          pp.k_norm, pp.eps, cs, sn, pp.interleaved, hd, knew);
+            } else {
+                head_post(pp.v + (size_t)t * pp.ldv + (size_t)g * hd, pp.bv ? pp.bv + (size_t)g * hd : nullptr,
+                          nullptr, 0.0f, nullptr, nullptr, 0, hd, vnew);
+            }
+        }
+        __syncthreads();
+        if (c == 0)
+            for (int i = tid; i < hd; i += AC_THREADS) {
+                pp.kc[((size_t)g * pp.max_seq + pos) * hd + i] = knew[i];
+                pp.vc[((size_t)g * pp.max_seq + pos) * hd + i] = vnew[i];
+            }
+    } else {  // the n_rep query heads: n_rep*hd/4 16-byte loads, all issued before any store
         const float4 *q4 = (const float4 *)(q + (size_t)t * ldq + (size_t)h0 * hd);
         const int n4 = n_rep * hd / 4;
         for (int i0 = 0; i0 < n4; i0 += 4 * AC_THREADS) {
@@ -161,6 +245,13 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
             cp_async_wait<0>();
         }
         __syncthreads();
+        if (post) {  // the tile holding the new key: its row from knew
+            const int j0 = jb + it * AC_KT, jn = n_kv - 1 - j0;
+            if (jn >= 0 && jn < AC_KT && j0 + jn < je) {
+                for (int i = tid; i < hd; i += AC_THREADS) work[(it & 1) * AC_KT * ldk + jn * ldk + i] = knew[i];
+                __syncthreads();
+            }
+        }
         const int jl = it * AC_KT + kk;  // index within this CTA's keys
         if (jb + jl < je) {
             const float *row = work + (it & 1) * AC_KT * ldk + kk * ldk;
@@ -284,6 +375,11 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
             cp_async_commit();
         }
         __syncthreads();
+        if (post && ic == nchunk - 1) {  // the chunk holding the new key: its V columns from vnew
+            const int jn = n_kv - 1 - ic * AC_KC;
+            for (int i = tid; i < S; i += AC_THREADS) vb[(ic & 1) * AC_KC * S + jn * S + i] = vnew[e0 + i];
+            __syncthreads();
+        }
         if (chain) {
             const float *pr = push ? work + ch_r * ldp + ic * AC_KC
                                    : work + (ic & 1) * n_rep * AC_PLD + ch_r * AC_PLD;
@@ -500,11 +596,17 @@ bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
 void attention(float *out, const float *q, int64_t ldq, const float *kc, const float *vc, int n_tok, int n_head,
                int n_kv_head, int hd, int pos0, const int32_t *pos_dev, int stride, float *scratch, int fixed_nkv,
-               cudaStream_t s) {
+               cudaStream_t s, const PostQKV *post) {
     if (n_tok <= 0) return;
     if (hd % 4 || n_kv_head <= 0 || n_head % n_kv_head) {
         set_error("attention: head_dim %d / heads %d/%d not supported", hd, n_head, n_kv_head);
         return;
+    }
+    // The post-projection steps are fused into the single-token cluster kernel; otherwise they run first.
+    PostQKV pp{};
+    if (post && n_tok != 1) {
+        post_qkv(*post, n_tok, s);
+        post = nullptr;
     }
     // Many queries (prefill): the query-tile kernel (causal counts only; fixed_nkv is op_attention's
     // single query).
@@ -529,6 +631,11 @@ void attention(float *out, const float *q, int64_t ldq, const float *kc, const f
                          ldq % 4 == 0 &&
                          (size_t)ac_smem(n_rep, hd, stride, push).total * 4 <= AC_SMEM_LIMIT && n_kv_head <= 65535 &&
                          n_tok <= 65535;
+    if (post && !(cluster && hd <= 256 && fixed_nkv <= 0)) {
+        post_qkv(*post, n_tok, s);
+        post = nullptr;
+    }
+    if (post) pp = *post;
     if (cluster) {
         const size_t smem = (size_t)ac_smem(n_rep, hd, stride, push).total * 4;
         static bool configured = false;
@@ -538,7 +645,7 @@ void attention(float *out, const float *q, int64_t ldq, const float *kc, const f
             configured = true;
         }
         launch(attention_cluster_kernel, dim3(AC, n_kv_head, n_tok), AC_THREADS, smem, s, out, q, ldq, kc, vc, n_head,
-               n_kv_head, hd, pos0, pos_dev, stride, fixed_nkv, push);
+               n_kv_head, hd, pos0, pos_dev, stride, fixed_nkv, push, pp);
         SDY_LAUNCHED();
         return;
     }

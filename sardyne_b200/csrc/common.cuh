@@ -188,14 +188,18 @@ void xq_import(int vtype, const uint8_t *raw, int n_tok, int n_in, const XQ &xq,
 void xq_export(const XQ &xq, uint8_t *raw, cudaStream_t s);
 // out[t*ldo + (r - out_row0)] = W[r] . x[t] for rows r in [row0, row1) and tokens t < xq.n_tok.
 // With `residual`, out = residual + product (same indexing; residual may alias out).
-// A row-wise RMSNorm (ops.c:346-351) that a product kernel applies to its own input rows x[t]
-// (weight w, epsilon eps) instead of reading quantized activations: the decode step's norms are
-// fused into the kernels that consume them.
-struct NormIn {
+// The input rows a product kernel prepares and quantizes itself, instead of reading quantized
+// activations, so that the decode step's elementwise producers fuse into their consumers:
+//   w set:  RMSNorm(x[t]) * w, epsilon eps (ops.c:346-351);
+//   u set:  silu(x[t]) * u[t], the SwiGLU gate (ops.c:366-371);
+//   else:   x[t] as is.
+struct ActIn {
     const float *x = nullptr;
     int64_t ldx = 0;
     const float *w = nullptr;
     float eps = 0.0f;
+    const float *u = nullptr;
+    int64_t ldu = 0;
 };
 
 // Token count from which products go to the tensor-core GEMM (0 = never).
@@ -213,15 +217,21 @@ constexpr int GEMM_TILE_TOKENS = 128;
 void qgemm_grouped(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq, int xdiv, const int32_t *grp_off,
                    const int32_t *grp_slot, const int32_t *grp_tiles, int max_slots, int64_t rows_per_expert,
                    float *out, int64_t ldo_slot, cudaStream_t s);
-// norm: x -> RMSNorm -> quantize inside the kernel (xq then only gives the activation geometry).
+// act: the input rows are prepared and quantized inside the kernel (xq then only gives the
+// activation geometry).
 void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
-             cudaStream_t s, const float *residual = nullptr, const NormIn *norm = nullptr);
+             cudaStream_t s, const float *residual = nullptr, const ActIn *act = nullptr);
+// Two matrices with one single-token input in one launch: outa[r] = A[r] . x, outb[r] = B[r] . x
+// over all rows (the parts of a projection whose weight types differ).
+bool qmatvec2_supported(int ta, int tb);
+void qmatvec2(const QMat &wa, float *outa, const QMat &wb, float *outb, const XQ &xq, cudaStream_t s,
+              const ActIn *act = nullptr);
 // MoE: for each slot s < n_slots, out[s*ldo_slot + r] = E[slot_expert[s]][r] . x[s / tok_div] for
 // r < rows_per_expert. `experts` holds n_expert matrices (global experts expert0 .. expert0 +
 // n_expert - 1), each padded to gpe groups; slots naming other experts are left untouched. The
 // expert ids are read on the device, so no host round trip sits between the router and the experts.
 void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq, int tok_div, const int32_t *slot_expert,
                     int n_slots, int64_t rows_per_expert, float *out, int64_t ldo_slot, cudaStream_t s,
-                    int expert0 = 0, const NormIn *norm = nullptr);
+                    int expert0 = 0, const ActIn *act = nullptr);
 
 }  // namespace sdy

@@ -175,6 +175,11 @@ struct engine_ctx {
     int max_seq = 0, n_batch = 0, logits_all = 0, n_past = 0, n_logits = 0, n_threads = 0;
     int qkv_ld = 0, gu_ld = 0;
     cudaStream_t st = nullptr;
+    // Side branch of a single-token step: the next layer's weights are pulled into L2 there while
+    // this layer's kernels run on st (forked and joined with the two events).
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    bool forked = false;
     void *arena = nullptr;
     float *k_cache = nullptr, *v_cache = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
     float *x = nullptr, *xb = nullptr, *qkv = nullptr, *att = nullptr, *hgu = nullptr, *tmp = nullptr,
@@ -641,32 +646,45 @@ void project(engine_ctx *c, const Proj &p, float *out, int64_t ldo, const float 
     for (const Part &part : p.parts) matmul(c, out + part.col, ldo, x, ldx, part.m, n);
 }
 
-// Decode-step norm fusion: a single-token step whose norm feeds only quantized matrices (and the
-// float router) lets each consuming kernel normalise and quantize x itself (NormIn) instead of a
-// separate norm kernel writing xb and the quantized activations (SARDYNE_NO_FUSED_NORM: off).
-// Fused only where one kernel consumes the norm: each consumer pays the norm in its prologue
-// (about as long as the separate kernel on the critical path), so two consumers (q|k and v in
-// different formats, or the MoE router and its experts) are slower fused than not.
-bool fused_norm_ok(int n, const std::vector<const DMat *> &mats) {
+// Decode-step fusion of elementwise producers into their consumers: a single-token step whose
+// norm (or SwiGLU gate, or plain activation) feeds quantized matrices lets the consuming kernel
+// prepare and quantize its input itself (ActIn) instead of a separate kernel writing the
+// quantized activations (SARDYNE_NO_FUSED_NORM: off). Used where ONE kernel consumes the input:
+// each consumer pays the preparation in its prologue (about as long as the separate kernel on
+// the critical path), so the parts of a projection go in one launch (qmatvec2) when their types
+// differ.
+bool fusion_enabled() {
     static const bool off = getenv("SARDYNE_NO_FUSED_NORM") != nullptr;
-    if (off || n != 1 || mats.size() != 1) return false;
-    return mats[0]->quant();
+    return !off;
+}
+bool fused_norm_ok(int n, const std::vector<const DMat *> &mats) {
+    if (!fusion_enabled() || n != 1) return false;
+    if (mats.size() == 1) return mats[0]->quant();
+    return mats.size() == 2 && mats[0]->quant() && mats[1]->quant() && mats[0]->n_in == mats[1]->n_in &&
+           qmatvec2_supported(mats[0]->type, mats[1]->type);
 }
 
-// out = W . RMSNorm(x) for quantized W, the norm applied inside the matvec.
-void matmul_norm(engine_ctx *c, float *out, int64_t ldo, const DMat &w, const NormIn &nin, int n) {
+// out = W . act for quantized W, the input prepared inside the matvec (+ residual).
+void matmul_act(engine_ctx *c, float *out, int64_t ldo, const DMat &w, const ActIn &act, int n,
+                const float *residual = nullptr) {
     const XQ geo = xq_carve(nullptr, vec_dot_type(w.type), w.n_in, n);  // geometry only
-    qmatvec(w.q, geo, out, ldo, 0, w.n_out, 0, c->st, nullptr, &nin);
+    qmatvec(w.q, geo, out, ldo, 0, w.n_out, 0, c->st, residual, &act);
 }
 
-void project_norm(engine_ctx *c, const Proj &p, float *out, int64_t ldo, const NormIn &nin, int n) {
+void project_act(engine_ctx *c, const Proj &p, float *out, int64_t ldo, const ActIn &act, int n) {
     forget_activations(c);
-    for (const Part &part : p.parts) matmul_norm(c, out + part.col, ldo, part.m, nin, n);
+    if (p.parts.size() == 2) {
+        const DMat &a = p.parts[0].m, &b = p.parts[1].m;
+        const XQ geo = xq_carve(nullptr, vec_dot_type(a.type), a.n_in, n);
+        qmatvec2(a.q, out + p.parts[0].col, b.q, out + p.parts[1].col, geo, c->st, &act);
+        return;
+    }
+    for (const Part &part : p.parts) matmul_act(c, out + part.col, ldo, part.m, act, n);
 }
 
 // Experts: out[s*ldo + part.col + r] = E[top[s]][r] . x[s / tok_div] for every part.
 void project_experts(engine_ctx *c, const Proj &p, float *out, int64_t ldo, const float *x, int64_t ldx, int n_x,
-                     int n_slots, int tok_div, const NormIn *nin = nullptr) {
+                     int n_slots, int tok_div, const ActIn *act = nullptr) {
     for (const Part &part : p.parts) {
         const DMat &w = part.m;
         if (!w.quant()) {
@@ -676,10 +694,10 @@ void project_experts(engine_ctx *c, const Proj &p, float *out, int64_t ldo, cons
             SDY_LAUNCHED();
             continue;
         }
-        if (nin) {
+        if (act) {
             const XQ geo = xq_carve(nullptr, vec_dot_type(w.type), w.n_in, n_x);  // geometry only
             qmatvec_gather(w.q, w.gpe, w.n_expert, geo, tok_div, c->moe_top, n_slots, w.n_out, out + part.col, ldo,
-                           c->st, (int)c->m->e0, nin);
+                           c->st, (int)c->m->e0, act);
             continue;
         }
         const XQ &xq = activations(c, x, ldx, n_x, w.n_in, w.type);
@@ -695,8 +713,64 @@ void all_reduce(engine_ctx *c, const float *send, float *recv, size_t count) {
     if (r != ncclSuccess) set_error("ncclAllReduce: %s", nccl()->error_string(r));
 }
 
+// L2 prefetch in single-token steps (SARDYNE_L2_PREFETCH = off | layer | experts | all): the next
+// layer's matrices, and the chosen experts' down matrices. Default: experts. Measured: the down
+// prefetch gains ~1% on the Qwen3-30B-A3B shape; the next layer's matrices cost 5% on the
+// Qwen2.5-3B shape (their reads compete with the current layer's) and gain 1% on the MoE one.
+enum { PF_LAYER = 1, PF_EXPERTS = 2 };
+int prefetch_mode() {
+    static const int mode = [] {
+        const char *v = getenv("SARDYNE_L2_PREFETCH");
+        if (!v) return (int)PF_EXPERTS;
+        return !strcmp(v, "off") ? 0 : !strcmp(v, "layer") ? PF_LAYER : !strcmp(v, "experts") ? PF_EXPERTS
+                                                                                  : PF_LAYER | PF_EXPERTS;
+    }();
+    return mode;
+}
+
+// The side stream continues from the work queued on st so far; the layer loop joins it back.
+void fork_side(engine_ctx *c) {
+    SDY_CUDA(cudaEventRecord(c->ev_fork, c->st));
+    SDY_CUDA(cudaStreamWaitEvent(c->side, c->ev_fork, 0));
+    c->forked = true;
+}
+
+// Fork: layer L's weights (all but the experts, which the router prefetches once chosen) into L2
+// on the side stream; the branch is joined at the end of the current layer.
+void prefetch_layer(engine_ctx *c, const DLayer &L) {
+    L2Ranges r;
+    auto add = [&](const DMat &w) {
+        if (w.n_expert) return;
+        if (w.quant()) r.add(w.q.slabs, w.q.bytes());
+        else if (w.f) r.add(w.f, (size_t)w.n_out * w.n_in * block_bytes(w.type));
+    };
+    for (const Part &p : L.qkv.parts) add(p.m);
+    add(L.wo);
+    add(L.gate_inp);
+    for (const Part &p : L.gateup.parts) add(p.m);
+    add(L.down);
+    fork_side(c);
+    l2_prefetch(r, c->side);
+    SDY_CUDA(cudaEventRecord(c->ev_join, c->side));
+}
+
+// A single-token MoE step can take its ffn norm inside the float router and the gate|up expert
+// kernels (two consumers, each normalising x itself) with SARDYNE_MOE_NORM=fused. Off by default:
+// measured on the Qwen3-30B-A3B shape the router's prologue costs more than the norm kernel
+// (327 against 336 tok/s).
+bool moe_norm_fused(int n, const DLayer &L) {
+    static const bool fused = [] {
+        const char *v = getenv("SARDYNE_MOE_NORM");
+        return v && !strcmp(v, "fused");
+    }();
+    if (!fused || !fusion_enabled() || n != 1 || L.gate_inp.quant()) return false;
+    for (const Part &p : L.gateup.parts)
+        if (!p.m.quant()) return false;
+    return true;
+}
+
 // nin: the step's ffn norm is fused into the router and the gate|up experts (x = the residual).
-void moe_ffn(engine_ctx *c, const DLayer &L, int n, const NormIn *nin = nullptr) {
+void moe_ffn(engine_ctx *c, const DLayer &L, int n, const ActIn *nin = nullptr) {
     const engine_model_info &in = c->m->info;
     const int dim = in.dim, fe = in.ffn_exp_dim, ne = in.n_expert, k = in.n_expert_used;
     const DMat &r = L.gate_inp;
@@ -713,6 +787,17 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n, const NormIn *nin = nullptr)
         SDY_LAUNCHED();
     }
     const int slots = n * k, gu = 2 * fe;
+    if (n == 1 && (prefetch_mode() & PF_EXPERTS) && L.down.quant()) {
+        // the chosen experts' down matrices into L2 while their gate|up products run
+        ExpertPrefetch ep;
+        ep.base[0] = L.down.q.slabs;
+        ep.bytes[0] = (size_t)L.down.gpe * L.down.q.nb * slab_bytes(L.down.type);
+        ep.e0 = (int)c->m->e0;
+        ep.n_local = L.down.n_expert;
+        fork_side(c);
+        expert_prefetch(ep, c->moe_top, k, c->side);
+        SDY_CUDA(cudaEventRecord(c->ev_join, c->side));
+    }
     // Many tokens: experts as grouped tensor-core GEMMs over the slots sorted by expert.
     bool grouped = !nin && gemm_min_tokens() > 0 && n >= gemm_min_tokens() && L.down.quant() &&
                    qgemm_supported(L.down.type, L.down.n_in);
@@ -730,9 +815,13 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n, const NormIn *nin = nullptr)
     } else {
         project_experts(c, L.gateup, c->moe_gu, gu, c->xb, dim, n, slots, k, nin);
     }
-    const XQ *q8k, *q80;
-    want_activations(c, {&L.down}, c->moe_gu, gu, slots, fe, &q8k, &q80);
-    silu_quant(c->moe_gu, gu, c->moe_gu + fe, gu, fe, slots, q8k, q80, c->st);
+    // Expert products one slot at a time: the down kernels apply the SwiGLU gate to their own input.
+    const bool silu_fused = !grouped && fusion_enabled() && L.down.quant();
+    if (!silu_fused) {
+        const XQ *q8k, *q80;
+        want_activations(c, {&L.down}, c->moe_gu, gu, slots, fe, &q8k, &q80);
+        silu_quant(c->moe_gu, gu, c->moe_gu + fe, gu, fe, slots, q8k, q80, c->st);
+    }
     Proj down;
     down.parts.push_back(Part{L.down, 0});
     const bool sharded = c->m->world > 1;
@@ -742,7 +831,12 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n, const NormIn *nin = nullptr)
         qgemm_grouped(L.down.q, L.down.gpe, ne_local, xq, 1, c->grp_off, c->grp_slot, c->grp_tiles, slots,
                       L.down.n_out, c->moe_y, dim, c->st);
     } else {
-        project_experts(c, down, c->moe_y, dim, c->moe_gu, gu, slots, slots, 1);
+        ActIn gate;
+        gate.x = c->moe_gu;
+        gate.ldx = gu;
+        gate.u = c->moe_gu + fe;
+        gate.ldu = gu;
+        project_experts(c, down, c->moe_y, dim, c->moe_gu, gu, slots, slots, 1, silu_fused ? &gate : nullptr);
     }
     if (sharded) all_reduce(c, c->moe_y, c->moe_y, (size_t)slots * dim);  // every slot from its expert's rank
     moe_combine(c->moe_y, dim, c->moe_top, c->moe_w, k, dim, n, c->x, dim, c->st);
@@ -780,10 +874,11 @@ void forward(engine_ctx *c, int n, int out_rows) {
     for (int l = 0; l < in.n_layer; l++) {
         maybe_segment(c, l);
         const DLayer &L = m->layers[l];
+        if (n == 1 && l + 1 < in.n_layer && (prefetch_mode() & PF_LAYER)) prefetch_layer(c, m->layers[l + 1]);
         float *kc = c->k_cache + l * layer_stride, *vc = c->v_cache + l * layer_stride;
         // attention: x = x + Wo . Attn(RoPE(Wq.norm(x)), RoPE(Wk.norm(x)), Wv.norm(x))
         if (fused_norm_ok(n, mats_of(L.qkv))) {
-            project_norm(c, L.qkv, c->qkv, QL, NormIn{c->x, dim, L.attn_norm, in.norm_eps}, n);
+            project_act(c, L.qkv, c->qkv, QL, ActIn{c->x, dim, L.attn_norm, in.norm_eps}, n);
         } else {
             want_activations(c, mats_of(L.qkv), c->xb, dim, n, dim, &q8k, &q80);
             rmsnorm_quant(c->x, dim, L.attn_norm, dim, n, in.norm_eps, c->xb, dim, q8k, q80, c->st);
@@ -810,23 +905,29 @@ void forward(engine_ctx *c, int n, int out_rows) {
         p.kc = kc;
         p.vc = vc;
         p.max_seq = c->max_seq;
-        post_qkv(p, n, c->st);
         attention(c->att, c->qkv, QL, kc, vc, n, in.n_head, in.n_kv_head, hd, 0, c->tokpos, c->max_seq, c->scores, 0,
-                  c->st);
+                  c->st, &p);
         forget_activations(c);
-        matmul(c, c->x, dim, c->att, q_dim, L.wo, n, c->x);
+        if (n == 1 && fusion_enabled() && L.wo.quant())  // the attention output quantized in the prologue
+            matmul_act(c, c->x, dim, L.wo, ActIn{c->att, q_dim}, n, c->x);
+        else
+            matmul(c, c->x, dim, c->att, q_dim, L.wo, n, c->x);
         // MLP: x = x + down(silu(gate.norm(x)) * up.norm(x)), or its MoE
-        const NormIn ffn_nin{c->x, dim, L.ffn_norm, in.norm_eps};
+        const ActIn ffn_nin{c->x, dim, L.ffn_norm, in.norm_eps};
         if (in.n_expert) {
             std::vector<const DMat *> need = mats_of(L.gateup);
             if (L.gate_inp.quant()) need.push_back(&L.gate_inp);
-            want_activations(c, need, c->xb, dim, n, dim, &q8k, &q80);
-            rmsnorm_quant(c->x, dim, L.ffn_norm, dim, n, in.norm_eps, c->xb, dim, q8k, q80, c->st);
-            moe_ffn(c, L, n);
+            if (moe_norm_fused(n, L)) {
+                moe_ffn(c, L, n, &ffn_nin);
+            } else {
+                want_activations(c, need, c->xb, dim, n, dim, &q8k, &q80);
+                rmsnorm_quant(c->x, dim, L.ffn_norm, dim, n, in.norm_eps, c->xb, dim, q8k, q80, c->st);
+                moe_ffn(c, L, n);
+            }
         } else {
             const int F = in.ffn_dim, GU = c->gu_ld;
             if (fused_norm_ok(n, mats_of(L.gateup))) {
-                project_norm(c, L.gateup, c->hgu, GU, ffn_nin, n);
+                project_act(c, L.gateup, c->hgu, GU, ffn_nin, n);
             } else {
                 want_activations(c, mats_of(L.gateup), c->xb, dim, n, dim, &q8k, &q80);
                 rmsnorm_quant(c->x, dim, L.ffn_norm, dim, n, in.norm_eps, c->xb, dim, q8k, q80, c->st);
@@ -847,6 +948,8 @@ void forward(engine_ctx *c, int n, int out_rows) {
                 matmul(c, c->x, dim, c->hgu, GU, L.down, n, c->x);
             }
         }
+        if (c->forked) SDY_CUDA(cudaStreamWaitEvent(c->st, c->ev_join, 0));  // the side branch rejoins
+        c->forked = false;
     }
     if (out_rows > 0) {
         // final norm and vocabulary projection for the requested rows only
@@ -854,7 +957,7 @@ void forward(engine_ctx *c, int n, int out_rows) {
         float *lout = m->world > 1 ? c->lsend + m->v0 : c->logits;  // sharded: this rank's vocabulary rows
         if (fused_norm_ok(out_rows, {&m->output})) {
             forget_activations(c);
-            matmul_norm(c, lout, in.n_vocab, m->output, NormIn{xs, dim, m->output_norm, in.norm_eps}, out_rows);
+            matmul_act(c, lout, in.n_vocab, m->output, ActIn{xs, dim, m->output_norm, in.norm_eps}, out_rows);
         } else {
             want_activations(c, {&m->output}, c->xb, dim, out_rows, dim, &q8k, &q80);
             rmsnorm_quant(xs, dim, m->output_norm, dim, out_rows, in.norm_eps, c->xb, dim, q8k, q80, c->st);
@@ -1147,6 +1250,9 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
     }
     size_t lbytes = (c->logits_all ? B : 1) * in.n_vocab * 4;
     if (!SDY_CUDA(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking)) ||
+        !SDY_CUDA(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking)) ||
+        !SDY_CUDA(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming)) ||
+        !SDY_CUDA(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming)) ||
         !SDY_CUDA(cudaMallocHost(&c->h_logits, lbytes)) || !SDY_CUDA(cudaMallocHost(&c->h_tokpos, (B + 1) * 4))) {
         put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
         engine_ctx_free(c);
@@ -1167,6 +1273,9 @@ void engine_ctx_free(engine_ctx *c) {
     if (!c) return;
     drop_graphs(c);
     if (c->st) cudaStreamDestroy(c->st);
+    if (c->side) cudaStreamDestroy(c->side);
+    if (c->ev_fork) cudaEventDestroy(c->ev_fork);
+    if (c->ev_join) cudaEventDestroy(c->ev_join);
     if (c->arena) cudaFree(c->arena);
     if (c->h_logits) cudaFreeHost(c->h_logits);
     if (c->h_tokpos) cudaFreeHost(c->h_tokpos);

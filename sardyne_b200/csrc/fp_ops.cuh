@@ -13,9 +13,12 @@ void silu_mul(float *gate, const float *up, int64_t n, cudaStream_t s);
 void rope_table(float *c, float *sn, int n_pos, int head_dim, float theta, cudaStream_t s);
 void rope(float *x, int64_t ldx, int n_tok, int n_heads, int head_dim, const float *c, const float *sn, int pos0,
           const int32_t *pos, int interleaved, cudaStream_t s);
+struct PostQKV;
+// post: the bias / qk-norm / RoPE / KV-store step of the same tokens, fused into the kernel for a
+// single token and run before it otherwise.
 void attention(float *out, const float *q, int64_t ldq, const float *kc, const float *vc, int n_tok, int n_head,
                int n_kv_head, int hd, int pos0, const int32_t *pos_dev, int stride, float *scratch, int fixed_nkv,
-               cudaStream_t s);
+               cudaStream_t s, const PostQKV *post = nullptr);
 void axpy(float *y, float a, const float *x, int64_t n, cudaStream_t s);
 void add(float *out, const float *a, const float *b, int64_t n, cudaStream_t s);
 void add_bias(float *x, int64_t ldx, const float *b, int n, int n_tok, cudaStream_t s);

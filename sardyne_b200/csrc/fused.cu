@@ -67,8 +67,7 @@ __global__ void silu_quant_kernel(float *g, int64_t ldg, const float *u, int64_t
     for (int j = 0; j < 8; j++) {
         v[j] = 0.0f;
         if (e0 + j < n) {
-            float a = gv[e0 + j];
-            v[j] = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, exp_cr(-a))), uv[e0 + j]);
+            v[j] = silu_mul(gv[e0 + j], uv[e0 + j]);
             gv[e0 + j] = v[j];
         }
     }
@@ -328,8 +327,7 @@ __global__ void silu_scatter_kernel(const float *g, int64_t ldg, const float *u,
     pdl_wait();
     const int t = blockIdx.y;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const float a = g[(size_t)t * ldg + i];
-        dst[(size_t)t * ldd + i] = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, exp_cr(-a))), u[(size_t)t * ldu + i]);
+        dst[(size_t)t * ldd + i] = silu_mul(g[(size_t)t * ldg + i], u[(size_t)t * ldu + i]);
     }
 }
 
@@ -369,6 +367,30 @@ __global__ void moe_group_kernel(const int32_t *top, int n_slots, int e0, int ne
         const int e = top[i] - e0;
         if (e >= 0 && e < ne) slots[atomicAdd(&cnt[e], 1)] = i;
     }
+}
+
+// L2 prefetch of byte ranges (cp.async.bulk.prefetch.L2, PF_CHUNK bytes per request): a hint
+// that pulls upcoming weights from HBM into L2 while other kernels run. One request per thread
+// per pass, spread over many CTAs, since the requests of one SM issue one after another.
+constexpr size_t PF_CHUNK = 16384;
+__device__ __forceinline__ void prefetch_l2(const char *p, size_t n) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"((uint32_t)n) : "memory");
+}
+__device__ void prefetch_range(const char *p, size_t bytes, size_t thread, size_t n_threads) {
+    bytes &= ~(size_t)15;
+    for (size_t off = thread * PF_CHUNK; off < bytes; off += n_threads * PF_CHUNK)
+        prefetch_l2(p + off, bytes - off < PF_CHUNK ? bytes - off : PF_CHUNK);
+}
+__global__ void l2_prefetch_kernel(L2Ranges r) {
+    const size_t thread = (size_t)blockIdx.x * blockDim.x + threadIdx.x, n = (size_t)gridDim.x * blockDim.x;
+    for (int k = 0; k < r.n; k++) prefetch_range((const char *)r.p[k], r.bytes[k], thread, n);
+}
+// The chosen experts' matrices: blockIdx.y = slot, blockIdx.z = matrix.
+__global__ void expert_prefetch_kernel(ExpertPrefetch ep, const int32_t *top) {
+    const int m = blockIdx.z, e = top[blockIdx.y] - ep.e0;
+    if (!ep.base[m] || e < 0 || e >= ep.n_local) return;
+    prefetch_range((const char *)ep.base[m] + (size_t)e * ep.bytes[m], ep.bytes[m],
+                   (size_t)blockIdx.x * blockDim.x + threadIdx.x, (size_t)gridDim.x * blockDim.x);
 }
 
 XQ pick(const XQ *q) {
@@ -448,6 +470,23 @@ void moe_group(const int32_t *top, int n_slots, int e0, int ne, int tile, int32_
         return;
     }
     launch(moe_group_kernel, 1, 1024, (size_t)ne * 4, s, top, n_slots, e0, ne, tile, off, slots, tiles);
+    SDY_LAUNCHED();
+}
+
+void l2_prefetch(const L2Ranges &r, cudaStream_t s) {
+    size_t chunks = 0;
+    for (int k = 0; k < r.n; k++) chunks += (r.bytes[k] + PF_CHUNK - 1) / PF_CHUNK;
+    if (!chunks) return;
+    l2_prefetch_kernel<<<(unsigned)std::min<size_t>((chunks + 31) / 32, 296), 32, 0, s>>>(r);
+    SDY_LAUNCHED();
+}
+
+void expert_prefetch(const ExpertPrefetch &ep, const int32_t *top, int n_slots, cudaStream_t s) {
+    size_t most = 0;
+    for (int m = 0; m < PF_EXPERT_MATS; m++) most = std::max(most, ep.base[m] ? ep.bytes[m] : 0);
+    if (!most || n_slots <= 0) return;
+    const unsigned per = (unsigned)std::min<size_t>(((most + PF_CHUNK - 1) / PF_CHUNK + 31) / 32, 16);
+    expert_prefetch_kernel<<<dim3(per, n_slots, PF_EXPERT_MATS), 32, 0, s>>>(ep, top);
     SDY_LAUNCHED();
 }
 

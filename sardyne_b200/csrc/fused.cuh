@@ -34,6 +34,30 @@ void post_qkv(const PostQKV &p, int n_tok, cudaStream_t s);
 
 // Float router: top [n_tok][k] expert ids and renormalised weights; logits is scratch [n_tok][ne];
 // counters: n_tok int32 that start at zero (the kernel leaves them at zero).
+// Byte ranges to pull into L2 (hints): upcoming weights.
+constexpr int PF_RANGES = 8;
+struct L2Ranges {
+    const void *p[PF_RANGES];
+    size_t bytes[PF_RANGES];
+    int n = 0;
+    void add(const void *ptr, size_t b) {
+        if (ptr && b && n < PF_RANGES) {
+            p[n] = ptr;
+            bytes[n++] = b;
+        }
+    }
+};
+void l2_prefetch(const L2Ranges &r, cudaStream_t s);
+// Expert matrices [m] (gate, up, down or gate|up, down): expert e0 + e at base[m] + e * bytes[m],
+// e < n_local.
+constexpr int PF_EXPERT_MATS = 3;
+struct ExpertPrefetch {
+    const void *base[PF_EXPERT_MATS] = {};
+    size_t bytes[PF_EXPERT_MATS] = {};
+    int e0 = 0, n_local = 0;
+};
+// Pulls the matrices of the experts named by top[0, n_slots) into L2.
+void expert_prefetch(const ExpertPrefetch &ep, const int32_t *top, int n_slots, cudaStream_t s);
 // norm_w: the router input is RMSNorm(x) * norm_w, computed inside the kernel (x the residual).
 void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, int n_tok,
                  int32_t *top, float *wout, float *logits, int32_t *counters, cudaStream_t s,

@@ -57,11 +57,9 @@ struct Args {
     // groups start at expert * gpe, with the activations of token s / tok_div, into out + s*ldo_slot.
     const int32_t *slot_expert;
     int64_t gpe, ldo_slot;
-    // When nx is set, the activations are not read from the XQ: each CTA normalises its tokens'
-    // rows x[t] (RMSNorm with weight nw, eps neps) and quantizes them into shared memory itself.
-    const float *nx, *nw;
-    int64_t ldnx;
-    float neps;
+    // When act.x is set, the activations are not read from the XQ: each CTA prepares its tokens'
+    // rows (RMSNorm, SwiGLU gate or as is) and quantizes them into shared memory itself.
+    ActIn act;
     int tok_div, n_expert, expert0;  // slot_expert ids are global; this matrix holds experts expert0..
 };
 
@@ -281,9 +279,9 @@ __device__ __forceinline__ void pair_compute(const Raw<TYPE> &w, int u, const ui
 
 // ---------------------------------------------------------------------------- the kernel
 
+// The CTA's work: CTA `cta` of the n_cta that share the launch's groups.
 template <int TYPE, int NT>
-__global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
-    extern __shared__ __align__(16) uint8_t smem[];
+__device__ __forceinline__ void qmv_body(const Args &a, int cta, int n_cta, uint8_t *smem) {
     constexpr bool KQ = (TYPE == T_Q4_K || TYPE == T_Q6_K);
     constexpr int SB = slab_bytes(TYPE);
     const Smem plan = smem_plan(TYPE, NT, a.qrow, a.nb, a.G);
@@ -299,8 +297,8 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
     const int32_t *xsums = (const int32_t *)a.xsums;
     float *out = a.out;
     // This CTA's contiguous share of the launch's groups, swept in batches of a.G groups.
-    const int64_t gA = a.g_begin + a.n_groups * blockIdx.x / gridDim.x;
-    const int64_t gB = a.g_begin + a.n_groups * (blockIdx.x + 1) / gridDim.x;
+    const int64_t gA = a.g_begin + a.n_groups * cta / n_cta;
+    const int64_t gB = a.g_begin + a.n_groups * (cta + 1) / n_cta;
     const int units = KQ ? nb : (nb + 7) / 8;  // pair columns per row
     const int ppg = GROUP_ROWS * units;        // pairs per group
     // The thread's first pair (pair tid of the first batch): loaded before waiting on the
@@ -313,7 +311,7 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
         load_pair(w, slabs + (size_t)(gA + gl) * nb * SB, rem >> 3, rem & 7, nb);
     }
     pdl_wait();
-    const float *nx = a.nx;
+    ActIn act = a.act;
     if (a.slot_expert) {
         const int slot = blockIdx.y, e = a.slot_expert[slot] - a.expert0;
         if (e < 0 || e >= a.n_expert) return;  // another rank's expert (or an invalid id)
@@ -322,11 +320,12 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
         xqs += (size_t)tok * a.qrow;
         xd += (size_t)tok * a.nbx;
         xsums += (size_t)tok * a.nbx * (KQ ? 8 : 1);
-        if (nx) nx += (size_t)tok * a.ldnx;
+        if (act.x) act.x += (size_t)tok * act.ldx;
+        if (act.u) act.u += (size_t)tok * act.ldu;
         out += (size_t)slot * a.ldo_slot;
     }
 
-    if (nx) {  // normalise and quantize the NT rows into the shared-memory XQ
+    if (act.x) {  // prepare and quantize the NT rows into the shared-memory XQ
         __shared__ double part[32];
         XQ v;
         v.vtype = KQ ? T_Q8_K : T_Q8_0;
@@ -339,9 +338,7 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
         v.sums = ss;
         XQ none;
         none.qs = nullptr;
-        for (int t = 0; t < NT; t++)
-            norm_quant_row(nx + (size_t)t * a.ldnx, a.nw, v.n_in, a.neps, t, KQ ? v : none, KQ ? none : v, nullptr,
-                           part);
+        for (int t = 0; t < NT; t++) act_quant_row(act, v.n_in, t, KQ ? v : none, KQ ? none : v, part);
     } else {  // stage the activations of NT tokens (broadcast operands for every pair)
         const int qv = NT * a.qrow / 16;
         for (int i = tid; i < qv; i += THREADS) {
@@ -388,8 +385,26 @@ __global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
 }
 
 template <int TYPE, int NT>
-void launch_one(const Args &a, int smem, dim3 grid, cudaStream_t s) {
-    static std::atomic<uint64_t> configured{0};  // one attribute call per instantiation and device
+__global__ void __launch_bounds__(THREADS) qmv_kernel(Args a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    qmv_body<TYPE, NT>(a, blockIdx.x, gridDim.x, smem);
+}
+
+// Two matrices that share one single-token input (the parts of a projection whose weight types
+// differ, e.g. Q/K in Q4_K and V in Q6_K) in one launch: CTAs [0, na) multiply the first, the
+// rest the second.
+template <int TA, int TB>
+__global__ void __launch_bounds__(THREADS) qmv2_kernel(Args a, Args b, int na) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    if ((int)blockIdx.x < na) qmv_body<TA, 1>(a, blockIdx.x, na, smem);
+    else qmv_body<TB, 1>(b, blockIdx.x - na, gridDim.x - na, smem);
+}
+
+// Raises the instantiation's dynamic shared memory limit to SMEM_LIMIT on the current device
+// (once): without it a launch or occupancy query above 48 KB minus the static shared memory fails.
+template <int TYPE, int NT>
+void configure_one() {
+    static std::atomic<uint64_t> configured{0};
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
@@ -397,6 +412,11 @@ void launch_one(const Args &a, int smem, dim3 grid, cudaStream_t s) {
         SDY_CUDA(cudaFuncSetAttribute(qmv_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT));
         configured.fetch_or(bit);
     }
+}
+
+template <int TYPE, int NT>
+void launch_one(const Args &a, int smem, dim3 grid, cudaStream_t s) {
+    configure_one<TYPE, NT>();
     launch(qmv_kernel<TYPE, NT>, grid, THREADS, smem, s, a);
 }
 
@@ -426,10 +446,17 @@ int sm_count() {
 // by format and token count), at most CTAS_PER_SM; cached per (type, nt).
 template <int TYPE, int NT>
 int occupancy_one() {
+    static const int cap = [] {  // SARDYNE_QMV_CTAS_PER_SM: a lower cap, for tuning
+        const char *e = getenv("SARDYNE_QMV_CTAS_PER_SM");
+        return e && atoi(e) > 0 ? std::min(atoi(e), CTAS_PER_SM) : CTAS_PER_SM;
+    }();
+    configure_one<TYPE, NT>();
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qmv_kernel<TYPE, NT>, THREADS, SMEM_BUDGET) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qmv_kernel<TYPE, NT>, THREADS, SMEM_BUDGET) != cudaSuccess) {
+        cudaGetLastError();  // not sticky: fall back to one CTA per SM
         n = 1;
-    return std::max(1, std::min(n, CTAS_PER_SM));
+    }
+    return std::max(1, std::min(n, cap));
 }
 template <int TYPE>
 int occupancy_nt(int nt) {
@@ -514,10 +541,10 @@ int gemm_min_tokens() {
 }
 
 void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
-             cudaStream_t s, const float *residual, const NormIn *norm) {
+             cudaStream_t s, const float *residual, const ActIn *act) {
     if (row1 <= row0 || xq.n_tok <= 0) return;
     const int gmin = gemm_min_tokens();
-    if (!norm && gmin > 0 && xq.n_tok >= gmin && qgemm_supported(w.type, w.n_in) && xq.vtype == T_Q8_K &&
+    if (!act && gmin > 0 && xq.n_tok >= gmin && qgemm_supported(w.type, w.n_in) && xq.vtype == T_Q8_K &&
         xq.n_in == w.n_in) {
         qgemm(w, xq, out, ldo, row0, row1, out_row0, s, residual);
         return;
@@ -552,11 +579,10 @@ void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0,
         a.nbx = xq.nbx;
         a.out = out + (size_t)t0 * ldo;
         a.residual = residual ? residual + (size_t)t0 * ldo : nullptr;
-        if (norm) {
-            a.nx = norm->x + (size_t)t0 * norm->ldx;
-            a.ldnx = norm->ldx;
-            a.nw = norm->w;
-            a.neps = norm->eps;
+        if (act) {
+            a.act = *act;
+            a.act.x += (size_t)t0 * act->ldx;
+            if (act->u) a.act.u += (size_t)t0 * act->ldu;
         }
         a.ldo = ldo;
         a.row0 = row0;
@@ -573,7 +599,7 @@ namespace sdy {
 
 void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq, int tok_div, const int32_t *slot_expert,
                     int n_slots, int64_t rows_per_expert, float *out, int64_t ldo_slot, cudaStream_t s, int expert0,
-                    const NormIn *norm) {
+                    const ActIn *act) {
     if (n_slots <= 0) return;
     if (xq.vtype != vec_dot_type(experts.type) || xq.n_in != experts.n_in) {
         set_error("qmatvec_gather: activation type/size does not match the weights");
@@ -608,13 +634,72 @@ void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq
     a.tok_div = tok_div;
     a.n_expert = n_expert;
     a.expert0 = expert0;
-    if (norm) {
-        a.nx = norm->x;
-        a.ldnx = norm->ldx;
-        a.nw = norm->w;
-        a.neps = norm->eps;
-    }
+    if (act) a.act = *act;
     dispatch(experts.type, 1, a, plan.smem, dim3(plan.grid, n_slots), s);
+}
+
+namespace {
+
+template <int TA, int TB>
+void launch_pair(const Args &a, const Args &b, int na, int grid, int smem, cudaStream_t s) {
+    static std::atomic<uint64_t> configured{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(configured.load() & bit)) {
+        SDY_CUDA(cudaFuncSetAttribute(qmv2_kernel<TA, TB>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT));
+        configured.fetch_or(bit);
+    }
+    launch(qmv2_kernel<TA, TB>, dim3(grid), THREADS, smem, s, a, b, na);
+    SDY_LAUNCHED();
+}
+
+Args pair_args(const QMat &w, const Plan &plan, const XQ &xq, float *out, const ActIn *act) {
+    Args a{};
+    a.slabs = w.slabs;
+    a.nb = w.nb;
+    a.g_begin = 0;
+    a.n_groups = w.n_groups();
+    a.G = plan.G;
+    a.xqs = xq.qs;
+    a.xd = xq.d;
+    a.xsums = xq.sums;
+    a.qrow = xq.qrow;
+    a.nbx = xq.nbx;
+    a.out = out;
+    a.row0 = 0;
+    a.row1 = w.n_rows;
+    if (act) a.act = *act;
+    return a;
+}
+
+}  // namespace
+
+bool qmatvec2_supported(int ta, int tb) {
+    return (ta == T_Q4_K && tb == T_Q6_K) || (ta == T_Q6_K && tb == T_Q4_K);
+}
+
+void qmatvec2(const QMat &wa, float *outa, const QMat &wb, float *outb, const XQ &xq, cudaStream_t s,
+              const ActIn *act) {
+    if (!qmatvec2_supported(wa.type, wb.type) || xq.n_tok != 1 || wa.n_in != wb.n_in ||
+        xq.vtype != vec_dot_type(wa.type) || xq.vtype != vec_dot_type(wb.type) || xq.n_in != wa.n_in) {
+        set_error("qmatvec2: unsupported pair of matrices");
+        return;
+    }
+    // The SMs' CTA slots split in proportion to the bytes of each matrix.
+    const int64_t cap = (int64_t)sm_count() * std::min(ctas_per_sm(wa.type, 1), ctas_per_sm(wb.type, 1));
+    const double fa = (double)wa.bytes() / (double)(wa.bytes() + wb.bytes());
+    const int64_t cap_a = std::max<int64_t>(1, std::min<int64_t>(cap - 1, (int64_t)(cap * fa + 0.5)));
+    Plan pa, pb;
+    if (!plan_launch(wa.type, wa.nb, xq.qrow, wa.n_groups(), cap_a, 1, &pa) ||
+        !plan_launch(wb.type, wb.nb, xq.qrow, wb.n_groups(), std::max<int64_t>(1, cap - cap_a), 1, &pb)) {
+        set_error("qmatvec2: row of %d elements too long for one CTA", wa.n_in);
+        return;
+    }
+    const Args a = pair_args(wa, pa, xq, outa, act), b = pair_args(wb, pb, xq, outb, act);
+    const int smem = std::max(pa.smem, pb.smem), grid = pa.grid + pb.grid;
+    if (wa.type == T_Q4_K) launch_pair<T_Q4_K, T_Q6_K>(a, b, pa.grid, grid, smem, s);
+    else launch_pair<T_Q6_K, T_Q4_K>(a, b, pa.grid, grid, smem, s);
 }
 
 }  // namespace sdy

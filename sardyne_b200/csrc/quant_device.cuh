@@ -4,6 +4,7 @@
 // Every function is warp-collective: lane l holds elements span*256 + 8l .. +7 of token t.
 #pragma once
 #include "common.cuh"
+#include "fp_device.cuh"
 
 namespace sdy {
 
@@ -133,15 +134,17 @@ __device__ inline void norm_quant_row(const float *x, const float *w, int n, flo
                                       const XQ &q80, float *xb, double *part) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5, ns = (n + 255) / 256;
     double ss;
-    float r[8];
+    float r[8], wr[8];
     const bool one = ns <= nw;
     if (one) {
         const int e0 = warp * 256 + lane * 8;
-        double p = 0.0;
-        for (int j = 0; j < 8; j++) {
-            r[j] = warp < ns && e0 + j < n ? x[e0 + j] : 0.0f;
-            p += (double)r[j] * r[j];
+        for (int j = 0; j < 8; j++) {  // x and the norm weights requested together
+            const bool in = warp < ns && e0 + j < n;
+            r[j] = in ? x[e0 + j] : 0.0f;
+            wr[j] = in ? w[e0 + j] : 0.0f;
         }
+        double p = 0.0;
+        for (int j = 0; j < 8; j++) p += (double)r[j] * r[j];
         for (int o = 16; o; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
         if (lane == 0 && warp < ns) part[warp] = p;
         __syncthreads();
@@ -157,9 +160,40 @@ __device__ inline void norm_quant_row(const float *x, const float *w, int n, flo
         float v[8];
         for (int j = 0; j < 8; j++) {
             const float xv = one ? r[j] : (e0 + j < n ? x[e0 + j] : 0.0f);
-            v[j] = e0 + j < n ? __fmul_rn(__fmul_rn(xv, scale), w[e0 + j]) : 0.0f;
+            const float wv = one ? wr[j] : (e0 + j < n ? w[e0 + j] : 0.0f);
+            v[j] = e0 + j < n ? __fmul_rn(__fmul_rn(xv, scale), wv) : 0.0f;
             if (xb && e0 + j < n) xb[e0 + j] = v[j];
         }
+        if (q8k.qs) quant_q8k_vals(v, t, s, q8k);
+        if (q80.qs) quant_q80_vals(v, e0 < n, t, s, q80);
+    }
+}
+
+// The SwiGLU gate of one element, silu(g) * u, in the reference's operation order (ops.c:369).
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_cr(-g))), u);
+}
+
+// Token t's input row as ActIn describes it (RMSNorm, SwiGLU gate or x as is), quantized into
+// q8k and/or q80 by the whole block; the values equal those of the standalone kernels
+// (rmsnorm_quant, silu_quant, quantize), warp w quantizing spans w, w + warps, ...
+__device__ inline void act_quant_row(const ActIn &in, int n, int t, const XQ &q8k, const XQ &q80, double *part) {
+    const float *x = in.x + (size_t)t * in.ldx;
+    if (in.w) {
+        norm_quant_row(x, in.w, n, in.eps, t, q8k, q80, nullptr, part);
+        return;
+    }
+    const float *u = in.u ? in.u + (size_t)t * in.ldu : nullptr;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5, ns = (n + 255) / 256;
+    for (int s = warp; s < ns; s += nw) {
+        const int e0 = s * 256 + lane * 8;
+        float r[8], ur[8], v[8];
+        for (int j = 0; j < 8; j++) {  // every load of the span issued before the arithmetic
+            const bool live = e0 + j < n;
+            r[j] = live ? x[e0 + j] : 0.0f;
+            ur[j] = live && u ? u[e0 + j] : 0.0f;
+        }
+        for (int j = 0; j < 8; j++) v[j] = e0 + j < n ? (u ? silu_mul(r[j], ur[j]) : r[j]) : 0.0f;
         if (q8k.qs) quant_q8k_vals(v, t, s, q8k);
         if (q80.qs) quant_q80_vals(v, e0 < n, t, s, q80);
     }
