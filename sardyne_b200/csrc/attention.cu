@@ -77,31 +77,47 @@ __host__ __device__ inline AcSmem ac_smem(int n_rep, int hd, int stride, bool pu
 
 // One head of the reference's post-projection steps (model_llama.c:781-800) by one warp: bias,
 // per-head RMSNorm (qk-norm: double sum of squares, lane-strided then a shuffle tree), RoPE
-// (ops.c:388-403) at table row `pos`; result in dst (shared, hd floats; hd % 32 == 0).
-__device__ void head_post(const float *src, const float *bias, const float *norm, float eps, const float *cs,
-                          const float *sn, int interleaved, int hd, float *dst) {
-    const int lane = threadIdx.x & 31, nu = hd / 32, half = hd / 2;
-    // every global operand requested first (one round of load latency)
-    float v[8], bv[8], nv[8], c[4], sv[4];
+// (ops.c:388-403) at table row `pos`; result in dst (shared, hd floats; hd % 32 == 0, hd <= 256).
+// Split in three so that a kernel can load the operands that do not depend on the projection
+// (head_consts, rope_consts) before pdl_wait, and the rows of all of a warp's heads at once.
+struct HeadConsts {
+    float b[8], n[8];  // bias and norm weight, element lane + 32u
+};
+struct RopeConsts {
+    float c[4], s[4];  // cos / sin of pair lane + 32u
+};
+__device__ __forceinline__ void head_consts(const float *bias, const float *norm, int hd, HeadConsts &h) {
+    const int lane = threadIdx.x & 31, nu = hd / 32;
 #pragma unroll
     for (int u = 0; u < 8; u++)
         if (u < nu) {
-            const int i = lane + 32 * u;
-            v[u] = src[i];
-            bv[u] = bias ? bias[i] : 0.0f;
-            nv[u] = norm ? norm[i] : 0.0f;
+            h.b[u] = bias ? bias[lane + 32 * u] : 0.0f;
+            h.n[u] = norm ? norm[lane + 32 * u] : 0.0f;
         }
+}
+__device__ __forceinline__ void rope_consts(const float *cs, const float *sn, int hd, RopeConsts &r) {
+    const int lane = threadIdx.x & 31, half = hd / 2;
 #pragma unroll
     for (int u = 0; u < 4; u++)
-        if (cs && lane + 32 * u < half) {
-            c[u] = cs[lane + 32 * u];
-            sv[u] = sn[lane + 32 * u];
+        if (lane + 32 * u < half) {
+            r.c[u] = cs[lane + 32 * u];
+            r.s[u] = sn[lane + 32 * u];
         }
+}
+__device__ __forceinline__ void head_load(const float *src, int hd, float v[8]) {
+    const int lane = threadIdx.x & 31, nu = hd / 32;
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+        if (u < nu) v[u] = src[lane + 32 * u];
+}
+__device__ __forceinline__ void head_finish(float v[8], const HeadConsts &h, bool bias, bool norm, float eps,
+                                            bool rope, const RopeConsts &rc, int interleaved, int hd, float *dst) {
+    const int lane = threadIdx.x & 31, nu = hd / 32, half = hd / 2;
     double ss = 0.0;
 #pragma unroll
     for (int u = 0; u < 8; u++)
         if (u < nu) {
-            if (bias) v[u] = __fadd_rn(v[u], bv[u]);
+            if (bias) v[u] = __fadd_rn(v[u], h.b[u]);
             ss += (double)v[u] * v[u];
         }
     if (norm) {
@@ -109,24 +125,44 @@ __device__ void head_post(const float *src, const float *bias, const float *norm
         const float scale = (float)(1.0 / sqrt(ss / hd + (double)eps));
 #pragma unroll
         for (int u = 0; u < 8; u++)
-            if (u < nu) v[u] = __fmul_rn(__fmul_rn(v[u], scale), nv[u]);
+            if (u < nu) v[u] = __fmul_rn(__fmul_rn(v[u], scale), h.n[u]);
     }
 #pragma unroll
     for (int u = 0; u < 8; u++)
         if (u < nu) dst[lane + 32 * u] = v[u];
     __syncwarp();
-    if (cs)
+    if (rope)
 #pragma unroll
         for (int u = 0; u < 4; u++) {
             const int i = lane + 32 * u;
             if (i < half) {
                 const int ia = interleaved ? 2 * i : i, ib = interleaved ? 2 * i + 1 : i + half;
                 const float a = dst[ia], b = dst[ib];
-                dst[ia] = __fsub_rn(__fmul_rn(a, c[u]), __fmul_rn(b, sv[u]));
-                dst[ib] = __fadd_rn(__fmul_rn(a, sv[u]), __fmul_rn(b, c[u]));
+                dst[ia] = __fsub_rn(__fmul_rn(a, rc.c[u]), __fmul_rn(b, rc.s[u]));
+                dst[ib] = __fadd_rn(__fmul_rn(a, rc.s[u]), __fmul_rn(b, rc.c[u]));
             }
         }
     __syncwarp();
+}
+
+// Head r of a KV group's post step: r < n_rep the query heads h0 + r, then the K head, then V.
+struct HeadOp {
+    const float *src, *bias, *norm;
+    bool rope;
+    float *dst;
+};
+__device__ __forceinline__ HeadOp head_op(const PostQKV &pp, int r, int n_rep, int h0, int g, int t, int hd,
+                                          float *qs, float *knew, float *vnew) {
+    if (r < n_rep) {
+        const int h = h0 + r;
+        return {pp.q + (size_t)t * pp.ldq + (size_t)h * hd, pp.bq ? pp.bq + (size_t)h * hd : nullptr, pp.q_norm,
+                true, qs + r * hd};
+    }
+    if (r == n_rep)
+        return {pp.k + (size_t)t * pp.ldk + (size_t)g * hd, pp.bk ? pp.bk + (size_t)g * hd : nullptr, pp.k_norm,
+                true, knew};
+    return {pp.v + (size_t)t * pp.ldv + (size_t)g * hd, pp.bv ? pp.bv + (size_t)g * hd : nullptr, nullptr, false,
+            vnew};
 }
 
 // q: token t at q + t*ldq, heads of hd; k/v cache [n_kv_head][stride][hd]; the first token's
@@ -137,14 +173,14 @@ __device__ void head_post(const float *src, const float *bias, const float *norm
 // other CTAs of the cluster read in phase C through distributed shared memory; two V chunks of
 // this CTA's column slice (the first one requested together with the first K tile); and a work
 // area holding the K tiles in phase A and the probability chunks in phase C.
-__global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
+__global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS, 1)
     attention_cluster_kernel(float *__restrict__ out, const float *__restrict__ q, int64_t ldq,
                              const float *__restrict__ kc, const float *__restrict__ vc, int n_head, int n_kv_head,
                              int hd, int pos0, const int32_t *pos_dev, int stride, int fixed_nkv, int push,
                              PostQKV pp) {
     extern __shared__ __align__(16) float sm[];
     __shared__ float cmax[AC_MAX_REP], gmax[AC_MAX_REP], ginv[AC_MAX_REP];
-    __shared__ double csum[AC_MAX_REP];
+    __shared__ double csum[AC][AC_MAX_REP];  // [rank][head]: every CTA's partial sums, pushed to all
     cg::cluster_group cl = cg::this_cluster();
     const int c = (int)cl.block_rank();
     const int g = blockIdx.y, t = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -169,7 +205,25 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(kh + (size_t)jb * hd), "r"(bytes) : "memory");
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(vh + (size_t)jb * hd), "r"(bytes) : "memory");
     }
+    // Fused post-QKV: warp w handles heads w and w + 8 of the group (n_rep + 2 <= 16). Their
+    // biases, norm weights and the RoPE row do not depend on the projection: loaded here.
+    constexpr int NWARP = AC_THREADS / 32;
+    const int n_post = n_rep + 2;
+    const bool post_regs = post && n_post <= 2 * NWARP;
+    HeadConsts hc[2];
+    RopeConsts rc;
+    if (post_regs) {
+        const int pos = n_kv - 1, half = hd / 2;
+        rope_consts(pp.cos + (size_t)pos * half, pp.sin + (size_t)pos * half, hd, rc);
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+            if (warp + NWARP * i < n_post) {
+                const HeadOp op = head_op(pp, warp + NWARP * i, n_rep, h0, g, t, hd, qs, knew, vnew);
+                head_consts(op.bias, op.norm, hd, hc[i]);
+            }
+    }
     pdl_wait();
+    pdl_release();
 
     // ---- phase A: scores of this CTA's keys into scl
     const int ldk = hd + 4, hd4 = hd / 4;  // padded rows: a quarter-warp's 16-byte reads hit all banks once
@@ -191,6 +245,14 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
             cp_async16(dst + j * S + i, vh + (size_t)(j0 + j) * hd + e0 + i);
         }
     };
+    // The projection rows of the warp's post heads are requested first (before the K/V tiles
+    // below, which would otherwise sit ahead of them in the memory pipeline).
+    float v[2][8];
+    if (post_regs)
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+            if (warp + NWARP * i < n_post)
+                head_load(head_op(pp, warp + NWARP * i, n_rep, h0, g, t, hd, qs, knew, vnew).src, hd, v[i]);
     if (ntile > 0) load_k(0);
     load_v(0);  // phase C's first chunk travels with the first K tile
     cp_async_commit();
@@ -198,22 +260,30 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
         // Each CTA transforms its query heads and the new K and V rows itself; rank 0 stores the
         // rows in the cache for later steps, and every CTA patches them into its staged tiles
         // below (its own copies of the cache rows may predate rank 0's store).
-        const int pos = n_kv - 1, half = hd / 2;
-        const float *cs = pp.cos + (size_t)pos * half, *sn = pp.sin + (size_t)pos * half;
-        for (int r = warp; r < n_rep + 2; r += AC_THREADS / 32) {
-            if (r < n_rep) {
-                const int h = h0 + r;
-                head_post(pp.q + (size_t)t * pp.ldq + (size_t)h * hd, pp.bq ? pp.bq + (size_t)h * hd : nullptr,
-                          pp.q_norm, pp.eps, cs, sn, pp.interleaved, hd, qs + r * hd);
-            } else if (r == n_rep) {
-                head_post(pp.k + (size_t)t * pp.ldk + (size_t)g * hd, pp.bk ? pp.bk + (size_t)g * hd : nullptr,
-                          pp.k_norm, pp.eps, cs, sn, pp.interleaved, hd, knew);
-            } else {
-                head_post(pp.v + (size_t)t * pp.ldv + (size_t)g * hd, pp.bv ? pp.bv + (size_t)g * hd : nullptr,
-                          nullptr, 0.0f, nullptr, nullptr, 0, hd, vnew);
+        if (post_regs) {
+#pragma unroll
+            for (int i = 0; i < 2; i++)
+                if (warp + NWARP * i < n_post) {
+                    const HeadOp op = head_op(pp, warp + NWARP * i, n_rep, h0, g, t, hd, qs, knew, vnew);
+                    head_finish(v[i], hc[i], op.bias != nullptr, op.norm != nullptr, pp.eps, op.rope, rc,
+                                pp.interleaved, hd, op.dst);
+                }
+        } else {
+            const int pos = n_kv - 1, half = hd / 2;
+            RopeConsts r1;
+            rope_consts(pp.cos + (size_t)pos * half, pp.sin + (size_t)pos * half, hd, r1);
+            for (int r = warp; r < n_post; r += NWARP) {
+                const HeadOp op = head_op(pp, r, n_rep, h0, g, t, hd, qs, knew, vnew);
+                HeadConsts h1;
+                float v[8];
+                head_consts(op.bias, op.norm, hd, h1);
+                head_load(op.src, hd, v);
+                head_finish(v, h1, op.bias != nullptr, op.norm != nullptr, pp.eps, op.rope, r1, pp.interleaved, hd,
+                            op.dst);
             }
         }
         __syncthreads();
+        const int pos = n_kv - 1;
         if (c == 0)
             for (int i = tid; i < hd; i += AC_THREADS) {
                 pp.kc[((size_t)g * pp.max_seq + pos) * hd + i] = knew[i];
@@ -321,12 +391,14 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
                 for (int p = 0; p < AC; p++) *cl.map_shared_rank(work + r * ldp + jb + j, p) = e;
         }
         for (int o = 16; o; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
-        if (lane == 0) csum[r] = sacc;
+        if (lane < AC) *cl.map_shared_rank(&csum[c][r], lane) = sacc;
     }
-    cl.sync();  // also publishes every CTA's exponentials for phase C
+    cl.sync();  // publishes every CTA's partial sums and (push mode) exponentials
+    // From here on a CTA reads another's shared memory only in pull mode (load_p), which then
+    // ends with a cluster barrier before any CTA exits.
     if (tid < n_rep) {
         double sacc = 0.0;
-        for (int p = 0; p < AC; p++) sacc += *cl.map_shared_rank(csum + tid, p);
+        for (int p = 0; p < AC; p++) sacc += csum[p][tid];
         ginv[tid] = (float)(1.0 / sacc);
     }
     __syncthreads();
@@ -355,20 +427,14 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
                 const int idx = i0 + u * AC_THREADS + tid;
                 if (idx < tot) {
                     const int r = idx / nk, jj = idx - r * nk;
-                    pb[r * AC_PLD + jj] = __fmul_rn(v[u], ginv[r]);
+                    pb[r * AC_PLD + jj] = v[u];
                 }
             }
         }
     };
     float acc = 0.0f;
-    if (push) {  // p_j = e_j * inv in place, every key of every head
-        for (int idx = tid; idx < n_rep * n_kv; idx += AC_THREADS) {
-            const int r = idx / n_kv, j = idx - r * n_kv;
-            work[r * ldp + j] = __fmul_rn(work[r * ldp + j], ginv[r]);
-        }
-    } else {
-        load_p(0);
-    }
+    if (!push) load_p(0);
+    const float inv = chain ? ginv[ch_r] : 0.0f;
     for (int ic = 0; ic < nchunk; ic++) {
         if (ic + 1 < nchunk) {
             load_v(ic + 1);
@@ -385,26 +451,41 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS)
                                    : work + (ic & 1) * n_rep * AC_PLD + ch_r * AC_PLD;
             const float *vr = vb + (ic & 1) * AC_KC * S + ch_e;
             const int nk = min(AC_KC, n_kv - ic * AC_KC);
-            const float4 *p4 = (const float4 *)pr;  // 4 keys' probabilities per 16-byte load
-#pragma unroll 4
-            for (int q = 0; q < (nk >> 2); q++) {
-                const float4 p = p4[q];
-                const float *v = vr + 4 * q * S;
-                const float v0 = v[0], v1 = v[S], v2 = v[2 * S], v3 = v[3 * S];
-                acc = __fadd_rn(acc, __fmul_rn(p.x, v0));
-                acc = __fadd_rn(acc, __fmul_rn(p.y, v1));
-                acc = __fadd_rn(acc, __fmul_rn(p.z, v2));
-                acc = __fadd_rn(acc, __fmul_rn(p.w, v3));
+            // p_j = e_j * inv (ops.c:363), then acc += p_j * v_j[e]: the FADD chain is the
+            // critical path, so the next 8 keys' operands are loaded while the current 8 are added.
+            const float4 *e4 = (const float4 *)pr;  // 4 keys' exponentials per 16-byte load
+            const int n8 = nk >> 3;
+            float4 ea0, ea1, eb0, eb1;
+            float va[8], vbb[8];
+            auto fetch = [&](int q, float4 &x0, float4 &x1, float *vv) {
+                x0 = e4[2 * q];
+                x1 = e4[2 * q + 1];
+#pragma unroll
+                for (int k = 0; k < 8; k++) vv[k] = vr[(8 * q + k) * S];
+            };
+            auto add8 = [&](const float4 &x0, const float4 &x1, const float *vv) {
+                const float ev[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                for (int k = 0; k < 8; k++) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(ev[k], inv), vv[k]));
+            };
+            if (n8 > 0) fetch(0, ea0, ea1, va);
+            int q = 0;
+            for (; q + 2 <= n8; q += 2) {
+                fetch(q + 1, eb0, eb1, vbb);
+                add8(ea0, ea1, va);
+                if (q + 2 < n8) fetch(q + 2, ea0, ea1, va);
+                add8(eb0, eb1, vbb);
             }
-            for (int j = nk & ~3; j < nk; j++) acc = __fadd_rn(acc, __fmul_rn(pr[j], vr[j * S]));
+            if (q < n8) add8(ea0, ea1, va);
+            for (int j = n8 * 8; j < nk; j++) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(pr[j], inv), vr[j * S]));
         }
         if (!push && ic + 1 < nchunk) load_p(ic + 1);
         cp_async_wait<0>();
         __syncthreads();
     }
-    cluster_arrive();  // done reading the other CTAs' shared memory; the matching wait is at the end
+    if (!push) cluster_arrive();  // done reading the other CTAs' shared memory; the wait is below
     if (chain) out[((size_t)t * n_head + h0 + ch_r) * hd + e0 + ch_e] = acc;
-    cluster_wait();
+    if (!push) cluster_wait();
 }
 
 // General per-(head, token) kernel, one CTA of ATT_THREADS each: K and V staged through shared

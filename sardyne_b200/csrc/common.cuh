@@ -126,15 +126,24 @@ void note_launch();
 // ------------------------------------------------------------------------------ dependent launch
 // Kernels are launched with programmatic dependent launch: a kernel's CTAs are set up while the
 // previous kernel's last CTAs retire and block in pdl_wait() until it has completed and its writes
-// are visible, which takes launch latency off the critical path. Kernels do not signal their
-// dependents early (griddepcontrol.launch_dependents): the next kernel's CTAs would then be placed
-// while this one still occupies the SMs, packed onto the few with room, which measured slower than
-// launching without PDL. So every kernel reads or writes no activation before pdl_wait(); only
-// weights may be read before it (the matvec loads its first weight pair there). Kernels that write
-// weights (repacking, format conversion) complete before any later kernel starts. Launched without
-// the attribute (SARDYNE_NO_PDL set), pdl_wait() is a no-op.
+// are visible, which takes launch latency off the critical path. Only kernels of few CTAs signal
+// their dependents early (pdl_release, griddepcontrol.launch_dependents): after a kernel that
+// fills the SMs the next kernel's CTAs would be placed while it still occupies them, packed onto
+// the few with room (measured slower than launching without PDL), while after a small kernel they
+// find most SMs free and load their weights during it (+3-5% per decode step). Every kernel reads
+// or writes no activation before pdl_wait(); only weights may be read before it (the matvec loads
+// its first weight pair there). Kernels that write weights (repacking, format conversion) neither
+// signal early nor run inside a step. Launched without the attribute (SARDYNE_NO_PDL set),
+// pdl_wait() and pdl_release() are no-ops.
 #ifdef __CUDACC__
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+// The early signal, for kernels of few CTAs only: called after pdl_wait(), it lets the next
+// kernel's CTAs start and load their weights while this kernel runs.
+__device__ __forceinline__ void pdl_release() {
+#ifndef SDY_NO_EARLY_RELEASE
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+#endif
+}
 
 // acc + term(0) + term(1) + ... + term(n-1), added left to right with every sum rounded (the
 // reference's sequential loops). Software-pipelined: the terms of batch k+1 (their loads) are

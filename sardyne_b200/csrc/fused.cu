@@ -50,6 +50,7 @@ __device__ __forceinline__ void quantize_span(const float v[8], int e0, int n, i
 __global__ void rmsnorm_quant_kernel(const float *x, int64_t ldx, const float *w, int n, float eps, float *xb,
                                      int64_t ldb, XQ q8k, XQ q80) {
     pdl_wait();
+    pdl_release();
     __shared__ double part[32];
     const int t = blockIdx.x;
     norm_quant_row(x + (size_t)t * ldx, w, n, eps, t, q8k, q80, xb ? xb + (size_t)t * ldb : nullptr, part);
@@ -58,6 +59,7 @@ __global__ void rmsnorm_quant_kernel(const float *x, int64_t ldx, const float *w
 // grid (ceil(n/2048), rows), 256 threads: warp w of block b owns span 8b + w.
 __global__ void silu_quant_kernel(float *g, int64_t ldg, const float *u, int64_t ldu, int n, XQ q8k, XQ q80) {
     pdl_wait();
+    pdl_release();
     const int t = blockIdx.y, span = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (span * 256 >= n) return;  // whole warps leave together
     const int e0 = span * 256 + (threadIdx.x & 31) * 8;
@@ -226,6 +228,7 @@ __global__ void __launch_bounds__(ROUTER_THREADS)
         }
     }
     pdl_wait();
+    pdl_release();
     const float *xv = x + (size_t)t * ldx;
     // nw: the router input is RMSNorm(x) * nw, computed here in the shared fixed order (the value
     // the standalone norm kernel would have stored), instead of a normalised copy read from memory.
@@ -295,6 +298,7 @@ __global__ void __launch_bounds__(ROUTER_THREADS)
 __global__ void moe_combine_kernel(const float *y, int64_t ldy, const int32_t *top, const float *w, int k, int dim,
                                    float *x, int64_t ldx) {
     pdl_wait();
+    pdl_release();
     __shared__ int order[64];
     __shared__ float ws[64];
     const int t = blockIdx.y;

@@ -119,6 +119,7 @@ void dequant_rows(const QMat &w, const int32_t *row_ids, int n_ids, int64_t firs
 
 __global__ void quantize_kernel(int vtype, const float *__restrict__ x, int64_t ldx, int n_in, XQ xq) {
     pdl_wait();
+    pdl_release();
     const int t = blockIdx.y;
     const int span = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (span * 256 >= n_in) return;
