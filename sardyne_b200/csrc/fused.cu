@@ -126,7 +126,7 @@ __global__ void post_qkv_kernel(PostQKV p) {
 // Router logits for float weights: one warp per expert row. The warp copies x and its row into
 // shared memory with coalesced loads; lanes 0..3 then run the reference's four accumulator
 // chains (ops.c:155-167: s_k over i = 4g + k, the tail into s0) and combine (s0+s1)+(s2+s3).
-constexpr int ROUTER_EPC = 2;  // experts per CTA: one warp each (chains of few warps share an SM's shared-memory pipe)
+constexpr int ROUTER_EPC = 8;  // experts per CTA: one warp each
 constexpr int ROUTER_THREADS = 32 * ROUTER_EPC;
 
 __device__ __forceinline__ float4 load4_w(const void *w, int wtype, size_t i) {  // i a multiple of 4
@@ -258,15 +258,30 @@ __global__ void __launch_bounds__(ROUTER_THREADS)
     __syncthreads();
     if (e < ne) {
         float s = 0.0f;
-        if (lane < 4 && vec) {  // G % 4 == 0: one 16-byte load per operand per 4 terms
-            const float4 *xa = (const float4 *)(xs + lane * G), *ra = (const float4 *)(row + lane * G);
-#pragma unroll 4
-            for (int q = 0; q < G / 4; q++) {
-                const float4 a = xa[q], b = ra[q];
-                s = __fadd_rn(s, __fmul_rn(a.x, b.x));
-                s = __fadd_rn(s, __fmul_rn(a.y, b.y));
-                s = __fadd_rn(s, __fmul_rn(a.z, b.z));
-                s = __fadd_rn(s, __fmul_rn(a.w, b.w));
+        if (vec) {
+            // The products x_i * w_i by the whole warp (each rounded once, as in the chain), in place
+            // in the row; then lane a adds accumulator a's terms in order, one 16-byte load per 4
+            // (G % 4 == 0), so the chains wait on the adds alone.
+            for (int i = lane * 4; i < dim; i += 128) {
+                const float4 a = *(const float4 *)(xs + i);
+                float4 b = *(const float4 *)(row + i);
+                b.x = __fmul_rn(a.x, b.x);
+                b.y = __fmul_rn(a.y, b.y);
+                b.z = __fmul_rn(a.z, b.z);
+                b.w = __fmul_rn(a.w, b.w);
+                *(float4 *)(row + i) = b;
+            }
+            __syncwarp();
+            if (lane < 4) {
+                const float4 *ra = (const float4 *)(row + lane * G);
+#pragma unroll 8
+                for (int q = 0; q < G / 4; q++) {
+                    const float4 b = ra[q];
+                    s = __fadd_rn(s, b.x);
+                    s = __fadd_rn(s, b.y);
+                    s = __fadd_rn(s, b.z);
+                    s = __fadd_rn(s, b.w);
+                }
             }
         } else if (lane < 4) {
             const int groups = dim / 4;
