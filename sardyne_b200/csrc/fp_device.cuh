@@ -78,4 +78,34 @@ __device__ inline void softmax_block(float *v, int n) {
     for (int i = threadIdx.x; i < n; i += blockDim.x) v[i] = __fmul_rn(v[i], inv);
 }
 
+// x[t] += sum over t's k slots, in ascending expert id, of w * y[slot] (model_llama.c:723-750),
+// elements i0, i0 + step, ... of the row by the calling CTA (k <= 64). The slots are ranked in
+// shared memory (ties keep slot order); each element then adds its k terms in that order with the
+// loads issued ahead of the adds.
+__device__ inline void moe_combine_token(const float *y, int64_t ldy, const int32_t *top, const float *w, int k,
+                                         int dim, float *x, int64_t ldx, int t, int i0, int step) {
+    __shared__ int order[64];
+    __shared__ float ws[64];
+    const int32_t *tt = top + (size_t)t * k;
+    if ((int)threadIdx.x < k) {
+        const int i = threadIdx.x, ei = tt[i];
+        int rank = 0;
+        for (int j = 0; j < k; j++) {
+            const int ej = tt[j];
+            rank += (ej < ei || (ej == ei && j < i));
+        }
+        order[rank] = i;
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < k) ws[threadIdx.x] = w[(size_t)t * k + order[threadIdx.x]];
+    __syncthreads();
+    for (int i = i0 + threadIdx.x; i < dim; i += step) {
+        const float acc = ordered_sum<8>(0.0f, k, [&](int j) {
+            return __fmul_rn(ws[j], y[((size_t)t * k + order[j]) * ldy + i]);
+        });
+        float *xp = x + (size_t)t * ldx + i;
+        *xp = __fadd_rn(*xp, acc);
+    }
+}
+
 }  // namespace sdy

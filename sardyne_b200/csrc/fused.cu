@@ -307,36 +307,12 @@ __global__ void __launch_bounds__(ROUTER_THREADS)
                        fpart);
 }
 
-// x[t] += sum over t's k slots, in ascending expert id, of w * y[slot]. The slots are ranked once
-// per CTA in shared memory (ties keep slot order); each element then adds its k terms in that
-// order with the loads issued ahead of the adds.
+// One CTA-column of the MoE combine (moe_combine_token in fp_device.cuh) per (element block, token).
 __global__ void moe_combine_kernel(const float *y, int64_t ldy, const int32_t *top, const float *w, int k, int dim,
                                    float *x, int64_t ldx) {
     pdl_wait();
     pdl_release();
-    __shared__ int order[64];
-    __shared__ float ws[64];
-    const int t = blockIdx.y;
-    const int32_t *tt = top + (size_t)t * k;
-    if ((int)threadIdx.x < k) {
-        const int i = threadIdx.x, ei = tt[i];
-        int rank = 0;
-        for (int j = 0; j < k; j++) {
-            const int ej = tt[j];
-            rank += (ej < ei || (ej == ei && j < i));
-        }
-        order[rank] = i;
-    }
-    __syncthreads();
-    if ((int)threadIdx.x < k) ws[threadIdx.x] = w[(size_t)t * k + order[threadIdx.x]];
-    __syncthreads();
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) {
-        const float acc = ordered_sum<8>(0.0f, k, [&](int j) {
-            return __fmul_rn(ws[j], y[((size_t)t * k + order[j]) * ldy + i]);
-        });
-        float *xp = x + (size_t)t * ldx + i;
-        *xp = __fadd_rn(*xp, acc);
-    }
+    moe_combine_token(y, ldy, top, w, k, dim, x, ldx, blockIdx.y, blockIdx.x * blockDim.x, gridDim.x * blockDim.x);
 }
 
 // dst[t][i] = silu(g[t][i]) * u[t][i] (ops.c:366-371): the SiLU product of one rank's rows of a
