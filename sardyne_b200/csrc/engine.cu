@@ -714,17 +714,19 @@ void all_reduce(engine_ctx *c, const float *send, float *recv, size_t count) {
 }
 
 // L2 prefetch in single-token steps (SARDYNE_L2_PREFETCH = off | layer | experts | all): the next
-// layer's matrices, and the chosen experts' down matrices. Default: experts. Measured: the down
-// prefetch gains ~1% on the Qwen3-30B-A3B shape; the next layer's matrices cost 5% on the
-// Qwen2.5-3B shape (their reads compete with the current layer's) and gain 1% on the MoE one.
-enum { PF_LAYER = 1, PF_EXPERTS = 2 };
-int prefetch_mode() {
+// layer's matrices, and the chosen experts' down matrices. Default: all on MoE models, none on
+// dense ones. Measured: the down prefetch gains ~1% on the Qwen3-30B-A3B shape and the next
+// layer's (non-expert, ~12 MB) matrices another 1%; on the Qwen2.5-3B shape the next layer's
+// ~47 MB cost 5% (their reads compete with the current layer's).
+enum { PF_LAYER = 1, PF_EXPERTS = 2, PF_DEFAULT = -1 };
+int prefetch_mode(const engine_model_info &in) {
     static const int mode = [] {
         const char *v = getenv("SARDYNE_L2_PREFETCH");
-        if (!v) return (int)PF_EXPERTS;
+        if (!v) return (int)PF_DEFAULT;
         return !strcmp(v, "off") ? 0 : !strcmp(v, "layer") ? PF_LAYER : !strcmp(v, "experts") ? PF_EXPERTS
                                                                                   : PF_LAYER | PF_EXPERTS;
     }();
+    if (mode == PF_DEFAULT) return in.n_expert ? PF_LAYER | PF_EXPERTS : 0;
     return mode;
 }
 
@@ -787,7 +789,7 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n, const ActIn *nin = nullptr) 
         SDY_LAUNCHED();
     }
     const int slots = n * k, gu = 2 * fe;
-    if (n == 1 && (prefetch_mode() & PF_EXPERTS) && L.down.quant()) {
+    if (n == 1 && (prefetch_mode(in) & PF_EXPERTS) && L.down.quant()) {
         // the chosen experts' down matrices into L2 while their gate|up products run
         ExpertPrefetch ep;
         ep.base[0] = L.down.q.slabs;
@@ -874,7 +876,7 @@ void forward(engine_ctx *c, int n, int out_rows) {
     for (int l = 0; l < in.n_layer; l++) {
         maybe_segment(c, l);
         const DLayer &L = m->layers[l];
-        if (n == 1 && l + 1 < in.n_layer && (prefetch_mode() & PF_LAYER)) prefetch_layer(c, m->layers[l + 1]);
+        if (n == 1 && l + 1 < in.n_layer && (prefetch_mode(in) & PF_LAYER)) prefetch_layer(c, m->layers[l + 1]);
         float *kc = c->k_cache + l * layer_stride, *vc = c->v_cache + l * layer_stride;
         // attention: x = x + Wo . Attn(RoPE(Wq.norm(x)), RoPE(Wk.norm(x)), Wv.norm(x))
         if (fused_norm_ok(n, mats_of(L.qkv))) {
