@@ -760,7 +760,8 @@ void prefetch_layer(engine_ctx *c, const DLayer &L) {
 // kernels (two consumers, each normalising x itself) with SARDYNE_MOE_NORM=fused. Off by default:
 // measured on the Qwen3-30B-A3B shape the router's prologue costs more than the norm kernel
 // (327 against 336 tok/s).
-bool moe_norm_fused(int n, const DLayer &L) {
+bool moe_norm_fused(int n, const DLayer &L, const engine_model_info &in) {
+    if (!router_topk_supported(in.dim, in.n_expert, in.n_expert_used, n, true)) return false;
     static const bool fused = [] {
         const char *v = getenv("SARDYNE_MOE_NORM");
         return v && !strcmp(v, "fused");
@@ -779,7 +780,7 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n, const ActIn *nin = nullptr) 
     if (nin) {
         router_topk(nin->x, dim, r.f, r.type, dim, ne, k, n, c->moe_top, c->moe_w, c->moe_probs, c->moe_count, c->st,
                     nin->w, nin->eps);
-    } else if (!r.quant()) {
+    } else if (!r.quant() && router_topk_supported(dim, ne, k, n, false)) {
         router_topk(c->xb, dim, r.f, r.type, dim, ne, k, n, c->moe_top, c->moe_w, c->moe_probs, c->moe_count,
                     c->st);
     } else {
@@ -919,7 +920,7 @@ void forward(engine_ctx *c, int n, int out_rows) {
         if (in.n_expert) {
             std::vector<const DMat *> need = mats_of(L.gateup);
             if (L.gate_inp.quant()) need.push_back(&L.gate_inp);
-            if (moe_norm_fused(n, L)) {
+            if (moe_norm_fused(n, L, in)) {
                 moe_ffn(c, L, n, &ffn_nin);
             } else {
                 want_activations(c, need, c->xb, dim, n, dim, &q8k, &q80);

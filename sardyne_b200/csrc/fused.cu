@@ -421,13 +421,23 @@ void post_qkv(const PostQKV &p, int n_tok, cudaStream_t s) {
     SDY_LAUNCHED();
 }
 
+namespace {
+size_t router_smem(int dim, int ne) {
+    const size_t dp = (size_t)((dim + 3) & ~3);
+    return std::max((size_t)(1 + ROUTER_EPC) * dp, (size_t)2 * ne) * 4;
+}
+}  // namespace
+
+bool router_topk_supported(int dim, int ne, int k, int n_tok, bool norm) {
+    return router_smem(dim, ne) <= 200 * 1024 && n_tok <= 65535 && k <= ne && k <= 64 && (!norm || dim <= 8192);
+}
+
 void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, int n_tok,
                  int32_t *top, float *wout, float *logits, int32_t *counters, cudaStream_t s, const float *norm_w,
                  float norm_eps) {
     if (n_tok <= 0) return;
-    const size_t dp = (size_t)((dim + 3) & ~3);
-    const size_t smem = std::max((size_t)(1 + ROUTER_EPC) * dp, (size_t)2 * ne) * 4;
-    if (smem > 200 * 1024 || n_tok > 65535 || k > ne || (norm_w && dim > 8192)) {
+    const size_t smem = router_smem(dim, ne);
+    if (!router_topk_supported(dim, ne, k, n_tok, norm_w != nullptr)) {
         set_error("router_topk: hidden size %d / %d tokens / top-%d of %d not supported", dim, n_tok, k, ne);
         return;
     }

@@ -58,6 +58,8 @@ struct ExpertPrefetch {
 };
 // Pulls the matrices of the experts named by top[0, n_slots) into L2.
 void expert_prefetch(const ExpertPrefetch &ep, const int32_t *top, int n_slots, cudaStream_t s);
+// Whether router_topk takes this shape (its shared memory holds the CTA's router rows and x).
+bool router_topk_supported(int dim, int ne, int k, int n_tok, bool norm);
 // norm_w: the router input is RMSNorm(x) * norm_w, computed inside the kernel (x the residual).
 void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim, int ne, int k, int n_tok,
                  int32_t *top, float *wout, float *logits, int32_t *counters, cudaStream_t s,
