@@ -694,12 +694,8 @@ void attention(float *out, const float *q, int64_t ldq, const float *kc, const f
     if (n_tok >= PQ && fixed_nkv <= 0 && hd <= 128 && aligned16(q) && ldq % 4 == 0 && aligned16(kc) &&
         aligned16(vc) && n_tok <= 65535 * PQ) {
         const size_t smem = (size_t)pf_smem_floats(hd) * 4;
-        static bool configured = false;
-        if (!configured) {
-            SDY_CUDA(cudaFuncSetAttribute(attention_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          pf_smem_floats(128) * 4));
-            configured = true;
-        }
+        static std::atomic<uint64_t> configured{0};
+        smem_limit_once(attention_prefill_kernel, pf_smem_floats(128) * 4, configured);
         launch(attention_prefill_kernel, dim3(n_head, (n_tok + PQ - 1) / PQ), PF_THREADS, smem, s, out, q, ldq, kc, vc,
                n_tok, n_head, n_kv_head, hd, pos0, pos_dev, stride, scratch);
         SDY_LAUNCHED();
@@ -719,12 +715,8 @@ void attention(float *out, const float *q, int64_t ldq, const float *kc, const f
     if (post) pp = *post;
     if (cluster) {
         const size_t smem = (size_t)ac_smem(n_rep, hd, stride, push).total * 4;
-        static bool configured = false;
-        if (!configured) {
-            SDY_CUDA(cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          AC_SMEM_LIMIT));
-            configured = true;
-        }
+        static std::atomic<uint64_t> configured{0};
+        smem_limit_once(attention_cluster_kernel, AC_SMEM_LIMIT, configured);
         launch(attention_cluster_kernel, dim3(AC, n_kv_head, n_tok), AC_THREADS, smem, s, out, q, ldq, kc, vc, n_head,
                n_kv_head, hd, pos0, pos_dev, stride, fixed_nkv, push, pp);
         SDY_LAUNCHED();
@@ -735,12 +727,8 @@ void attention(float *out, const float *q, int64_t ldq, const float *kc, const f
         return;
     }
     const size_t smem = (size_t)att_smem_floats(hd) * 4;
-    static bool configured = false;
-    if (!configured) {
-        SDY_CUDA(cudaFuncSetAttribute(attention_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      att_smem_floats(2 * ATT_THREADS) * 4));
-        configured = true;
-    }
+    static std::atomic<uint64_t> configured{0};
+    smem_limit_once(attention_head_kernel, att_smem_floats(2 * ATT_THREADS) * 4, configured);
     launch(attention_head_kernel, dim3(n_head, n_tok), ATT_THREADS, smem, s, out, q, ldq, kc, vc, n_head, n_kv_head, hd,
                                                                          pos0, pos_dev, stride, scratch, fixed_nkv);
     SDY_LAUNCHED();

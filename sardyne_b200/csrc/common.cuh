@@ -7,6 +7,7 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <string>
 #include <utility>
 
@@ -117,6 +118,17 @@ bool cuda_check(cudaError_t e, const char *what, const char *file, int line);
 #define SDY_CUDA(call) ::sdy::cuda_check((call), #call, __FILE__, __LINE__)
 // After every kernel launch: count it and surface launch errors.
 void note_launch();
+// Raises `kernel`'s dynamic shared memory limit to `bytes` on the current device the first time
+// it is called there: the attribute is per device, so `done` keeps one bit per device ordinal.
+template <class Kernel>
+inline void smem_limit_once(Kernel kernel, int bytes, std::atomic<uint64_t> &done) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (done.load() & bit) return;
+    if (SDY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) done.fetch_or(bit);
+}
+
 #define SDY_LAUNCHED()                                   \
     do {                                                 \
         ::sdy::note_launch();                            \

@@ -441,11 +441,8 @@ void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim,
         set_error("router_topk: hidden size %d / %d tokens / top-%d of %d not supported", dim, n_tok, k, ne);
         return;
     }
-    static bool configured = false;
-    if (!configured) {
-        SDY_CUDA(cudaFuncSetAttribute(router_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        configured = true;
-    }
+    static std::atomic<uint64_t> configured{0};
+    smem_limit_once(router_topk_kernel, 200 * 1024, configured);
     const bool w_aligned = wtype == T_F32 ? ((uintptr_t)w & 15) == 0 : ((uintptr_t)w & 7) == 0;
     const int vec = dim % 16 == 0 && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0 && w_aligned;
     launch(router_topk_kernel, dim3((ne + ROUTER_EPC - 1) / ROUTER_EPC, n_tok), ROUTER_THREADS, smem, s, x, ldx, w,

@@ -408,20 +408,14 @@ void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, i
     const int64_t tiles_m = (a.g_end - a.g_begin + GM / GROUP_ROWS - 1) / (GM / GROUP_ROWS);
     const dim3 grid((unsigned)tiles_m, (unsigned)((xq.n_tok + GN - 1) / GN));
     if (w.type == T_Q4_K) {
-        static bool configured = false;
+        static std::atomic<uint64_t> configured{0};
         const int smem = g_smem_bytes(3, T_Q4_K);
-        if (!configured) {
-            SDY_CUDA(cudaFuncSetAttribute(qgemm_kernel<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            configured = true;
-        }
+        smem_limit_once(qgemm_kernel<T_Q4_K>, smem, configured);
         launch(qgemm_kernel<T_Q4_K>, grid, G_THREADS, smem, s, a);
     } else {
-        static bool configured = false;
+        static std::atomic<uint64_t> configured{0};
         const int smem = g_smem_bytes(2, T_Q6_K);
-        if (!configured) {
-            SDY_CUDA(cudaFuncSetAttribute(qgemm_kernel<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            configured = true;
-        }
+        smem_limit_once(qgemm_kernel<T_Q6_K>, smem, configured);
         launch(qgemm_kernel<T_Q6_K>, grid, G_THREADS, smem, s, a);
     }
     SDY_LAUNCHED();
@@ -460,20 +454,14 @@ void qgemm_grouped(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq,
     // at most ceil(count_e / GN) tiles per expert: sum <= max_slots / GN + n_expert
     const dim3 grid((unsigned)tiles_m, (unsigned)(max_slots / GN + n_expert));
     if (experts.type == T_Q4_K) {
-        static bool configured = false;
+        static std::atomic<uint64_t> configured{0};
         const int smem = g_smem_bytes(3, T_Q4_K);
-        if (!configured) {
-            SDY_CUDA(cudaFuncSetAttribute(qgemm_kernel<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            configured = true;
-        }
+        smem_limit_once(qgemm_kernel<T_Q4_K>, smem, configured);
         launch(qgemm_kernel<T_Q4_K>, grid, G_THREADS, smem, s, a);
     } else {
-        static bool configured = false;
+        static std::atomic<uint64_t> configured{0};
         const int smem = g_smem_bytes(2, T_Q6_K);
-        if (!configured) {
-            SDY_CUDA(cudaFuncSetAttribute(qgemm_kernel<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            configured = true;
-        }
+        smem_limit_once(qgemm_kernel<T_Q6_K>, smem, configured);
         launch(qgemm_kernel<T_Q6_K>, grid, G_THREADS, smem, s, a);
     }
     SDY_LAUNCHED();

@@ -405,13 +405,7 @@ __global__ void __launch_bounds__(THREADS) qmv2_kernel(Args a, Args b, int na) {
 template <int TYPE, int NT>
 void configure_one() {
     static std::atomic<uint64_t> configured{0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const uint64_t bit = 1ull << (dev & 63);
-    if (!(configured.load() & bit)) {
-        SDY_CUDA(cudaFuncSetAttribute(qmv_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT));
-        configured.fetch_or(bit);
-    }
+    smem_limit_once(qmv_kernel<TYPE, NT>, SMEM_LIMIT, configured);
 }
 
 template <int TYPE, int NT>
@@ -643,13 +637,7 @@ namespace {
 template <int TA, int TB>
 void launch_pair(const Args &a, const Args &b, int na, int grid, int smem, cudaStream_t s) {
     static std::atomic<uint64_t> configured{0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const uint64_t bit = 1ull << (dev & 63);
-    if (!(configured.load() & bit)) {
-        SDY_CUDA(cudaFuncSetAttribute(qmv2_kernel<TA, TB>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT));
-        configured.fetch_or(bit);
-    }
+    smem_limit_once(qmv2_kernel<TA, TB>, SMEM_LIMIT, configured);
     launch(qmv2_kernel<TA, TB>, dim3(grid), THREADS, smem, s, a, b, na);
     SDY_LAUNCHED();
 }
