@@ -49,19 +49,18 @@ struct Nccl {
     const char *(*error_string)(ncclResult_t) = nullptr;
 };
 const Nccl *nccl() {
-    static Nccl n;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
+    static const Nccl n = [] {  // resolved once (thread-safe static initialisation)
+        Nccl r;
         void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
         if (h) {
-            n.get_unique_id = (decltype(n.get_unique_id))dlsym(h, "ncclGetUniqueId");
-            n.comm_init_rank = (decltype(n.comm_init_rank))dlsym(h, "ncclCommInitRank");
-            n.all_reduce = (decltype(n.all_reduce))dlsym(h, "ncclAllReduce");
-            n.comm_destroy = (decltype(n.comm_destroy))dlsym(h, "ncclCommDestroy");
-            n.error_string = (decltype(n.error_string))dlsym(h, "ncclGetErrorString");
+            r.get_unique_id = (decltype(r.get_unique_id))dlsym(h, "ncclGetUniqueId");
+            r.comm_init_rank = (decltype(r.comm_init_rank))dlsym(h, "ncclCommInitRank");
+            r.all_reduce = (decltype(r.all_reduce))dlsym(h, "ncclAllReduce");
+            r.comm_destroy = (decltype(r.comm_destroy))dlsym(h, "ncclCommDestroy");
+            r.error_string = (decltype(r.error_string))dlsym(h, "ncclGetErrorString");
         }
-    }
+        return r;
+    }();
     return n.get_unique_id && n.comm_init_rank && n.all_reduce && n.comm_destroy && n.error_string ? &n : nullptr;
 }
 
