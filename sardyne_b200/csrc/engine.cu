@@ -20,7 +20,9 @@
 #include <string.h>
 
 #include <algorithm>
+#include <iterator>
 #include <string>
+#include <string_view>
 #include <vector>
 
 namespace sdy {
@@ -107,31 +109,40 @@ struct DLayer {
     DMat wo, down, gate_inp;
 };
 
-const char *LAYER_SUFFIXES[] = {
+// The per-layer tensors the loader reads, by role. Their GGUF names ("blk.<i>.<name>") are the
+// file format's; the set is the one the reference runtime accepts (model_llama.c:128-154).
+enum LayerTensor {
+    LT_ATTN_NORM, LT_Q, LT_Q_BIAS, LT_K, LT_K_BIAS, LT_V, LT_V_BIAS, LT_Q_NORM, LT_K_NORM, LT_WO, LT_FFN_NORM,
+    LT_GATE, LT_UP, LT_DOWN, LT_ROUTER, LT_GATE_EXPS, LT_UP_EXPS, LT_DOWN_EXPS, LT_COUNT
+};
+constexpr std::string_view kLayerTensorName[LT_COUNT] = {
     "attn_norm.weight", "attn_q.weight", "attn_q.bias", "attn_k.weight", "attn_k.bias", "attn_v.weight",
     "attn_v.bias", "attn_q_norm.weight", "attn_k_norm.weight", "attn_output.weight", "ffn_norm.weight",
     "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight", "ffn_gate_inp.weight", "ffn_gate_exps.weight",
     "ffn_up_exps.weight", "ffn_down_exps.weight",
 };
+constexpr std::string_view kModelTensorName[] = {"token_embd.weight", "output_norm.weight", "output.weight"};
 
-// Tensor names the runtime knows (model_llama.c:128-154): anything else is a model variant it
-// cannot run, and loading fails.
-bool known_tensor(const char *name, int n_layer) {
-    if (!strcmp(name, "token_embd.weight") || !strcmp(name, "output_norm.weight") || !strcmp(name, "output.weight"))
-        return true;
-    if (strncmp(name, "blk.", 4)) return false;
-    const char *p = name + 4;
-    if (*p < '0' || *p > '9') return false;
-    long idx = 0;
-    while (*p >= '0' && *p <= '9') {
-        idx = idx * 10 + (*p - '0');
-        if (idx >= n_layer) return false;
-        p++;
-    }
-    if (*p++ != '.') return false;
-    for (const char *s : LAYER_SUFFIXES)
-        if (!strcmp(p, s)) return true;
-    return false;
+std::string layer_tensor(int layer, LayerTensor t) {
+    return "blk." + std::to_string(layer) + "." + std::string(kLayerTensorName[t]);
+}
+
+// True when the loader has a use for a tensor of this name in a model of n_layer layers: a
+// model-level name, or "blk.<i>.<layer tensor>" with i < n_layer in decimal digits (leading
+// zeros allowed). Any other tensor marks an architecture variant this runtime cannot run.
+bool runtime_reads(std::string_view name, int n_layer) {
+    for (std::string_view top : kModelTensorName)
+        if (name == top) return true;
+    constexpr std::string_view prefix = "blk.";
+    if (name.substr(0, prefix.size()) != prefix) return false;
+    name.remove_prefix(prefix.size());
+    const size_t ndig = name.find_first_not_of("0123456789");
+    if (ndig == 0 || ndig == std::string_view::npos || name[ndig] != '.') return false;
+    uint64_t layer = 0;  // saturates far above any layer count
+    for (char ch : name.substr(0, ndig)) layer = std::min<uint64_t>(layer * 10 + (uint64_t)(ch - '0'), 1ull << 32);
+    if (layer >= (uint64_t)n_layer) return false;
+    const std::string_view rest = name.substr(ndig + 1);
+    return std::find(std::begin(kLayerTensorName), std::end(kLayerTensorName), rest) != std::end(kLayerTensorName);
 }
 
 bool type_supported(uint32_t t) { return is_quant_weight((int)t) || is_float_weight((int)t); }
@@ -211,126 +222,144 @@ namespace eng {
 
 // ------------------------------------------------------------------------------ metadata
 
-struct Meta {
-    const gguf_file *gf;
-    std::string arch;
-    char *err;
-    size_t len;
-    int64_t key(const char *suffix) const {
-        std::string k = arch + "." + suffix;
-        return gguf_find_kv(gf, k.c_str());
-    }
-    // Required (def < 0) or defaulted integer in 1..2^30; -1 on error (model_llama.c:92-105).
-    int64_t integer(const char *suffix, int64_t def) const {
-        int64_t i = key(suffix);
-        uint64_t v;
-        if (i < 0) {
-            if (def < 0) put_err(err, len, "metadato mancante: %s.%s", arch.c_str(), suffix);
-            return def;
-        }
-        if (gguf_kv_get_u64(gf, i, &v) || v == 0 || v > (1u << 30)) {
-            put_err(err, len, "metadato non valido: %s.%s", arch.c_str(), suffix);
-            return -1;
-        }
-        return (int64_t)v;
-    }
-    int real(const char *suffix, double def, float *out) const {
-        int64_t i = key(suffix);
-        double v = def;
-        if (i < 0 && def < 0) {
-            put_err(err, len, "metadato mancante: %s.%s", arch.c_str(), suffix);
-            return -1;
-        }
-        if (i >= 0 && gguf_kv_get_f64(gf, i, &v)) {
-            put_err(err, len, "metadato non valido: %s.%s", arch.c_str(), suffix);
-            return -1;
-        }
-        if (!(v > 0.0) || v > 1e12) {
-            put_err(err, len, "valore non valido per %s.%s", arch.c_str(), suffix);
-            return -1;
-        }
-        *out = (float)v;
-        return 0;
-    }
-};
-
 const gguf_tensor *find(const gguf_file *gf, const char *name) {
     int64_t i = gguf_find_tensor(gf, name);
     return i < 0 ? nullptr : gguf_get_tensor(gf, (uint64_t)i);
 }
 
-// Same checks and messages as the reference's read_config (model_llama.c:225-319).
+// The model header, checked as a table. Each row is one "<arch>.<key>" entry and the
+// engine_model_info field it fills; rows run in order and the first failure is reported. The
+// files accepted and the messages of the refused ones are the reference runtime's
+// (model_llama.c:225-319), because callers and tests match those texts.
+using I = engine_model_info;
+using IntField = int32_t I::*;
+using RealField = float I::*;
+
+struct HeaderRow {
+    const char *key;
+    bool moe_only;
+    IntField int_field;    // integer entry in 1..2^30, stored here ...
+    RealField real_field;  // ... or real entry in (0, 1e12], stored here
+    // Value taken when the key is absent, from the fields read so far (nullptr: required).
+    double (*absent)(const I &);
+    const char *zero_msg;  // failure when the absent-key value is 0
+    IntField must_equal;   // the entry must equal this field (and is not stored) ...
+    const char *unequal;   // ... else this failure, whatever made it differ
+    // Checked once the row is read: a failure message, or nullptr.
+    const char *(*rule)(const I &, char *buf, size_t len);
+};
+
+const char *used_within_count(const I &in, char *buf, size_t len) {
+    if (in.n_expert_used <= in.n_expert) return nullptr;
+    snprintf(buf, len, "expert_used_count=%d oltre expert_count=%d", in.n_expert_used, in.n_expert);
+    return buf;
+}
+const char *used_within_combine(const I &in, char *buf, size_t len) {
+    if (in.n_expert_used <= 64) return nullptr;  // moe_combine_kernel orders at most 64 slots per token
+    snprintf(buf, len, "expert_used_count=%d oltre il massimo di 64 di questa build", in.n_expert_used);
+    return buf;
+}
+const char *heads_consistent(const I &in, char *, size_t) {
+    const bool ok = in.n_head % in.n_kv_head == 0 && in.head_dim % 2 == 0;
+    return ok ? nullptr : "teste o head_dim non validi (n_head % n_kv_head, head_dim pari)";
+}
+double experts_share_ffn(const I &in) { return in.ffn_dim / in.n_expert_used; }
+double kv_heads_default(const I &in) { return in.n_head; }
+double head_dim_default(const I &in) { return in.dim / in.n_head; }
+double same_as_head_dim(const I &in) { return in.head_dim; }
+double context_default(const I &) { return 2048; }
+double theta_default(const I &) { return 10000; }
+
+const HeaderRow kHeaderRows[] = {
+    {"embedding_length", false, &I::dim, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr},
+    {"block_count", false, &I::n_layer, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr},
+    {"feed_forward_length", false, &I::ffn_dim, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr},
+    {"expert_count", true, &I::n_expert, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr},
+    {"expert_used_count", true, &I::n_expert_used, nullptr, nullptr, nullptr, nullptr, nullptr, used_within_count},
+    {"expert_feed_forward_length", true, &I::ffn_exp_dim, nullptr, experts_share_ffn,
+     "dimensione degli esperti nulla", nullptr, nullptr, used_within_combine},
+    {"attention.head_count", false, &I::n_head, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr},
+    {"attention.head_count_kv", false, &I::n_kv_head, nullptr, kv_heads_default, nullptr, nullptr, nullptr, nullptr},
+    {"attention.key_length", false, &I::head_dim, nullptr, head_dim_default, "head_dim nullo", nullptr, nullptr,
+     nullptr},
+    {"attention.value_length", false, nullptr, nullptr, same_as_head_dim, nullptr, &I::head_dim,
+     "key_length diverso da value_length", nullptr},
+    {"rope.dimension_count", false, nullptr, nullptr, same_as_head_dim, nullptr, &I::head_dim,
+     "RoPE parziale (rope.dimension_count < head_dim) non supportata", nullptr},
+    {"context_length", false, &I::max_pos, nullptr, context_default, nullptr, nullptr, nullptr, nullptr},
+    {"attention.layer_norm_rms_epsilon", false, nullptr, &I::norm_eps, nullptr, nullptr, nullptr, nullptr, nullptr},
+    {"rope.freq_base", false, nullptr, &I::rope_theta, theta_default, nullptr, nullptr, nullptr, heads_consistent},
+};
+
+// One row: reads (or defaults) its entry and stores or compares it. nullptr, or the failure.
+const char *check_row(const gguf_file *gf, const std::string &arch, const HeaderRow &r, I *in, char *buf,
+                      size_t len) {
+    const std::string key = arch + "." + r.key;
+    const int64_t at = gguf_find_kv(gf, key.c_str());
+    const bool is_int = r.real_field == nullptr;
+    double v = 0;
+    const char *fail = nullptr;
+    if (at < 0 && !r.absent) {
+        snprintf(buf, len, "metadato mancante: %s", key.c_str());
+        fail = buf;
+    } else if (at < 0) {
+        v = r.absent(*in);
+        if (is_int && v == 0 && r.zero_msg) fail = r.zero_msg;
+    } else if (is_int) {
+        uint64_t u = 0;
+        if (gguf_kv_get_u64(gf, at, &u) || u == 0 || u > (1u << 30)) {
+            snprintf(buf, len, "metadato non valido: %s", key.c_str());
+            fail = buf;
+        }
+        v = (double)u;
+    } else if (gguf_kv_get_f64(gf, at, &v)) {
+        snprintf(buf, len, "metadato non valido: %s", key.c_str());
+        fail = buf;
+    }
+    if (!fail && !is_int && (!(v > 0.0) || v > 1e12)) {
+        snprintf(buf, len, "valore non valido per %s", key.c_str());
+        fail = buf;
+    }
+    if (r.must_equal) return fail || (int64_t)v != in->*r.must_equal ? r.unequal : nullptr;
+    if (fail) return fail;
+    if (is_int) in->*r.int_field = (int32_t)v;
+    else in->*r.real_field = (float)v;
+    return r.rule ? r.rule(*in, buf, len) : nullptr;
+}
+
+// Header and tensor-name checks of a GGUF before anything is uploaded.
 int read_config(engine_model *m, char *err, size_t len) {
     const gguf_file *gf = m->gf;
-    uint64_t n;
-    const char *arch = gguf_kv_get_str(gf, gguf_find_kv(gf, "general.architecture"), &n);
-    if (!arch || n == 0 || n >= 32) {
+    I *in = &m->info;
+    uint64_t n = 0;
+    const char *arch_s = gguf_kv_get_str(gf, gguf_find_kv(gf, "general.architecture"), &n);
+    if (!arch_s || n == 0 || n >= 32) {
         put_err(err, len, "general.architecture mancante o non valido");
         return -1;
     }
-    Meta mt{gf, std::string(arch, n), err, len};
-    engine_model_info *in = &m->info;
-    if (mt.arch == "llama") in->rope_interleaved = 1;
-    else if (mt.arch == "qwen2" || mt.arch == "qwen3" || mt.arch == "qwen3moe") in->rope_interleaved = 0;
-    else {
-        put_err(err, len, "architettura %s non supportata", mt.arch.c_str());
+    const std::string arch(arch_s, n);
+    // llama rotates interleaved pairs; the qwen families rotate the two halves of a head
+    static const std::pair<const char *, int> kArchs[] = {{"llama", 1}, {"qwen2", 0}, {"qwen3", 0}, {"qwen3moe", 0}};
+    const auto *a = std::find_if(std::begin(kArchs), std::end(kArchs), [&](auto &p) { return arch == p.first; });
+    if (a == std::end(kArchs)) {
+        put_err(err, len, "architettura %s non supportata", arch.c_str());
         return -1;
     }
-    const char *scaling = gguf_kv_get_str(gf, mt.key("rope.scaling.type"), &n);
-    if ((scaling && !(n == 4 && !memcmp(scaling, "none", 4))) || find(gf, "rope_freqs.weight")) {
+    in->rope_interleaved = a->second;
+    const bool moe = arch == "qwen3moe";
+    const char *scaling = gguf_kv_get_str(gf, gguf_find_kv(gf, (arch + ".rope.scaling.type").c_str()), &n);
+    const bool plain_rope = !scaling || std::string_view(scaling, n) == "none";
+    if (!plain_rope || find(gf, "rope_freqs.weight")) {
         put_err(err, len, "rope scaling (anche 'llama3' via rope_freqs.weight) non supportato");
         return -1;
     }
-    int64_t v;
-    if ((v = mt.integer("embedding_length", -1)) < 0) return -1;
-    in->dim = (int32_t)v;
-    if ((v = mt.integer("block_count", -1)) < 0) return -1;
-    in->n_layer = (int32_t)v;
-    if ((v = mt.integer("feed_forward_length", -1)) < 0) return -1;
-    in->ffn_dim = (int32_t)v;
-    if (mt.arch == "qwen3moe") {
-        if ((v = mt.integer("expert_count", -1)) < 0) return -1;
-        in->n_expert = (int32_t)v;
-        if ((v = mt.integer("expert_used_count", -1)) < 0) return -1;
-        in->n_expert_used = (int32_t)v;
-        if (in->n_expert_used > in->n_expert) {
-            put_err(err, len, "expert_used_count=%d oltre expert_count=%d", in->n_expert_used, in->n_expert);
+    char buf[192];
+    for (const HeaderRow &r : kHeaderRows) {
+        if (r.moe_only && !moe) continue;
+        if (const char *fail = check_row(gf, arch, r, in, buf, sizeof buf)) {
+            put_err(err, len, "%s", fail);
             return -1;
         }
-        if ((v = mt.integer("expert_feed_forward_length", in->ffn_dim / in->n_expert_used)) <= 0) {
-            if (v == 0) put_err(err, len, "dimensione degli esperti nulla");
-            return -1;
-        }
-        in->ffn_exp_dim = (int32_t)v;
-        if (in->n_expert_used > 64) {  // moe_combine_kernel orders at most 64 slots per token
-            put_err(err, len, "expert_used_count=%d oltre il massimo di 64 di questa build", in->n_expert_used);
-            return -1;
-        }
-    }
-    if ((v = mt.integer("attention.head_count", -1)) < 0) return -1;
-    in->n_head = (int32_t)v;
-    if ((v = mt.integer("attention.head_count_kv", in->n_head)) < 0) return -1;
-    in->n_kv_head = (int32_t)v;
-    if ((v = mt.integer("attention.key_length", in->dim / in->n_head)) <= 0) {
-        if (v == 0) put_err(err, len, "head_dim nullo");
-        return -1;
-    }
-    in->head_dim = (int32_t)v;
-    if (mt.integer("attention.value_length", in->head_dim) != in->head_dim) {
-        put_err(err, len, "key_length diverso da value_length");
-        return -1;
-    }
-    if (mt.integer("rope.dimension_count", in->head_dim) != in->head_dim) {
-        put_err(err, len, "RoPE parziale (rope.dimension_count < head_dim) non supportata");
-        return -1;
-    }
-    if ((v = mt.integer("context_length", 2048)) < 0) return -1;
-    in->max_pos = (int32_t)v;
-    if (mt.real("attention.layer_norm_rms_epsilon", -1.0, &in->norm_eps)) return -1;
-    if (mt.real("rope.freq_base", 10000.0, &in->rope_theta)) return -1;
-    if (in->n_head % in->n_kv_head || in->head_dim % 2) {
-        put_err(err, len, "teste o head_dim non validi (n_head %% n_kv_head, head_dim pari)");
-        return -1;
     }
     const gguf_tensor *emb = find(gf, "token_embd.weight");
     if (!emb || emb->n_dims != 2 || emb->ne[1] == 0 || emb->ne[1] > (1u << 30)) {
@@ -339,11 +368,11 @@ int read_config(engine_model *m, char *err, size_t len) {
     }
     in->n_vocab = (int32_t)emb->ne[1];
     in->tied_embeddings = find(gf, "output.weight") == nullptr;
-    in->qkv_bias = find(gf, "blk.0.attn_q.bias") != nullptr;
-    in->qk_norm = find(gf, "blk.0.attn_q_norm.weight") != nullptr;
+    in->qkv_bias = find(gf, layer_tensor(0, LT_Q_BIAS).c_str()) != nullptr;
+    in->qk_norm = find(gf, layer_tensor(0, LT_Q_NORM).c_str()) != nullptr;
     for (uint64_t i = 0; i < gguf_n_tensors(gf); i++) {
         const char *name = gguf_get_tensor(gf, i)->name;
-        if (!known_tensor(name, in->n_layer)) {
+        if (!runtime_reads(name, in->n_layer)) {
             put_err(err, len, "tensore non supportato: %s", name);
             return -1;
         }
@@ -1110,33 +1139,33 @@ engine_model *engine_model_load(const char *path, char *err, size_t err_len) {
     }
     for (int l = 0; ok && l < in.n_layer; l++) {
         DLayer &L = m->layers[l];
-        auto nm = [&](const char *suffix) { return "blk." + std::to_string(l) + "." + suffix; };
-        ok = !get_vector(m, nm("attn_norm.weight").c_str(), dim, &L.attn_norm, err, err_len) &&
-             !get_vector(m, nm("ffn_norm.weight").c_str(), dim, &L.ffn_norm, err, err_len) &&
-             !get_proj(m, {nm("attn_q.weight"), nm("attn_k.weight"), nm("attn_v.weight")}, {q_dim, kv_dim, kv_dim},
+        auto nm = [&](LayerTensor t) { return layer_tensor(l, t); };
+        ok = !get_vector(m, nm(LT_ATTN_NORM).c_str(), dim, &L.attn_norm, err, err_len) &&
+             !get_vector(m, nm(LT_FFN_NORM).c_str(), dim, &L.ffn_norm, err, err_len) &&
+             !get_proj(m, {nm(LT_Q), nm(LT_K), nm(LT_V)}, {q_dim, kv_dim, kv_dim},
                        dim, 0, &L.qkv, err, err_len) &&
-             !get_tensor(m, nm("attn_output.weight").c_str(), q_dim, dim, 0, &L.wo, err, err_len);
+             !get_tensor(m, nm(LT_WO).c_str(), q_dim, dim, 0, &L.wo, err, err_len);
         if (!ok) break;
         if (in.n_expert) {
             int ne = in.n_expert, fe = in.ffn_exp_dim;
-            ok = !get_tensor(m, nm("ffn_gate_inp.weight").c_str(), dim, ne, 0, &L.gate_inp, err, err_len) &&
-                 !get_proj(m, {nm("ffn_gate_exps.weight"), nm("ffn_up_exps.weight")}, {fe, fe}, dim, ne, &L.gateup, err,
+            ok = !get_tensor(m, nm(LT_ROUTER).c_str(), dim, ne, 0, &L.gate_inp, err, err_len) &&
+                 !get_proj(m, {nm(LT_GATE_EXPS), nm(LT_UP_EXPS)}, {fe, fe}, dim, ne, &L.gateup, err,
                            err_len, 0, -1, m->e0, m->e1) &&
-                 !get_tensor(m, nm("ffn_down_exps.weight").c_str(), fe, dim, ne, &L.down, err, err_len, 0, -1, m->e0,
+                 !get_tensor(m, nm(LT_DOWN_EXPS).c_str(), fe, dim, ne, &L.down, err, err_len, 0, -1, m->e0,
                              m->e1);
         } else {
-            ok = !get_proj(m, {nm("ffn_gate.weight"), nm("ffn_up.weight")}, {in.ffn_dim, in.ffn_dim}, dim, 0,
+            ok = !get_proj(m, {nm(LT_GATE), nm(LT_UP)}, {in.ffn_dim, in.ffn_dim}, dim, 0,
                            &L.gateup, err, err_len, m->f0, m->f1) &&
-                 !get_tensor(m, nm("ffn_down.weight").c_str(), in.ffn_dim, dim, 0, &L.down, err, err_len, m->d0,
+                 !get_tensor(m, nm(LT_DOWN).c_str(), in.ffn_dim, dim, 0, &L.down, err, err_len, m->d0,
                              m->d1);
         }
         if (ok && in.qkv_bias)
-            ok = !get_vector(m, nm("attn_q.bias").c_str(), q_dim, &L.bq, err, err_len) &&
-                 !get_vector(m, nm("attn_k.bias").c_str(), kv_dim, &L.bk, err, err_len) &&
-                 !get_vector(m, nm("attn_v.bias").c_str(), kv_dim, &L.bv, err, err_len);
+            ok = !get_vector(m, nm(LT_Q_BIAS).c_str(), q_dim, &L.bq, err, err_len) &&
+                 !get_vector(m, nm(LT_K_BIAS).c_str(), kv_dim, &L.bk, err, err_len) &&
+                 !get_vector(m, nm(LT_V_BIAS).c_str(), kv_dim, &L.bv, err, err_len);
         if (ok && in.qk_norm)
-            ok = !get_vector(m, nm("attn_q_norm.weight").c_str(), in.head_dim, &L.q_norm, err, err_len) &&
-                 !get_vector(m, nm("attn_k_norm.weight").c_str(), in.head_dim, &L.k_norm, err, err_len);
+            ok = !get_vector(m, nm(LT_Q_NORM).c_str(), in.head_dim, &L.q_norm, err, err_len) &&
+                 !get_vector(m, nm(LT_K_NORM).c_str(), in.head_dim, &L.k_norm, err, err_len);
     }
     if (m->raw) {
         cudaFree(m->raw);
