@@ -162,17 +162,18 @@ int sdy_quantize_rows_dev(int vtype, const float *d_x, int n_tok, int n_in, void
 int sdy_qmatvec_dev(const void *w, const void *d_xq, int n_tok, float *d_out, int64_t ldo, int64_t row0,
                     int64_t row1, void *stream);
 
-/* No counterpart in the reference. For callers that cannot allocate device memory when they
- * call (during a CUDA stream capture, in an allocation-free serving loop, or under a framework
- * that owns every device allocation): f32 activations d_x [n_tok][n_in] are quantized and
- * multiplied by w (d_out[t*ldo + (r - row0)] = w[r] . x[t], as sdy_quantize_rows_dev +
- * sdy_qmatvec_dev) with no scratch argument and no allocation. The quantized activations live
- * in a fixed 512 KiB device array inside the library (held by every GPU that loads it until
- * exit): requests that need more (sdy_xq_bytes > 512 KiB, e.g. more than 8 tokens of 16384
- * elements) return -1 with a message and launch nothing. The first call on a device looks up
- * the array's address with that device current; make it before any stream capture. All calls
- * on a device share the array: calls whose GPU work may overlap (unordered streams) race.
- * 0 or -1 (sdy_last_error). */
+/* No counterpart in the reference. For callers that cannot allocate device memory where they
+ * call: a host framework that accounts for all device memory through its own pool, or a serving
+ * loop that keeps cudaMalloc/cudaFree (which can stall or synchronise the device) out of its
+ * steady state. f32 activations d_x [n_tok][n_in] are quantized and multiplied by w
+ * (d_out[t*ldo + (r - row0)] = w[r] . x[t], as sdy_quantize_rows_dev + sdy_qmatvec_dev) with no
+ * scratch argument and no allocation. The quantized activations live in a fixed 512 KiB device
+ * array inside the library (held by every GPU that loads it until exit): requests that need
+ * more (sdy_xq_bytes(vtype, n_in, n_tok) > 512 KiB; for 16384-element rows, more than 26 tokens)
+ * return -1 with a message and launch nothing. The first call on a device looks up the array's
+ * address with that device current and keeps it: make it before any stream capture, and do not
+ * reset the device afterwards. All calls on a device share the array: calls whose GPU work may
+ * overlap (unordered streams) race. 0 or -1 (sdy_last_error). */
 int sdy_qmatvec_f32_noalloc(const void *w, const float *d_x, int n_tok, float *d_out, int64_t ldo, int64_t row0,
                             int64_t row1, void *stream);
 

@@ -4,17 +4,21 @@
 // sdy_quantize_rows_dev followed by sdy_qmatvec_dev, but it takes no scratch buffer from the
 // caller and allocates none: the quantized activations live in g_noalloc_scratch, a fixed
 // file-scope device array that every GPU loading this library holds until the process exits.
-// It is meant for callers that must not call cudaMalloc/cudaFree or a framework allocator at
-// this point of their program: code running while a CUDA stream is being captured, a serving
-// loop that keeps all allocation out of its steady state, or a host framework that owns every
-// device allocation itself. The caller still provides the weights (an sdy_qmat_upload handle),
-// the activations and the output, all in device memory.
+// It serves callers that must not call cudaMalloc/cudaFree or a framework allocator where they
+// call it: a host framework that accounts for every byte of device memory through its own pool
+// (a library allocation behind its back breaks that accounting), and serving loops that keep
+// allocation out of their steady state (cudaFree waits for the whole device, and a fresh
+// cudaMalloc can stall the step that makes it). The caller still provides the weights (an
+// sdy_qmat_upload handle), the activations and the output, all in device memory.
 //
 // Rules of use (also stated in include/sardyne_b200.h):
-//   * at most NOALLOC_SCRATCH_BYTES of quantized activations per call; larger requests fail
-//     with -1 and a message in sdy_last_error, before anything is launched;
+//   * at most NOALLOC_SCRATCH_BYTES of quantized activations per call (sdy_xq_bytes; for
+//     16384-element rows that is 26 tokens); larger requests fail with -1 and a message in
+//     sdy_last_error, before anything is launched;
 //   * the first call on a device looks up the array's device address (cudaGetSymbolAddress)
-//     with that device current; make that first call before any stream capture begins;
+//     with that device current and keeps it for the process: make that first call before any
+//     stream capture begins, and do not reset the device (cudaDeviceReset) afterwards, since
+//     the kept address would then be stale;
 //   * every call on a device shares the one array, so calls whose GPU work overlaps in time
 //     (different streams, no ordering between them) race on it and must not be issued;
 //   * the array keeps whatever the last call left there. Nothing needs clearing: each call

@@ -1,6 +1,6 @@
 """Generate the golden vectors that pin the CPU oracle (run where the reference is mounted).
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py <reference source tree>   (or SARDYNE_REFERENCE=<tree>)
 
 Everything stored here is produced by the reference itself:
   * block bytes from the reference's own fixture generator ``random_blocks``
@@ -20,7 +20,7 @@ import numpy as np
 
 HERE = pathlib.Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = pathlib.Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+REF = pathlib.Path(sys.argv[1] if len(sys.argv) > 1 else os.environ["SARDYNE_REFERENCE"])
 os.environ["SARDYNE_LIB"] = str(REPO / "oracle" / "_ref" / "libsardyne_ref.so")
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(REF / "tests"))

@@ -1,8 +1,10 @@
-"""sdy_qmatvec_f32_noalloc: the entry point for callers that cannot allocate device memory
-(inside a stream capture, in an allocation-free serving loop, under a framework that owns all
-device allocations). Its output must equal the allocating entry points' (op_matmul through
-host buffers, and sdy_quantize_rows_dev + sdy_qmatvec_dev), bit for bit as every product
-test here, on consecutive calls that reuse its one internal scratch array.
+"""sdy_qmatvec_f32_noalloc: the entry point for callers that cannot allocate device memory where
+they call it (a host framework that accounts for all device memory through its own pool, or a
+serving loop that keeps cudaMalloc/cudaFree out of its steady state). Its output must equal the
+allocating entry points' (op_matmul through host buffers, and sdy_quantize_rows_dev +
+sdy_qmatvec_dev), bit for bit as every product test here, on consecutive calls that reuse its one
+internal scratch array, on both the CUDA-core matvec (under 32 tokens) and the tensor-core route
+(32 tokens and more for Q4_K/Q6_K).
 
 The file name sorts last so that a run stopping at the first failure has run everything else.
 """
@@ -36,7 +38,10 @@ def test_noalloc_matches_allocating_entry_points(kind):
         rng = np.random.default_rng(7)
         # two calls in a row with different data and token counts: the shared scratch keeps
         # the first call's contents when the second starts
-        for n_tok, (r0, r1) in [(5, (0, n_out)), (2, (129, 871))]:
+        calls = [(5, (0, n_out)), (2, (129, 871))]
+        if kind in ("Q4_K", "Q6_K"):
+            calls.append((40, (8, 1000)))  # 32 tokens and more: the tensor-core GEMM
+        for n_tok, (r0, r1) in calls:
             x = rng.standard_normal((n_tok, n_in)).astype(np.float32)
             dx = torch.from_numpy(x).cuda()
             got = torch.full((n_tok, r1 - r0), float("nan"), device="cuda")
@@ -58,6 +63,7 @@ def test_noalloc_matches_allocating_entry_points(kind):
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch():
+    """512 KiB of quantized activations: 26 tokens of 16384 elements fit, 27 do not."""
     import torch
 
     lib = capi.lib()
@@ -66,11 +72,14 @@ def test_noalloc_rejects_requests_beyond_its_scratch():
     h = lib.sdy_qmat_upload(w.ctypes.data, oracle.TYPE_ID["Q4_K"], n_out, n_in)
     assert h, capi.last_error()
     try:
-        n_tok = 32  # 32 x 16384 int8 alone is 512 KiB: over the limit
-        x = torch.zeros((n_tok, n_in), device="cuda")
-        out = torch.zeros((n_tok, n_out), device="cuda")
-        assert lib.sdy_qmatvec_f32_noalloc(h, vp(x), n_tok, vp(out), n_out, 0, n_out, None) == -1
+        assert lib.sdy_xq_bytes(15, n_in, 26) <= 512 * 1024 < lib.sdy_xq_bytes(15, n_in, 27)
+        x = torch.zeros((27, n_in), device="cuda")
+        out = torch.zeros((27, n_out), device="cuda")
+        assert lib.sdy_qmatvec_f32_noalloc(h, vp(x), 27, vp(out), n_out, 0, n_out, None) == -1
         assert b"scratch" in lib.sdy_last_error()
         lib.sdy_clear_error()
+        assert lib.sdy_qmatvec_f32_noalloc(h, vp(x), 26, vp(out), n_out, 0, n_out, None) == 0, capi.last_error()
+        torch.cuda.synchronize()
+        assert not out[:26].any()  # zero activations give zero products
     finally:
         lib.sdy_qmat_free(h)
