@@ -15,11 +15,18 @@ is weight+activation bytes streamed per second (GB/s).
   e2e    the same products through the reference-facing C-ABI (op_matmul: host f32 activations
          in pinned memory, host outputs), weights resident after sdy_weights_register (the
          counterpart of the reference's mmap); includes the H2D copy of x and the D2H of y.
+  decode the second half of the metric, in the same line: BASELINE config 5 (Qwen3-30B-A3B
+         shape, random-init Q4_K_M mix) through engine_eval, host token ids in and host logits
+         out: a 256-token prompt, then 256 greedy decode steps; tok/s, prefill tok/s, the
+         whole-step HBM roofline, and the reference engine's own CPU decode on a bounded sample.
   --impl reference  the reference's own CPU kernels (oracle/_ref/libsardyne_ref.so, built from
-         its sources) on all host threads, row ranges split as its thread pool does.
+         its sources) on all host threads, row ranges split as its thread pool does, and its
+         engine's CPU decode of the same model.
 
-Multi-GPU (torchrun, one rank per GPU): every rank runs its own copy of the sweep (independent
-matrices, no collective on the data path): weak scaling, value = all ranks' bytes / max time.
+Multi-GPU (torchrun, one rank per GPU): every matrix of the sweep is split by rows over the
+ranks and each step ends with one NCCL all-gather of the y slices (strong scaling: value = the
+full matrices' bytes / the slowest rank's time); decode runs the sharded engine (experts split
+across the ranks, NCCL inside the engine), one token stream, times as the max over ranks.
 """
 import argparse
 import concurrent.futures as cf
@@ -211,14 +218,26 @@ def run_reference_arm(args, rank, world):
                              "sample": f"each step: the six matrices with LM heads cut to 18992 rows "
                                        f"({nbytes / 1e6:.0f} MB), reference AVX2 kernels on {threads} threads"},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not args.no_decode:
+        from sardyne_b200 import synth
+        path = synth.baseline_model("qwen3moe", args.model_dir)
+        n_prompt = DECODE_MODELS["qwen3moe"][0]
+        info_vocab = synth.QWEN3_30B_A3B["vocab"]
+        prompt = np.random.default_rng(0).integers(0, info_vocab, n_prompt).tolist()
+        d = decode_reference("qwen3moe", path, prompt)
+        line["decode"] = {"metric": "decode tok/s qwen3moe shape (greedy, e2e through engine_eval)",
+                          "value": d["value"], "unit": "tok/s", "prefill_tok_s": d["prefill_tok_s"],
+                          "cpu_baseline": d}
     print(json.dumps(line))
     return 0
 
 
-def config():
-    return {"workload": WORKLOAD, "formats": FORMATS, "shapes_out_in": SHAPES, "batch": 1,
-            "l2": "inputs larger than L2: 492 MB of weights per step against a 126 MB L2",
-            "weights": "N(0,0.02), package quantizer; LM heads from a pool of quantized Gaussian blocks"}
+def config(world=1):
+    c = {"workload": WORKLOAD, "formats": FORMATS, "shapes_out_in": SHAPES, "batch": 1,
+         "l2": "inputs larger than L2: 492 MB of weights per step against a 126 MB L2",
+         "weights": "N(0,0.02), package quantizer; LM heads from a pool of quantized Gaussian blocks"}
+    c["parallelism"] = f"rows of every matrix split over {world} GPUs, y all-gathered" if world > 1 else "1 GPU"
+    return c
 
 
 # ------------------------------------------------------------------------------ B200 arm
@@ -242,47 +261,83 @@ def load_traffic():
     return None
 
 
+def shard_rows(n_out, rank, world):
+    """Rows [r0, r1) of an n_out-row matrix for `rank` of `world`: whole 8-row groups, as the
+    engine shards its matrices (sdy_shard_range)."""
+    from sardyne_b200 import capi
+    b, e = ctypes.c_int64(), ctypes.c_int64()
+    capi.lib().sdy_shard_range(n_out, world, rank, 8, ctypes.byref(b), ctypes.byref(e))
+    return b.value, e.value
+
+
 def run_b200(args, rank, world, local_rank):
+    """The config-2 sweep at batch 1. With N ranks every matrix is split by rows (whole 8-row
+    groups): each GPU streams its slice and the step ends with one all-gather of every matrix's
+    y slices (NCCL), so value = all bytes of the full matrices / the slowest rank's time."""
     import torch
+    import torch.distributed as dist
     from sardyne_b200 import capi
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     lib = capi.lib()
-    mats, xs = make_inputs(only=args.only)
-    if not mats:
+    full, xs = make_inputs(only=args.only)
+    if not full:
         raise SystemExit(f"--only {args.only}: no such matrix in the sweep")
     stream = torch.cuda.Stream(device=dev)
     sp = ctypes.c_void_p(stream.cuda_stream)
 
-    # device-resident inputs
-    handles, d_out, d_x, d_xq = [], {}, {}, {}
-    for fmt, n_out, n_in, w in mats:
+    # this rank's row slices; each matrix's y slice goes to a fixed place of the gather buffer
+    mats, ranges, share_off, share = [], [], [], 0
+    for fmt, n_out, n_in, w in full:
+        r0, r1 = shard_rows(n_out, rank, world)
+        mats.append((fmt, r1 - r0, n_in, np.ascontiguousarray(w[r0:r1])))
+        ranges.append((r0, r1))
+        share_off.append(share)
+        share += max(e - b for b, e in (shard_rows(n_out, q, world) for q in range(world)))
+    handles, d_out, d_x, d_xq = [], [], {}, {}
+    send = torch.zeros(share, dtype=torch.float32, device=dev)
+    recv = torch.zeros(world * share, dtype=torch.float32, device=dev) if world > 1 else None
+    for i, (fmt, n_out, n_in, w) in enumerate(mats):
         h = lib.sdy_qmat_upload(w.ctypes.data, TYPE_ID[fmt], n_out, n_in)
         if not h:
             raise RuntimeError(capi.last_error())
         handles.append(h)
-        d_out[(fmt, n_out, n_in)] = torch.empty(n_out, dtype=torch.float32, device=dev)
+        d_out.append(send[share_off[i]:share_off[i] + n_out])
     for n_in, x in xs.items():
         d_x[n_in] = torch.from_numpy(x).to(dev)
         d_xq[n_in] = torch.empty(lib.sdy_xq_bytes(TYPE_ID["Q8_K"], n_in, 1), dtype=torch.uint8, device=dev)
     dominant = max(range(len(mats)), key=lambda i: alg_bytes(*mats[i][:3]))
     step_bytes = sum(alg_bytes(fmt, n_out, n_in) for fmt, n_out, n_in, _ in mats)
 
-    def step(ev=None):
+    def matvecs(ev=None):
         for i, (fmt, n_out, n_in, _) in enumerate(mats):
             lib.sdy_quantize_rows_dev(TYPE_ID["Q8_K"], ctypes.c_void_p(d_x[n_in].data_ptr()), 1, n_in,
                                       ctypes.c_void_p(d_xq[n_in].data_ptr()), sp)
             if ev is not None and i == dominant:
                 ev[0].record(stream)
             lib.sdy_qmatvec_dev(handles[i], ctypes.c_void_p(d_xq[n_in].data_ptr()), 1,
-                                ctypes.c_void_p(d_out[(fmt, n_out, n_in)].data_ptr()), n_out, 0, n_out, sp)
+                                ctypes.c_void_p(d_out[i].data_ptr()), n_out, 0, n_out, sp)
             if ev is not None and i == dominant:
                 ev[1].record(stream)
 
+    def step(ev=None):
+        matvecs(ev)
+        if world > 1:  # every rank ends the step with every matrix's full y
+            dist.all_gather_into_tensor(recv, send)
+
+    def gathered_y(i):
+        if world == 1:
+            return d_out[i]
+        parts = []
+        for q in range(world):
+            b, e = shard_rows(full[i][1], q, world)
+            parts.append(recv[q * share + share_off[i]: q * share + share_off[i] + (e - b)])
+        return torch.cat(parts)
+
     def barrier():
         if world > 1:
-            torch.distributed.barrier()
+            dist.barrier()
 
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
@@ -290,7 +345,7 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.synchronize()
     capi.check()
 
-    # per-matrix device time (informational breakdown, separate from the timed region)
+    # per-matrix device time of this rank's slices (informational, outside the timed region)
     per = []
     for i, (fmt, n_out, n_in, _) in enumerate(mats):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -301,19 +356,22 @@ def run_b200(args, rank, world, local_rank):
                 if j == i:
                     continue
                 lib.sdy_qmatvec_dev(handles[j], ctypes.c_void_p(d_xq[i2].data_ptr()), 1,
-                                    ctypes.c_void_p(d_out[(f2, o2, i2)].data_ptr()), o2, 0, o2, sp)
+                                    ctypes.c_void_p(d_out[j].data_ptr()), o2, 0, o2, sp)
         e1.record(stream)
         e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e2.record(stream)
         for _ in range(reps):
             for j, (f2, o2, i2, _) in enumerate(mats):
                 lib.sdy_qmatvec_dev(handles[j], ctypes.c_void_p(d_xq[i2].data_ptr()), 1,
-                                    ctypes.c_void_p(d_out[(f2, o2, i2)].data_ptr()), o2, 0, o2, sp)
+                                    ctypes.c_void_p(d_out[j].data_ptr()), o2, 0, o2, sp)
         e3.record(stream)
         torch.cuda.synchronize()
         ms = (e2.elapsed_time(e3) - e0.elapsed_time(e1)) / reps
         per.append({"format": fmt, "n_out": n_out, "n_in": n_in, "us": round(ms * 1e3, 2),
                     "GB/s": round(alg_bytes(fmt, n_out, n_in) / (ms * 1e-3) / 1e9, 1)})
+    with torch.cuda.stream(stream):
+        step()  # leave every rank's full y in place again
+    torch.cuda.synchronize()
 
     # timed region
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -332,28 +390,40 @@ def run_b200(args, rank, world, local_rank):
     launches = lib.sdy_kernel_launches() - launches0
     capi.check()
     ms_total = start.elapsed_time(end)
-    t = torch.tensor([ms_total], device=dev)
+    tm = torch.tensor([ms_total], dtype=torch.float64, device=dev)
+    tb = torch.tensor([step_bytes], dtype=torch.float64, device=dev)
     if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = world * step_bytes * args.steps / (ms_max * 1e-3) / 1e9
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tb, op=dist.ReduceOp.SUM)
+    ms_max, all_bytes = float(tm.item()), float(tb.item())
+    value = all_bytes * args.steps / (ms_max * 1e-3) / 1e9
     dom_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
     fmt, n_out, n_in, _ = mats[dominant]
     peak, peak_kind = load_peaks()
     achieved = alg_bytes(fmt, n_out, n_in) / (dom_ms * 1e-3) / 1e9
-    traffic = load_traffic()
+    traffic = load_traffic() if world == 1 else None
+    y_dev = [gathered_y(i).cpu() for i in range(len(mats))]
 
-    # e2e through the reference-facing C-ABI with host buffers
+    # e2e through the reference-facing C-ABI with host buffers: op_matmul of this rank's slices
+    # (pinned f32 x in, host y out), then (N > 1) the host slices gathered over NCCL
     x_pin = {n_in: torch.from_numpy(x).pin_memory() for n_in, x in xs.items()}
-    y_pin = {(fmt, n_out, n_in): torch.empty(n_out, dtype=torch.float32).pin_memory() for fmt, n_out, n_in, _ in mats}
+    y_pin = [torch.empty(n_out, dtype=torch.float32).pin_memory() for _, n_out, _, _ in mats]
+    h_send = torch.empty(share, dtype=torch.float32).pin_memory()
+    h_recv = torch.empty(world * share, dtype=torch.float32).pin_memory()
     for fmt, n_out, n_in, w in mats:
         if lib.sdy_weights_register(w.ctypes.data, TYPE_ID[fmt], n_out, n_in) != 0:
             raise RuntimeError(capi.last_error())
 
     def e2e_step():
-        for fmt, n_out, n_in, w in mats:
-            lib.op_matmul(ctypes.c_void_p(y_pin[(fmt, n_out, n_in)].data_ptr()), ctypes.c_void_p(x_pin[n_in].data_ptr()),
+        for i, (fmt, n_out, n_in, w) in enumerate(mats):
+            lib.op_matmul(ctypes.c_void_p(y_pin[i].data_ptr()), ctypes.c_void_p(x_pin[n_in].data_ptr()),
                           w.ctypes.data, TYPE_ID[fmt], 1, n_in, n_out)
+        if world > 1:
+            for i, y in enumerate(y_pin):
+                h_send[share_off[i]:share_off[i] + y.numel()].copy_(y)
+            send.copy_(h_send, non_blocking=True)
+            dist.all_gather_into_tensor(recv, send)
+            h_recv.copy_(recv)
 
     for _ in range(max(args.warmup, 3)):
         e2e_step()
@@ -365,22 +435,31 @@ def run_b200(args, rank, world, local_rank):
     e2e_s = time.perf_counter() - t0
     te = torch.tensor([e2e_s], device=dev)
     if world > 1:
-        torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
     capi.check()
-    # the resident product through the C-ABI equals the device-resident one
-    for fmt, n_out, n_in, _ in mats:
-        assert torch.equal(y_pin[(fmt, n_out, n_in)], d_out[(fmt, n_out, n_in)].cpu()), "e2e/device mismatch"
-    e2e_value = world * step_bytes * e2e_steps / float(te.item()) / 1e9
+    # the product through the C-ABI equals the device-resident one, and (N > 1) the gathered y
+    # equals every rank's slices in row order
+    for i in range(len(mats)):
+        assert torch.equal(y_pin[i], d_out[i].cpu()), "e2e/device mismatch"
+    if world > 1:
+        for i in range(len(mats)):
+            r0, r1 = ranges[i]
+            assert torch.equal(y_dev[i][r0:r1], y_pin[i]), "gathered y differs from this rank's slice"
+    e2e_value = all_bytes * e2e_steps / float(te.item()) / 1e9
     for _, _, _, w in mats:
         lib.sdy_weights_unregister(w.ctypes.data)
     for h in handles:
         lib.sdy_qmat_free(h)
 
+    decode = None
+    if not args.no_decode:
+        decode = measure_decode("qwen3moe", args, rank, world, cpu_baseline=not args.no_cpu_baseline)
     if rank != 0:
         return 0
     line = {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config(),
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": config(world),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": f"qmv {fmt} {n_out}x{n_in} batch 1", "peak_source": peak_kind,
@@ -388,14 +467,17 @@ def run_b200(args, rank, world, local_rank):
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": sum(4 * n_in for _, _, n_in, _ in mats),
                     "d2h_bytes_per_step": sum(4 * n_out for _, n_out, _, _ in mats),
-                    "steps": e2e_steps, "api": "op_matmul (C-ABI), weights resident via sdy_weights_register"},
+                    "steps": e2e_steps, "api": "op_matmul (C-ABI), weights resident via sdy_weights_register"
+                                               + (", y slices all-gathered over NCCL" if world > 1 else "")},
             "gpu_launches": int(launches), "clocks": clk.summary(),
             "frac_of_8tbs": round(value / world / 8000.0, 4), "per_matrix": per}
     if world == 1 and not args.no_cpu_baseline:
         try:
-            line["cpu_baseline"] = time_reference(mats, xs)
+            line["cpu_baseline"] = time_reference(full, xs)
         except OSError as e:
             line["cpu_baseline"] = {"value": None, "unavailable": str(e)}
+    if decode is not None:
+        line["decode"] = decode
     print(json.dumps(line))
     return 0
 
@@ -467,22 +549,37 @@ def run_gemm(args):
 
 # ------------------------------------------------------------------------------ decode workload
 
-DECODE_MODELS = {  # shape, prompt length, decode steps, max context
-    "smollm2": ("SMOLLM2_135M", 128, 256, 2048),
-    "qwen25_3b": ("QWEN25_3B", 512, 512, 4096),
-    "qwen3moe": ("QWEN3_30B_A3B", 256, 256, 4096),
+DECODE_MODELS = {  # prompt length, decode steps, max context
+    "smollm2": (128, 256, 2048),
+    "qwen25_3b": (512, 512, 4096),
+    "qwen3moe": (256, 256, 4096),
 }
+REF_DECODE_SAMPLE = (32, 16)  # reference CPU sample: prompt tokens, decode steps
 
 
-def decode_model_path(name, directory):
-    from sardyne_b200 import synth
-    spec_name = DECODE_MODELS[name][0]
-    path = pathlib.Path(directory) / f"{name}.gguf"
-    if not path.exists():
-        t0 = time.perf_counter()
-        synth.write_model(path, synth.Spec(**getattr(synth, spec_name), synth=True, seed=0))
-        log(f"wrote {path} ({path.stat().st_size / 1e9:.2f} GB) in {time.perf_counter() - t0:.1f} s")
-    return path
+def engine_open(lib, path, max_seq, n_batch, n_threads=0):
+    """(model, context, info) handles of the engine_* C-ABI of `lib` (this build or the reference)."""
+    from sardyne_b200 import capi
+    err = ctypes.create_string_buffer(512)
+    model = lib.engine_model_load(str(path).encode(), err, len(err))
+    if not model:
+        raise RuntimeError(err.value.decode(errors="replace"))
+    info = capi.EngineModelInfo()
+    lib.engine_model_get_info(model, ctypes.byref(info))
+    ctx = lib.engine_ctx_new(model, max_seq, n_batch, 0, n_threads, err, len(err))
+    if not ctx:
+        lib.engine_model_free(model)
+        raise RuntimeError(err.value.decode(errors="replace"))
+    return model, ctx, info
+
+
+def engine_next(lib, ctx, tokens, n_vocab):
+    """engine_eval of `tokens`, then the greedy choice from the host logits it returns."""
+    arr = (ctypes.c_int32 * len(tokens))(*tokens)
+    if lib.engine_eval(ctx, arr, len(tokens)) != 0:
+        raise RuntimeError(lib.engine_last_error(ctx).decode(errors="replace"))
+    logits = np.ctypeslib.as_array(lib.engine_logits(ctx), shape=(n_vocab,))
+    return int(np.argmax(logits))
 
 
 def weight_bytes_per_token(path, info):
@@ -505,91 +602,124 @@ def weight_bytes_per_token(path, info):
     return total
 
 
-def run_decode(args):
-    """Decode of a BASELINE config 3-5 model through engine_eval. Under torchrun every rank runs the
+def decode_reference(name, path, prompt):
+    """The reference engine (oracle/_ref, AVX2 kernels, one thread per host core) on a bounded
+    sample of the same workload: the first 32 prompt tokens, then 16 greedy decode steps."""
+    import oracle
+    n_prompt, n_decode = REF_DECODE_SAMPLE
+    ref = oracle.ref()
+    ref.op_set_simd(1)
+    model, ctx, info = engine_open(ref, path, n_prompt + n_decode + 1, n_prompt)
+    try:
+        t0 = time.perf_counter()
+        nxt = engine_next(ref, ctx, prompt[:n_prompt], info.n_vocab)
+        t1 = time.perf_counter()
+        for _ in range(n_decode):
+            nxt = engine_next(ref, ctx, [nxt], info.n_vocab)
+        t2 = time.perf_counter()
+    finally:
+        ref.engine_ctx_free(ctx)
+        ref.engine_model_free(model)
+    cores = os.cpu_count() or 1
+    return {"value": round(n_decode / (t2 - t1), 3), "unit": "tok/s", "cores": cores, "kind": "reference",
+            "prefill_tok_s": round(n_prompt / (t1 - t0), 2),
+            "sample": f"reference engine_eval (oracle/_ref, AVX2, {cores} threads) on the same model: "
+                      f"{n_prompt}-token prompt, then {n_decode} greedy decode steps"}
+
+
+def measure_decode(name, args, rank, world, cpu_baseline=True):
+    """Decode of a BASELINE config 3-5 model through engine_eval (host token ids in, host logits
+    out): the prompt's prefill, then greedy single-token steps. Under torchrun every rank runs the
     same token stream with its shard of the model (FFN rows / experts / vocabulary; attention
-    replicated) and the engine's NCCL all-reduces: strong scaling of one stream, device time as
-    the max over ranks."""
-    import datetime
+    replicated) and the engine's NCCL collectives: strong scaling of one stream; times are the max
+    over ranks. Returns the decode object (rank 0) or None."""
     import torch
     import torch.distributed as dist
-    from sardyne_b200 import capi, runtime
-    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
-    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
-    spec_name, n_prompt, n_decode, ctx_len = DECODE_MODELS[args.model]
+    from sardyne_b200 import capi, runtime, synth
+    n_prompt, n_decode, ctx_len = DECODE_MODELS[name]
     n_decode = args.decode_steps or n_decode
     if world > 1:
-        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
         if rank == 0:
-            decode_model_path(args.model, args.model_dir)  # written once, before the other ranks open it
+            synth.baseline_model(name, args.model_dir)  # written once, before the other ranks open it
         dist.barrier()
         runtime.shard_from_torch()
-    path = decode_model_path(args.model, args.model_dir)
+    path = synth.baseline_model(name, args.model_dir)
+    lib = capi.lib()
     t0 = time.perf_counter()
-    model = runtime.Model(path)
+    model, ctx, info = engine_open(lib, path, ctx_len, n_prompt)
     load_s = time.perf_counter() - t0
-    info = model.info
     prompt = np.random.default_rng(0).integers(0, info.n_vocab, n_prompt).tolist()
-    ctx = runtime.Context(model, max_seq=ctx_len, n_batch=n_prompt)
-    ctx.eval(prompt)  # warm-up: a prefill and a few decode steps (the second one captures the graph)
-    for _ in range(max(args.warmup, 3)):
-        ctx.eval([1])
-    ctx.reset()
-    launches0 = capi.lib().sdy_kernel_launches()
-    with ClockSampler(torch.cuda.current_device()) as clk:
-        t0 = time.perf_counter()
-        logits = ctx.eval(prompt)
-        t1 = time.perf_counter()
-        tokens = []
-        for _ in range(n_decode):
-            nxt = int(np.argmax(logits))
-            tokens.append(nxt)
-            logits = ctx.eval([nxt])
-        t2 = time.perf_counter()
-    capi.check()
-    if args.profile_step:  # one more decode step between profiler start/stop, after the timed region
-        import torch.cuda.profiler as prof
-        torch.cuda.synchronize()
-        prof.start()
-        ctx.eval([int(np.argmax(logits))])
-        torch.cuda.synchronize()
-        prof.stop()
-    launches = int(capi.lib().sdy_kernel_launches() - launches0)
+    try:
+        nxt = engine_next(lib, ctx, prompt, info.n_vocab)  # warm-up: prefill, then decode steps
+        for _ in range(max(args.warmup, 3)):               # (the second one captures the graphs)
+            nxt = engine_next(lib, ctx, [nxt], info.n_vocab)
+        lib.engine_reset(ctx)
+        launches0 = lib.sdy_kernel_launches()
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            if world > 1:
+                dist.barrier()
+            t0 = time.perf_counter()
+            nxt = engine_next(lib, ctx, prompt, info.n_vocab)
+            t1 = time.perf_counter()
+            tokens = []
+            for _ in range(n_decode):
+                tokens.append(nxt)
+                nxt = engine_next(lib, ctx, [nxt], info.n_vocab)
+            t2 = time.perf_counter()
+        launches = int(lib.sdy_kernel_launches() - launches0)
+        capi.check()
+    finally:
+        lib.engine_ctx_free(ctx)  # graphs and NCCL communicator released before the process group
+        lib.engine_model_free(model)
+        if world > 1:
+            runtime.set_shard(0, 1)
     if world > 1:  # the slowest rank's times; every rank must agree on the tokens
-        tt = torch.tensor([t1 - t0, t2 - t1], dtype=torch.float64)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        tt = torch.tensor([t1 - t0, t2 - t1], dtype=torch.float64, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t0, t1, t2 = 0.0, float(tt[0]), float(tt[0] + tt[1])
         toks = [None] * world
         dist.all_gather_object(toks, tokens)
         if any(tk != tokens for tk in toks):
             raise RuntimeError("ranks disagree on the greedy tokens")
-        del ctx, model  # NCCL communicator and graphs released before the process group
-        dist.barrier()
-        dist.destroy_process_group()
-        if rank != 0:
-            return 0
+    if rank != 0:
+        return None
     wbytes = weight_bytes_per_token(path, info)
     peak, peak_kind = load_peaks()
     tps = n_decode / (t2 - t1)
-    line = {"metric": f"decode tok/s {spec_name} shape (greedy, e2e through engine_eval)",
-            "value": round(tps, 2), "unit": "tok/s", "n_gpus": world, "steps": n_decode, "warmup": args.warmup,
-            "ms_per_step": round((t2 - t1) / n_decode * 1e3, 4), "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "weak",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": f"{spec_name}: {n_prompt}-token prompt (uniform ids, seed 0), {n_decode} greedy "
-                                   f"decode steps, context {ctx_len}", "model_gb": round(path.stat().st_size / 1e9, 2),
-                       "weight_bytes_per_token": wbytes,
-                       "parallelism": f"ffn/expert/vocab shards x{world}, attention replicated" if world > 1 else "1 GPU"},
-            "prefill_tok_s": round(n_prompt / (t1 - t0), 1),
-            "roofline": {"bound": "hbm", "achieved": round(wbytes * tps / 1e9, 1), "peak": round(peak * world, 1),
-                         "unit": "GB/s", "frac": round(wbytes * tps / 1e9 / (peak * world), 4), "traffic": None,
-                         "kernel": "whole decode step (weight bytes per token x tok/s, against N x peak)",
-                         "peak_source": peak_kind},
-            "e2e": {"value": round(tps, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": 4 * info.n_vocab},
-            "gpu_launches": launches, "clocks": clk.summary(),
-            "load_s": round(load_s, 2), "first_tokens": tokens[:8]}
+    out = {"metric": f"decode tok/s {name} shape (greedy, e2e through engine_eval)", "value": round(tps, 2),
+           "unit": "tok/s", "n_gpus": world, "steps": n_decode, "ms_per_step": round((t2 - t1) / n_decode * 1e3, 4),
+           "prefill_tok_s": round(n_prompt / (t1 - t0), 1),
+           "scaling": "strong" if world > 1 else "weak",
+           "workload": f"BASELINE {name} shape: {n_prompt}-token prompt (uniform ids, seed 0), {n_decode} greedy "
+                       f"decode steps, context {ctx_len}; random-init Q4_K_M mix",
+           "model_gb": round(path.stat().st_size / 1e9, 2), "weight_bytes_per_token": wbytes,
+           "parallelism": f"ffn/expert/vocab shards x{world}, attention replicated" if world > 1 else "1 GPU",
+           "roofline": {"bound": "hbm", "achieved": round(wbytes * tps / 1e9, 1), "peak": round(peak * world, 1),
+                        "unit": "GB/s", "frac": round(wbytes * tps / 1e9 / (peak * world), 4), "traffic": None,
+                        "kernel": "whole decode step (weight bytes per token x tok/s, against N x peak)",
+                        "peak_source": peak_kind},
+           "e2e": {"value": round(tps, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                   "d2h_bytes_per_step": 4 * info.n_vocab},
+           "gpu_launches": launches, "clocks": clk.summary(), "load_s": round(load_s, 2),
+           "first_tokens": tokens[:8]}
+    if cpu_baseline and world == 1:
+        try:
+            out["cpu_baseline"] = decode_reference(name, path, prompt)
+        except (OSError, RuntimeError) as e:
+            out["cpu_baseline"] = {"value": None, "unavailable": str(e)}
+    return out
+
+
+def run_decode(args, rank, world):
+    """--workload decode: the decode measurement alone, as the line's value."""
+    d = measure_decode(args.model, args, rank, world, cpu_baseline=not args.no_cpu_baseline)
+    if d is None:
+        return 0
+    line = {k: d[k] for k in ("metric", "value", "unit", "n_gpus", "steps", "ms_per_step", "scaling")}
+    line.update({"warmup": args.warmup, "higher_is_better": True, "vs_baseline": None, "dtype": "int8",
+                 "data": "synthetic", "config": {"workload": d["workload"], "parallelism": d["parallelism"]}})
+    line.update({k: v for k, v in d.items() if k not in line and k not in ("workload", "parallelism")})
     print(json.dumps(line))
     return 0
 
@@ -603,7 +733,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["matvec", "decode", "gemm"], default="matvec")
     ap.add_argument("--model", choices=sorted(DECODE_MODELS), default="qwen3moe")
-    ap.add_argument("--model-dir", default=os.environ.get("SARDYNE_BENCH_DIR", "/tmp"))
+    ap.add_argument("--model-dir", default=None, help="where the synthetic GGUFs are cached (default: "
+                                                         "SARDYNE_MODEL_DIR, /dev/shm or the temp dir)")
+    ap.add_argument("--no-decode", action="store_true", help="matvec: leave out the decode object")
     ap.add_argument("--decode-steps", type=int, default=0)
     ap.add_argument("--profile-step", action="store_true",
                     help="decode: run one extra step between cudaProfilerStart/Stop (ncu --profile-from-start off)")
@@ -611,8 +743,6 @@ def main():
     args = ap.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
-    if args.workload == "decode":
-        return run_decode(args)
     if args.workload == "gemm":
         return run_gemm(args)
     if args.impl == "reference":
@@ -624,6 +754,8 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     try:
+        if args.workload == "decode":
+            return run_decode(args, rank, world)
         return run_b200(args, rank, world, local_rank)
     finally:
         if world > 1:

@@ -89,23 +89,39 @@ class GGUFWriter:
             raise ValueError(f"{name}: {len(raw)} bytes do not match {kind} {tuple(ne)}")
         self.tensors.append((name, tuple(int(v) for v in ne), kind, bytes(raw)))
 
+    def add_lazy_tensor(self, name: str, ne, kind: str, produce):
+        """A tensor whose bytes `produce()` returns when the file is written (one tensor in
+        memory at a time, for multi-GB files)."""
+        block, _ = _BLOCK[kind]
+        if ne[0] % block:
+            raise ValueError(f"{name}: {tuple(ne)} is not whole {kind} blocks")
+        self.tensors.append((name, tuple(int(v) for v in ne), kind, produce))
+
+    def _nbytes(self, ne, kind):
+        block, size = _BLOCK[kind]
+        return int(np.prod(ne)) // block * size
+
     def write(self):
         head = b"GGUF" + struct.pack("<IQQ", 3, len(self.tensors), len(self.kv))
         for key, vtype, payload in self.kv:
             head += _str(key) + struct.pack("<I", vtype) + payload
         offsets, off = [], 0
-        for _, _, _, raw in self.tensors:
+        for _, ne, kind, _ in self.tensors:
             offsets.append(off)
-            off += len(raw)
+            off += self._nbytes(ne, kind)
             off += -off % self.alignment
         for (name, ne, kind, _), o in zip(self.tensors, offsets):
             head += _str(name) + struct.pack("<I", len(ne)) + struct.pack(f"<{len(ne)}Q", *ne)
             head += struct.pack("<IQ", GGML_TYPES[kind], o)
         head += b"\0" * (-len(head) % self.alignment)
-        tmp = self.path.with_name(self.path.name + ".tmp")
+        tmp = self.path.with_name(f"{self.path.name}.{os.getpid()}.tmp")
         with open(tmp, "wb") as f:
             f.write(head)
-            for (_, _, _, raw), o in zip(self.tensors, offsets):
+            for name, ne, kind, raw in self.tensors:
+                if callable(raw):
+                    raw = raw()
+                    if len(raw) != self._nbytes(ne, kind):
+                        raise ValueError(f"{name}: produced {len(raw)} bytes, expected {self._nbytes(ne, kind)}")
                 f.write(raw)
                 f.write(b"\0" * (-len(raw) % self.alignment))
         os.replace(tmp, self.path)

@@ -137,17 +137,23 @@ def quantize(x: np.ndarray, kind: str, chunk_rows: int = 4096) -> bytes:
     return np.concatenate(parts).tobytes() if parts else b""
 
 
+def synth_pool(kind: str, rng: np.random.Generator, std: float = 0.02, pool_blocks: int = 1 << 15) -> np.ndarray:
+    """pool_blocks genuinely quantized blocks of N(0, std) values, [pool_blocks][block bytes]."""
+    raw = quantize((rng.standard_normal((pool_blocks, QK[kind])) * std).astype(np.float32), kind)
+    return np.frombuffer(raw, np.uint8).reshape(pool_blocks, BLOCK_BYTES[kind])
+
+
 def synth_tensor(kind: str, n_rows: int, n_in: int, rng: np.random.Generator, std: float = 0.02,
-                 pool_blocks: int = 1 << 15) -> bytes:
+                 pool_blocks: int = 1 << 15, pool: np.ndarray | None = None) -> bytes:
     """Bytes of an n_rows x n_in `kind` tensor that looks like quantized N(0, std) weights, made
-    fast for multi-GB models: a pool of genuinely quantized blocks is drawn once and the tensor
-    is filled with pool blocks picked at random (every block is a real quantization of Gaussian
-    values; only their arrangement is resampled)."""
-    qk, bb = QK[kind], BLOCK_BYTES[kind]
+    fast for multi-GB models: a pool of genuinely quantized blocks (drawn here, or `pool` shared
+    by the tensors of one model) fills the tensor with blocks picked at random (every block is a
+    real quantization of Gaussian values; only their arrangement is resampled)."""
+    qk = QK[kind]
     n_blocks = n_rows * (n_in // qk)
-    if n_blocks <= pool_blocks:
+    if pool is None and n_blocks <= pool_blocks:
         return quantize((rng.standard_normal((n_rows, n_in)) * std).astype(np.float32), kind)
-    pool = np.frombuffer(quantize((rng.standard_normal((pool_blocks, qk)) * std).astype(np.float32), kind),
-                         np.uint8).reshape(pool_blocks, bb)
-    idx = rng.integers(0, pool_blocks, n_blocks)
+    if pool is None:
+        pool = synth_pool(kind, rng, std, pool_blocks)
+    idx = rng.integers(0, len(pool), n_blocks)
     return pool[idx].tobytes()

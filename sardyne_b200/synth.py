@@ -37,7 +37,7 @@ class Spec:
     norm_noise: float = 0.1
     kinds: object = "F32"  # a type name, or a function (name, n_in) -> type name
     seed: int = 0
-    synth: bool = False    # fill quantized tensors from a pool of quantized blocks (fast, multi-GB)
+    synth: bool = False    # fill quantized tensors from one pool of quantized blocks per type (fast, multi-GB)
 
     def kind(self, name, n_in):
         k = self.kinds(name, n_in) if callable(self.kinds) else self.kinds
@@ -91,6 +91,8 @@ def write_model(path, spec: Spec):
         w.add(f"{a}.expert_used_count", s.n_used)
         w.add(f"{a}.expert_feed_forward_length", s.ffn_exp)
 
+    pools = {}  # synth: one pool of quantized blocks per type, shared by every tensor
+
     def tensor(name, *shape, vector=False, norm=False):
         n_in = shape[-1]
         if vector:
@@ -101,7 +103,11 @@ def write_model(path, spec: Spec):
         ne = tuple(reversed(shape))
         rows = int(np.prod(shape[:-1]))
         if kind in kquant.QK and s.synth:
-            w.add_raw_tensor(name, ne, kind, kquant.synth_tensor(kind, rows, n_in, rng, s.std or 0.02))
+            if kind not in pools:
+                pools[kind] = kquant.synth_pool(kind, rng, s.std or 0.02)
+            trng = np.random.default_rng([s.seed, len(w.tensors)])  # drawn when the file is written
+            w.add_lazy_tensor(name, ne, kind,
+                              lambda k=kind, r=rows, n=n_in, g=trng: kquant.synth_tensor(k, r, n, g, pool=pools[k]))
             return
         std = s.std or 1.0 / np.sqrt(n_in)
         data = (rng.standard_normal(shape) * std).astype(np.float32)
@@ -154,3 +160,33 @@ QWEN25_3B = dict(arch="qwen2", dim=2048, n_layer=36, n_head=16, n_kv_head=2, hea
 QWEN3_30B_A3B = dict(arch="qwen3moe", dim=2048, n_layer=48, n_head=32, n_kv_head=4, head_dim=128, ffn=6144,
                      vocab=151936, context=4096, eps=1e-6, theta=1e6, tied=False, qk_norm=True, n_expert=128,
                      n_used=8, ffn_exp=768, std=0.02, kinds=mix_q4_k_m_untied)
+BASELINE_MODELS = {"smollm2": SMOLLM2_135M, "qwen25_3b": QWEN25_3B, "qwen3moe": QWEN3_30B_A3B}
+SYNTH_LAYOUT = 2  # bumped whenever the bytes write_model produces for a spec change
+
+
+def model_cache_dir():
+    """SARDYNE_MODEL_DIR, else /dev/shm when it has room for the largest model, else the temp dir."""
+    import os
+    import shutil
+    import tempfile
+    if os.environ.get("SARDYNE_MODEL_DIR"):
+        return os.environ["SARDYNE_MODEL_DIR"]
+    shm = "/dev/shm"
+    try:
+        if os.access(shm, os.W_OK) and shutil.disk_usage(shm).free > 24e9:
+            return shm
+    except OSError:
+        pass
+    return tempfile.gettempdir()
+
+
+def baseline_model(name, directory=None):
+    """Path of the synthetic GGUF of a BASELINE config (3: smollm2, 4: qwen25_3b, 5: qwen3moe),
+    written once (quantized blocks from one pool per type, seed 0) and reused from the cache."""
+    import os
+    import pathlib
+    path = pathlib.Path(directory or model_cache_dir()) / f"sardyne-{name}-v{SYNTH_LAYOUT}.gguf"
+    if not path.exists():
+        write_model(path, Spec(**BASELINE_MODELS[name], synth=True, seed=0))
+        os.chmod(path, 0o644)
+    return path

@@ -1,16 +1,20 @@
 """The GPU engine (engine_* C-ABI) against the reference engine on the same synthetic GGUFs.
 
 The reference side is the reference's own libsardyne built from its sources (oracle/_ref), run
-on the CPU with its scalar kernels. The quantized products agree bit for bit; RMSNorm, RoPE,
-softmax and attention run in fp32 on both sides in different summation orders, so logits are
-compared with a tolerance proportional to their scale, plus greedy-token identity. Mirrors the
-reference's tests/test_runtime.py:160-284 and tests/test_moe.py:286-435.
+on the CPU with its scalar kernels. Both are driven by the reference's own, unmodified Python
+runtime (sardyne.runtime through sardyne.capi, with SARDYNE_LIB naming the library), which is the
+drop-in claim. The quantized products agree bit for bit; RMSNorm, RoPE, softmax and attention run
+in fp32 on both sides in different summation orders, so logits are compared with a tolerance
+proportional to their scale, plus greedy-token identity. Mirrors the reference's
+tests/test_runtime.py:160-284 and tests/test_moe.py:286-435.
 """
 import numpy as np
 import pytest
 
 import oracle
-from sardyne_b200 import runtime, synth
+import refruntime as rt
+from refruntime import Context, generate
+from sardyne_b200 import synth
 from sardyne_b200.gguf_writer import GGUFWriter
 
 pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not oracle.ref_available(), reason="reference library not built")]
@@ -44,16 +48,22 @@ SPECS = {
 @pytest.fixture(scope="module", params=sorted(SPECS))
 def model_path(request, tmp_path_factory):
     path = tmp_path_factory.mktemp(request.param) / "m.gguf"
-    synth.write_model(path, synth.Spec(**SPECS[request.param], seed=len(request.param)))
+    synth.write_model(path, synth.Spec(**{"context": 128, **SPECS[request.param]}, seed=len(request.param)))
     return path
 
 
 @pytest.fixture(scope="module")
 def ref_lib():
+    """The reference library's path; its scalar kernels (the order the GPU products reproduce
+    bit for bit) are selected for the module."""
     lib = oracle.ref()
-    lib.op_set_simd(0)  # scalar kernels: the order the GPU products reproduce bit for bit
-    yield lib
+    lib.op_set_simd(0)
+    yield oracle.REF_LIB
     lib.op_set_simd(1)
+
+
+def Model(path, lib=None):
+    return rt.model(path, lib)
 
 
 def close(got, want, scale=1e-3):
@@ -62,9 +72,9 @@ def close(got, want, scale=1e-3):
 
 
 def test_forward_matches_reference(model_path, ref_lib):
-    want = runtime.Context(runtime.Model(model_path, lib=ref_lib), max_seq=32, n_batch=len(TOKENS),
+    want = Context(Model(model_path, ref_lib), max_seq=32, n_batch=len(TOKENS),
                            logits_all=True).eval(TOKENS)
-    got = runtime.Context(runtime.Model(model_path), max_seq=32, n_batch=len(TOKENS), logits_all=True).eval(TOKENS)
+    got = Context(Model(model_path), max_seq=32, n_batch=len(TOKENS), logits_all=True).eval(TOKENS)
     close(got, want)
     assert (got.argmax(-1) == want.argmax(-1)).all()
 
@@ -76,30 +86,31 @@ LONG = [(7 * i + 3) % 60 + 1 for i in range(45)]
 def test_long_prompt_matches_reference(model_path, ref_lib, n_batch):
     """A 45-token prompt in one chunk or in chunks of 20 (the second and third start at positions
     20 and 40): the tensor-core GEMM and the query-tile prefill attention."""
-    want = runtime.Context(runtime.Model(model_path, lib=ref_lib), max_seq=64, n_batch=n_batch,
+    want = Context(Model(model_path, ref_lib), max_seq=64, n_batch=n_batch,
                            logits_all=True).eval(LONG)
-    got = runtime.Context(runtime.Model(model_path), max_seq=64, n_batch=n_batch, logits_all=True).eval(LONG)
+    got = Context(Model(model_path), max_seq=64, n_batch=n_batch, logits_all=True).eval(LONG)
     close(got, want)
     assert (got.argmax(-1) == want.argmax(-1)).all()
 
 
 def test_generate_matches_reference(model_path, ref_lib):
-    want = runtime.generate(runtime.Context(runtime.Model(model_path, lib=ref_lib), max_seq=32), TOKENS[:4], 16)
-    got = runtime.generate(runtime.Context(runtime.Model(model_path), max_seq=32), TOKENS[:4], 16)
-    assert got == want
+    """64 greedy steps (the reference's greedy loop, sardyne/runtime.py:115-140)."""
+    want = generate(Context(Model(model_path, ref_lib), max_seq=80), TOKENS[:4], 64)
+    got = generate(Context(Model(model_path), max_seq=80), TOKENS[:4], 64)
+    assert len(want) == 64 and got == want
 
 
 def test_info_matches_reference(model_path, ref_lib):
-    a, b = runtime.Model(model_path).info, runtime.Model(model_path, lib=ref_lib).info
+    a, b = Model(model_path).info, Model(model_path, ref_lib).info
     assert bytes(a) == bytes(b)
 
 
 def test_kv_cache_and_batching(model_path):
-    model = runtime.Model(model_path)
-    full = runtime.Context(model, max_seq=32, n_batch=len(TOKENS), logits_all=True).eval(TOKENS)
-    chunked = runtime.Context(model, max_seq=32, n_batch=5, logits_all=True).eval(TOKENS)
+    model = Model(model_path)
+    full = Context(model, max_seq=32, n_batch=len(TOKENS), logits_all=True).eval(TOKENS)
+    chunked = Context(model, max_seq=32, n_batch=5, logits_all=True).eval(TOKENS)
     close(chunked, full, 1e-4)
-    ctx = runtime.Context(model, max_seq=32, n_batch=4)
+    ctx = Context(model, max_seq=32, n_batch=4)
     close(ctx.eval(TOKENS[:7]), full[6], 1e-4)
     for i, t in enumerate(TOKENS[7:], start=7):
         close(ctx.eval([t]), full[i], 1e-4)
@@ -110,9 +121,9 @@ def test_kv_cache_and_batching(model_path):
 
 
 def test_truncate(model_path):
-    model = runtime.Model(model_path)
-    full = runtime.Context(model, max_seq=32, n_batch=len(TOKENS), logits_all=True).eval(TOKENS)
-    ctx = runtime.Context(model, max_seq=32, n_batch=4)
+    model = Model(model_path)
+    full = Context(model, max_seq=32, n_batch=len(TOKENS), logits_all=True).eval(TOKENS)
+    ctx = Context(model, max_seq=32, n_batch=4)
     ctx.eval(TOKENS[:7])
     ctx.truncate(3)
     assert ctx.n_past == 3
@@ -126,10 +137,10 @@ def test_truncate(model_path):
 
 
 def test_results_are_deterministic(model_path):
-    model = runtime.Model(model_path)
+    model = Model(model_path)
     outs = []
     for n_threads in (0, 1, 7):
-        ctx = runtime.Context(model, max_seq=32, n_batch=len(TOKENS), logits_all=True, n_threads=n_threads)
+        ctx = Context(model, max_seq=32, n_batch=len(TOKENS), logits_all=True, n_threads=n_threads)
         assert ctx.n_threads == n_threads
         outs.append(np.concatenate([ctx.eval(TOKENS[:8]), ctx.eval(TOKENS[8:])]))
     for o in outs[1:]:
@@ -138,26 +149,26 @@ def test_results_are_deterministic(model_path):
 
 def test_errors_leave_context_unchanged(tmp_path):
     path = synth.write_model(tmp_path / "m.gguf", synth.Spec(context=8))
-    model = runtime.Model(path)
-    ctx = runtime.Context(model, max_seq=8, n_batch=4)
+    model = Model(path)
+    ctx = Context(model, max_seq=8, n_batch=4)
     ctx.eval([1, 2, 3])
     for bad, msg in [([1] * 6, "contesto pieno"), ([64], "vocabolario"), ([-1], "vocabolario"), ([], "nessun")]:
         with pytest.raises(ValueError, match=msg):
             ctx.eval(bad)
         assert ctx.n_past == 3
     with pytest.raises(ValueError, match="n_batch"):
-        runtime.Context(model, max_seq=8, n_batch=0)
+        Context(model, max_seq=8, n_batch=0)
     with pytest.raises(ValueError, match="max_seq"):
-        runtime.Context(model, max_seq=0)
+        Context(model, max_seq=0)
     with pytest.raises(ValueError, match="n_threads"):
-        runtime.Context(model, max_seq=8, n_threads=-1)
-    all_ctx = runtime.Context(model, max_seq=8, n_batch=2, logits_all=True)
+        Context(model, max_seq=8, n_threads=-1)
+    all_ctx = Context(model, max_seq=8, n_batch=2, logits_all=True)
     assert all_ctx.eval([1, 2, 3, 4, 5]).shape == (5, model.info.n_vocab)
 
 
 def test_load_errors(tmp_path):
     with pytest.raises(ValueError, match="impossibile aprire"):
-        runtime.Model(tmp_path / "missing.gguf")
+        Model(tmp_path / "missing.gguf")
     for n_expert, n_used, msg in [(0, 3, "expert_count"), (8, 0, "expert_used_count"), (8, 9, "expert_used_count")]:
         p = tmp_path / f"e{n_expert}_{n_used}.gguf"
         w = GGUFWriter(p)
@@ -171,7 +182,7 @@ def test_load_errors(tmp_path):
         w.add_tensor("token_embd.weight", np.zeros((8, 32), np.float32))
         w.write()
         with pytest.raises(ValueError, match=msg):
-            runtime.Model(p)
+            Model(p)
 
 
 def rewrite_gguf(src, dst, tensor_fn):
@@ -217,7 +228,7 @@ def test_unsupported_tensors_are_rejected(tmp_path):
         return kind, raw
 
     with pytest.raises(ValueError, match="Q4_1 non supportato"):
-        runtime.Model(rewrite_gguf(src, tmp_path / "q41.gguf", q41))
+        Model(rewrite_gguf(src, tmp_path / "q41.gguf", q41))
 
 
 def test_moe_ties_choose_the_lowest_experts(tmp_path, ref_lib):
@@ -228,7 +239,7 @@ def test_moe_ties_choose_the_lowest_experts(tmp_path, ref_lib):
         return kind, (bytes(len(raw)) if "gate_inp" in name else raw)
 
     path = rewrite_gguf(src, tmp_path / "ties.gguf", zero_router)
-    want = runtime.Context(runtime.Model(path, lib=ref_lib), max_seq=32, n_batch=len(TOKENS),
+    want = Context(Model(path, ref_lib), max_seq=32, n_batch=len(TOKENS),
                            logits_all=True).eval(TOKENS)
-    got = runtime.Context(runtime.Model(path), max_seq=32, n_batch=len(TOKENS), logits_all=True).eval(TOKENS)
+    got = Context(Model(path), max_seq=32, n_batch=len(TOKENS), logits_all=True).eval(TOKENS)
     close(got, want)

@@ -26,10 +26,11 @@ STEPS = 6
 
 RUN = """
 import json, sys, numpy as np
-from sardyne_b200 import runtime
+sys.path.insert(0, sys.argv[5])
+import refruntime as rt
 path, out, prompt, steps = sys.argv[1], sys.argv[2], json.loads(sys.argv[3]), int(sys.argv[4])
-m = runtime.Model(path)
-ctx = runtime.Context(m, max_seq=64, n_batch=len(prompt))
+m = rt.model(path)
+ctx = rt.Context(m, max_seq=64, n_batch=len(prompt))
 logits = [ctx.eval(prompt)]
 for i in range(steps):
     logits.append(ctx.eval([int(np.argmax(logits[-1])) + i % 3]))
@@ -53,7 +54,8 @@ def run(path, out, env_extra):
     env.update(env_extra)
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     env["PYTHONPATH"] = root + os.pathsep + env.get("PYTHONPATH", "")
-    r = subprocess.run([sys.executable, "-c", RUN, str(path), str(out), json.dumps(PROMPT), str(STEPS)], env=env,
+    tests = os.path.dirname(os.path.abspath(__file__))
+    r = subprocess.run([sys.executable, "-c", RUN, str(path), str(out), json.dumps(PROMPT), str(STEPS), tests], env=env,
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
     return np.load(out)

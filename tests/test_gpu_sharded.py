@@ -23,9 +23,9 @@ STEPS = 5
 
 
 def run_model(path):
-    from sardyne_b200 import runtime
-    m = runtime.Model(str(path))
-    ctx = runtime.Context(m, max_seq=96, n_batch=len(PROMPT))
+    import refruntime as rt
+    m = rt.model(str(path))
+    ctx = rt.Context(m, max_seq=96, n_batch=len(PROMPT))
     out = [ctx.eval(PROMPT)]
     for i in range(STEPS):
         out.append(ctx.eval([int(np.argmax(out[-1])) + i % 2]))
