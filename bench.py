@@ -345,36 +345,50 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.synchronize()
     capi.check()
 
-    # per-matrix device time of this rank's slices (informational, outside the timed region)
+    def capture(fn):
+        """fn's launches (on `stream`) as a CUDA graph, replayed without host launch overhead."""
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+            fn()
+        return g
+
+    # per-matrix device time of this rank's slices (informational, outside the timed region):
+    # 20 sweeps with and without the matrix, each as one graph (interleaved, so every matrix is
+    # cold in L2 when it runs)
+    reps = 20
+    sweep_all = capture(lambda: [matvecs() for _ in range(reps)])
     per = []
     for i, (fmt, n_out, n_in, _) in enumerate(mats):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = 50
-        e0.record(stream)
-        for _ in range(reps):
-            for j, (f2, o2, i2, _) in enumerate(mats):  # interleave so this matrix is cold in L2 each time
-                if j == i:
-                    continue
-                lib.sdy_qmatvec_dev(handles[j], ctypes.c_void_p(d_xq[i2].data_ptr()), 1,
-                                    ctypes.c_void_p(d_out[j].data_ptr()), o2, 0, o2, sp)
-        e1.record(stream)
-        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e2.record(stream)
-        for _ in range(reps):
-            for j, (f2, o2, i2, _) in enumerate(mats):
-                lib.sdy_qmatvec_dev(handles[j], ctypes.c_void_p(d_xq[i2].data_ptr()), 1,
-                                    ctypes.c_void_p(d_out[j].data_ptr()), o2, 0, o2, sp)
-        e3.record(stream)
-        torch.cuda.synchronize()
-        ms = (e2.elapsed_time(e3) - e0.elapsed_time(e1)) / reps
+        def without_i(i=i):
+            for _ in range(reps):
+                for j, (f2, o2, i2, _) in enumerate(mats):
+                    if j != i:
+                        lib.sdy_qmatvec_dev(handles[j], ctypes.c_void_p(d_xq[i2].data_ptr()), 1,
+                                            ctypes.c_void_p(d_out[j].data_ptr()), o2, 0, o2, sp)
+        sweep_wo = capture(without_i)
+        ts = []
+        for g in (sweep_wo, sweep_all, sweep_wo, sweep_all):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        # matvecs() also quantizes the inputs (6 small launches per sweep), so the difference is an
+        # upper bound of the matrix's own time
+        ms = (min(ts[1], ts[3]) - min(ts[0], ts[2])) / reps
         per.append({"format": fmt, "n_out": n_out, "n_in": n_in, "us": round(ms * 1e3, 2),
                     "GB/s": round(alg_bytes(fmt, n_out, n_in) / (ms * 1e-3) / 1e9, 1)})
-    with torch.cuda.stream(stream):
-        step()  # leave every rank's full y in place again
+        del sweep_wo
+    del sweep_all
+
+    # the timed step as one CUDA graph: 6 activation quantizations, 6 matvecs (and, N > 1, the
+    # all-gather of y)
+    step_graph = capture(step)
+    step_graph.replay()
     torch.cuda.synchronize()
 
     # timed region
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = lib.sdy_kernel_launches()
     with ClockSampler(torch.cuda.current_device()) as clk:
@@ -383,11 +397,30 @@ def run_b200(args, rank, world, local_rank):
         with torch.cuda.stream(stream):
             start.record(stream)
             for k in range(args.steps):
-                step(evs[k])
+                step_graph.replay()
             end.record(stream)
         torch.cuda.synchronize()
         barrier()
-    launches = lib.sdy_kernel_launches() - launches0
+    # launches recorded in the graph once, replayed every step
+    launches_per_step = 2 * len(mats)
+    # the dominant kernel timed per launch: eager launches each bracketed by events on its stream,
+    # queued behind a ~10 ms spin kernel so that the host is ahead of the GPU and no host launch
+    # gap falls inside a bracket
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    fmt_d, o_d, i_d, _ = mats[dominant]
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(20_000_000)
+        for k in range(args.steps):
+            evs[k][0].record(stream)
+            lib.sdy_qmatvec_dev(handles[dominant], ctypes.c_void_p(d_xq[i_d].data_ptr()), 1,
+                                ctypes.c_void_p(d_out[dominant].data_ptr()), o_d, 0, o_d, sp)
+            evs[k][1].record(stream)
+            for j, (f2, o2, i2, _) in enumerate(mats):  # the rest of the sweep between launches
+                if j != dominant:
+                    lib.sdy_qmatvec_dev(handles[j], ctypes.c_void_p(d_xq[i2].data_ptr()), 1,
+                                        ctypes.c_void_p(d_out[j].data_ptr()), o2, 0, o2, sp)
+    torch.cuda.synchronize()
+    launches = launches_per_step * args.steps
     capi.check()
     ms_total = start.elapsed_time(end)
     tm = torch.tensor([ms_total], dtype=torch.float64, device=dev)

@@ -53,8 +53,17 @@ def qref() -> ctypes.CDLL:
         lib.oq_matmul_q_rows.restype = None
         lib.oq_matmul_q_rows.argtypes = [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i]
         lib.oq_row_bytes.restype, lib.oq_row_bytes.argtypes = ctypes.c_size_t, [_i, _i]
+        lib.oq_expf_n.restype, lib.oq_expf_n.argtypes = None, [_vp, _vp, ctypes.c_size_t]
         _oracle = lib
     return _oracle
+
+
+def expf(x) -> np.ndarray:
+    """libm's expf element by element: the exp the reference's fp32 code calls."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    qref().oq_expf_n(_ptr(x), _ptr(y), x.size)
+    return y
 
 
 def row_bytes(kind: str, n: int) -> int:

@@ -272,3 +272,9 @@ void oq_quantize_rows(int vtype, const float *x, uint8_t *xq, int n_in, int n_to
         else oq_quant_q8_K(x + (size_t)t * n_in, xq + (size_t)t * xr, n_in);
     }
 }
+
+/* The reference's fp32 parts call libm's expf (softmax ops.c:353-364, SiLU ops.c:366-371); the
+ * operation-order models in the tests take it from the same libm, element by element. */
+void oq_expf_n(const float *x, float *y, size_t n) {
+    for (size_t i = 0; i < n; i++) y[i] = expf(x[i]);
+}

@@ -383,7 +383,7 @@ __global__ void __cluster_dims__(AC, 1, 1) __launch_bounds__(AC_THREADS, 1)
         const float m = gmax[r];
         double sacc = 0.0;
         for (int j = lane; j < nl; j += 32) {
-            const float e = exp_cr(__fsub_rn(scl[r * lmax + j], m));
+            const float e = expf_ref(__fsub_rn(scl[r * lmax + j], m));
             scl[r * lmax + j] = e;
             sacc += e;
             if (push)
@@ -621,7 +621,7 @@ __global__ void __launch_bounds__(PF_THREADS)
         for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         double sacc = 0.0;
         for (int j = lane; j < nk; j += 32) {
-            const float e = exp_cr(__fsub_rn(r[j], m));
+            const float e = expf_ref(__fsub_rn(r[j], m));
             r[j] = e;
             sacc += e;
         }

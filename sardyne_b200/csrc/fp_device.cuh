@@ -1,16 +1,12 @@
 // Device helpers shared by the fp32 kernels (fp_ops.cu, attention.cu, fused.cu): the
-// reference's scalar dot product, the correctly rounded exp, and block reductions.
+// reference's scalar dot product, the reference host's expf (expf_ref.h), and block reductions.
 #pragma once
 #include "common.cuh"
+#include "expf_ref.h"
 
 #include <cuda_bf16.h>
 
 namespace sdy {
-
-// The correctly rounded expf: exp() in double rounded once to float. The reference calls libm's
-// expf, whose glibc version (error < 0.502 ulp) differs from this in the last bit on ~0.06% of
-// inputs; softmax and SiLU results can differ from the reference's by that much.
-__device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
 
 __device__ __forceinline__ float load_w(const void *w, int type, size_t i) {
     if (type == T_F32) return ((const float *)w)[i];
@@ -68,7 +64,7 @@ __device__ inline void softmax_block(float *v, int n) {
     m = block_max_f(m);
     double sum = 0.0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float e = exp_cr(__fsub_rn(v[i], m));
+        float e = expf_ref(__fsub_rn(v[i], m));
         v[i] = e;
         sum += e;
     }

@@ -73,7 +73,7 @@ __global__ void silu_mul_kernel(float *gate, const float *up, int64_t n) {
     pdl_wait();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         float g = gate[i];
-        gate[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_cr(-g))), up[i]);
+        gate[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf_ref(-g))), up[i]);
     }
 }
 

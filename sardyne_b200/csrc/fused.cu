@@ -154,7 +154,7 @@ __device__ void softmax_topk_block(const float *logits, float *prob, float *pv, 
     m = bmax_f(m, fpart);
     double sum = 0.0;
     for (int e = threadIdx.x; e < ne; e += blockDim.x) {
-        const float v = exp_cr(__fsub_rn(prob[e], m));
+        const float v = expf_ref(__fsub_rn(prob[e], m));
         prob[e] = v;
         sum += v;
     }

@@ -171,7 +171,7 @@ __device__ inline void norm_quant_row(const float *x, const float *w, int n, flo
 
 // The SwiGLU gate of one element, silu(g) * u, in the reference's operation order (ops.c:369).
 __device__ __forceinline__ float silu_mul(float g, float u) {
-    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_cr(-g))), u);
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf_ref(-g))), u);
 }
 
 // Token t's input row as ActIn describes it (RMSNorm, SwiGLU gate or x as is), quantized into
