@@ -196,6 +196,8 @@ struct engine_ctx {
           *logits = nullptr, *scores = nullptr;
     float *moe_probs = nullptr, *moe_w = nullptr, *moe_gu = nullptr, *moe_y = nullptr;
     int32_t *moe_count = nullptr;  // per-token router counters (router_topk)
+    unsigned *md_sync = nullptr;   // fused MoE decode block: 3 barrier words + 1 status word
+    unsigned *h_md_status = nullptr;  // pinned copy of the status word, read after each eval
     int32_t *grp_off = nullptr, *grp_slot = nullptr, *grp_tiles = nullptr;  // slots by expert (prefill GEMM)
     // Sharded models: all-reduce sources, zero outside this rank's columns (hsend: FFN activations
     // [B][ffn_dim], xsend: residual [B][dim], lsend: logits), and the gathered FFN activations.
@@ -800,6 +802,52 @@ bool moe_norm_fused(int n, const DLayer &L, const engine_model_info &in) {
     return true;
 }
 
+// A single-token MoE block as one kernel (moe_decode.cu; SARDYNE_MOE_DECODE=off: the separate
+// norm, router, expert and combine kernels). One GPU only: sharded experts need the exchange of
+// the expert outputs before the combine.
+bool moe_decode_ok(const engine_ctx *c, const DLayer &L, int n) {
+    static const bool off = [] {
+        const char *v = getenv("SARDYNE_MOE_DECODE");
+        return v && !strcmp(v, "off");
+    }();
+    const engine_model_info &in = c->m->info;
+    if (off || n != 1 || c->m->world > 1 || !fusion_enabled() || L.gateup.parts.size() != 1 || L.gate_inp.quant() ||
+        !L.down.quant())
+        return false;
+    const DMat &gu = L.gateup.parts[0].m;
+    return gu.quant() && gu.n_out == 2 * in.ffn_exp_dim &&
+           moe_decode_supported(gu.type, L.down.type, L.gate_inp.type, in.dim, in.ffn_exp_dim, in.n_expert,
+                                in.n_expert_used);
+}
+
+bool moe_block_decode(engine_ctx *c, const DLayer &L) {
+    const engine_model_info &in = c->m->info;
+    const DMat &gu = L.gateup.parts[0].m;
+    MoeDecode a;
+    a.x = c->x;
+    a.norm_w = L.ffn_norm;
+    a.eps = in.norm_eps;
+    a.dim = in.dim;
+    a.router = L.gate_inp.f;
+    a.rtype = L.gate_inp.type;
+    a.ne = in.n_expert;
+    a.k = in.n_expert_used;
+    a.gu_slabs = gu.q.slabs;
+    a.gpe_gu = gu.gpe;
+    a.fe = in.ffn_exp_dim;
+    a.dn_slabs = L.down.q.slabs;
+    a.gpe_dn = L.down.gpe;
+    a.logits = c->moe_probs;
+    a.top = c->moe_top;
+    a.wts = c->moe_w;
+    a.gu = c->moe_gu;
+    a.y = c->moe_y;
+    a.bar = c->md_sync;
+    a.status = c->md_sync + 3;
+    if (!moe_decode(a, gu.type, L.down.type, c->st)) return false;
+    return true;
+}
+
 // nin: the step's ffn norm is fused into the router and the gate|up experts (x = the residual).
 void moe_ffn(engine_ctx *c, const DLayer &L, int n, const ActIn *nin = nullptr) {
     const engine_model_info &in = c->m->info;
@@ -945,7 +993,9 @@ void forward(engine_ctx *c, int n, int out_rows) {
             matmul(c, c->x, dim, c->att, q_dim, L.wo, n, c->x);
         // MLP: x = x + down(silu(gate.norm(x)) * up.norm(x)), or its MoE
         const ActIn ffn_nin{c->x, dim, L.ffn_norm, in.norm_eps};
-        if (in.n_expert) {
+        if (in.n_expert && moe_decode_ok(c, L, n) && moe_block_decode(c, L)) {
+            // norm, router, experts and combine in one kernel
+        } else if (in.n_expert) {
             std::vector<const DMat *> need = mats_of(L.gateup);
             if (L.gate_inp.quant()) need.push_back(&L.gate_inp);
             if (moe_norm_fused(n, L, in)) {
@@ -1233,6 +1283,7 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
     if (in.n_expert) {
         items.push_back({(void **)&c->moe_probs, B * in.n_expert * 4});
         items.push_back({(void **)&c->moe_count, B * 4});
+        items.push_back({(void **)&c->md_sync, 4 * sizeof(unsigned)});
         items.push_back({(void **)&c->grp_off, ((size_t)in.n_expert + 2) * 4});
         items.push_back({(void **)&c->grp_slot, slots * 4});
         items.push_back({(void **)&c->grp_tiles, (slots / GEMM_TILE_TOKENS + in.n_expert) * 4});
@@ -1274,6 +1325,7 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
     bool zeroed = true;  // all-reduce sources start (and outside this rank's columns stay) zero
     if (c->hsend) zeroed = SDY_CUDA(cudaMemset(c->hsend, 0, B * ffn * 4)) && SDY_CUDA(cudaMemset(c->xsend, 0, B * in.dim * 4));
     if (c->lsend) zeroed = zeroed && SDY_CUDA(cudaMemset(c->lsend, 0, logit_rows * in.n_vocab * 4));
+    if (c->md_sync) zeroed = zeroed && SDY_CUDA(cudaMemset(c->md_sync, 0, 4 * sizeof(unsigned)));
     if (!zeroed || (c->moe_count && !SDY_CUDA(cudaMemset(c->moe_count, 0, B * 4)))) {  // router counters start at zero
         put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
         engine_ctx_free(c);
@@ -1284,7 +1336,8 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
         !SDY_CUDA(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking)) ||
         !SDY_CUDA(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming)) ||
         !SDY_CUDA(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming)) ||
-        !SDY_CUDA(cudaMallocHost(&c->h_logits, lbytes)) || !SDY_CUDA(cudaMallocHost(&c->h_tokpos, (B + 1) * 4))) {
+        !SDY_CUDA(cudaMallocHost(&c->h_logits, lbytes)) || !SDY_CUDA(cudaMallocHost(&c->h_tokpos, (B + 1) * 4)) ||
+        !SDY_CUDA(cudaMallocHost(&c->h_md_status, sizeof(unsigned)))) {
         put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
         engine_ctx_free(c);
         return nullptr;
@@ -1310,6 +1363,7 @@ void engine_ctx_free(engine_ctx *c) {
     if (c->arena) cudaFree(c->arena);
     if (c->h_logits) cudaFreeHost(c->h_logits);
     if (c->h_tokpos) cudaFreeHost(c->h_tokpos);
+    if (c->h_md_status) cudaFreeHost(c->h_md_status);
     delete c;
 }
 
@@ -1349,7 +1403,14 @@ int engine_eval(engine_ctx *c, const int32_t *tokens, int32_t n) {
     }
     size_t lb = (size_t)out_rows * c->m->info.n_vocab * 4;
     SDY_CUDA(cudaMemcpyAsync(c->h_logits, c->logits, lb, cudaMemcpyDeviceToHost, c->st));
+    if (c->md_sync) SDY_CUDA(cudaMemcpyAsync(c->h_md_status, c->md_sync + 3, sizeof(unsigned), cudaMemcpyDeviceToHost, c->st));
     SDY_CUDA(cudaStreamSynchronize(c->st));
+    if (c->md_sync && *c->h_md_status) {  // a grid barrier of the fused MoE block gave up
+        set_error("blocco MoE: attesa tra i blocchi della griglia scaduta");
+        cudaMemsetAsync(c->md_sync, 0, 4 * sizeof(unsigned), c->st);
+        cudaStreamSynchronize(c->st);
+        *c->h_md_status = 0;
+    }
     if (last_error()[0]) {
         c->n_past = saved;
         snprintf(c->err, sizeof c->err, "errore GPU: %s", last_error());

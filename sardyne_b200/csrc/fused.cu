@@ -18,27 +18,6 @@ namespace sdy {
 namespace {
 
 
-__device__ double bsum_d(double v, double *part) {
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __syncthreads();
-    if (lane == 0) part[w] = v;
-    __syncthreads();
-    v = lane < (int)(blockDim.x >> 5) ? part[lane] : 0.0;
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-__device__ float bmax_f(float v, float *part) {
-    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __syncthreads();
-    if (lane == 0) part[w] = v;
-    __syncthreads();
-    v = lane < (int)(blockDim.x >> 5) ? part[lane] : -INFINITY;
-    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-
 // Quantize the warp's span (values in registers) into the requested activation types.
 __device__ __forceinline__ void quantize_span(const float v[8], int e0, int n, int t, int span, const XQ &q8k,
                                               const XQ &q80) {
@@ -129,60 +108,6 @@ __global__ void post_qkv_kernel(PostQKV p) {
 constexpr int ROUTER_EPC = 8;  // experts per CTA: one warp each
 constexpr int ROUTER_THREADS = 32 * ROUTER_EPC;
 
-__device__ __forceinline__ float4 load4_w(const void *w, int wtype, size_t i) {  // i a multiple of 4
-    if (wtype == T_F32) return *(const float4 *)((const float *)w + i);
-    const uint2 u = *(const uint2 *)((const uint16_t *)w + i);
-    if (wtype == T_F16) {
-        const float2 a = __half22float2(*(const __half2 *)&u.x), b = __half22float2(*(const __half2 *)&u.y);
-        return make_float4(a.x, a.y, b.x, b.y);
-    }
-    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
-                       __uint_as_float(u.y & 0xFFFF0000u));
-}
-
-// Softmax (ops.c:353-364) and top-k (model_llama.c:653-666) of one token's ne logits by the whole
-// block; prob: shared array of ne floats, pv: k floats. The reference's insertion keeps the k
-// largest probabilities in descending order, equal values in ascending expert id: expert e is at
-// position rank(e) = #{j : p_j > p_e} + #{j < e : p_j == p_e}, computed for every expert in
-// parallel. Weights are renormalised by their float sum taken in that order.
-__device__ void softmax_topk_block(const float *logits, float *prob, float *pv, int ne, int k, int32_t *tp,
-                                   float *wout, double *dpart, float *fpart) {
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = __ldcg(logits + e);
-    __syncthreads();
-    float m = -INFINITY;
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) m = fmaxf(m, prob[e]);
-    m = bmax_f(m, fpart);
-    double sum = 0.0;
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) {
-        const float v = expf_ref(__fsub_rn(prob[e], m));
-        prob[e] = v;
-        sum += v;
-    }
-    sum = bsum_d(sum, dpart);
-    const float inv = (float)(1.0 / sum);
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = __fmul_rn(prob[e], inv);
-    __syncthreads();
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) {
-        const float pe = prob[e];
-        int rank = 0;
-        for (int j = 0; j < ne; j++) {
-            const float pj = prob[j];
-            rank += (pj > pe) | ((pj == pe) & (j < e));
-        }
-        if (rank < k) {
-            tp[rank] = e;
-            pv[rank] = pe;
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float s = 0.0f;
-        for (int i = 0; i < k; i++) s = __fadd_rn(s, pv[i]);
-        fpart[0] = s;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < k; i += blockDim.x) wout[i] = __fdiv_rn(pv[i], fpart[0]);
-}
 
 // Float router, one warp per (expert, token), ROUTER_EPC experts per CTA: logits[t][e] = x[t].w[e]
 // with the reference's four-accumulator dot (ops.c:155-167) — the row (a constant weight, staged

@@ -72,4 +72,31 @@ void moe_group(const int32_t *top, int n_slots, int e0, int ne, int tile, int32_
 void moe_combine(const float *y, int64_t ldy, const int32_t *top, const float *w, int k, int dim, int n_tok, float *x,
                  int64_t ldx, cudaStream_t s);
 
+// The MoE block of one token in one kernel (moe_decode.cu): x += the k chosen experts' SwiGLU
+// FFNs of RMSNorm(x) * norm_w, weighted by the renormalised router probabilities. gu_slabs: the
+// fused gate|up matrices of all experts (2 * fe rows each, gpe_gu groups per expert); dn_slabs:
+// the down matrices (dim rows each, gpe_dn groups). Scratch: logits [ne], top/wts [k],
+// gu [k][2 fe], y [k][dim]; bar: 3 words and status: 1 word, zero before the first launch (a
+// nonzero status after a step means a grid barrier gave up; the words must then be cleared).
+struct MoeDecode {
+    float *x;
+    const float *norm_w;
+    float eps;
+    int dim;
+    const void *router;
+    int rtype, ne, k;
+    const uint8_t *gu_slabs;
+    int64_t gpe_gu;
+    int fe;
+    const uint8_t *dn_slabs;
+    int64_t gpe_dn;
+    float *logits;
+    int32_t *top;
+    float *wts, *gu, *y;
+    unsigned *bar, *status;
+};
+bool moe_decode_supported(int tg, int td, int rtype, int dim, int fe, int ne, int k);
+// False (nothing launched) when this GPU cannot hold the grid at once.
+bool moe_decode(const MoeDecode &a, int tg, int td, cudaStream_t s);
+
 }  // namespace sdy

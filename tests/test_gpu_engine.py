@@ -42,6 +42,14 @@ SPECS = {
     "moe-one": dict(arch="qwen3moe", dim=32, head_dim=16, n_expert=1, n_used=1, ffn_exp=64, tied=False, qk_norm=True),
     "moe-kquant": dict(arch="qwen3moe", dim=256, head_dim=64, n_expert=8, n_used=3, ffn_exp=256, tied=False,
                        qk_norm=True, kinds=synth.mix_q4_k_m_untied),
+    # single-token steps take the one-kernel MoE block (hidden size a multiple of 1024)
+    "moe-block": dict(arch="qwen3moe", dim=1024, n_head=8, n_kv_head=2, head_dim=128, n_expert=16, n_used=4,
+                      ffn_exp=512, vocab=512, tied=False, qk_norm=True, std=0.02, kinds=synth.mix_q4_k_m_untied),
+    # a float router wider than the fused router kernel's shared memory: the generic matmul,
+    # softmax and top-k kernels
+    "moe-wide-router": dict(arch="qwen3moe", dim=6144, n_layer=1, n_head=4, n_kv_head=2, head_dim=64, n_expert=8,
+                            n_used=2, ffn_exp=256, vocab=256, tied=False, qk_norm=True, std=0.02,
+                            kinds=lambda name, n_in: "F32" if "gate_inp" in name or "norm" in name else "Q8_0"),
 }
 
 

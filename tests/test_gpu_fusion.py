@@ -1,7 +1,7 @@
 """The decode step's fused kernels return exactly what the separate kernels return: the norm,
 SwiGLU gate and activation quantization moved into the prologue of the consuming matvec, the
 two-format projection launch (Q/K in Q4_K and V in Q6_K as one kernel), the MoE norm inside the
-router and expert kernels, and the L2 prefetch hints. Each configuration runs in its own process
+router and expert kernels, the whole MoE block as one kernel, and the L2 prefetch hints. Each configuration runs in its own process
 (the switches are read once per process); logits must match bit for bit."""
 import json
 import os
@@ -20,6 +20,10 @@ SPECS = {
                          tied=False, std=0.02, kinds=synth.mix_q4_k_m_untied),
     "moe-kquant": dict(arch="qwen3moe", dim=256, n_layer=3, head_dim=64, n_expert=8, n_used=3, ffn_exp=256,
                        vocab=512, tied=False, qk_norm=True, std=0.02, kinds=synth.mix_q4_k_m_untied),
+    # wide enough for the one-kernel MoE decode block (hidden size a multiple of 1024)
+    "moe-block": dict(arch="qwen3moe", dim=1024, n_layer=3, n_head=8, n_kv_head=2, head_dim=128, n_expert=16,
+                      n_used=4, ffn_exp=512, vocab=512, tied=False, qk_norm=True, std=0.02,
+                      kinds=synth.mix_q4_k_m_untied),
 }
 PROMPT = [3, 14, 15, 9, 26, 5, 35, 8]
 STEPS = 6
@@ -44,12 +48,14 @@ CONFIGS = {
     "no-prefetch": {"SARDYNE_L2_PREFETCH": "off"},
     "prefetch-all": {"SARDYNE_L2_PREFETCH": "all"},
     "no-graph": {"SARDYNE_NO_GRAPH": "1"},
+    "moe-block-off": {"SARDYNE_MOE_DECODE": "off"},
 }
 
 
 def run(path, out, env_extra):
     env = dict(os.environ)
-    for k in ("SARDYNE_NO_FUSED_NORM", "SARDYNE_MOE_NORM", "SARDYNE_L2_PREFETCH", "SARDYNE_NO_GRAPH"):
+    for k in ("SARDYNE_NO_FUSED_NORM", "SARDYNE_MOE_NORM", "SARDYNE_L2_PREFETCH", "SARDYNE_NO_GRAPH",
+              "SARDYNE_MOE_DECODE"):
         env.pop(k, None)
     env.update(env_extra)
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
