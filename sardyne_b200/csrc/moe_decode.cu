@@ -237,7 +237,9 @@ __global__ void __launch_bounds__(MD_THREADS) moe_decode_kernel(MoeDecode a) {
     }
     if (!grid_barrier(a.bar, P, a.status)) return;
 
-    // 2: softmax and top-k (every CTA the same), weights renormalised.
+    // 2: softmax and top-k (every CTA the same), weights renormalised. The slots start at expert
+    // 0, so that no expert id outside [0, ne) can reach the weight addressing below.
+    if (tid < k) top_s[tid] = 0;
     softmax_topk_block(a.logits, prob, prob + ne, ne, k, top_s, w_s, dpart, fpart);
     __syncthreads();
     if (cta == 0 && tid < k) {
