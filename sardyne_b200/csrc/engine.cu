@@ -802,13 +802,13 @@ bool moe_norm_fused(int n, const DLayer &L, const engine_model_info &in) {
     return true;
 }
 
-// A single-token MoE block as one kernel (moe_decode.cu; SARDYNE_MOE_DECODE=off: the separate
-// norm, router, expert and combine kernels). One GPU only: sharded experts need the exchange of
-// the expert outputs before the combine.
+// A single-token MoE block as one kernel (moe_decode.cu) with SARDYNE_MOE_DECODE=on; by default
+// the separate norm, router, expert and combine kernels, measured faster so far. One GPU only:
+// sharded experts need the exchange of the expert outputs before the combine.
 bool moe_decode_ok(const engine_ctx *c, const DLayer &L, int n) {
     static const bool off = [] {
         const char *v = getenv("SARDYNE_MOE_DECODE");
-        return v && !strcmp(v, "off");
+        return !(v && !strcmp(v, "on"));
     }();
     const engine_model_info &in = c->m->info;
     if (off || n != 1 || c->m->world > 1 || !fusion_enabled() || L.gateup.parts.size() != 1 || L.gate_inp.quant() ||

@@ -48,7 +48,7 @@ CONFIGS = {
     "no-prefetch": {"SARDYNE_L2_PREFETCH": "off"},
     "prefetch-all": {"SARDYNE_L2_PREFETCH": "all"},
     "no-graph": {"SARDYNE_NO_GRAPH": "1"},
-    "moe-block-off": {"SARDYNE_MOE_DECODE": "off"},
+    "moe-block-on": {"SARDYNE_MOE_DECODE": "on"},
 }
 
 
