@@ -369,9 +369,10 @@ def run_b200(args, rank, world, local_rank):
         ts = []
         for g in (sweep_wo, sweep_all, sweep_wo, sweep_all):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            g.replay()
-            e1.record(stream)
+            with torch.cuda.stream(stream):  # a graph replays on the current stream
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
             torch.cuda.synchronize()
             ts.append(e0.elapsed_time(e1))
         # matvecs() also quantizes the inputs (6 small launches per sweep), so the difference is an
@@ -385,7 +386,8 @@ def run_b200(args, rank, world, local_rank):
     # the timed step as one CUDA graph: 6 activation quantizations, 6 matvecs (and, N > 1, the
     # all-gather of y)
     step_graph = capture(step)
-    step_graph.replay()
+    with torch.cuda.stream(stream):
+        step_graph.replay()
     torch.cuda.synchronize()
 
     # timed region
