@@ -673,12 +673,13 @@ def measure_decode(name, args, rank, world, cpu_baseline=True):
     from sardyne_b200 import capi, runtime, synth
     n_prompt, n_decode, ctx_len = DECODE_MODELS[name]
     n_decode = args.decode_steps or n_decode
+    layers = getattr(args, "layers", 0) or 0
     if world > 1:
         if rank == 0:
-            synth.baseline_model(name, args.model_dir)  # written once, before the other ranks open it
+            synth.baseline_model(name, args.model_dir, layers)  # written once, before the other ranks open it
         dist.barrier()
         runtime.shard_from_torch()
-    path = synth.baseline_model(name, args.model_dir)
+    path = synth.baseline_model(name, args.model_dir, layers)
     lib = capi.lib()
     t0 = time.perf_counter()
     model, ctx, info = engine_open(lib, path, ctx_len, n_prompt)
@@ -726,8 +727,9 @@ def measure_decode(name, args, rank, world, cpu_baseline=True):
            "unit": "tok/s", "n_gpus": world, "steps": n_decode, "ms_per_step": round((t2 - t1) / n_decode * 1e3, 4),
            "prefill_tok_s": round(n_prompt / (t1 - t0), 1),
            "scaling": "strong" if world > 1 else "weak",
-           "workload": f"BASELINE {name} shape: {n_prompt}-token prompt (uniform ids, seed 0), {n_decode} greedy "
-                       f"decode steps, context {ctx_len}; random-init Q4_K_M mix",
+           "workload": f"BASELINE {name} shape{f' cut to {layers} layers' if layers else ''}: {n_prompt}-token "
+                       f"prompt (uniform ids, seed 0), {n_decode} greedy decode steps, context {ctx_len}; "
+                       f"random-init Q4_K_M mix",
            "model_gb": round(path.stat().st_size / 1e9, 2), "weight_bytes_per_token": wbytes,
            "parallelism": f"ffn/expert/vocab shards x{world}, attention replicated" if world > 1 else "1 GPU",
            "roofline": {"bound": "hbm", "achieved": round(wbytes * tps / 1e9, 1), "peak": round(peak * world, 1),
@@ -772,6 +774,8 @@ def main():
                                                          "SARDYNE_MODEL_DIR, /dev/shm or the temp dir)")
     ap.add_argument("--no-decode", action="store_true", help="matvec: leave out the decode object")
     ap.add_argument("--decode-steps", type=int, default=0)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decode: the model's shape with only this many layers (small cases for ncu captures)")
     ap.add_argument("--profile-step", action="store_true",
                     help="decode: run one extra step between cudaProfilerStart/Stop (ncu --profile-from-start off)")
     ap.add_argument("--only", default=None, help="matvec: keep one matrix, e.g. Q6_K:151936 (for ncu captures)")

@@ -28,9 +28,11 @@
 namespace sdy {
 
 // Bit patterns of 2^(i/32) rounded to nearest double, minus i << 47 (the table entry is added to
-// k << 47, which puts k div 32 into the exponent field).
+// k << 47, which puts k div 32 into the exponent field). On the GPU the table sits in global
+// memory and is read through the read-only L1 path: the lanes of a warp index different entries,
+// which the constant cache would serve one address at a time.
 #if defined(__CUDACC__)
-__device__ __constant__
+__device__
 #endif
 static const uint64_t kExp2Tab32[32] = {
     0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
@@ -66,7 +68,7 @@ SDY_EXPF_FN float expf_ref(float x) {
     memcpy(&ki, &kd_shifted, 8);
     const double kd = __dsub_rn(kd_shifted, SHIFT);
     const double r = __fma_rn(INV_LN2_N, xd, -kd);
-    uint64_t t = kExp2Tab32[ki % 32] + (ki << 47);
+    uint64_t t = __ldg((const unsigned long long *)&kExp2Tab32[ki % 32]) + (ki << 47);
     double s;
     memcpy(&s, &t, 8);
     const double p = __fma_rn(C0, r, C1), r2 = __dmul_rn(r, r);

@@ -141,23 +141,55 @@ __device__ __forceinline__ float4 load4_w(const void *w, int wtype, size_t i) { 
 // block; prob: shared array of ne floats, pv: k floats. The reference's insertion keeps the k
 // largest probabilities in descending order, equal values in ascending expert id: expert e is at
 // position rank(e) = #{j : p_j > p_e} + #{j < e : p_j == p_e}, computed for every expert in
-// parallel. Weights are renormalised by their float sum taken in that order.
+// parallel. Weights are renormalised by their float sum taken in that order. The caller syncs the
+// block before reading tp / wout.
 __device__ inline void softmax_topk_block(const float *logits, float *prob, float *pv, int ne, int k, int32_t *tp,
-                                   float *wout, double *dpart, float *fpart) {
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = __ldcg(logits + e);
-    __syncthreads();
-    float m = -INFINITY;
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) m = fmaxf(m, prob[e]);
-    m = bmax_f(m, fpart);
-    double sum = 0.0;
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) {
-        const float v = expf_ref(__fsub_rn(prob[e], m));
-        prob[e] = v;
-        sum += v;
+                                          float *wout, double *dpart, float *fpart) {
+    constexpr int PER = 8;  // logits per lane when one warp takes the softmax (ne <= 256)
+    if (ne <= 32 * PER) {
+        // Softmax by warp 0 alone, its logits in registers (lane l: e = l + 32 i): no block barrier
+        // until the probabilities are in shared memory.
+        if (threadIdx.x < 32) {
+            const int lane = threadIdx.x;
+            float v[PER];
+            float m = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < PER; i++) {
+                const int e = lane + 32 * i;
+                v[i] = e < ne ? __ldcg(logits + e) : -INFINITY;
+            }
+#pragma unroll
+            for (int i = 0; i < PER; i++) m = fmaxf(m, v[i]);
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            double sum = 0.0;
+#pragma unroll
+            for (int i = 0; i < PER; i++)
+                if (lane + 32 * i < ne) {
+                    v[i] = expf_ref(__fsub_rn(v[i], m));
+                    sum += v[i];
+                }
+            for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            const float inv = (float)(1.0 / sum);
+#pragma unroll
+            for (int i = 0; i < PER; i++)
+                if (lane + 32 * i < ne) prob[lane + 32 * i] = __fmul_rn(v[i], inv);
+        }
+    } else {
+        for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = __ldcg(logits + e);
+        __syncthreads();
+        float m = -INFINITY;
+        for (int e = threadIdx.x; e < ne; e += blockDim.x) m = fmaxf(m, prob[e]);
+        m = bmax_f(m, fpart);
+        double sum = 0.0;
+        for (int e = threadIdx.x; e < ne; e += blockDim.x) {
+            const float v = expf_ref(__fsub_rn(prob[e], m));
+            prob[e] = v;
+            sum += v;
+        }
+        sum = bsum_d(sum, dpart);
+        const float inv = (float)(1.0 / sum);
+        for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = __fmul_rn(prob[e], inv);
     }
-    sum = bsum_d(sum, dpart);
-    const float inv = (float)(1.0 / sum);
-    for (int e = threadIdx.x; e < ne; e += blockDim.x) prob[e] = __fmul_rn(prob[e], inv);
     __syncthreads();
     for (int e = threadIdx.x; e < ne; e += blockDim.x) {
         const float pe = prob[e];
@@ -172,13 +204,13 @@ __device__ inline void softmax_topk_block(const float *logits, float *prob, floa
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float s = 0.0f;
-        for (int i = 0; i < k; i++) s = __fadd_rn(s, pv[i]);
-        fpart[0] = s;
+    if (threadIdx.x < 32) {  // the float sum of the k weights in order, then the renormalisation
+        float sm = 0.0f;
+        if (threadIdx.x == 0)
+            for (int i = 0; i < k; i++) sm = __fadd_rn(sm, pv[i]);
+        sm = __shfl_sync(0xffffffffu, sm, 0);
+        for (int i = threadIdx.x; i < k; i += 32) wout[i] = __fdiv_rn(pv[i], sm);
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < k; i += blockDim.x) wout[i] = __fdiv_rn(pv[i], fpart[0]);
 }
 
 }  // namespace sdy

@@ -4,7 +4,7 @@
 // into the residual. It replaces the decode step's norm, router, gate|up, down and combine
 // launches (five dependent kernels) with one.
 //
-// Shape. A persistent grid of P CTAs, as many as the SMs hold at once (2 per SM), so all are
+// Shape. A persistent grid of P CTAs, one per SM (all resident at once), so all are
 // resident together, runs the phases with two grid barriers between them:
 //   0  every CTA: RMSNorm of x, kept as floats (router input) and as Q8_K (gate|up input) in
 //      shared memory (norm_quant_row, the same floats as the standalone norm kernel);
@@ -34,7 +34,8 @@
 namespace sdy {
 namespace {
 
-constexpr int MD_THREADS = 256;
+constexpr int MD_THREADS = 512;
+constexpr int MD_CTAS_PER_SM = 1;
 constexpr int MD_MAX_K = 64;
 constexpr long long MD_SPIN_LIMIT = 1ll << 22;  // polls of ~32 ns sleep: well under a second
 
@@ -71,7 +72,7 @@ __device__ bool grid_barrier(unsigned *bar, unsigned n, unsigned *status) {
                     good = 0;
                     break;
                 }
-                __nanosleep(32);
+                if (it > 4096) __nanosleep(64);  // tight polling first: most waits are short
             }
         }
         __threadfence();
@@ -170,15 +171,16 @@ __global__ void __launch_bounds__(MD_THREADS) moe_decode_kernel(MoeDecode a) {
     float *xs = (float *)(smem + plan.xs), *prod = (float *)(smem + plan.prod);
     float *terms = (float *)(smem + plan.terms), *prob = (float *)(smem + plan.prob);
 
-    // The CTA's first router row (a weight: read before the dependency wait), 8 floats a thread.
-    const int per = dim / MD_THREADS;  // dim % 2048 == 0 is not required: per is 8 at dim 2048
+    // The CTA's first router row (a weight: read before the dependency wait): float4 column
+    // f = tid + j * MD_THREADS of the row (dim <= 8192).
+    const int nf = dim / 4;
     float4 wrow[4];
     int e_router = (int)cta;
     if (e_router < ne) {
 #pragma unroll
         for (int j = 0; j < 4; j++)
-            if (j < per / 4)
-                wrow[j] = load4_w(a.router, a.rtype, (size_t)e_router * dim + 4 * ((size_t)tid * (per / 4) + j));
+            if (tid + j * MD_THREADS < nf)
+                wrow[j] = load4_w(a.router, a.rtype, (size_t)e_router * dim + 4 * (size_t)(tid + j * MD_THREADS));
     }
     pdl_wait();
 
@@ -203,13 +205,14 @@ __global__ void __launch_bounds__(MD_THREADS) moe_decode_kernel(MoeDecode a) {
         if (e_router != (int)cta) {
 #pragma unroll
             for (int j = 0; j < 4; j++)
-                if (j < per / 4)
-                    wrow[j] = load4_w(a.router, a.rtype, (size_t)e_router * dim + 4 * ((size_t)tid * (per / 4) + j));
+                if (tid + j * MD_THREADS < nf)
+                    wrow[j] = load4_w(a.router, a.rtype, (size_t)e_router * dim + 4 * (size_t)(tid + j * MD_THREADS));
         }
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            if (j >= per / 4) break;
-            const int i = 4 * (tid * (per / 4) + j), g = i / 4;
+            const int g = tid + j * MD_THREADS;
+            if (g >= nf) break;
+            const int i = 4 * g;
             prod[g] = __fmul_rn(xs[i], wrow[j].x);
             prod[G + g] = __fmul_rn(xs[i + 1], wrow[j].y);
             prod[2 * G + g] = __fmul_rn(xs[i + 2], wrow[j].z);
@@ -266,7 +269,19 @@ __global__ void __launch_bounds__(MD_THREADS) moe_decode_kernel(MoeDecode a) {
     if (u4b > u4a) {
         const int s0 = (int)(u4a / a.gpe_dn), s1 = (int)((u4b - 1) / a.gpe_dn), ns = s1 - s0 + 1;
         float *gs = (float *)(smem + plan.gs);
-        for (int i = tid; i < ns * 2 * fe; i += MD_THREADS) gs[i] = __ldcg(a.gu + (size_t)s0 * 2 * fe + i);
+        {  // the slots' gate|up rows, float4 loads all issued before the stores
+            const float4 *src = (const float4 *)(a.gu + (size_t)s0 * 2 * fe);
+            const int n4 = ns * 2 * fe / 4;
+            for (int i0 = tid; i0 < n4; i0 += 4 * MD_THREADS) {
+                float4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++)
+                    if (i0 + u * MD_THREADS < n4) v[u] = __ldcg(src + i0 + u * MD_THREADS);
+#pragma unroll
+                for (int u = 0; u < 4; u++)
+                    if (i0 + u * MD_THREADS < n4) ((float4 *)gs)[i0 + u * MD_THREADS] = v[u];
+            }
+        }
         __syncthreads();
         XQ qd;
         qd.vtype = T_Q8_K;
@@ -307,11 +322,30 @@ __global__ void __launch_bounds__(MD_THREADS) moe_decode_kernel(MoeDecode a) {
     __syncthreads();
     if (tid < k) ws[tid] = w_s[order[tid]];
     __syncthreads();
-    for (int i = tid; i < dim; i += MD_THREADS) {
-        const float acc = ordered_sum<8>(0.0f, k, [&](int j) {
-            return __fmul_rn(ws[j], __ldcg(a.y + (size_t)order[j] * dim + i));
-        });
-        a.x[i] = __fadd_rn(a.x[i], acc);
+    // four elements a thread, the k rows' loads issued 8 at a time ahead of their ordered adds
+    for (int f = tid; f < nf; f += MD_THREADS) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int j0 = 0; j0 < k; j0 += 8) {
+            float4 yv[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (j0 + u < k) yv[u] = __ldcg((const float4 *)(a.y + (size_t)order[j0 + u] * dim) + f);
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (j0 + u < k) {
+                    const float w = ws[j0 + u];
+                    acc.x = __fadd_rn(acc.x, __fmul_rn(w, yv[u].x));
+                    acc.y = __fadd_rn(acc.y, __fmul_rn(w, yv[u].y));
+                    acc.z = __fadd_rn(acc.z, __fmul_rn(w, yv[u].z));
+                    acc.w = __fadd_rn(acc.w, __fmul_rn(w, yv[u].w));
+                }
+        }
+        float4 xv = ((float4 *)a.x)[f];
+        xv.x = __fadd_rn(xv.x, acc.x);
+        xv.y = __fadd_rn(xv.y, acc.y);
+        xv.z = __fadd_rn(xv.z, acc.z);
+        xv.w = __fadd_rn(xv.w, acc.w);
+        ((float4 *)a.x)[f] = xv;
     }
 }
 
@@ -328,7 +362,7 @@ int grid_for(int smem) {
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    return std::min(n, 2) * sms;
+    return std::min(n, MD_CTAS_PER_SM) * sms;
 }
 
 template <int TG, int TD>
@@ -337,12 +371,12 @@ void launch_md(const MoeDecode &a, int grid, int smem, cudaStream_t s) {
 }
 
 int plan_grid(int tg, int td, const MoeDecode &a, int *smem) {
-    // the shared memory depends on the grid (units per CTA); take the grid at the plan for 2 CTAs
-    // per SM, then check the plan for that grid
+    // the shared memory depends on the grid (units per CTA): plan for MD_CTAS_PER_SM CTAs per SM,
+    // then check that the SMs hold that many
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t P = 2 * (int64_t)sms;
+    const int64_t P = (int64_t)MD_CTAS_PER_SM * sms;
     const int64_t U3 = (int64_t)a.k * a.gpe_gu, U4 = (int64_t)a.k * a.gpe_dn;
     *smem = md_plan(a.dim, a.fe, a.ne, (U3 + P - 1) / P, (U4 + P - 1) / P, a.gpe_dn).total;
     int grid = 0;
@@ -358,7 +392,7 @@ int plan_grid(int tg, int td, const MoeDecode &a, int *smem) {
 bool moe_decode_supported(int tg, int td, int rtype, int dim, int fe, int ne, int k) {
     const bool kq = (tg == T_Q4_K || tg == T_Q6_K) && (td == T_Q4_K || td == T_Q6_K);
     const bool ft = rtype == T_F32 || rtype == T_F16 || rtype == T_BF16;
-    return kq && ft && dim % 256 == 0 && dim >= 1024 && dim <= 4096 && dim % (4 * MD_THREADS) == 0 &&
+    return kq && ft && dim % 256 == 0 && dim >= 1024 && dim <= 4 * 4 * MD_THREADS &&
            fe % 256 == 0 && fe <= 4096 && k >= 1 && k <= MD_MAX_K && k <= ne && ne <= 4096;
 }
 

@@ -180,13 +180,16 @@ def model_cache_dir():
     return tempfile.gettempdir()
 
 
-def baseline_model(name, directory=None):
+def baseline_model(name, directory=None, layers=0):
     """Path of the synthetic GGUF of a BASELINE config (3: smollm2, 4: qwen25_3b, 5: qwen3moe),
-    written once (quantized blocks from one pool per type, seed 0) and reused from the cache."""
+    written once (quantized blocks from one pool per type, seed 0) and reused from the cache.
+    layers > 0: the same shape with only that many layers (small cases for profiling)."""
     import os
     import pathlib
-    path = pathlib.Path(directory or model_cache_dir()) / f"sardyne-{name}-v{SYNTH_LAYOUT}.gguf"
+    cut = f"-L{layers}" if layers else ""
+    path = pathlib.Path(directory or model_cache_dir()) / f"sardyne-{name}{cut}-v{SYNTH_LAYOUT}.gguf"
     if not path.exists():
-        write_model(path, Spec(**BASELINE_MODELS[name], synth=True, seed=0))
+        spec = dict(BASELINE_MODELS[name], **({"n_layer": layers} if layers else {}))
+        write_model(path, Spec(**spec, synth=True, seed=0))
         os.chmod(path, 0o644)
     return path
