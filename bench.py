@@ -704,6 +704,26 @@ def measure_decode(name, args, rank, world, cpu_baseline=True):
             t2 = time.perf_counter()
         launches = int(lib.sdy_kernel_launches() - launches0)
         capi.check()
+        # the same stream with the greedy choice made on the device (sdy_engine_eval_greedy): no
+        # logits copied back; every rank must choose the same ids as through the host logits
+        lib.engine_reset(ctx)
+        nxt_dev = ctypes.c_int32()
+        arr = (ctypes.c_int32 * n_prompt)(*prompt)
+        if world > 1:
+            dist.barrier()
+        t3 = time.perf_counter()
+        if lib.sdy_engine_eval_greedy(ctx, arr, n_prompt, ctypes.byref(nxt_dev)) != 0:
+            raise RuntimeError(lib.engine_last_error(ctx).decode(errors="replace"))
+        t4 = time.perf_counter()
+        dev_tokens = []
+        for _ in range(n_decode):
+            dev_tokens.append(nxt_dev.value)
+            one = (ctypes.c_int32 * 1)(nxt_dev.value)
+            if lib.sdy_engine_eval_greedy(ctx, one, 1, ctypes.byref(nxt_dev)) != 0:
+                raise RuntimeError(lib.engine_last_error(ctx).decode(errors="replace"))
+        t5 = time.perf_counter()
+        if dev_tokens != tokens:
+            raise RuntimeError("device greedy choice differs from numpy.argmax of the logits")
     finally:
         lib.engine_ctx_free(ctx)  # graphs and NCCL communicator released before the process group
         lib.engine_model_free(model)
@@ -711,9 +731,10 @@ def measure_decode(name, args, rank, world, cpu_baseline=True):
             runtime.set_shard(0, 1)
     if world > 1:  # the slowest rank's times; every rank must agree on the tokens
         dev = torch.device("cuda", torch.cuda.current_device())
-        tt = torch.tensor([t1 - t0, t2 - t1], dtype=torch.float64, device=dev)
+        tt = torch.tensor([t1 - t0, t2 - t1, t5 - t4], dtype=torch.float64, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t0, t1, t2 = 0.0, float(tt[0]), float(tt[0] + tt[1])
+        t4, t5 = 0.0, float(tt[2])
         toks = [None] * world
         dist.all_gather_object(toks, tokens)
         if any(tk != tokens for tk in toks):
@@ -738,6 +759,7 @@ def measure_decode(name, args, rank, world, cpu_baseline=True):
                         "peak_source": peak_kind},
            "e2e": {"value": round(tps, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                    "d2h_bytes_per_step": 4 * info.n_vocab},
+           "greedy_on_device_tok_s": round(n_decode / (t5 - t4), 2),
            "gpu_launches": launches, "clocks": clk.summary(), "load_s": round(load_s, 2),
            "first_tokens": tokens[:8]}
     if cpu_baseline and world == 1:

@@ -145,6 +145,12 @@ uint32_t sdy_kernel_status(void);
  * gathered on every rank and equal the one-GPU logits bit for bit. */
 int sdy_nccl_unique_id(void *out);
 int sdy_engine_set_shard(int32_t rank, int32_t world, const void *nccl_id);
+/* No counterpart in the reference, whose greedy loop takes numpy.argmax of the host logits
+ * (sardyne/runtime.py:115-140). engine_eval of `tokens`, then the id of the largest logit of the
+ * last token chosen on the device (the first on ties, the first NaN if any, as numpy.argmax) into
+ * *next; no logits are copied to the host (engine_logits returns NULL until the next engine_eval).
+ * Same errors as engine_eval. 0 or -1. */
+int sdy_engine_eval_greedy(engine_ctx *c, const int32_t *tokens, int32_t n, int32_t *next);
 void sdy_engine_get_shard(int32_t *rank, int32_t *world);
 /* Rows [*begin, *end) of n that `rank` of `world` holds, in whole units of `align` rows. */
 void sdy_shard_range(int64_t n, int32_t world, int32_t rank, int64_t align, int64_t *begin, int64_t *end);

@@ -197,6 +197,12 @@ struct engine_ctx {
     float *moe_probs = nullptr, *moe_w = nullptr, *moe_gu = nullptr, *moe_y = nullptr;
     int32_t *moe_count = nullptr;  // per-token router counters (router_topk)
     unsigned *md_sync = nullptr;   // fused MoE decode block: 3 barrier words + 1 status word
+    // greedy choice on the device: per-block candidates, the counter, the chosen id (and its
+    // pinned host copy)
+    float *am_v = nullptr;
+    int *am_i = nullptr;
+    unsigned *am_count = nullptr;
+    int32_t *am_out = nullptr, *h_am_out = nullptr;
     unsigned *h_md_status = nullptr;  // pinned copy of the status word, read after each eval
     int32_t *grp_off = nullptr, *grp_slot = nullptr, *grp_tiles = nullptr;  // slots by expert (prefill GEMM)
     // Sharded models: all-reduce sources, zero outside this rank's columns (hsend: FFN activations
@@ -620,6 +626,62 @@ __global__ void fmatmul_gather_kernel(const void *w, int type, int n_in, int64_t
     }
     for (; i < n_in; i++) s0 = __fadd_rn(s0, __fmul_rn(xv[i], wv(i)));
     out[(size_t)s * ldo + r] = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
+// Greedy choice on the device: the index of the largest logit, the first one on ties and the first
+// NaN if there is one (numpy.argmax, which the reference's greedy loop applies to the host logits,
+// sardyne/runtime.py:115-140). ARGMAX_CTAS blocks take strided elements; the last block to finish
+// (a counter it leaves at zero) reduces their candidates.
+constexpr int ARGMAX_CTAS = 32, ARGMAX_THREADS = 512;
+struct Cand {
+    float v;
+    int i;
+};
+__device__ __forceinline__ Cand better(Cand a, Cand b) {  // a before b in the scan order when equal
+    const bool an = a.v != a.v, bn = b.v != b.v;
+    if (an || bn) return an && (!bn || a.i < b.i) ? a : b;
+    return (b.v > a.v || (b.v == a.v && b.i < a.i)) ? b : a;
+}
+__device__ Cand block_best(Cand c, Cand *part) {
+    for (int o = 16; o; o >>= 1) {
+        Cand d{__shfl_xor_sync(0xffffffffu, c.v, o), __shfl_xor_sync(0xffffffffu, c.i, o)};
+        c = better(c, d);
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) part[w] = c;
+    __syncthreads();
+    c = lane < nw ? part[lane] : Cand{-INFINITY, 0x7fffffff};
+    for (int o = 16; o; o >>= 1) {
+        Cand d{__shfl_xor_sync(0xffffffffu, c.v, o), __shfl_xor_sync(0xffffffffu, c.i, o)};
+        c = better(c, d);
+    }
+    return c;
+}
+__global__ void __launch_bounds__(ARGMAX_THREADS) argmax_kernel(const float *x, int n, float *cand_v, int *cand_i,
+                                                                unsigned *counter, int32_t *out) {
+    pdl_wait();
+    __shared__ Cand part[32];
+    __shared__ int last;
+    Cand c{-INFINITY, 0x7fffffff};
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) c = better(c, Cand{x[i], i});
+    c = block_best(c, part);
+    if (threadIdx.x == 0) {
+        cand_v[blockIdx.x] = c.v;
+        cand_i[blockIdx.x] = c.i;
+        __threadfence();
+        last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    c = threadIdx.x < gridDim.x ? Cand{__ldcg(cand_v + threadIdx.x), __ldcg(cand_i + threadIdx.x)}
+                                : Cand{-INFINITY, 0x7fffffff};
+    c = block_best(c, part);
+    if (threadIdx.x == 0) {
+        *out = c.i;
+        *counter = 0;
+    }
 }
 
 // ------------------------------------------------------------------------------ forward
@@ -1279,6 +1341,8 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
         {(void **)&c->scores, B * in.n_head * S * 4},
         {(void **)&c->logits, (c->logits_all ? B : 1) * in.n_vocab * 4},
         {(void **)&c->tokpos, (B + 1) * 4},
+        {(void **)&c->am_v, ARGMAX_CTAS * 4}, {(void **)&c->am_i, ARGMAX_CTAS * 4},
+        {(void **)&c->am_count, 4}, {(void **)&c->am_out, 4},
     };
     if (in.n_expert) {
         items.push_back({(void **)&c->moe_probs, B * in.n_expert * 4});
@@ -1326,6 +1390,7 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
     if (c->hsend) zeroed = SDY_CUDA(cudaMemset(c->hsend, 0, B * ffn * 4)) && SDY_CUDA(cudaMemset(c->xsend, 0, B * in.dim * 4));
     if (c->lsend) zeroed = zeroed && SDY_CUDA(cudaMemset(c->lsend, 0, logit_rows * in.n_vocab * 4));
     if (c->md_sync) zeroed = zeroed && SDY_CUDA(cudaMemset(c->md_sync, 0, 4 * sizeof(unsigned)));
+    zeroed = zeroed && SDY_CUDA(cudaMemset(c->am_count, 0, 4));
     if (!zeroed || (c->moe_count && !SDY_CUDA(cudaMemset(c->moe_count, 0, B * 4)))) {  // router counters start at zero
         put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
         engine_ctx_free(c);
@@ -1337,7 +1402,8 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
         !SDY_CUDA(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming)) ||
         !SDY_CUDA(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming)) ||
         !SDY_CUDA(cudaMallocHost(&c->h_logits, lbytes)) || !SDY_CUDA(cudaMallocHost(&c->h_tokpos, (B + 1) * 4)) ||
-        !SDY_CUDA(cudaMallocHost(&c->h_md_status, sizeof(unsigned)))) {
+        !SDY_CUDA(cudaMallocHost(&c->h_md_status, sizeof(unsigned))) ||
+        !SDY_CUDA(cudaMallocHost(&c->h_am_out, sizeof(int32_t)))) {
         put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
         engine_ctx_free(c);
         return nullptr;
@@ -1364,10 +1430,14 @@ void engine_ctx_free(engine_ctx *c) {
     if (c->h_logits) cudaFreeHost(c->h_logits);
     if (c->h_tokpos) cudaFreeHost(c->h_tokpos);
     if (c->h_md_status) cudaFreeHost(c->h_md_status);
+    if (c->h_am_out) cudaFreeHost(c->h_am_out);
     delete c;
 }
 
-int engine_eval(engine_ctx *c, const int32_t *tokens, int32_t n) {
+namespace {
+// engine_eval, with the last token's greedy choice made on the device instead of the logits
+// copied back when `next` is set.
+int eval_tokens(engine_ctx *c, const int32_t *tokens, int32_t n, int32_t *next) {
     if (!c) return -1;
     c->err[0] = '\0';
     if (!tokens || n < 1) {
@@ -1401,8 +1471,15 @@ int engine_eval(engine_ctx *c, const int32_t *tokens, int32_t n) {
         c->n_past += chunk;
         done += chunk;
     }
-    size_t lb = (size_t)out_rows * c->m->info.n_vocab * 4;
-    SDY_CUDA(cudaMemcpyAsync(c->h_logits, c->logits, lb, cudaMemcpyDeviceToHost, c->st));
+    const int nv = c->m->info.n_vocab;
+    if (next) {
+        launch(argmax_kernel, ARGMAX_CTAS, ARGMAX_THREADS, 0, c->st, c->logits + (size_t)(out_rows - 1) * nv, nv,
+               c->am_v, c->am_i, c->am_count, c->am_out);
+        SDY_LAUNCHED();
+        SDY_CUDA(cudaMemcpyAsync(c->h_am_out, c->am_out, 4, cudaMemcpyDeviceToHost, c->st));
+    } else {
+        SDY_CUDA(cudaMemcpyAsync(c->h_logits, c->logits, (size_t)out_rows * nv * 4, cudaMemcpyDeviceToHost, c->st));
+    }
     if (c->md_sync) SDY_CUDA(cudaMemcpyAsync(c->h_md_status, c->md_sync + 3, sizeof(unsigned), cudaMemcpyDeviceToHost, c->st));
     SDY_CUDA(cudaStreamSynchronize(c->st));
     if (c->md_sync && *c->h_md_status) {  // a grid barrier of the fused MoE block gave up
@@ -1416,8 +1493,20 @@ int engine_eval(engine_ctx *c, const int32_t *tokens, int32_t n) {
         snprintf(c->err, sizeof c->err, "errore GPU: %s", last_error());
         return -1;
     }
-    c->n_logits = c->logits_all ? n : 1;
+    c->n_logits = next ? 0 : c->logits_all ? n : 1;
+    if (next) *next = *c->h_am_out;
     return 0;
+}
+}  // namespace
+
+int engine_eval(engine_ctx *c, const int32_t *tokens, int32_t n) { return eval_tokens(c, tokens, n, nullptr); }
+
+int sdy_engine_eval_greedy(engine_ctx *c, const int32_t *tokens, int32_t n, int32_t *next) {
+    if (c && !next) {
+        snprintf(c->err, sizeof c->err, "sdy_engine_eval_greedy: next NULL");
+        return -1;
+    }
+    return eval_tokens(c, tokens, n, next);
 }
 
 const float *engine_logits(const engine_ctx *c) { return c && c->n_logits ? c->h_logits : nullptr; }

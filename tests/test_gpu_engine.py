@@ -251,3 +251,40 @@ def test_moe_ties_choose_the_lowest_experts(tmp_path, ref_lib):
                            logits_all=True).eval(TOKENS)
     got = Context(Model(path), max_seq=32, n_batch=len(TOKENS), logits_all=True).eval(TOKENS)
     close(got, want)
+
+
+def greedy_on_device(ctx, tokens):
+    """sdy_engine_eval_greedy through the C-ABI on a reference-runtime Context's handle."""
+    import ctypes
+    from sardyne_b200 import capi
+    arr = (ctypes.c_int32 * len(tokens))(*tokens)
+    nxt = ctypes.c_int32(-1)
+    assert capi.lib().sdy_engine_eval_greedy(ctx._h, arr, len(tokens), ctypes.byref(nxt)) == 0, \
+        capi.lib().engine_last_error(ctx._h)
+    return nxt.value
+
+
+def test_greedy_on_device_matches_host_argmax(model_path):
+    """The device's greedy choice equals numpy.argmax of engine_eval's logits, step by step."""
+    model = Model(model_path)
+    host, dev = Context(model, max_seq=48, n_batch=8), Context(model, max_seq=48, n_batch=8)
+    want = int(np.argmax(host.eval(TOKENS[:5])))
+    got = greedy_on_device(dev, TOKENS[:5])
+    for _ in range(24):
+        assert got == want
+        want = int(np.argmax(host.eval([want])))
+        got = greedy_on_device(dev, [got])
+    assert dev.n_past == host.n_past
+
+
+def test_greedy_on_device_ties_take_the_lowest_id(tmp_path):
+    """All logits equal (zero embeddings): the first id, as numpy.argmax."""
+    src = synth.write_model(tmp_path / "src.gguf", synth.Spec())
+
+    def zero_embd(name, ne, kind, raw):
+        return kind, (bytes(len(raw)) if name == "token_embd.weight" else raw)
+
+    model = Model(rewrite_gguf(src, tmp_path / "zero.gguf", zero_embd))
+    ctx = Context(model, max_seq=16, n_batch=4)
+    assert greedy_on_device(ctx, [3, 5]) == 0
+    assert not ctx.eval([7]).any()  # the logits themselves are all zero
