@@ -6,12 +6,14 @@
 One step = one pass of the hot path over the config-2 sweep at batch 1: Q4_K and Q6_K weights of
 2048x11008, 11008x2048 and 151936x2048 ([n_out][n_in], N(0, 0.02) quantized by the package's
 quantizer; the 151936-row LM heads are filled from a pool of quantized Gaussian blocks), and an
-f32 N(0, 1) activation vector quantized on the device to Q8_K before each product. The metric
+f32 N(0, 1) activation vector per input width quantized on the device to Q8_K once per step (the
+reference quantizes each distinct input once and reuses it). The metric
 is weight+activation bytes streamed per second (GB/s).
 
   value  device-resident inputs (weights in the slab layout, activations in HBM), device time
-         with CUDA events on the launching stream; the step's working set (492 MB) exceeds the
-         126 MB L2, so every matrix is re-read from HBM.
+         with CUDA events on the launching stream; the step (the two activation quantizations and
+         the six products as one grouped launch, sdy_qmatvec_batch_dev) replays as a CUDA graph;
+         its working set (492 MB) exceeds the 126 MB L2, so every matrix is re-read from HBM.
   e2e    the same products through the reference-facing C-ABI (op_matmul: host f32 activations
          in pinned memory, host outputs), weights resident after sdy_weights_register (the
          counterpart of the reference's mmap); includes the H2D copy of x and the D2H of y.
@@ -50,7 +52,7 @@ FORMATS = ["Q4_K", "Q6_K"]
 TYPE_ID = {"Q4_K": 12, "Q6_K": 14, "Q8_K": 15}
 BLOCK = {"Q4_K": (256, 144), "Q6_K": (256, 210)}
 WORKLOAD = ("BASELINE config 2 at batch 1: Q4_K and Q6_K matvec over 2048x11008, 11008x2048 and "
-            "151936x2048 ([n_out][n_in]), Q8_K activations quantized on the device each product")
+            "151936x2048 ([n_out][n_in]), Q8_K activations quantized on the device once per input width")
 
 
 def log(*a):
@@ -251,14 +253,16 @@ def load_peaks():
 
 
 def load_traffic():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if present."""
-    p = REPO / "profiles" / "qmv_q6k_lmhead_traffic.json"
-    if p.exists():
+    """DRAM bytes per launch of the grouped sweep kernel and of the single Q6_K LM-head kernel, from
+    the committed ncu summaries where present."""
+    out = []
+    for name in ("qmvb_config2_sweep_traffic.json", "qmv_q6k_lmhead_traffic.json"):
+        p = REPO / "profiles" / name
         try:
-            return json.loads(p.read_text()).get("dram_bytes_per_launch")
+            out.append(json.loads(p.read_text()).get("dram_bytes_per_launch") if p.exists() else None)
         except (ValueError, KeyError):
-            return None
-    return None
+            out.append(None)
+    return tuple(out)
 
 
 def shard_rows(n_out, rank, world):
@@ -310,19 +314,33 @@ def run_b200(args, rank, world, local_rank):
     dominant = max(range(len(mats)), key=lambda i: alg_bytes(*mats[i][:3]))
     step_bytes = sum(alg_bytes(fmt, n_out, n_in) for fmt, n_out, n_in, _ in mats)
 
-    def matvecs(ev=None):
-        for i, (fmt, n_out, n_in, _) in enumerate(mats):
+    def quantize_inputs():
+        # once per distinct input, as the reference reuses its quantized activations across the
+        # products that share them (csrc/model_llama.c:590-611)
+        for n_in in xs:
             lib.sdy_quantize_rows_dev(TYPE_ID["Q8_K"], ctypes.c_void_p(d_x[n_in].data_ptr()), 1, n_in,
                                       ctypes.c_void_p(d_xq[n_in].data_ptr()), sp)
-            if ev is not None and i == dominant:
-                ev[0].record(stream)
-            lib.sdy_qmatvec_dev(handles[i], ctypes.c_void_p(d_xq[n_in].data_ptr()), 1,
-                                ctypes.c_void_p(d_out[i].data_ptr()), n_out, 0, n_out, sp)
-            if ev is not None and i == dominant:
-                ev[1].record(stream)
 
-    def step(ev=None):
-        matvecs(ev)
+    def matvecs(skip=-1):
+        """The sweep as single-product launches (the per-matrix breakdown), without product `skip`."""
+        quantize_inputs()
+        for i, (fmt, n_out, n_in, _) in enumerate(mats):
+            if i != skip:
+                lib.sdy_qmatvec_dev(handles[i], ctypes.c_void_p(d_xq[n_in].data_ptr()), 1,
+                                    ctypes.c_void_p(d_out[i].data_ptr()), n_out, 0, n_out, sp)
+
+    hs_arr = (ctypes.c_void_p * len(mats))(*handles)
+    xq_arr = (ctypes.c_void_p * len(mats))(*[d_xq[n_in].data_ptr() for _, _, n_in, _ in mats])
+    out_arr = (ctypes.c_void_p * len(mats))(*[o.data_ptr() for o in d_out])
+
+    def grouped():
+        """This rank's products of the sweep in one launch (sdy_qmatvec_batch_dev)."""
+        if lib.sdy_qmatvec_batch_dev(len(mats), hs_arr, xq_arr, out_arr, sp) != 0:
+            raise RuntimeError(capi.last_error())
+
+    def step():
+        quantize_inputs()
+        grouped()
         if world > 1:  # every rank ends the step with every matrix's full y
             dist.all_gather_into_tensor(recv, send)
 
@@ -359,13 +377,7 @@ def run_b200(args, rank, world, local_rank):
     sweep_all = capture(lambda: [matvecs() for _ in range(reps)])
     per = []
     for i, (fmt, n_out, n_in, _) in enumerate(mats):
-        def without_i(i=i):
-            for _ in range(reps):
-                for j, (f2, o2, i2, _) in enumerate(mats):
-                    if j != i:
-                        lib.sdy_qmatvec_dev(handles[j], ctypes.c_void_p(d_xq[i2].data_ptr()), 1,
-                                            ctypes.c_void_p(d_out[j].data_ptr()), o2, 0, o2, sp)
-        sweep_wo = capture(without_i)
+        sweep_wo = capture(lambda i=i: [matvecs(skip=i) for _ in range(reps)])
         ts = []
         for g in (sweep_wo, sweep_all, sweep_wo, sweep_all):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -375,15 +387,13 @@ def run_b200(args, rank, world, local_rank):
                 e1.record(stream)
             torch.cuda.synchronize()
             ts.append(e0.elapsed_time(e1))
-        # matvecs() also quantizes the inputs (6 small launches per sweep), so the difference is an
-        # upper bound of the matrix's own time
         ms = (min(ts[1], ts[3]) - min(ts[0], ts[2])) / reps
         per.append({"format": fmt, "n_out": n_out, "n_in": n_in, "us": round(ms * 1e3, 2),
                     "GB/s": round(alg_bytes(fmt, n_out, n_in) / (ms * 1e-3) / 1e9, 1)})
         del sweep_wo
     del sweep_all
 
-    # the timed step as one CUDA graph: 6 activation quantizations, 6 matvecs (and, N > 1, the
+    # the timed step as one CUDA graph: the 2 activation quantizations, 6 matvecs (and, N > 1, the
     # all-gather of y)
     step_graph = capture(step)
     with torch.cuda.stream(stream):
@@ -404,23 +414,27 @@ def run_b200(args, rank, world, local_rank):
         torch.cuda.synchronize()
         barrier()
     # launches recorded in the graph once, replayed every step
-    launches_per_step = 2 * len(mats)
-    # the dominant kernel timed per launch: eager launches each bracketed by events on its stream,
-    # queued behind a ~10 ms spin kernel so that the host is ahead of the GPU and no host launch
-    # gap falls inside a bracket
+    launches_per_step = len(xs) + 1
+    # The step's dominant kernel, the grouped launch, timed per launch: eager launches each bracketed
+    # by events on its stream, queued behind a ~10 ms spin kernel so that the host is ahead of the
+    # GPU and no host launch gap falls inside a bracket. The single largest product (the Q6_K LM
+    # head) is timed the same way for comparison.
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    evs1 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     fmt_d, o_d, i_d, _ = mats[dominant]
     with torch.cuda.stream(stream):
         torch.cuda._sleep(20_000_000)
         for k in range(args.steps):
             evs[k][0].record(stream)
+            grouped()
+            evs[k][1].record(stream)
+        torch.cuda._sleep(20_000_000)
+        for k in range(args.steps):
+            evs1[k][0].record(stream)
             lib.sdy_qmatvec_dev(handles[dominant], ctypes.c_void_p(d_xq[i_d].data_ptr()), 1,
                                 ctypes.c_void_p(d_out[dominant].data_ptr()), o_d, 0, o_d, sp)
-            evs[k][1].record(stream)
-            for j, (f2, o2, i2, _) in enumerate(mats):  # the rest of the sweep between launches
-                if j != dominant:
-                    lib.sdy_qmatvec_dev(handles[j], ctypes.c_void_p(d_xq[i2].data_ptr()), 1,
-                                        ctypes.c_void_p(d_out[j].data_ptr()), o2, 0, o2, sp)
+            evs1[k][1].record(stream)
+            grouped()  # the rest of the sweep between launches (the next LM head launch is cold in L2)
     torch.cuda.synchronize()
     launches = launches_per_step * args.steps
     capi.check()
@@ -432,11 +446,13 @@ def run_b200(args, rank, world, local_rank):
         dist.all_reduce(tb, op=dist.ReduceOp.SUM)
     ms_max, all_bytes = float(tm.item()), float(tb.item())
     value = all_bytes * args.steps / (ms_max * 1e-3) / 1e9
-    dom_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    grp_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    dom_ms = statistics.mean(a.elapsed_time(b) for a, b in evs1)
     fmt, n_out, n_in, _ = mats[dominant]
     peak, peak_kind = load_peaks()
-    achieved = alg_bytes(fmt, n_out, n_in) / (dom_ms * 1e-3) / 1e9
-    traffic = load_traffic() if world == 1 else None
+    achieved = step_bytes / (grp_ms * 1e-3) / 1e9
+    achieved1 = alg_bytes(fmt, n_out, n_in) / (dom_ms * 1e-3) / 1e9
+    traffic, traffic1 = load_traffic() if world == 1 and not args.only else (None, None)
     y_dev = [gathered_y(i).cpu() for i in range(len(mats))]
 
     # e2e through the reference-facing C-ABI with host buffers: op_matmul of this rank's slices
@@ -497,8 +513,13 @@ def run_b200(args, rank, world, local_rank):
             "config": config(world),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": f"qmv {fmt} {n_out}x{n_in} batch 1", "peak_source": peak_kind,
-                         "algorithmic_bytes": alg_bytes(fmt, n_out, n_in), "launch_us": round(dom_ms * 1e3, 2)},
+                         "kernel": f"grouped qmv: this rank's {len(mats)} products in one launch",
+                         "peak_source": peak_kind, "algorithmic_bytes": step_bytes,
+                         "launch_us": round(grp_ms * 1e3, 2)},
+            "roofline_single": {"bound": "hbm", "achieved": round(achieved1, 1), "peak": peak, "unit": "GB/s",
+                                "frac": round(achieved1 / peak, 4), "traffic": traffic1,
+                                "kernel": f"qmv {fmt} {n_out}x{n_in} batch 1", "peak_source": peak_kind,
+                                "algorithmic_bytes": alg_bytes(fmt, n_out, n_in), "launch_us": round(dom_ms * 1e3, 2)},
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s",
                     "h2d_bytes_per_step": sum(4 * n_in for _, _, n_in, _ in mats),
                     "d2h_bytes_per_step": sum(4 * n_out for _, n_out, _, _ in mats),

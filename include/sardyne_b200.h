@@ -168,6 +168,13 @@ int sdy_quantize_rows_dev(int vtype, const float *d_x, int n_tok, int n_in, void
 int sdy_qmatvec_dev(const void *w, const void *d_xq, int n_tok, float *d_out, int64_t ldo, int64_t row0,
                     int64_t row1, void *stream);
 
+/* No counterpart in the reference (its products run one after another, csrc/model_llama.c:554-611).
+ * n independent single-token products in one launch (a grouped matvec): d_out[i][r] = w_i[r] . x_i
+ * for every row of each matrix, x_i the Q8_K row at d_xq[i] (sdy_xq_bytes(15, n_in_i, 1) bytes,
+ * from sdy_quantize_rows_dev). 1 <= n <= 8, Q4_K / Q6_K weights; each result equals
+ * sdy_qmatvec_dev's bit for bit. 0 or -1. */
+int sdy_qmatvec_batch_dev(int n, const void *const *w, const void *const *d_xq, float *const *d_out, void *stream);
+
 /* No counterpart in the reference. For callers that cannot allocate device memory where they
  * call: a host framework that accounts for all device memory through its own pool, or a serving
  * loop that keeps cudaMalloc/cudaFree (which can stall or synchronise the device) out of its

@@ -114,6 +114,7 @@ EXTENSIONS = {
     "sdy_xq_bytes": (_sz, [_i, _i, _i]),
     "sdy_quantize_rows_dev": (_i, [_i, _vp, _i, _i, _vp, _vp]),
     "sdy_qmatvec_dev": (_i, [_vp, _vp, _i, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp]),
+    "sdy_qmatvec_batch_dev": (_i, [_i, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp]),
     "sdy_qmatvec_f32_noalloc": (_i, [_vp, _vp, _i, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp]),
 }
 

@@ -544,4 +544,27 @@ int sdy_qmatvec_dev(const void *h, const void *d_xq, int n_tok, float *d_out, in
     return last_error()[0] ? -1 : 0;
 }
 
+int sdy_qmatvec_batch_dev(int n, const void *const *hs, const void *const *d_xq, float *const *d_out, void *stream) {
+    clear_error();
+    if (n < 1 || n > 8 || !hs || !d_xq || !d_out) {
+        set_error("sdy_qmatvec_batch_dev: 1..8 products with their weights, activations and outputs");
+        return -1;
+    }
+    const QMat *w[8];
+    XQ q[8];
+    const XQ *qp[8];
+    for (int i = 0; i < n; i++) {
+        const sdy_qmat_s *h = (const sdy_qmat_s *)hs[i];
+        if (!h || !d_xq[i] || !d_out[i]) {
+            set_error("sdy_qmatvec_batch_dev: product %d: null argument", i);
+            return -1;
+        }
+        w[i] = &h->m;
+        q[i] = xq_carve((void *)d_xq[i], vec_dot_type(h->m.type), h->m.n_in, 1);
+        qp[i] = &q[i];
+    }
+    qmatvec_batch(n, w, qp, d_out, (cudaStream_t)stream);
+    return last_error()[0] ? -1 : 0;
+}
+
 }  // extern "C"

@@ -194,6 +194,27 @@ __global__ void __launch_bounds__(THREADS) qmv2_kernel(Args a, Args b, int na) {
     else qmv_body<TB, 1>(b, blockIdx.x - na, gridDim.x - na, smem);
 }
 
+
+// Independent single-token products in one launch (a grouped matvec): CTAs [cta0[i], cta0[i+1])
+// sweep matrix i, of type TA or TB. One launch latency for all of them, and their bytes stream
+// from HBM together.
+constexpr int BATCH_MAX = 8;
+struct BatchArgs {
+    Args a[BATCH_MAX];
+    int type[BATCH_MAX];
+    int cta0[BATCH_MAX + 1];
+    int n;
+};
+template <int TA, int TB>
+__global__ void __launch_bounds__(THREADS) qmvb_kernel(BatchArgs b) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    int i = 0;
+    while (i + 1 < b.n && (int)blockIdx.x >= b.cta0[i + 1]) i++;
+    const int c = blockIdx.x - b.cta0[i], nc = b.cta0[i + 1] - b.cta0[i];
+    if (b.type[i] == TA) qmv_body<TA, 1>(b.a[i], c, nc, smem);
+    else qmv_body<TB, 1>(b.a[i], c, nc, smem);
+}
+
 // Raises the instantiation's dynamic shared memory limit to SMEM_LIMIT on the current device
 // (once): without it a launch or occupancy query above 48 KB minus the static shared memory fails.
 template <int TYPE, int NT>
@@ -482,6 +503,51 @@ void qmatvec2(const QMat &wa, float *outa, const QMat &wb, float *outb, const XQ
     const int smem = std::max(pa.smem, pb.smem), grid = pa.grid + pb.grid;
     if (wa.type == T_Q4_K) launch_pair<T_Q4_K, T_Q6_K>(a, b, pa.grid, grid, smem, s);
     else launch_pair<T_Q6_K, T_Q4_K>(a, b, pa.grid, grid, smem, s);
+}
+
+
+bool qmatvec_batch_supported(int n, const QMat *const *w) {
+    if (n < 1 || n > BATCH_MAX) return false;
+    for (int i = 0; i < n; i++)
+        if (!w[i] || (w[i]->type != T_Q4_K && w[i]->type != T_Q6_K)) return false;
+    return true;
+}
+
+void qmatvec_batch(int n, const QMat *const *w, const XQ *const *xq, float *const *out, cudaStream_t s) {
+    if (!qmatvec_batch_supported(n, w)) {
+        set_error("qmatvec_batch: 1..%d matrices of Q4_K / Q6_K", BATCH_MAX);
+        return;
+    }
+    for (int i = 0; i < n; i++)
+        if (xq[i]->n_tok != 1 || xq[i]->vtype != T_Q8_K || xq[i]->n_in != w[i]->n_in) {
+            set_error("qmatvec_batch: product %d: activations are not one Q8_K row of %d", i, w[i]->n_in);
+            return;
+        }
+    // the SMs' CTA slots split in proportion to each matrix's bytes (at least one CTA each)
+    const int64_t cap = (int64_t)sm_count() * std::min(ctas_per_sm(T_Q4_K, 1), ctas_per_sm(T_Q6_K, 1));
+    double total = 0;
+    for (int i = 0; i < n; i++) total += (double)w[i]->bytes();
+    BatchArgs b{};
+    b.n = n;
+    int grid = 0, smem = 0;
+    for (int i = 0; i < n; i++) {
+        const int64_t ci = std::max<int64_t>(1, (int64_t)(cap * (double)w[i]->bytes() / total));
+        Plan p;
+        if (!plan_launch(w[i]->type, w[i]->nb, xq[i]->qrow, w[i]->n_groups(), ci, 1, &p)) {
+            set_error("qmatvec_batch: row of %d elements too long for one CTA", w[i]->n_in);
+            return;
+        }
+        b.a[i] = pair_args(*w[i], p, *xq[i], out[i], nullptr);
+        b.type[i] = w[i]->type;
+        b.cta0[i] = grid;
+        grid += p.grid;
+        smem = std::max(smem, p.smem);
+    }
+    b.cta0[n] = grid;
+    static std::atomic<uint64_t> configured{0};
+    smem_limit_once(qmvb_kernel<T_Q4_K, T_Q6_K>, SMEM_LIMIT, configured);
+    launch(qmvb_kernel<T_Q4_K, T_Q6_K>, dim3(grid), THREADS, smem, s, b);
+    SDY_LAUNCHED();
 }
 
 }  // namespace sdy

@@ -210,3 +210,42 @@ def test_errors_are_reported_not_crashing():
     lib().op_matmul_q_rows(ptr(out), ptr(w), ptr(w), 3, 1, 32, 1, 0, 1)  # Q4_1: unsupported
     assert b"unsupported" in lib().sdy_last_error()
     lib().sdy_clear_error()
+
+
+def test_grouped_products_equal_single_launches():
+    """sdy_qmatvec_batch_dev: independent products of both K-quant formats, different input widths
+    and row counts (ragged groups), in one launch: each equal to its own sdy_qmatvec_dev bit for bit."""
+    import torch
+    lib_ = lib()
+    shapes = [("Q4_K", 300, 2048), ("Q6_K", 1001, 2048), ("Q4_K", 77, 11008), ("Q6_K", 2048, 1024),
+              ("Q4_K", 4096, 256), ("Q6_K", 9, 11008)]
+    handles, xqs, outs, want = [], [], [], []
+    try:
+        for i, (kind, n_out, n_in) in enumerate(shapes):
+            w = oracle.random_blocks(kind, n_out * n_in // 256, seed=50 + i)
+            h = lib_.sdy_qmat_upload(ptr(w), TID[kind], n_out, n_in)
+            assert h, capi.last_error()
+            handles.append(h)
+            x = torch.from_numpy(np.random.default_rng(i).standard_normal(n_in).astype(np.float32)).cuda()
+            xq = torch.empty(lib_.sdy_xq_bytes(TID["Q8_K"], n_in, 1), dtype=torch.uint8, device="cuda")
+            assert lib_.sdy_quantize_rows_dev(TID["Q8_K"], ctypes.c_void_p(x.data_ptr()), 1, n_in,
+                                              ctypes.c_void_p(xq.data_ptr()), None) == 0
+            xqs.append(xq)
+            outs.append(torch.full((n_out,), float("nan"), device="cuda"))
+            ref = torch.full((n_out,), float("nan"), device="cuda")
+            assert lib_.sdy_qmatvec_dev(h, ctypes.c_void_p(xq.data_ptr()), 1, ctypes.c_void_p(ref.data_ptr()), n_out,
+                                        0, n_out, None) == 0
+            want.append(ref)
+        n = len(shapes)
+        arr = lambda vals: (ctypes.c_void_p * len(vals))(*vals)  # noqa: E731
+        assert lib_.sdy_qmatvec_batch_dev(n, arr(handles), arr([t.data_ptr() for t in xqs]),
+                                          arr([t.data_ptr() for t in outs]), None) == 0, capi.last_error()
+        torch.cuda.synchronize()
+        for got, ref in zip(outs, want):
+            assert torch.equal(got, ref)
+        # more than 8 products are refused
+        assert lib_.sdy_qmatvec_batch_dev(9, arr(handles + [handles[0]] * 3), arr([0] * 9), arr([0] * 9), None) == -1
+        lib_.sdy_clear_error()
+    finally:
+        for h in handles:
+            lib_.sdy_qmat_free(h)
