@@ -234,11 +234,13 @@ def run_reference_arm(args, rank, world):
     return 0
 
 
-def config(world=1):
+def config(world=1, gather="p2p"):
     c = {"workload": WORKLOAD, "formats": FORMATS, "shapes_out_in": SHAPES, "batch": 1,
          "l2": "inputs larger than L2: 492 MB of weights per step against a 126 MB L2",
          "weights": "N(0,0.02), package quantizer; LM heads from a pool of quantized Gaussian blocks"}
-    c["parallelism"] = f"rows of every matrix split over {world} GPUs, y all-gathered" if world > 1 else "1 GPU"
+    c["parallelism"] = (f"rows of every matrix split over {world} GPUs, y all-gathered "
+                        f"({'over NVLink peer memory, own kernel' if gather == 'p2p' else 'NCCL'})"
+                        if world > 1 else "1 GPU")
     return c
 
 
@@ -302,6 +304,43 @@ def run_b200(args, rank, world, local_rank):
     handles, d_out, d_x, d_xq = [], [], {}, {}
     send = torch.zeros(share, dtype=torch.float32, device=dev)
     recv = torch.zeros(world * share, dtype=torch.float32, device=dev) if world > 1 else None
+    # N > 1: the y slices are gathered over NVLink peer memory (sdy_allgather_p2p: each rank's GPU
+    # stores its slice into every rank's buffer), or with NCCL's all-gather (--gather nccl)
+    p2p = world > 1 and args.gather == "p2p"
+    p2p_buf, p2p_bases = None, None
+    if p2p:
+        p2p_buf = lib.sdy_p2p_alloc(lib.sdy_allgather_p2p_bytes(share, world))
+        if not p2p_buf:
+            raise RuntimeError(capi.last_error())
+        hbuf = (ctypes.c_char * 64)()
+        if lib.sdy_p2p_handle(p2p_buf, hbuf) != 0:
+            raise RuntimeError(capi.last_error())
+        peer_handles = [None] * world
+        dist.all_gather_object(peer_handles, bytes(hbuf))
+        bases = []
+        for q in range(world):
+            p = p2p_buf if q == rank else lib.sdy_p2p_open((ctypes.c_char * 64).from_buffer_copy(peer_handles[q]))
+            if not p:
+                raise RuntimeError(capi.last_error())
+            bases.append(p)
+        p2p_bases = (ctypes.c_void_p * world)(*bases)
+
+    def gather(stream_handle):
+        if p2p:
+            if lib.sdy_allgather_p2p(ctypes.c_void_p(send.data_ptr()), share, p2p_bases, rank, world,
+                                     stream_handle) != 0:
+                raise RuntimeError(capi.last_error())
+        else:
+            dist.all_gather_into_tensor(recv, send)
+
+    def gathered_all():
+        """Every rank's y slices as this rank holds them after the last gather (host copy)."""
+        if p2p:
+            out = torch.empty(world * share, dtype=torch.float32)
+            torch.cuda.synchronize()
+            lib.sdy_p2p_read(ctypes.c_void_p(out.data_ptr()), p2p_buf, out.numel() * 4)
+            return out
+        return recv.cpu()
     for i, (fmt, n_out, n_in, w) in enumerate(mats):
         h = lib.sdy_qmat_upload(w.ctypes.data, TYPE_ID[fmt], n_out, n_in)
         if not h:
@@ -342,15 +381,15 @@ def run_b200(args, rank, world, local_rank):
         quantize_inputs()
         grouped()
         if world > 1:  # every rank ends the step with every matrix's full y
-            dist.all_gather_into_tensor(recv, send)
+            gather(sp)
 
-    def gathered_y(i):
+    def gathered_y(i, allv=None):
         if world == 1:
-            return d_out[i]
+            return d_out[i].cpu()
         parts = []
         for q in range(world):
             b, e = shard_rows(full[i][1], q, world)
-            parts.append(recv[q * share + share_off[i]: q * share + share_off[i] + (e - b)])
+            parts.append(allv[q * share + share_off[i]: q * share + share_off[i] + (e - b)])
         return torch.cat(parts)
 
     def barrier():
@@ -453,7 +492,8 @@ def run_b200(args, rank, world, local_rank):
     achieved = step_bytes / (grp_ms * 1e-3) / 1e9
     achieved1 = alg_bytes(fmt, n_out, n_in) / (dom_ms * 1e-3) / 1e9
     traffic, traffic1 = load_traffic() if world == 1 and not args.only else (None, None)
-    y_dev = [gathered_y(i).cpu() for i in range(len(mats))]
+    allv = gathered_all() if world > 1 else None
+    y_dev = [gathered_y(i, allv) for i in range(len(mats))]
 
     # e2e through the reference-facing C-ABI with host buffers: op_matmul of this rank's slices
     # (pinned f32 x in, host y out), then (N > 1) the host slices gathered over NCCL
@@ -472,9 +512,14 @@ def run_b200(args, rank, world, local_rank):
         if world > 1:
             for i, y in enumerate(y_pin):
                 h_send[share_off[i]:share_off[i] + y.numel()].copy_(y)
-            send.copy_(h_send, non_blocking=True)
-            dist.all_gather_into_tensor(recv, send)
-            h_recv.copy_(recv)
+            send.copy_(h_send)
+            if p2p:
+                gather(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+                torch.cuda.current_stream().synchronize()
+                lib.sdy_p2p_read(ctypes.c_void_p(h_recv.data_ptr()), p2p_buf, h_recv.numel() * 4)
+            else:
+                dist.all_gather_into_tensor(recv, send)
+                h_recv.copy_(recv)
 
     for _ in range(max(args.warmup, 3)):
         e2e_step()
@@ -501,6 +546,16 @@ def run_b200(args, rank, world, local_rank):
         lib.sdy_weights_unregister(w.ctypes.data)
     for h in handles:
         lib.sdy_qmat_free(h)
+    if p2p:
+        if lib.sdy_p2p_status() != 0:
+            raise RuntimeError("a peer-memory gather wait gave up")
+        del step_graph  # holds launches that name the peers' buffers
+        barrier()
+        for q in range(world):
+            if q != rank:
+                lib.sdy_p2p_close(p2p_bases[q])
+        barrier()
+        lib.sdy_p2p_free(p2p_buf)
 
     decode = None
     if not args.no_decode:
@@ -510,7 +565,7 @@ def run_b200(args, rank, world, local_rank):
     line = {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
             "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": config(world),
+            "config": config(world, args.gather),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": f"grouped qmv: this rank's {len(mats)} products in one launch",
@@ -524,7 +579,7 @@ def run_b200(args, rank, world, local_rank):
                     "h2d_bytes_per_step": sum(4 * n_in for _, _, n_in, _ in mats),
                     "d2h_bytes_per_step": sum(4 * n_out for _, n_out, _, _ in mats),
                     "steps": e2e_steps, "api": "op_matmul (C-ABI), weights resident via sdy_weights_register"
-                                               + (", y slices all-gathered over NCCL" if world > 1 else "")},
+                                               + (f", y slices all-gathered ({args.gather})" if world > 1 else "")},
             "gpu_launches": int(launches), "clocks": clk.summary(),
             "frac_of_8tbs": round(value / world / 8000.0, 4), "per_matrix": per}
     if world == 1 and not args.no_cpu_baseline:
@@ -816,6 +871,8 @@ def main():
     ap.add_argument("--model-dir", default=None, help="where the synthetic GGUFs are cached (default: "
                                                          "SARDYNE_MODEL_DIR, /dev/shm or the temp dir)")
     ap.add_argument("--no-decode", action="store_true", help="matvec: leave out the decode object")
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
+                    help="matvec, N > 1: all-gather of y over peer memory (own kernel) or with NCCL")
     ap.add_argument("--decode-steps", type=int, default=0)
     ap.add_argument("--layers", type=int, default=0,
                     help="decode: the model's shape with only this many layers (small cases for ncu captures)")

@@ -175,6 +175,27 @@ int sdy_qmatvec_dev(const void *w, const void *d_xq, int n_tok, float *d_out, in
  * sdy_qmatvec_dev's bit for bit. 0 or -1. */
 int sdy_qmatvec_batch_dev(int n, const void *const *w, const void *const *d_xq, float *const *d_out, void *stream);
 
+/* No counterpart in the reference (it runs on one host). All-gather over NVLink peer memory for
+ * processes that drive one GPU each: rank r's count floats (d_send) are stored by the GPU into
+ * offset r * count of every rank's buffer. bases[q]: rank q's buffer as mapped in this process
+ * (bases[rank] its own, from sdy_p2p_alloc(sdy_allgather_p2p_bytes(count, world)); the others from
+ * sdy_p2p_open of their sdy_p2p_handle). Every rank makes the same sequence of calls; when this
+ * call's work ends on `stream`, the own buffer holds every rank's slice. A rank may begin writing
+ * the next call's slices as soon as every rank has finished this call, so a caller that reads the
+ * buffer between calls alternates two buffers. world <= 8. 0 or -1; a peer that never arrives
+ * makes the wait give up after one second and sets sdy_p2p_status. */
+size_t sdy_allgather_p2p_bytes(int64_t count, int32_t world);
+void *sdy_p2p_alloc(size_t bytes); /* zeroed device memory that can be shared; NULL on error */
+void sdy_p2p_free(void *d_ptr);
+int sdy_p2p_handle(const void *d_ptr, void *handle_out); /* 64-byte IPC handle of an sdy_p2p_alloc buffer */
+void *sdy_p2p_open(const void *handle);                  /* a peer's buffer mapped here; NULL on error */
+int sdy_p2p_close(void *d_peer);
+int sdy_allgather_p2p(const float *d_send, int64_t count, void *const *bases, int32_t rank, int32_t world,
+                      void *stream);
+int sdy_p2p_read(void *host_dst, const void *d_src, size_t bytes); /* device -> host copy, synchronous */
+uint32_t sdy_p2p_status(void); /* nonzero: an sdy_allgather_p2p wait gave up */
+void sdy_p2p_clear_status(void);
+
 /* No counterpart in the reference. For callers that cannot allocate device memory where they
  * call: a host framework that accounts for all device memory through its own pool, or a serving
  * loop that keeps cudaMalloc/cudaFree (which can stall or synchronise the device) out of its

@@ -115,6 +115,16 @@ EXTENSIONS = {
     "sdy_quantize_rows_dev": (_i, [_i, _vp, _i, _i, _vp, _vp]),
     "sdy_qmatvec_dev": (_i, [_vp, _vp, _i, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp]),
     "sdy_qmatvec_batch_dev": (_i, [_i, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp]),
+    "sdy_allgather_p2p_bytes": (_sz, [ctypes.c_int64, ctypes.c_int32]),
+    "sdy_p2p_alloc": (_vp, [_sz]),
+    "sdy_p2p_free": (None, [_vp]),
+    "sdy_p2p_handle": (_i, [_vp, _vp]),
+    "sdy_p2p_open": (_vp, [_vp]),
+    "sdy_p2p_close": (_i, [_vp]),
+    "sdy_allgather_p2p": (_i, [_vp, ctypes.c_int64, ctypes.POINTER(_vp), ctypes.c_int32, ctypes.c_int32, _vp]),
+    "sdy_p2p_read": (_i, [_vp, _vp, _sz]),
+    "sdy_p2p_status": (ctypes.c_uint32, []),
+    "sdy_p2p_clear_status": (None, []),
     "sdy_qmatvec_f32_noalloc": (_i, [_vp, _vp, _i, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp]),
 }
 
