@@ -1,0 +1,228 @@
+"""Hugging Face checkpoint (config.json + *.safetensors) to GGUF, in the block formats this library
+runs, K-quants included.
+
+    python -m sardyne_b200.convert HF_DIR OUT.gguf [--outtype q4_k_m|q6_k|q4_k|q8_0|q4_0|bf16|f16|f32]
+
+The reference's converter (sardyne/loader/convert.py:31,78-103) writes F32/F16/BF16/Q8_0/Q4_0 of the
+dense architectures only; this one adds the K-quants, in particular the Q4_K_M mix the BASELINE
+models use (sardyne_b200.synth.q4_k_m: Q4_K by default, Q6_K on attn_v, on the ffn_down of even
+layers and on the output matrix; rows that are not whole 256-element superblocks fall back to Q5_0
+and Q8_0), and Qwen3-MoE checkpoints (the experts' matrices stacked into the GGUF expert tensors).
+It follows the GGUF conventions the engine reads (tensor names, metadata keys, llama's q/k rows
+reordered for RoPE on adjacent pairs); norms, biases and the MoE router stay F32. Tokenizer
+metadata is not written (the engine does not read it). Tensors are read, converted and written one
+at a time.
+"""
+import argparse
+import json
+import mmap
+import pathlib
+import struct
+
+import numpy as np
+
+from . import kquant, synth
+from .gguf_writer import GGUFWriter, f32_to_bf16
+
+ARCHS = {"LlamaForCausalLM": "llama", "Qwen2ForCausalLM": "qwen2", "Qwen3ForCausalLM": "qwen3",
+         "Qwen3MoeForCausalLM": "qwen3moe"}
+# general.file_type values (the llama_ftype numbering GGUF readers use)
+FILE_TYPES = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 7, "q4_k": 14, "q4_k_m": 15, "q6_k": 18, "bf16": 32}
+
+# tensors below model.layers.<i>.: HF suffix -> GGUF suffix below blk.<i>.
+LAYER_TENSORS = (
+    ("input_layernorm.weight", "attn_norm.weight"),
+    ("post_attention_layernorm.weight", "ffn_norm.weight"),
+    ("self_attn.q_proj.weight", "attn_q.weight"),
+    ("self_attn.k_proj.weight", "attn_k.weight"),
+    ("self_attn.v_proj.weight", "attn_v.weight"),
+    ("self_attn.o_proj.weight", "attn_output.weight"),
+    ("self_attn.q_proj.bias", "attn_q.bias"),
+    ("self_attn.k_proj.bias", "attn_k.bias"),
+    ("self_attn.v_proj.bias", "attn_v.bias"),
+    ("self_attn.q_norm.weight", "attn_q_norm.weight"),
+    ("self_attn.k_norm.weight", "attn_k_norm.weight"),
+    ("mlp.gate_proj.weight", "ffn_gate.weight"),
+    ("mlp.up_proj.weight", "ffn_up.weight"),
+    ("mlp.down_proj.weight", "ffn_down.weight"),
+    ("mlp.gate.weight", "ffn_gate_inp.weight"),
+)
+# MoE experts: mlp.experts.<e>.<HF> of every expert stacked into one GGUF tensor
+EXPERT_TENSORS = (("gate_proj.weight", "ffn_gate_exps.weight"), ("up_proj.weight", "ffn_up_exps.weight"),
+                  ("down_proj.weight", "ffn_down_exps.weight"))
+MODEL_TENSORS = (("model.embed_tokens.weight", "token_embd.weight"), ("model.norm.weight", "output_norm.weight"),
+                 ("lm_head.weight", "output.weight"))
+
+_ST_DTYPES = {"F32": np.float32, "F16": np.float16, "BF16": np.uint16, "F64": np.float64}
+
+
+class SafeTensors:
+    """The tensors of every *.safetensors file of a directory (8-byte header length, JSON header,
+    raw row-major data), mapped read-only; get() returns float32."""
+
+    def __init__(self, directory):
+        self.index = {}
+        self._maps = []
+        for path in sorted(pathlib.Path(directory).glob("*.safetensors")):
+            f = open(path, "rb")
+            mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+            f.close()
+            (hlen,) = struct.unpack("<Q", mm[:8])
+            header = json.loads(mm[8:8 + hlen])
+            base = 8 + hlen
+            for name, info in header.items():
+                if name == "__metadata__":
+                    continue
+                if info["dtype"] not in _ST_DTYPES:
+                    raise ValueError(f"{path.name}: {name}: dtype {info['dtype']} not supported")
+                b, e = info["data_offsets"]
+                self.index[name] = (mm, info["dtype"], tuple(info["shape"]), base + b, base + e)
+            self._maps.append(mm)
+        if not self.index:
+            raise FileNotFoundError(f"no *.safetensors in {directory}")
+
+    def __contains__(self, name):
+        return name in self.index
+
+    def shape(self, name):
+        return self.index[name][2]
+
+    def get(self, name) -> np.ndarray:
+        mm, dtype, shape, b, e = self.index[name]
+        raw = np.frombuffer(mm, dtype=_ST_DTYPES[dtype], count=(e - b) // np.dtype(_ST_DTYPES[dtype]).itemsize,
+                            offset=b)
+        if dtype == "BF16":
+            return (raw.astype(np.uint32) << 16).view(np.float32).reshape(shape)
+        return raw.astype(np.float32).reshape(shape)
+
+
+def rope_theta(cfg) -> float:
+    """RoPE base; scaled RoPE variants are refused (the engine runs plain RoPE only)."""
+    params = cfg.get("rope_parameters") or {}
+    if params and all(isinstance(v, dict) for v in params.values()):
+        params = params.get("full_attention", {})
+    for p in (params, cfg.get("rope_scaling") or {}):
+        kind = p.get("rope_type", p.get("type", "default"))
+        if kind not in ("default", None):
+            raise NotImplementedError(f"RoPE scaling '{kind}' is not supported")
+    return float(params.get("rope_theta", cfg.get("rope_theta", 10000.0)))
+
+
+def interleave_rope_rows(w: np.ndarray, n_head: int) -> np.ndarray:
+    """HF rotates the two halves of each head; GGUF llama rotates adjacent pairs: within every head
+    of rows [a0 .. a(h/2-1) | b0 .. b(h/2-1)] the order becomes a0 b0 a1 b1 ... (matrices and biases)."""
+    rows = w.shape[0]
+    half = rows // n_head // 2
+    return w.reshape(n_head, 2, half, *w.shape[1:]).transpose(0, 2, 1, *range(3, w.ndim + 2)).reshape(w.shape)
+
+
+def block_type(gguf_name: str, n_in: int, outtype: str, tied: bool) -> str:
+    """The ggml type of a tensor: vectors, norms, biases and the router F32; matrices the requested
+    type, with the fallbacks of the 32-element formats for rows that are not whole superblocks."""
+    if gguf_name.endswith(("norm.weight", ".bias")) or "gate_inp" in gguf_name:
+        return "F32"
+    if outtype == "q4_k_m":
+        return (synth.mix_q4_k_m_tied if tied else synth.mix_q4_k_m_untied)(gguf_name, n_in)
+    kind = {"f32": "F32", "f16": "F16", "bf16": "BF16", "q8_0": "Q8_0", "q4_0": "Q4_0", "q4_k": "Q4_K",
+            "q6_k": "Q6_K"}[outtype]
+    if kind in kquant.QK and n_in % kquant.QK[kind]:
+        kind = {"Q4_K": "Q5_0", "Q6_K": "Q8_0"}.get(kind, "F16") if n_in % 32 == 0 else "F16"
+    return kind
+
+
+def encode(data: np.ndarray, kind: str):
+    if kind == "F32":
+        return np.ascontiguousarray(data, np.float32).view(np.uint8)
+    if kind == "F16":
+        return np.ascontiguousarray(data, np.float16).view(np.uint8)
+    if kind == "BF16":
+        return f32_to_bf16(data).view(np.uint8)
+    return np.frombuffer(kquant.quantize(data.reshape(-1, data.shape[-1]), kind), np.uint8)
+
+
+def convert(hf_dir, out_path, outtype: str = "q4_k_m") -> pathlib.Path:
+    hf_dir = pathlib.Path(hf_dir)
+    cfg = json.loads((hf_dir / "config.json").read_text())
+    arch = ARCHS.get((cfg.get("architectures") or [""])[0])
+    if arch is None:
+        raise NotImplementedError(f"architecture {cfg.get('architectures')} is not supported")
+    if outtype not in FILE_TYPES:
+        raise ValueError(f"outtype {outtype} is not one of {sorted(FILE_TYPES)}")
+    st = SafeTensors(hf_dir)
+    n_layer, dim = cfg["num_hidden_layers"], cfg["hidden_size"]
+    n_head = cfg["num_attention_heads"]
+    n_kv = cfg.get("num_key_value_heads", n_head)
+    head_dim = cfg.get("head_dim") or dim // n_head
+    tied = bool(cfg.get("tie_word_embeddings", False)) or "lm_head.weight" not in st
+    moe = arch == "qwen3moe"
+
+    w = GGUFWriter(out_path)
+    meta = [("vocab_size", cfg["vocab_size"]), ("context_length", cfg.get("max_position_embeddings", 2048)),
+            ("embedding_length", dim), ("block_count", n_layer), ("feed_forward_length", cfg["intermediate_size"]),
+            ("attention.head_count", n_head), ("attention.head_count_kv", n_kv),
+            ("rope.freq_base", rope_theta(cfg)), ("rope.dimension_count", head_dim),
+            ("attention.layer_norm_rms_epsilon", float(cfg["rms_norm_eps"]))]
+    if cfg.get("head_dim"):
+        meta += [("attention.key_length", head_dim), ("attention.value_length", head_dim)]
+    if moe:
+        meta += [("expert_count", cfg["num_experts"]), ("expert_used_count", cfg["num_experts_per_tok"]),
+                 ("expert_feed_forward_length", cfg["moe_intermediate_size"])]
+    w.add("general.architecture", arch)
+    w.add("general.name", hf_dir.name)
+    for key, value in meta:
+        w.add(f"{arch}.{key}", value)
+    w.add("general.file_type", FILE_TYPES[outtype])
+    for key, gkey in (("bos_token_id", "tokenizer.ggml.bos_token_id"), ("eos_token_id", "tokenizer.ggml.eos_token_id")):
+        v = cfg.get(key)
+        v = v[0] if isinstance(v, list) and v else v
+        if isinstance(v, int):
+            w.add(gkey, v)
+
+    def add(gguf_name, shape, load):
+        kind = block_type(gguf_name, shape[-1], outtype, tied)
+
+        def produce(load=load, kind=kind):
+            return encode(load(), kind).tobytes()
+
+        w.add_lazy_tensor(gguf_name, tuple(reversed(shape)), kind, produce)
+
+    def plain(hf_name, gguf_name, heads=None):
+        def load():
+            x = st.get(hf_name)
+            return interleave_rope_rows(x, heads) if heads else x
+
+        add(gguf_name, st.shape(hf_name), load)
+
+    plain("model.embed_tokens.weight", "token_embd.weight")
+    plain("model.norm.weight", "output_norm.weight")
+    if not tied:
+        plain("lm_head.weight", "output.weight")
+    for i in range(n_layer):
+        pre = f"model.layers.{i}."
+        for hf, gg in LAYER_TENSORS:
+            if pre + hf not in st:
+                continue
+            heads = None
+            if arch == "llama" and gg.startswith(("attn_q.", "attn_k.")):
+                heads = n_head if gg.startswith("attn_q.") else n_kv
+            plain(pre + hf, f"blk.{i}.{gg}", heads)
+        if moe:
+            n_exp = cfg["num_experts"]
+            for hf, gg in EXPERT_TENSORS:
+                names = [f"{pre}mlp.experts.{e}.{hf}" for e in range(n_exp)]
+                shape = (n_exp,) + st.shape(names[0])
+                add(f"blk.{i}.{gg}", shape, lambda names=names: np.stack([st.get(n) for n in names]))
+    return w.write()
+
+
+def main():
+    ap = argparse.ArgumentParser(description="Convert a Hugging Face checkpoint to GGUF (K-quants included)")
+    ap.add_argument("hf_dir")
+    ap.add_argument("out")
+    ap.add_argument("--outtype", choices=sorted(FILE_TYPES), default="q4_k_m")
+    args = ap.parse_args()
+    print(convert(args.hf_dir, args.out, args.outtype))
+
+
+if __name__ == "__main__":
+    main()

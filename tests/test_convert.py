@@ -1,0 +1,169 @@
+"""The HF -> GGUF converter with K-quants (sardyne_b200.convert), on the CPU.
+
+Tiny llama / qwen2 / qwen3moe checkpoints are written as safetensors here. Checked:
+  * at F32 the output equals the reference's own converter's (sardyne/loader/convert.py) tensor for
+    tensor, byte for byte (names, shapes, llama's q/k row order), with the same model metadata
+    (the reference's converter has no MoE, so qwen3moe is checked against its checkpoint directly);
+  * in the Q4_K_M mix every tensor gets the type the mix names, and dequantizes (oracle) to the
+    checkpoint's weights within the reference's own error bounds for published files
+    (tests/test_quant.py:53: Q4_K < 0.11, Q6_K < 0.03, Q5_0 < 0.07 relative RMS; Q8_0 < 0.01);
+  * the reference engine (oracle/_ref) runs the Q4_K_M file, and its logits follow those of the F32
+    file (the quantization error only).
+"""
+import ctypes
+import json
+import struct
+
+import numpy as np
+import pytest
+
+import oracle
+import refruntime as rt
+from sardyne_b200 import capi, convert, synth
+
+BOUND = {"Q4_K": 0.11, "Q6_K": 0.03, "Q5_0": 0.07, "Q8_0": 0.01, "F32": 0.0, "F16": 1e-3}
+
+
+def write_safetensors(path, tensors, dtype="F32"):
+    header, blobs, off = {}, [], 0
+    for name, a in tensors.items():
+        a = np.ascontiguousarray(a, np.float32)
+        raw = ((a.view(np.uint32) + 0x8000) >> 16).astype(np.uint16).tobytes() if dtype == "BF16" else a.tobytes()
+        header[name] = {"dtype": dtype, "shape": list(a.shape), "data_offsets": [off, off + len(raw)]}
+        blobs.append(raw)
+        off += len(raw)
+    h = json.dumps(header).encode()
+    h += b" " * (-len(h) % 8)
+    path.write_bytes(struct.pack("<Q", len(h)) + h + b"".join(blobs))
+
+
+def checkpoint(tmp_path, arch, tied, dtype="F32"):
+    rng = np.random.default_rng(len(arch))
+    dim, n_head, n_kv, hd, ffn, vocab, n_layer = 256, 4, 2, 64, 512, 96, 2
+    hf = {"llama": "LlamaForCausalLM", "qwen2": "Qwen2ForCausalLM", "qwen3moe": "Qwen3MoeForCausalLM"}[arch]
+    cfg = {"architectures": [hf], "hidden_size": dim, "num_hidden_layers": n_layer, "num_attention_heads": n_head,
+           "num_key_value_heads": n_kv, "intermediate_size": ffn, "vocab_size": vocab, "rms_norm_eps": 1e-6,
+           "rope_theta": 10000.0, "max_position_embeddings": 128, "tie_word_embeddings": tied}
+    if arch == "qwen3moe":
+        cfg.update(num_experts=4, num_experts_per_tok=2, moe_intermediate_size=256, head_dim=hd)
+    t = {"model.embed_tokens.weight": rng.standard_normal((vocab, dim)) * 0.02,
+         "model.norm.weight": 1 + rng.standard_normal(dim) * 0.1}
+    if not tied:
+        t["lm_head.weight"] = rng.standard_normal((vocab, dim)) * 0.02
+    for i in range(n_layer):
+        p = f"model.layers.{i}."
+        t[p + "input_layernorm.weight"] = 1 + rng.standard_normal(dim) * 0.1
+        t[p + "post_attention_layernorm.weight"] = 1 + rng.standard_normal(dim) * 0.1
+        t[p + "self_attn.q_proj.weight"] = rng.standard_normal((n_head * hd, dim)) * 0.02
+        t[p + "self_attn.k_proj.weight"] = rng.standard_normal((n_kv * hd, dim)) * 0.02
+        t[p + "self_attn.v_proj.weight"] = rng.standard_normal((n_kv * hd, dim)) * 0.02
+        t[p + "self_attn.o_proj.weight"] = rng.standard_normal((dim, n_head * hd)) * 0.02
+        if arch == "qwen2":
+            for n, r in (("q", n_head * hd), ("k", n_kv * hd), ("v", n_kv * hd)):
+                t[p + f"self_attn.{n}_proj.bias"] = rng.standard_normal(r) * 0.1
+        if arch == "qwen3moe":
+            t[p + "self_attn.q_norm.weight"] = 1 + rng.standard_normal(hd) * 0.1
+            t[p + "self_attn.k_norm.weight"] = 1 + rng.standard_normal(hd) * 0.1
+            t[p + "mlp.gate.weight"] = rng.standard_normal((4, dim)) * 0.1
+            for e in range(4):
+                t[p + f"mlp.experts.{e}.gate_proj.weight"] = rng.standard_normal((256, dim)) * 0.02
+                t[p + f"mlp.experts.{e}.up_proj.weight"] = rng.standard_normal((256, dim)) * 0.02
+                t[p + f"mlp.experts.{e}.down_proj.weight"] = rng.standard_normal((dim, 256)) * 0.02
+        else:
+            t[p + "mlp.gate_proj.weight"] = rng.standard_normal((ffn, dim)) * 0.02
+            t[p + "mlp.up_proj.weight"] = rng.standard_normal((ffn, dim)) * 0.02
+            t[p + "mlp.down_proj.weight"] = rng.standard_normal((dim, ffn)) * 0.02
+    d = tmp_path / f"{arch}-{'tied' if tied else 'untied'}-{dtype}"
+    d.mkdir()
+    (d / "config.json").write_text(json.dumps(cfg))
+    write_safetensors(d / "model.safetensors", t, dtype)
+    return d
+
+
+def read_gguf(path):
+    """{name: (type name, ne, bytes)} and {key: raw value bytes or str} through this library's reader."""
+    lib = capi.lib()
+    err = ctypes.create_string_buffer(256)
+    h = lib.gguf_open(str(path).encode(), err, len(err))
+    assert h, err.value
+    tensors, kvs = {}, {}
+    try:
+        for i in range(lib.gguf_n_tensors(h)):
+            t = lib.gguf_get_tensor(h, i).contents
+            tensors[t.name.decode()] = (lib.gguf_type_name(t.type).decode(), tuple(t.ne[:t.n_dims]),
+                                        ctypes.string_at(t.data, t.nbytes))
+        for i in range(lib.gguf_n_kv(h)):
+            kv = lib.gguf_get_kv(h, i).contents
+            key = kv.key.decode()
+            if kv.type == 8:
+                n = ctypes.c_uint64()
+                kvs[key] = ctypes.string_at(lib.gguf_kv_get_str(h, i, ctypes.byref(n)), n.value).decode()
+            else:
+                v = ctypes.c_double()
+                u = ctypes.c_uint64()
+                kvs[key] = u.value if lib.gguf_kv_get_u64(h, i, ctypes.byref(u)) == 0 else \
+                    (v.value if lib.gguf_kv_get_f64(h, i, ctypes.byref(v)) == 0 else None)
+    finally:
+        lib.gguf_close(h)
+    return tensors, kvs
+
+
+def floats(kind, ne, raw):
+    n_in = ne[0]
+    if kind == "F32":
+        return np.frombuffer(raw, np.float32).reshape(-1, n_in)
+    if kind == "F16":
+        return np.frombuffer(raw, np.float16).astype(np.float32).reshape(-1, n_in)
+    return oracle.dequant(np.frombuffer(raw, np.uint8), kind, n_in)
+
+
+@pytest.mark.skipif(not rt.available(), reason="the reference's Python package is not installed")
+@pytest.mark.parametrize("arch,tied", [("llama", True), ("qwen2", False)])
+def test_f32_equals_the_reference_converter(tmp_path, arch, tied):
+    rt.modules()
+    from sardyne.loader import convert as ref_convert  # the reference's converter
+    ck = checkpoint(tmp_path, arch, tied)
+    ours = convert.convert(ck, tmp_path / "ours.gguf", "f32")
+    ref_convert.convert(ck, tmp_path / "ref.gguf", "f32")
+    a, akv = read_gguf(ours)
+    b, bkv = read_gguf(tmp_path / "ref.gguf")
+    assert a.keys() == b.keys()
+    for name in a:
+        assert a[name] == b[name], name
+    for key, value in bkv.items():
+        if key.startswith(arch + ".") or key in ("general.architecture",):
+            assert akv.get(key) == value, key
+
+
+@pytest.mark.parametrize("arch,tied,dtype", [("llama", True, "F32"), ("qwen2", False, "BF16"),
+                                             ("qwen3moe", False, "F32")])
+def test_q4_k_m_mix_and_error_bounds(tmp_path, arch, tied, dtype):
+    ck = checkpoint(tmp_path, arch, tied, dtype)
+    f32, _ = read_gguf(convert.convert(ck, tmp_path / "f32.gguf", "f32"))
+    q, kv = read_gguf(convert.convert(ck, tmp_path / "q.gguf", "q4_k_m"))
+    assert kv["general.file_type"] == 15 and q.keys() == f32.keys()
+    mix = synth.mix_q4_k_m_tied if tied else synth.mix_q4_k_m_untied
+    for name, (kind, ne, raw) in q.items():
+        want_kind = "F32" if len(ne) == 1 or "gate_inp" in name else mix(name, ne[0])
+        assert kind == want_kind, name
+        ref = floats(*f32[name])
+        got = floats(kind, ne, raw)
+        rel = np.sqrt(np.mean((got - ref) ** 2) / np.mean(ref ** 2))
+        assert rel <= BOUND[kind], (name, kind, rel)
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference library not built")
+@pytest.mark.parametrize("arch,tied,min_corr", [("llama", True, 0.99), ("qwen3moe", False, 0.97)])
+def test_reference_engine_runs_the_conversion(tmp_path, arch, tied, min_corr):
+    """(The MoE model's bound is lower: its router picks 2 of 4 experts, and the quantization noise
+    can change a pick.)"""
+    ck = checkpoint(tmp_path, arch, tied)
+    tokens = [3, 14, 15, 9, 26, 5, 35, 8]
+    out = {}
+    for outtype in ("f32", "q4_k_m"):
+        path = convert.convert(ck, tmp_path / f"{outtype}.gguf", outtype)
+        m = rt.model(path, oracle.REF_LIB)
+        out[outtype] = rt.Context(m, max_seq=32, n_batch=8, logits_all=True).eval(tokens)
+    a, b = out["f32"].ravel(), out["q4_k_m"].ravel()
+    assert np.isfinite(b).all()
+    assert np.corrcoef(a, b)[0, 1] > min_corr
