@@ -152,6 +152,12 @@ int sdy_engine_set_shard(int32_t rank, int32_t world, const void *nccl_id);
  * Same errors as engine_eval. 0 or -1. */
 int sdy_engine_eval_greedy(engine_ctx *c, const int32_t *tokens, int32_t n, int32_t *next);
 void sdy_engine_get_shard(int32_t *rank, int32_t *world);
+/* The attention heads rank `rank` of `world` holds when the model is sharded: range = {first query
+ * head, end, first KV head, end}. 1: attention split by heads (query heads with their KV heads; a
+ * KV head shared by several ranks when world > n_kv_head); 0: attention replicated (range covers
+ * every head); -1: bad arguments. */
+int sdy_attention_split(int32_t n_head, int32_t n_kv_head, int32_t head_dim, int32_t world, int32_t rank,
+                        int32_t *range);
 /* Rows [*begin, *end) of n that `rank` of `world` holds, in whole units of `align` rows. */
 void sdy_shard_range(int64_t n, int32_t world, int32_t rank, int64_t align, int64_t *begin, int64_t *end);
 

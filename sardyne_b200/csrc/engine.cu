@@ -164,6 +164,11 @@ struct engine_model {
     int rank = 0, world = 1;
     ncclComm_t comm = nullptr;
     int64_t f0 = 0, f1 = 0, d0 = 0, d1 = 0, e0 = 0, e1 = 0, v0 = 0, v1 = 0;
+    // Tensor-parallel attention (world > 1 where the heads split evenly enough): this rank holds
+    // query heads [h0, h1) and KV heads [k0, k1) (q/k/v rows, their biases, its KV cache) and rows
+    // [d0, d1) of the attention output matrix; attn_tp false: attention replicated on every rank.
+    bool attn_tp = false;
+    int h0 = 0, h1 = 0, k0 = 0, k1 = 0;
     DMat tok_embd, output;
     float *output_norm = nullptr;
     std::vector<DLayer> layers;
@@ -208,6 +213,9 @@ struct engine_ctx {
     // Sharded models: all-reduce sources, zero outside this rank's columns (hsend: FFN activations
     // [B][ffn_dim], xsend: residual [B][dim], lsend: logits), and the gathered FFN activations.
     float *hsend = nullptr, *hfull = nullptr, *xsend = nullptr, *lsend = nullptr;
+    // Heads split across ranks: this rank's attention output (prefill: [B][local heads * hd]) and
+    // the all-reduce source of the gathered one (zero outside this rank's columns).
+    float *att_loc = nullptr, *attsend = nullptr;
     int32_t *moe_top = nullptr;
     int32_t *tokpos = nullptr;    // device: [0] position of the first token, [1..] token ids
     int32_t *h_tokpos = nullptr;  // pinned staging of the same
@@ -388,6 +396,31 @@ int read_config(engine_model *m, char *err, size_t len) {
     return 0;
 }
 
+// The attention heads of rank `rank` of `world`: whole KV heads with their query heads when every
+// rank can have one (world <= n_kv_head); otherwise, when the query heads divide evenly and each
+// rank's share lies within one KV head, that KV head is computed by every rank that shares it.
+// Any other shape keeps attention replicated (*tp false).
+void attention_split(const engine_model_info &in, int world, int rank, bool *tp, int *h0, int *h1, int *k0, int *k1) {
+    *tp = false;
+    *h0 = 0, *h1 = in.n_head, *k0 = 0, *k1 = in.n_kv_head;
+    if (world <= 1) return;
+    const int n_rep = in.n_head / in.n_kv_head;
+    if (world <= in.n_kv_head) {
+        int64_t b, e;
+        shard_range(in.n_kv_head, world, rank, 1, &b, &e);
+        *k0 = (int)b, *k1 = (int)e, *h0 = *k0 * n_rep, *h1 = *k1 * n_rep;
+        *tp = true;
+    } else if (world % in.n_kv_head == 0 && in.n_head % world == 0 && n_rep % (world / in.n_kv_head) == 0) {
+        const int per = in.n_head / world;
+        *h0 = rank * per, *h1 = *h0 + per, *k0 = *h0 / n_rep, *k1 = *k0 + 1;
+        *tp = true;
+    }
+    if (*tp && ((*h1 - *h0) * in.head_dim % GROUP_ROWS || (*k1 - *k0) * in.head_dim % GROUP_ROWS)) {
+        *tp = false;  // q/k/v row slices must be whole 8-row groups
+        *h0 = 0, *h1 = in.n_head, *k0 = 0, *k1 = in.n_kv_head;
+    }
+}
+
 // ------------------------------------------------------------------------------ upload
 
 void *dalloc(engine_model *m, size_t bytes) {
@@ -499,17 +532,23 @@ int get_tensor(engine_model *m, const char *name, int n_in, int64_t n_out, int n
 // A projection from one input: consecutive tensors of the same quantized type whose row counts
 // are whole 8-row groups share one device matrix (one launch); the others stay separate. Rows
 // [r0, r1) of every tensor (r1 < 0: all), experts [e_begin, e_end) (e_end < 0: all).
+// slices: per tensor (first row, row count), overriding [r0, r1).
 int get_proj(engine_model *m, const std::vector<std::string> &names, const std::vector<int64_t> &rows, int n_in,
              int n_expert, Proj *out, char *err, size_t len, int64_t r0 = 0, int64_t r1 = -1, int64_t e_begin = 0,
-             int64_t e_end = -1) {
+             int64_t e_end = -1, const std::vector<std::pair<int64_t, int64_t>> *slices = nullptr) {
     std::vector<const gguf_tensor *> ts;
     std::vector<int64_t> cnt, st;
     for (size_t i = 0; i < names.size(); i++) {
         const gguf_tensor *t = check_tensor(m, names[i].c_str(), n_in, rows[i], n_expert, err, len);
         if (!t) return -1;
         ts.push_back(t);
-        cnt.push_back(r1 < 0 ? rows[i] : r1 - r0);
-        st.push_back(r1 < 0 ? 0 : r0);
+        if (slices) {
+            st.push_back((*slices)[i].first);
+            cnt.push_back((*slices)[i].second);
+        } else {
+            cnt.push_back(r1 < 0 ? rows[i] : r1 - r0);
+            st.push_back(r1 < 0 ? 0 : r0);
+        }
     }
     if (e_end < 0) e_end = n_expert;
     const int ne = n_expert ? (int)(e_end - e_begin) : 0;
@@ -534,8 +573,10 @@ int get_proj(engine_model *m, const std::vector<std::string> &names, const std::
     return 0;
 }
 
-// A vector of n elements converted to f32 on the device.
-int get_vector(engine_model *m, const char *name, int n, float **out, char *err, size_t len) {
+// A vector of n elements converted to f32 on the device (elements [first, first + count) of it
+// when count > 0).
+int get_vector(engine_model *m, const char *name, int n, float **out, char *err, size_t len, int first = 0,
+               int count = 0) {
     const gguf_tensor *t = find(m->gf, name);
     if (!t) {
         put_err(err, len, "tensore mancante: %s", name);
@@ -549,13 +590,17 @@ int get_vector(engine_model *m, const char *name, int n, float **out, char *err,
         put_err(err, len, "%s: tipo %s non supportato", name, gguf_type_name(t->type));
         return -1;
     }
-    float *d = (float *)dalloc(m, (size_t)n * 4);
-    uint8_t *raw = bounce(m, t->nbytes);
-    if (!d || !raw || !SDY_CUDA(cudaMemcpyAsync(raw, t->data, t->nbytes, cudaMemcpyHostToDevice, m->st))) {
+    if (count <= 0) first = 0, count = n;
+    const size_t esz = block_bytes((int)t->type), bytes = (size_t)count * esz;
+    float *d = (float *)dalloc(m, (size_t)count * 4);
+    uint8_t *raw = bounce(m, bytes);
+    if (!d || !raw ||
+        !SDY_CUDA(cudaMemcpyAsync(raw, (const uint8_t *)t->data + (size_t)first * esz, bytes, cudaMemcpyHostToDevice,
+                                  m->st))) {
         put_err(err, len, "%s: caricamento sulla GPU fallito (%s)", name, last_error());
         return -1;
     }
-    convert_to_f32(raw, (int)t->type, d, n, m->st);
+    convert_to_f32(raw, (int)t->type, d, count, m->st);
     if (!SDY_CUDA(cudaStreamSynchronize(m->st))) return -1;
     *out = d;
     return 0;
@@ -1007,8 +1052,10 @@ void maybe_segment(engine_ctx *c, int layer);
 void forward(engine_ctx *c, int n, int out_rows) {
     const engine_model *m = c->m;
     const engine_model_info &in = m->info;
-    const int dim = in.dim, hd = in.head_dim, q_dim = in.n_head * hd, kv_dim = in.n_kv_head * hd;
-    const size_t layer_stride = (size_t)in.n_kv_head * c->max_seq * hd;
+    const int dim = in.dim, hd = in.head_dim, q_dim = in.n_head * hd;
+    // this rank's heads (all of them unless attention is split across ranks)
+    const int hq = m->h1 - m->h0, hkv = m->k1 - m->k0, q_loc = hq * hd, kv_loc = hkv * hd;
+    const size_t layer_stride = (size_t)hkv * c->max_seq * hd;
     const int64_t QL = c->qkv_ld;
     const XQ *q8k, *q80;
     embed(c, n);
@@ -1027,16 +1074,16 @@ void forward(engine_ctx *c, int n, int out_rows) {
         }
         PostQKV p{};
         p.q = c->qkv;
-        p.k = c->qkv + q_dim;
-        p.v = c->qkv + q_dim + kv_dim;
+        p.k = c->qkv + q_loc;
+        p.v = c->qkv + q_loc + kv_loc;
         p.ldq = p.ldk = p.ldv = QL;
         p.bq = L.bq;
         p.bk = L.bk;
         p.bv = L.bv;
         p.q_norm = L.q_norm;
         p.k_norm = L.k_norm;
-        p.n_head = in.n_head;
-        p.n_kv_head = in.n_kv_head;
+        p.n_head = hq;
+        p.n_kv_head = hkv;
         p.hd = hd;
         p.eps = in.norm_eps;
         p.cos = c->rope_cos;
@@ -1046,13 +1093,30 @@ void forward(engine_ctx *c, int n, int out_rows) {
         p.kc = kc;
         p.vc = vc;
         p.max_seq = c->max_seq;
-        attention(c->att, c->qkv, QL, kc, vc, n, in.n_head, in.n_kv_head, hd, 0, c->tokpos, c->max_seq, c->scores, 0,
-                  c->st, &p);
-        forget_activations(c);
-        if (n == 1 && fusion_enabled() && L.wo.quant())  // the attention output quantized in the prologue
-            matmul_act(c, c->x, dim, L.wo, ActIn{c->att, q_dim}, n, c->x);
-        else
-            matmul(c, c->x, dim, c->att, q_dim, L.wo, n, c->x);
+        if (m->attn_tp) {
+            // this rank's heads, then every rank's head outputs gathered (an all-reduce of buffers
+            // in which each column has one nonzero contributor), then this rank's rows [d0, d1) of
+            // x + Wo . att, gathered likewise: every value is the one-GPU value
+            float *aout = n == 1 ? c->attsend + (size_t)m->h0 * hd : c->att_loc;
+            attention(aout, c->qkv, QL, kc, vc, n, hq, hkv, hd, 0, c->tokpos, c->max_seq, c->scores, 0, c->st, &p);
+            if (n > 1)
+                SDY_CUDA(cudaMemcpy2DAsync(c->attsend + (size_t)m->h0 * hd, (size_t)q_dim * 4, c->att_loc,
+                                           (size_t)q_loc * 4, (size_t)q_loc * 4, n, cudaMemcpyDeviceToDevice, c->st));
+            all_reduce(c, c->attsend, c->att, (size_t)n * q_dim);
+            forget_activations(c);
+            if (n == 1 && fusion_enabled() && L.wo.quant())
+                matmul_act(c, c->xsend + m->d0, dim, L.wo, ActIn{c->att, q_dim}, n, c->x + m->d0);
+            else
+                matmul(c, c->xsend + m->d0, dim, c->att, q_dim, L.wo, n, c->x + m->d0);
+            all_reduce(c, c->xsend, c->x, (size_t)n * dim);
+        } else {
+            attention(c->att, c->qkv, QL, kc, vc, n, hq, hkv, hd, 0, c->tokpos, c->max_seq, c->scores, 0, c->st, &p);
+            forget_activations(c);
+            if (n == 1 && fusion_enabled() && L.wo.quant())  // the attention output quantized in the prologue
+                matmul_act(c, c->x, dim, L.wo, ActIn{c->att, q_dim}, n, c->x);
+            else
+                matmul(c, c->x, dim, c->att, q_dim, L.wo, n, c->x);
+        }
         // MLP: x = x + down(silu(gate.norm(x)) * up.norm(x)), or its MoE
         const ActIn ffn_nin{c->x, dim, L.ffn_norm, in.norm_eps};
         if (in.n_expert && moe_decode_ok(c, L, n) && moe_block_decode(c, L)) {
@@ -1229,6 +1293,7 @@ engine_model *engine_model_load(const char *path, char *err, size_t err_len) {
     shard_range(dim, m->world, m->rank, GROUP_ROWS, &m->d0, &m->d1);
     shard_range(in.n_expert, m->world, m->rank, 1, &m->e0, &m->e1);
     shard_range(in.n_vocab, m->world, m->rank, GROUP_ROWS, &m->v0, &m->v1);
+    attention_split(in, m->world, m->rank, &m->attn_tp, &m->h0, &m->h1, &m->k0, &m->k1);
     if (m->world > 1) {
         const Nccl *nc = nccl();
         ncclResult_t r = nc ? nc->comm_init_rank(&m->comm, m->world, g_shard.id, m->rank) : ncclSystemError;
@@ -1241,6 +1306,12 @@ engine_model *engine_model_load(const char *path, char *err, size_t err_len) {
         }
     }
     m->layers.resize(in.n_layer);
+    // q / k / v rows this rank holds (all of them unless attention is split by heads)
+    const int hd = in.head_dim;
+    const std::vector<std::pair<int64_t, int64_t>> qkv_rows = {
+        {(int64_t)m->h0 * hd, (int64_t)(m->h1 - m->h0) * hd},
+        {(int64_t)m->k0 * hd, (int64_t)(m->k1 - m->k0) * hd},
+        {(int64_t)m->k0 * hd, (int64_t)(m->k1 - m->k0) * hd}};
     bool ok = !get_tensor(m, "token_embd.weight", dim, in.n_vocab, 0, &m->tok_embd, err, err_len) &&
               !get_vector(m, "output_norm.weight", dim, &m->output_norm, err, err_len);
     if (ok) {
@@ -1254,9 +1325,10 @@ engine_model *engine_model_load(const char *path, char *err, size_t err_len) {
         auto nm = [&](LayerTensor t) { return layer_tensor(l, t); };
         ok = !get_vector(m, nm(LT_ATTN_NORM).c_str(), dim, &L.attn_norm, err, err_len) &&
              !get_vector(m, nm(LT_FFN_NORM).c_str(), dim, &L.ffn_norm, err, err_len) &&
-             !get_proj(m, {nm(LT_Q), nm(LT_K), nm(LT_V)}, {q_dim, kv_dim, kv_dim},
-                       dim, 0, &L.qkv, err, err_len) &&
-             !get_tensor(m, nm(LT_WO).c_str(), q_dim, dim, 0, &L.wo, err, err_len);
+             !get_proj(m, {nm(LT_Q), nm(LT_K), nm(LT_V)}, {q_dim, kv_dim, kv_dim}, dim, 0, &L.qkv, err, err_len, 0,
+                       -1, 0, -1, &qkv_rows) &&
+             (m->attn_tp ? !get_tensor(m, nm(LT_WO).c_str(), q_dim, dim, 0, &L.wo, err, err_len, m->d0, m->d1)
+                         : !get_tensor(m, nm(LT_WO).c_str(), q_dim, dim, 0, &L.wo, err, err_len));
         if (!ok) break;
         if (in.n_expert) {
             int ne = in.n_expert, fe = in.ffn_exp_dim;
@@ -1272,9 +1344,12 @@ engine_model *engine_model_load(const char *path, char *err, size_t err_len) {
                              m->d1);
         }
         if (ok && in.qkv_bias)
-            ok = !get_vector(m, nm(LT_Q_BIAS).c_str(), q_dim, &L.bq, err, err_len) &&
-                 !get_vector(m, nm(LT_K_BIAS).c_str(), kv_dim, &L.bk, err, err_len) &&
-                 !get_vector(m, nm(LT_V_BIAS).c_str(), kv_dim, &L.bv, err, err_len);
+            ok = !get_vector(m, nm(LT_Q_BIAS).c_str(), q_dim, &L.bq, err, err_len, qkv_rows[0].first,
+                             (int)qkv_rows[0].second) &&
+                 !get_vector(m, nm(LT_K_BIAS).c_str(), kv_dim, &L.bk, err, err_len, qkv_rows[1].first,
+                             (int)qkv_rows[1].second) &&
+                 !get_vector(m, nm(LT_V_BIAS).c_str(), kv_dim, &L.bv, err, err_len, qkv_rows[2].first,
+                             (int)qkv_rows[2].second);
         if (ok && in.qk_norm)
             ok = !get_vector(m, nm(LT_Q_NORM).c_str(), in.head_dim, &L.q_norm, err, err_len) &&
                  !get_vector(m, nm(LT_K_NORM).c_str(), in.head_dim, &L.k_norm, err, err_len);
@@ -1321,11 +1396,13 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
     if (getenv("SARDYNE_NO_GRAPH")) c->graph_state = -1;
     const engine_model_info &in = m->info;
     const size_t B = n_batch, S = max_seq, hd = in.head_dim;
-    const size_t q_dim = (size_t)in.n_head * hd, kv_dim = (size_t)in.n_kv_head * hd;
-    const size_t kv = (size_t)in.n_layer * in.n_kv_head * S * hd;
+    const size_t q_dim = (size_t)in.n_head * hd;
+    // this rank's heads (all of them unless attention is split across ranks)
+    const size_t q_loc = (size_t)(m->h1 - m->h0) * hd, kv_loc = (size_t)(m->k1 - m->k0) * hd;
+    const size_t kv = (size_t)in.n_layer * (m->k1 - m->k0) * S * hd;
     const size_t ffn = in.n_expert ? in.ffn_exp_dim : in.ffn_dim;
     const size_t K = in.n_expert ? in.n_expert_used : 0, slots = B * K;
-    c->qkv_ld = (int)(q_dim + 2 * kv_dim);
+    c->qkv_ld = (int)(q_loc + 2 * kv_loc);
     c->gu_ld = (int)(2 * (in.n_expert ? ffn : (size_t)(m->f1 - m->f0)));
     const size_t tmp_n = std::max<size_t>((size_t)in.dim, (size_t)in.n_vocab) * B;
     struct Item {
@@ -1361,7 +1438,11 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
         if (!in.n_expert) {
             items.push_back({(void **)&c->hsend, B * ffn * 4});
             items.push_back({(void **)&c->hfull, B * ffn * 4});
-            items.push_back({(void **)&c->xsend, B * in.dim * 4});
+        }
+        if (!in.n_expert || m->attn_tp) items.push_back({(void **)&c->xsend, B * in.dim * 4});
+        if (m->attn_tp) {
+            items.push_back({(void **)&c->att_loc, B * q_loc * 4});
+            items.push_back({(void **)&c->attsend, B * q_dim * 4});
         }
         items.push_back({(void **)&c->lsend, logit_rows * in.n_vocab * 4});
     }
@@ -1387,7 +1468,9 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
         p += align_up(it.bytes, 256);
     }
     bool zeroed = true;  // all-reduce sources start (and outside this rank's columns stay) zero
-    if (c->hsend) zeroed = SDY_CUDA(cudaMemset(c->hsend, 0, B * ffn * 4)) && SDY_CUDA(cudaMemset(c->xsend, 0, B * in.dim * 4));
+    if (c->hsend) zeroed = SDY_CUDA(cudaMemset(c->hsend, 0, B * ffn * 4));
+    if (c->xsend) zeroed = zeroed && SDY_CUDA(cudaMemset(c->xsend, 0, B * in.dim * 4));
+    if (c->attsend) zeroed = zeroed && SDY_CUDA(cudaMemset(c->attsend, 0, B * q_dim * 4));
     if (c->lsend) zeroed = zeroed && SDY_CUDA(cudaMemset(c->lsend, 0, logit_rows * in.n_vocab * 4));
     if (c->md_sync) zeroed = zeroed && SDY_CUDA(cudaMemset(c->md_sync, 0, 4 * sizeof(unsigned)));
     zeroed = zeroed && SDY_CUDA(cudaMemset(c->am_count, 0, 4));
@@ -1556,6 +1639,20 @@ int sdy_engine_set_shard(int32_t rank, int32_t world, const void *nccl_id) {
 void sdy_engine_get_shard(int32_t *rank, int32_t *world) {
     if (rank) *rank = g_shard.rank;
     if (world) *world = g_shard.world;
+}
+
+int sdy_attention_split(int32_t n_head, int32_t n_kv_head, int32_t head_dim, int32_t world, int32_t rank,
+                        int32_t *range) {
+    if (n_head < 1 || n_kv_head < 1 || n_head % n_kv_head || head_dim < 1 || world < 1 || rank < 0 || rank >= world ||
+        !range)
+        return -1;
+    engine_model_info in{};
+    in.n_head = n_head;
+    in.n_kv_head = n_kv_head;
+    in.head_dim = head_dim;
+    bool tp = false;
+    attention_split(in, world, rank, &tp, &range[0], &range[1], &range[2], &range[3]);
+    return tp ? 1 : 0;
 }
 
 void sdy_shard_range(int64_t n, int32_t world, int32_t rank, int64_t align, int64_t *begin, int64_t *end) {

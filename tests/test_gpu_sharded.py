@@ -1,6 +1,9 @@
 """The sharded engine on 2 GPUs (one process each, NCCL all-reduce) returns the one-GPU logits bit
-for bit: dense FFN rows and MoE experts split across the ranks, prefill through the tensor-core
-GEMM and single-token steps replayed from CUDA graphs. Needs two GPUs; skipped otherwise."""
+for bit: attention heads (with their KV cache and the attention-output rows), dense FFN rows and
+MoE experts split across the ranks, prefill through the tensor-core GEMM and single-token steps
+replayed from CUDA graphs; on small models and at the BASELINE Qwen2.5-3B and Qwen3-30B-A3B shapes
+(whose one-GPU logits equal the reference engine's, tests/test_gpu_baseline_shapes.py). Needs two
+GPUs; skipped otherwise."""
 import os
 import socket
 
@@ -26,6 +29,12 @@ def run_model(path):
     import refruntime as rt
     m = rt.model(str(path))
     ctx = rt.Context(m, max_seq=96, n_batch=len(PROMPT))
+    if m.info.n_vocab > 100000:  # BASELINE shapes: prompt ids spread over the vocabulary
+        prompt = np.random.default_rng(0).integers(0, m.info.n_vocab, len(PROMPT)).tolist()
+        out = [ctx.eval(prompt)]
+        for i in range(STEPS):
+            out.append(ctx.eval([int(np.argmax(out[-1]))]))
+        return np.stack(out)
     out = [ctx.eval(PROMPT)]
     for i in range(STEPS):
         out.append(ctx.eval([int(np.argmax(out[-1])) + i % 2]))
@@ -48,14 +57,17 @@ def _rank(rank, world, port, path, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name", sorted(SPECS))
+@pytest.mark.parametrize("name", sorted(SPECS) + ["qwen25_3b", "qwen3moe"])
 def test_two_ranks_match_one_gpu(tmp_path, name):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    path = tmp_path / f"{name}.gguf"
-    synth.write_model(path, synth.Spec(**SPECS[name], seed=11))
+    if name in SPECS:
+        path = tmp_path / f"{name}.gguf"
+        synth.write_model(path, synth.Spec(**SPECS[name], seed=11))
+    else:
+        path = synth.baseline_model(name)
     want = run_model(path)
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

@@ -78,3 +78,33 @@ def test_nccl_id_exchange_gloo():
         assert p.exitcode == 0
     assert [g[:3] for g in got] == [(0, 0, 2), (1, 1, 2)]
     assert got[0][3] == got[1][3] and len(got[0][3]) == 128
+
+
+@pytest.mark.parametrize("n_head,n_kv,hd", [(16, 2, 128), (32, 4, 128), (9, 3, 64), (4, 2, 64), (8, 8, 64)])
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+def test_attention_split_covers_every_head_once(n_head, n_kv, hd, world):
+    """Query heads split over the ranks exactly once, each rank holding the KV heads its query heads
+    read (GQA: head h reads KV head h / (n_head / n_kv)), and the local grouping consistent."""
+    lib = capi.lib()
+    n_rep = n_head // n_kv
+    owners = [0] * n_head
+    modes = set()
+    for r in range(world):
+        rng = (ctypes.c_int32 * 4)()
+        mode = lib.sdy_attention_split(n_head, n_kv, hd, world, r, rng)
+        assert mode in (0, 1)
+        modes.add(mode)
+        h0, h1, k0, k1 = list(rng)
+        if mode == 0:
+            assert (h0, h1, k0, k1) == (0, n_head, 0, n_kv)
+            continue
+        assert 0 <= h0 < h1 <= n_head and 0 <= k0 < k1 <= n_kv
+        assert (h1 - h0) % (k1 - k0) == 0
+        rep_local = (h1 - h0) // (k1 - k0)
+        for h in range(h0, h1):
+            owners[h] += 1
+            assert h // n_rep == k0 + (h - h0) // rep_local  # the local KV head is the global one
+        assert ((h1 - h0) * hd) % 8 == 0 and ((k1 - k0) * hd) % 8 == 0
+    assert len(modes) == 1  # every rank agrees on split or replicated
+    if modes == {1}:
+        assert owners == [1] * n_head
