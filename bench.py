@@ -49,8 +49,14 @@ sys.path.insert(0, str(REPO))
 METRIC = "Q4_K/Q6_K matvec HBM GB/s (% of 8 TB/s); decode tok/s Qwen3-30B-A3B-shape"
 SHAPES = [(2048, 11008), (11008, 2048), (151936, 2048)]  # [n_out][n_in]
 FORMATS = ["Q4_K", "Q6_K"]
-TYPE_ID = {"Q4_K": 12, "Q6_K": 14, "Q8_K": 15}
-BLOCK = {"Q4_K": (256, 144), "Q6_K": (256, 210)}
+FORMATS32 = ["Q8_0", "Q4_0", "Q5_0"]  # the rest of config 2's formats (not in the headline value)
+TYPE_ID = {"Q4_0": 2, "Q5_0": 6, "Q8_0": 8, "Q4_K": 12, "Q6_K": 14, "Q8_K": 15}
+BLOCK = {"Q4_K": (256, 144), "Q6_K": (256, 210), "Q8_0": (32, 34), "Q4_0": (32, 18), "Q5_0": (32, 22)}
+
+
+def act_type(fmt):
+    """The activation layout a weight format multiplies with (quant.c: vec_dot_type)."""
+    return "Q8_0" if fmt in FORMATS32 else "Q8_K"
 WORKLOAD = ("BASELINE config 2 at batch 1: Q4_K and Q6_K matvec over 2048x11008, 11008x2048 and "
             "151936x2048 ([n_out][n_in]), Q8_K activations quantized on the device once per input width")
 
@@ -69,12 +75,12 @@ def alg_bytes(fmt, n_out, n_in):
     return weight_bytes(fmt, n_out, n_in) + 4 * n_in + 4 * n_out
 
 
-def make_inputs(seed=0, only=None):
+def make_inputs(seed=0, only=None, formats=FORMATS):
     """The sweep's matrices; `only` ("Q6_K:151936") keeps one format/row count (profiling runs)."""
     from sardyne_b200 import kquant
     rng = np.random.default_rng(seed)
     mats = []
-    for fmt in FORMATS:
+    for fmt in formats:
         for n_out, n_in in SHAPES:
             if only and only != f"{fmt}:{n_out}":
                 continue
@@ -274,6 +280,70 @@ def shard_rows(n_out, rank, world):
     b, e = ctypes.c_int64(), ctypes.c_int64()
     capi.lib().sdy_shard_range(n_out, world, rank, 8, ctypes.byref(b), ctypes.byref(e))
     return b.value, e.value
+
+
+def measure_formats32(lib, dev, reps=20):
+    """Config 2's 32-element formats (Q8_0, Q4_0, Q5_0) at batch 1, one matvec per matrix with Q8_0
+    activations: per-matrix device time by the same sweep-with/without-it difference as the headline
+    breakdown (each matrix cold in L2 when it runs). Informational; not part of `value`."""
+    import torch
+    from sardyne_b200 import capi
+    mats, xs = make_inputs(seed=2, formats=FORMATS32)
+    stream = torch.cuda.Stream(device=dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    handles, outs, d_xq = [], [], {}
+    for fmt, n_out, n_in, w in mats:
+        h = lib.sdy_qmat_upload(w.ctypes.data, TYPE_ID[fmt], n_out, n_in)
+        if not h:
+            raise RuntimeError(capi.last_error())
+        handles.append(h)
+        outs.append(torch.empty(n_out, dtype=torch.float32, device=dev))
+    for n_in, x in xs.items():
+        d_x = torch.from_numpy(x).to(dev)
+        d_xq[n_in] = torch.empty(lib.sdy_xq_bytes(TYPE_ID["Q8_0"], n_in, 1), dtype=torch.uint8, device=dev)
+        lib.sdy_quantize_rows_dev(TYPE_ID["Q8_0"], ctypes.c_void_p(d_x.data_ptr()), 1, n_in,
+                                  ctypes.c_void_p(d_xq[n_in].data_ptr()), sp)
+
+    def sweep(skip=-1):
+        for i, (fmt, n_out, n_in, _) in enumerate(mats):
+            if i != skip:
+                lib.sdy_qmatvec_dev(handles[i], ctypes.c_void_p(d_xq[n_in].data_ptr()), 1,
+                                    ctypes.c_void_p(outs[i].data_ptr()), n_out, 0, n_out, sp)
+
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+            fn()
+        return g
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            sweep()
+    torch.cuda.synchronize()
+    capi.check()
+    g_all = capture(lambda: [sweep() for _ in range(reps)])
+    rows = []
+    for i, (fmt, n_out, n_in, _) in enumerate(mats):
+        g_wo = capture(lambda i=i: [sweep(skip=i) for _ in range(reps)])
+        ts = []
+        for g in (g_wo, g_all, g_wo, g_all):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ms = (min(ts[1], ts[3]) - min(ts[0], ts[2])) / reps
+        rows.append({"format": fmt, "n_out": n_out, "n_in": n_in, "us": round(ms * 1e3, 2),
+                     "GB/s": round(alg_bytes(fmt, n_out, n_in) / (ms * 1e-3) / 1e9, 1)})
+        del g_wo
+    del g_all
+    capi.check()
+    for h in handles:
+        lib.sdy_qmat_free(h)
+    return {"note": "batch 1, Q8_0 activations, per-matrix device time (sweep with / without it)",
+            "per_matrix": rows}
 
 
 def run_b200(args, rank, world, local_rank):
@@ -557,6 +627,7 @@ def run_b200(args, rank, world, local_rank):
         barrier()
         lib.sdy_p2p_free(p2p_buf)
 
+    formats32 = measure_formats32(lib, dev) if world == 1 and not args.only else None
     decode = None
     if not args.no_decode:
         decode = measure_decode("qwen3moe", args, rank, world, cpu_baseline=not args.no_cpu_baseline)
@@ -587,6 +658,8 @@ def run_b200(args, rank, world, local_rank):
             line["cpu_baseline"] = time_reference(full, xs)
         except OSError as e:
             line["cpu_baseline"] = {"value": None, "unavailable": str(e)}
+    if formats32 is not None:
+        line["formats_32"] = formats32
     if decode is not None:
         line["decode"] = decode
     print(json.dumps(line))
@@ -596,14 +669,15 @@ def run_b200(args, rank, world, local_rank):
 # ------------------------------------------------------------------------------ GEMM workload
 
 def run_gemm(args):
-    """BASELINE config 2 at batches 128 and 512: the sweep's Q4_K/Q6_K matrices times many tokens,
-    through the tensor-core GEMM (int8 tcgen05 MMAs, exact per-superblock combine). Reports useful
-    multiply-add throughput (2 * n_out * n_in * tokens per product) per matrix and batch."""
+    """BASELINE config 2 at batches 128 and 512: the sweep's matrices of every format times many
+    tokens, through the tensor-core GEMM (int8 tcgen05 MMAs, exact per-superblock / per-block
+    combine). Reports useful multiply-add throughput (2 * n_out * n_in * tokens per product) per
+    matrix and batch; `value` is the best Q4_K/Q6_K product."""
     import torch
     from sardyne_b200 import capi
     torch.cuda.set_device(0)
     lib = capi.lib()
-    mats, _ = make_inputs(only=args.only)
+    mats, _ = make_inputs(only=args.only, formats=FORMATS + FORMATS32)
     stream = torch.cuda.Stream()
     sp = ctypes.c_void_p(stream.cuda_stream)
     rows = []
@@ -616,12 +690,13 @@ def run_gemm(args):
         h = lib.sdy_qmat_upload(w.ctypes.data, TYPE_ID[fmt], n_out, n_in)
         if not h:
             raise RuntimeError(capi.last_error())
+        vt = TYPE_ID[act_type(fmt)]
         for batch in (128, 512):
             x = torch.randn(batch, n_in, device="cuda")
-            xq = torch.empty(lib.sdy_xq_bytes(TYPE_ID["Q8_K"], n_in, batch), dtype=torch.uint8, device="cuda")
+            xq = torch.empty(lib.sdy_xq_bytes(vt, n_in, batch), dtype=torch.uint8, device="cuda")
             y = torch.empty(batch, n_out, device="cuda")
             with torch.cuda.stream(stream):
-                lib.sdy_quantize_rows_dev(TYPE_ID["Q8_K"], ctypes.c_void_p(x.data_ptr()), batch, n_in,
+                lib.sdy_quantize_rows_dev(vt, ctypes.c_void_p(x.data_ptr()), batch, n_in,
                                           ctypes.c_void_p(xq.data_ptr()), sp)
 
                 def prod():
@@ -644,7 +719,7 @@ def run_gemm(args):
             rows.append({"format": fmt, "n_out": n_out, "n_in": n_in, "batch": batch, "us": round(us, 1),
                          "TOPS": round(tops, 1), "tok_s": round(batch / (us * 1e-6), 1)})
         lib.sdy_qmat_free(h)
-    best = max(rows, key=lambda r: r["TOPS"])
+    best = max((r for r in rows if r["format"] in FORMATS), key=lambda r: r["TOPS"])
     line = {"metric": "Q4_K/Q6_K prefill GEMM useful int8 TOPS (exact per-superblock combine)",
             "value": best["TOPS"], "unit": "TOPS", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",

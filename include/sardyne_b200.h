@@ -158,6 +158,10 @@ void sdy_engine_get_shard(int32_t *rank, int32_t *world);
  * every head); -1: bad arguments. */
 int sdy_attention_split(int32_t n_head, int32_t n_kv_head, int32_t head_dim, int32_t world, int32_t rank,
                         int32_t *range);
+/* How the context's cross-rank exchanges travel: 1 over NVLink peer memory for the single-token
+ * sizes (NCCL for larger ones), 0 all over NCCL (SARDYNE_EXCHANGE=nccl, or a rank could not map
+ * its peers), -1 not sharded or no context. No counterpart in the reference (one host). */
+int sdy_engine_exchange(const engine_ctx *c);
 /* Rows [*begin, *end) of n that `rank` of `world` holds, in whole units of `align` rows. */
 void sdy_shard_range(int64_t n, int32_t world, int32_t rank, int64_t align, int64_t *begin, int64_t *end);
 

@@ -108,6 +108,7 @@ EXTENSIONS = {
     "sdy_engine_eval_greedy": (_i, [_vp, ctypes.POINTER(_i32), _i32, ctypes.POINTER(_i32)]),
     "sdy_attention_split": (_i, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                  ctypes.POINTER(ctypes.c_int32)]),
+    "sdy_engine_exchange": (_i, [_vp]),
     "sdy_shard_range": (None, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
                                ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]),
     "sdy_qmat_upload": (_vp, [_vp, _i, ctypes.c_int64, _i32]),

@@ -259,4 +259,27 @@ void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq
                     int n_slots, int64_t rows_per_expert, float *out, int64_t ldo_slot, cudaStream_t s,
                     int expert0 = 0, const ActIn *act = nullptr);
 
+// Exchange of the sharded engine over NVLink peer memory (p2p.cu). Every rank owns one buffer of
+// peer_exchange_bytes(cap) bytes, zeroed before it is shared, and maps every peer's (CUDA IPC).
+// peer_gather assembles in `recv` the rows x ld floats of which each rank computed a disjoint part
+// in its own `send`: columns [lo, hi) of every row, and with `top` set only the rows j with
+// e0 <= top[j] < e1 (MoE slots of this rank's experts; the parts of all ranks must cover every
+// element). Each rank stores its part into every rank's staging area; the last CTA then
+// release-stores the round number into every rank's flag for this rank, and every CTA waits (at
+// most px.wait_ns, acquire loads) for all ranks' flags before copying the staging area to
+// `recv`. Two staging halves alternate by round, so a rank can run one exchange ahead of another.
+// All ranks make the same sequence of calls (eager or replayed from a graph; the round counter
+// lives on the device). A wait that runs out sets the status word (peer_status) and returns.
+constexpr int PX_MAX_WORLD = 8;
+struct PeerExchange {
+    void *base[PX_MAX_WORLD] = {};  // every rank's buffer as mapped in this process
+    int rank = 0, world = 1;
+    int64_t cap = 0;  // floats per staging half, a multiple of 64
+    unsigned long long wait_ns = 1000000000ull;  // a wait for the other ranks gives up after this
+};
+size_t peer_exchange_bytes(int64_t cap);
+unsigned *peer_status(const PeerExchange &px);  // this rank's status word (device)
+void peer_gather(const PeerExchange &px, const float *send, float *recv, int rows, int64_t ld, int64_t lo,
+                 int64_t hi, const int32_t *top, int e0, int e1, cudaStream_t s);
+
 }  // namespace sdy

@@ -47,6 +47,7 @@ struct Nccl {
     ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                                cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
     const char *(*error_string)(ncclResult_t) = nullptr;
 };
@@ -58,12 +59,15 @@ const Nccl *nccl() {
             r.get_unique_id = (decltype(r.get_unique_id))dlsym(h, "ncclGetUniqueId");
             r.comm_init_rank = (decltype(r.comm_init_rank))dlsym(h, "ncclCommInitRank");
             r.all_reduce = (decltype(r.all_reduce))dlsym(h, "ncclAllReduce");
+            r.all_gather = (decltype(r.all_gather))dlsym(h, "ncclAllGather");
             r.comm_destroy = (decltype(r.comm_destroy))dlsym(h, "ncclCommDestroy");
             r.error_string = (decltype(r.error_string))dlsym(h, "ncclGetErrorString");
         }
         return r;
     }();
-    return n.get_unique_id && n.comm_init_rank && n.all_reduce && n.comm_destroy && n.error_string ? &n : nullptr;
+    return n.get_unique_id && n.comm_init_rank && n.all_reduce && n.all_gather && n.comm_destroy && n.error_string
+               ? &n
+               : nullptr;
 }
 
 // Process-wide shard configuration for the next engine_model_load (sdy_engine_set_shard).
@@ -216,6 +220,12 @@ struct engine_ctx {
     // Heads split across ranks: this rank's attention output (prefill: [B][local heads * hd]) and
     // the all-reduce source of the gathered one (zero outside this rank's columns).
     float *att_loc = nullptr, *attsend = nullptr;
+    // Single-token exchanges over NVLink peer memory (peer_gather) instead of NCCL: this rank's
+    // exchange buffer, the peers' as mapped here, the pinned copy of its status word; px_failed
+    // once a wait ran out (the ranks' rounds may then disagree, so the context refuses work).
+    PeerExchange px;
+    bool px_on = false, px_failed = false;
+    unsigned *h_px_status = nullptr;
     int32_t *moe_top = nullptr;
     int32_t *tokpos = nullptr;    // device: [0] position of the first token, [1..] token ids
     int32_t *h_tokpos = nullptr;  // pinned staging of the same
@@ -400,10 +410,11 @@ int read_config(engine_model *m, char *err, size_t len) {
 // rank can have one (world <= n_kv_head); otherwise, when the query heads divide evenly and each
 // rank's share lies within one KV head, that KV head is computed by every rank that shares it.
 // Any other shape keeps attention replicated (*tp false).
-void attention_split(const engine_model_info &in, int world, int rank, bool *tp, int *h0, int *h1, int *k0, int *k1) {
+void attention_split(const engine_model_info &in, int world, int rank, bool *tp, int *h0, int *h1, int *k0, int *k1,
+                     bool allow = true) {
     *tp = false;
     *h0 = 0, *h1 = in.n_head, *k0 = 0, *k1 = in.n_kv_head;
-    if (world <= 1) return;
+    if (world <= 1 || !allow) return;
     const int n_rep = in.n_head / in.n_kv_head;
     if (world <= in.n_kv_head) {
         int64_t b, e;
@@ -850,6 +861,21 @@ void all_reduce(engine_ctx *c, const float *send, float *recv, size_t count) {
     if (r != ncclSuccess) set_error("ncclAllReduce: %s", nccl()->error_string(r));
 }
 
+// Whether the exchange of rows x ld floats goes over peer memory (the single-token sizes; the same
+// answer on every rank, which all run the same steps).
+bool peer_exchange(const engine_ctx *c, int rows, int64_t ld) { return c->px_on && (int64_t)rows * ld <= c->px.cap; }
+
+// recv = the rows x ld floats of which every rank computed columns [lo, hi) of each row in its own
+// send (rows of this rank's experts only, with `top`), the rest of send zero: over peer memory
+// where peer_exchange() says so, else as an NCCL all-reduce.
+void exchange(engine_ctx *c, const float *send, float *recv, int rows, int64_t ld, int64_t lo, int64_t hi,
+              const int32_t *top = nullptr) {
+    if (peer_exchange(c, rows, ld))
+        peer_gather(c->px, send, recv, rows, ld, lo, hi, top, (int)c->m->e0, (int)c->m->e1, c->st);
+    else
+        all_reduce(c, send, recv, (size_t)rows * ld);
+}
+
 // L2 prefetch in single-token steps (SARDYNE_L2_PREFETCH = off | layer | experts | all): the next
 // layer's matrices, and the chosen experts' down matrices. Default: all on MoE models, none on
 // dense ones. Measured: the down prefetch gains ~1% on the Qwen3-30B-A3B shape and the next
@@ -1011,7 +1037,9 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n, const ActIn *nin = nullptr) 
     Proj down;
     down.parts.push_back(Part{L.down, 0});
     const bool sharded = c->m->world > 1;
-    if (sharded) SDY_CUDA(cudaMemsetAsync(c->moe_y, 0, (size_t)slots * dim * 4, c->st));  // other ranks' slots
+    const bool over_peers = sharded && peer_exchange(c, slots, dim);
+    if (sharded && !over_peers)  // other ranks' slots zero for the all-reduce
+        SDY_CUDA(cudaMemsetAsync(c->moe_y, 0, (size_t)slots * dim * 4, c->st));
     if (grouped) {
         const XQ &xq = activations(c, c->moe_gu, gu, slots, fe, L.down.type);
         qgemm_grouped(L.down.q, L.down.gpe, ne_local, xq, 1, c->grp_off, c->grp_slot, c->grp_tiles, slots,
@@ -1024,7 +1052,7 @@ void moe_ffn(engine_ctx *c, const DLayer &L, int n, const ActIn *nin = nullptr) 
         gate.ldu = gu;
         project_experts(c, down, c->moe_y, dim, c->moe_gu, gu, slots, slots, 1, silu_fused ? &gate : nullptr);
     }
-    if (sharded) all_reduce(c, c->moe_y, c->moe_y, (size_t)slots * dim);  // every slot from its expert's rank
+    if (sharded) exchange(c, c->moe_y, c->moe_y, slots, dim, 0, dim, c->moe_top);  // each slot from its expert's rank
     moe_combine(c->moe_y, dim, c->moe_top, c->moe_w, k, dim, n, c->x, dim, c->st);
 }
 
@@ -1102,13 +1130,13 @@ void forward(engine_ctx *c, int n, int out_rows) {
             if (n > 1)
                 SDY_CUDA(cudaMemcpy2DAsync(c->attsend + (size_t)m->h0 * hd, (size_t)q_dim * 4, c->att_loc,
                                            (size_t)q_loc * 4, (size_t)q_loc * 4, n, cudaMemcpyDeviceToDevice, c->st));
-            all_reduce(c, c->attsend, c->att, (size_t)n * q_dim);
+            exchange(c, c->attsend, c->att, n, q_dim, (int64_t)m->h0 * hd, (int64_t)m->h1 * hd);
             forget_activations(c);
             if (n == 1 && fusion_enabled() && L.wo.quant())
                 matmul_act(c, c->xsend + m->d0, dim, L.wo, ActIn{c->att, q_dim}, n, c->x + m->d0);
             else
                 matmul(c, c->xsend + m->d0, dim, c->att, q_dim, L.wo, n, c->x + m->d0);
-            all_reduce(c, c->xsend, c->x, (size_t)n * dim);
+            exchange(c, c->xsend, c->x, n, dim, m->d0, m->d1);
         } else {
             attention(c->att, c->qkv, QL, kc, vc, n, hq, hkv, hd, 0, c->tokpos, c->max_seq, c->scores, 0, c->st, &p);
             forget_activations(c);
@@ -1145,10 +1173,10 @@ void forward(engine_ctx *c, int n, int out_rows) {
                 // every rank; its rows [d0, d1) of down -> its columns of x, gathered likewise
                 const int nf = (int)(m->f1 - m->f0);
                 silu_scatter(c->hgu, GU, c->hgu + nf, GU, nf, n, c->hsend + m->f0, F, c->st);
-                all_reduce(c, c->hsend, c->hfull, (size_t)n * F);
+                exchange(c, c->hsend, c->hfull, n, F, m->f0, m->f1);
                 forget_activations(c);
                 matmul(c, c->xsend + m->d0, dim, c->hfull, F, L.down, n, c->x + m->d0);
-                all_reduce(c, c->xsend, c->x, (size_t)n * dim);
+                exchange(c, c->xsend, c->x, n, dim, m->d0, m->d1);
             } else {
                 want_activations(c, {&L.down}, c->hgu, GU, n, F, &q8k, &q80);
                 silu_quant(c->hgu, GU, c->hgu + F, GU, F, n, q8k, q80, c->st);
@@ -1170,7 +1198,7 @@ void forward(engine_ctx *c, int n, int out_rows) {
             rmsnorm_quant(xs, dim, m->output_norm, dim, out_rows, in.norm_eps, c->xb, dim, q8k, q80, c->st);
             matmul(c, lout, in.n_vocab, c->xb, dim, m->output, out_rows);
         }
-        if (m->world > 1) all_reduce(c, c->lsend, c->logits, (size_t)out_rows * in.n_vocab);
+        if (m->world > 1) exchange(c, c->lsend, c->logits, out_rows, in.n_vocab, m->v0, m->v1);
     }
     forget_activations(c);
 }
@@ -1293,7 +1321,13 @@ engine_model *engine_model_load(const char *path, char *err, size_t err_len) {
     shard_range(dim, m->world, m->rank, GROUP_ROWS, &m->d0, &m->d1);
     shard_range(in.n_expert, m->world, m->rank, 1, &m->e0, &m->e1);
     shard_range(in.n_vocab, m->world, m->rank, GROUP_ROWS, &m->v0, &m->v1);
-    attention_split(in, m->world, m->rank, &m->attn_tp, &m->h0, &m->h1, &m->k0, &m->k1);
+    // SARDYNE_ATTN_TP=off: attention replicated on every rank (one exchange less per attention
+    // block: lower batch-1 latency, but every rank holds all q/k/v/o rows and the whole KV cache)
+    static const bool tp_off = [] {
+        const char *v = getenv("SARDYNE_ATTN_TP");
+        return v && !strcmp(v, "off");
+    }();
+    attention_split(in, m->world, m->rank, &m->attn_tp, &m->h0, &m->h1, &m->k0, &m->k1, !tp_off);
     if (m->world > 1) {
         const Nccl *nc = nccl();
         ncclResult_t r = nc ? nc->comm_init_rank(&m->comm, m->world, g_shard.id, m->rank) : ncclSystemError;
@@ -1364,6 +1398,101 @@ engine_model *engine_model_load(const char *path, char *err, size_t err_len) {
         return nullptr;
     }
     return m;
+}
+
+// Unmaps the peers' exchange buffers and frees this rank's.
+void close_peer_exchange(engine_ctx *c) {
+    for (int q = 0; q < c->px.world; q++) {
+        if (!c->px.base[q]) continue;
+        if (q == c->px.rank) cudaFree(c->px.base[q]);
+        else cudaIpcCloseMemHandle(c->px.base[q]);
+        c->px.base[q] = nullptr;
+    }
+    c->px_on = false;
+}
+
+// Context creation on the ranks of a sharded model, in step on all of them (every rank calls
+// engine_ctx_new in the same order, failed or not): this rank's exchange buffer is allocated,
+// zeroed and its CUDA IPC handle gathered to every rank (an NCCL all-gather), the peers' buffers
+// are mapped, and one all-reduce tells every rank whether all contexts were created and whether
+// all ranks can use the peer exchange; otherwise the exchanges stay on NCCL.
+// SARDYNE_EXCHANGE=nccl (to be set on every rank alike) keeps them on NCCL.
+bool shard_context(engine_ctx *c, bool ok, char *err, size_t err_len) {
+    const engine_model *m = c->m;
+    const engine_model_info &in = m->info;
+    const int world = m->world;
+    static const bool want = [] {
+        const char *v = getenv("SARDYNE_EXCHANGE");
+        return !(v && !strcmp(v, "nccl"));
+    }();
+    int64_t cap = std::max<int64_t>({(int64_t)in.n_head * in.head_dim, (int64_t)in.dim, (int64_t)in.n_vocab});
+    cap = std::max<int64_t>(cap, in.n_expert ? (int64_t)in.n_expert_used * in.dim : (int64_t)in.ffn_dim);
+    cap = (int64_t)align_up((size_t)cap, 64);  // the second staging half starts 256-byte aligned
+    c->px.cap = cap;
+    // how long an exchange waits for the other ranks before it gives up (the ranks' host threads
+    // only meet at these exchanges, so one may lag behind another by its own host work)
+    static const unsigned long long wait_ns = [] {
+        const char *v = getenv("SARDYNE_EXCHANGE_WAIT_MS");
+        const long long ms = v ? atoll(v) : 0;
+        return (unsigned long long)(ms > 0 ? ms : 4000) * 1000000ull;
+    }();
+    c->px.wait_ns = wait_ns;
+    c->px.rank = m->rank;
+    c->px.world = world;
+    cudaStream_t s = c->st;
+    bool own_stream = false;
+    if (!s) own_stream = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess;
+    uint8_t *scratch = nullptr;  // [0, 64): this rank's handle, [64, 64 + 64 * world): all, then 2 floats
+    const size_t sbytes = 64 + 64 * (size_t)world + 64;
+    bool px_ok = ok && want && world <= PX_MAX_WORLD;
+    std::vector<uint8_t> handles(64 * (size_t)world + 64, 0);
+    void *own = nullptr;
+    if (px_ok) {
+        const size_t bytes = peer_exchange_bytes(cap);
+        cudaIpcMemHandle_t h{};
+        px_ok = cudaMalloc(&own, bytes) == cudaSuccess && cudaMemset(own, 0, bytes) == cudaSuccess &&
+                cudaDeviceSynchronize() == cudaSuccess && cudaIpcGetMemHandle(&h, own) == cudaSuccess;
+        if (px_ok) memcpy(handles.data(), &h, sizeof h);
+    }
+    bool net = s && cudaMalloc((void **)&scratch, sbytes) == cudaSuccess;
+    const Nccl *nc = nccl();
+    if (net && want) {  // the handles, all ranks' to every rank (zeros from a rank that has none)
+        net = cudaMemcpy(scratch, handles.data(), 64, cudaMemcpyHostToDevice) == cudaSuccess &&
+              nc->all_gather(scratch, scratch + 64, 64, ncclUint8, m->comm, s) == ncclSuccess &&
+              cudaMemcpyAsync(handles.data() + 64, scratch + 64, 64 * (size_t)world, cudaMemcpyDeviceToHost, s) ==
+                  cudaSuccess &&
+              cudaStreamSynchronize(s) == cudaSuccess;
+    }
+    px_ok = px_ok && net;
+    if (px_ok) {
+        c->px.base[m->rank] = own;
+        own = nullptr;
+        for (int q = 0; q < world && px_ok; q++) {
+            if (q == m->rank) continue;
+            cudaIpcMemHandle_t h;
+            memcpy(&h, handles.data() + 64 + 64 * (size_t)q, sizeof h);
+            void *peer = nullptr;
+            px_ok = cudaIpcOpenMemHandle(&peer, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+            c->px.base[q] = px_ok ? peer : nullptr;
+        }
+    }
+    float votes[2] = {ok ? 1.f : 0.f, px_ok ? 1.f : 0.f};
+    float *dv = (float *)(scratch + 64 + 64 * (size_t)world);
+    net = net && cudaMemcpy(dv, votes, sizeof votes, cudaMemcpyHostToDevice) == cudaSuccess &&
+          nc->all_reduce(dv, dv, 2, ncclFloat32, ncclSum, m->comm, s) == ncclSuccess &&
+          cudaMemcpyAsync(votes, dv, sizeof votes, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+          cudaStreamSynchronize(s) == cudaSuccess;
+    if (own) cudaFree(own);
+    if (scratch) cudaFree(scratch);
+    if (own_stream) cudaStreamDestroy(s);
+    cudaGetLastError();  // a refused peer mapping is not an error of the context
+    const bool all_ok = net && votes[0] == (float)world;
+    c->px_on = all_ok && votes[1] == (float)world;
+    if (!c->px_on) close_peer_exchange(c);
+    if (ok && !all_ok)
+        put_err(err, err_len, net ? "un altro rank non ha potuto creare il contesto"
+                                  : "scambio NCCL fallito durante la creazione del contesto");
+    return all_ok;
 }
 
 engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_batch, int32_t logits_all,
@@ -1457,43 +1586,45 @@ engine_ctx *engine_ctx_new(const engine_model *m, int32_t max_seq, int32_t n_bat
     items.push_back({&c->xq_buf[1], xq_cap});
     size_t total = 0;
     for (auto &it : items) total += align_up(it.bytes, 256);
-    if (!SDY_CUDA(cudaMalloc(&c->arena, total))) {
-        put_err(err, err_len, "memoria GPU esaurita (%.1f MB per contesto e KV cache)", total / 1e6);
-        delete c;
-        return nullptr;
-    }
-    uint8_t *p = (uint8_t *)c->arena;
-    for (auto &it : items) {
-        *it.dst = p;
-        p += align_up(it.bytes, 256);
-    }
-    bool zeroed = true;  // all-reduce sources start (and outside this rank's columns stay) zero
-    if (c->hsend) zeroed = SDY_CUDA(cudaMemset(c->hsend, 0, B * ffn * 4));
-    if (c->xsend) zeroed = zeroed && SDY_CUDA(cudaMemset(c->xsend, 0, B * in.dim * 4));
-    if (c->attsend) zeroed = zeroed && SDY_CUDA(cudaMemset(c->attsend, 0, B * q_dim * 4));
-    if (c->lsend) zeroed = zeroed && SDY_CUDA(cudaMemset(c->lsend, 0, logit_rows * in.n_vocab * 4));
-    if (c->md_sync) zeroed = zeroed && SDY_CUDA(cudaMemset(c->md_sync, 0, 4 * sizeof(unsigned)));
-    zeroed = zeroed && SDY_CUDA(cudaMemset(c->am_count, 0, 4));
-    if (!zeroed || (c->moe_count && !SDY_CUDA(cudaMemset(c->moe_count, 0, B * 4)))) {  // router counters start at zero
-        put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
-        engine_ctx_free(c);
-        return nullptr;
+    // Failures below do not return at once: the ranks of a sharded model still agree on the
+    // outcome together (shard_context), so that none of them waits for a rank that gave up.
+    bool ok = SDY_CUDA(cudaMalloc(&c->arena, total));
+    if (!ok) put_err(err, err_len, "memoria GPU esaurita (%.1f MB per contesto e KV cache)", total / 1e6);
+    if (ok) {
+        uint8_t *p = (uint8_t *)c->arena;
+        for (auto &it : items) {
+            *it.dst = p;
+            p += align_up(it.bytes, 256);
+        }
+        bool zeroed = true;  // all-reduce sources start (and outside this rank's columns stay) zero
+        if (c->hsend) zeroed = SDY_CUDA(cudaMemset(c->hsend, 0, B * ffn * 4));
+        if (c->xsend) zeroed = zeroed && SDY_CUDA(cudaMemset(c->xsend, 0, B * in.dim * 4));
+        if (c->attsend) zeroed = zeroed && SDY_CUDA(cudaMemset(c->attsend, 0, B * q_dim * 4));
+        if (c->lsend) zeroed = zeroed && SDY_CUDA(cudaMemset(c->lsend, 0, logit_rows * in.n_vocab * 4));
+        if (c->md_sync) zeroed = zeroed && SDY_CUDA(cudaMemset(c->md_sync, 0, 4 * sizeof(unsigned)));
+        zeroed = zeroed && SDY_CUDA(cudaMemset(c->am_count, 0, 4));
+        ok = zeroed && (!c->moe_count || SDY_CUDA(cudaMemset(c->moe_count, 0, B * 4)));  // router counters start at zero
+        if (!ok) put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
     }
     size_t lbytes = (c->logits_all ? B : 1) * in.n_vocab * 4;
-    if (!SDY_CUDA(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking)) ||
-        !SDY_CUDA(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking)) ||
-        !SDY_CUDA(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming)) ||
-        !SDY_CUDA(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming)) ||
-        !SDY_CUDA(cudaMallocHost(&c->h_logits, lbytes)) || !SDY_CUDA(cudaMallocHost(&c->h_tokpos, (B + 1) * 4)) ||
-        !SDY_CUDA(cudaMallocHost(&c->h_md_status, sizeof(unsigned))) ||
-        !SDY_CUDA(cudaMallocHost(&c->h_am_out, sizeof(int32_t)))) {
+    if (ok && (!SDY_CUDA(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking)) ||
+               !SDY_CUDA(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking)) ||
+               !SDY_CUDA(cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming)) ||
+               !SDY_CUDA(cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming)) ||
+               !SDY_CUDA(cudaMallocHost(&c->h_logits, lbytes)) || !SDY_CUDA(cudaMallocHost(&c->h_tokpos, (B + 1) * 4)) ||
+               !SDY_CUDA(cudaMallocHost(&c->h_md_status, sizeof(unsigned))) ||
+               !SDY_CUDA(cudaMallocHost(&c->h_px_status, sizeof(unsigned))) ||
+               !SDY_CUDA(cudaMallocHost(&c->h_am_out, sizeof(int32_t))))) {
         put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
-        engine_ctx_free(c);
-        return nullptr;
+        ok = false;
     }
-    rope_table(c->rope_cos, c->rope_sin, max_seq, in.head_dim, in.rope_theta, c->st);
-    if (!SDY_CUDA(cudaStreamSynchronize(c->st))) {
-        put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
+    if (ok) {
+        rope_table(c->rope_cos, c->rope_sin, max_seq, in.head_dim, in.rope_theta, c->st);
+        ok = SDY_CUDA(cudaStreamSynchronize(c->st));
+        if (!ok) put_err(err, err_len, "inizializzazione del contesto fallita: %s", last_error());
+    }
+    if (m->world > 1) ok = shard_context(c, ok, err, err_len) && ok;
+    if (!ok) {
         engine_ctx_free(c);
         return nullptr;
     }
@@ -1505,6 +1636,8 @@ int32_t engine_ctx_n_threads(const engine_ctx *c) { return c ? c->n_threads : 0;
 void engine_ctx_free(engine_ctx *c) {
     if (!c) return;
     drop_graphs(c);
+    close_peer_exchange(c);
+    if (c->h_px_status) cudaFreeHost(c->h_px_status);
     if (c->st) cudaStreamDestroy(c->st);
     if (c->side) cudaStreamDestroy(c->side);
     if (c->ev_fork) cudaEventDestroy(c->ev_fork);
@@ -1541,6 +1674,10 @@ int eval_tokens(engine_ctx *c, const int32_t *tokens, int32_t n, int32_t *next) 
             return -1;
         }
     }
+    if (c->px_failed) {
+        snprintf(c->err, sizeof c->err, "contesto inutilizzabile: uno scambio tra GPU era scaduto");
+        return -1;
+    }
     cudaSetDevice(c->m->dev);
     clear_error();
     const int saved = c->n_past;
@@ -1564,7 +1701,12 @@ int eval_tokens(engine_ctx *c, const int32_t *tokens, int32_t n, int32_t *next) 
         SDY_CUDA(cudaMemcpyAsync(c->h_logits, c->logits, (size_t)out_rows * nv * 4, cudaMemcpyDeviceToHost, c->st));
     }
     if (c->md_sync) SDY_CUDA(cudaMemcpyAsync(c->h_md_status, c->md_sync + 3, sizeof(unsigned), cudaMemcpyDeviceToHost, c->st));
+    if (c->px_on) SDY_CUDA(cudaMemcpyAsync(c->h_px_status, peer_status(c->px), sizeof(unsigned), cudaMemcpyDeviceToHost, c->st));
     SDY_CUDA(cudaStreamSynchronize(c->st));
+    if (c->px_on && *c->h_px_status) {  // a peer exchange gave up waiting for another rank
+        set_error("scambio tra GPU: attesa di un altro rank scaduta");
+        c->px_failed = true;
+    }
     if (c->md_sync && *c->h_md_status) {  // a grid barrier of the fused MoE block gave up
         set_error("blocco MoE: attesa tra i blocchi della griglia scaduta");
         cudaMemsetAsync(c->md_sync, 0, 4 * sizeof(unsigned), c->st);
@@ -1654,6 +1796,8 @@ int sdy_attention_split(int32_t n_head, int32_t n_kv_head, int32_t head_dim, int
     attention_split(in, world, rank, &tp, &range[0], &range[1], &range[2], &range[3]);
     return tp ? 1 : 0;
 }
+
+int sdy_engine_exchange(const engine_ctx *c) { return !c || c->m->world < 2 ? -1 : c->px_on ? 1 : 0; }
 
 void sdy_shard_range(int64_t n, int32_t world, int32_t rank, int64_t align, int64_t *begin, int64_t *end) {
     int64_t b = 0, e = n;

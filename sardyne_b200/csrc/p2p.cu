@@ -97,7 +97,148 @@ __global__ void __launch_bounds__(P2P_THREADS) allgather_kernel(Gather g) {
     }
 }
 
+// ---------------------------------------------------------------- the sharded engine's exchange
+// Buffer: staging halves [2][cap] floats, then at X = align256(2 * cap * 4) the flag words
+// flags[0..8) (flag q: the last round rank q delivered here), the CTA counter (X + 64), the round
+// counter (X + 68) and the status word (X + 72).
+constexpr int PX_THREADS = 512;
+constexpr int PX_MAX_CTAS = 74;
+
+size_t px_flags_offset(int64_t cap) { return align_up((size_t)cap * 8, 256); }
+
+struct PxArgs {
+    const float *send;
+    float *recv;
+    int64_t ld, lo, hi;
+    int rows;
+    const int32_t *top;
+    int e0, e1;
+    float *stage[PX_MAX_WORLD];
+    unsigned *flags[PX_MAX_WORLD];
+    unsigned *done, *round, *status;
+    int64_t cap;
+    unsigned long long wait_ns;
+    int rank, world;
+};
+
+__device__ __forceinline__ bool px_owned(const PxArgs &a, int64_t row) {
+    if (!a.top) return true;
+    const int e = a.top[row];
+    return e >= a.e0 && e < a.e1;
+}
+
+__global__ void __launch_bounds__(PX_THREADS) peer_gather_kernel(PxArgs a) {
+    pdl_wait();
+    pdl_release();  // the consumer's CTAs start and load their weights while the ranks meet here
+    __shared__ int last;
+    const unsigned r = *(volatile unsigned *)a.round + 1;
+    const int64_t half = (int64_t)(r & 1) * a.cap;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, nth = (int64_t)gridDim.x * blockDim.x;
+    const int64_t w = a.hi - a.lo, count = (int64_t)a.rows * a.ld;
+    const bool vec = ((a.ld | a.lo | w | a.cap) & 3) == 0 && ((uintptr_t)a.send & 15) == 0 &&
+                     ((uintptr_t)a.recv & 15) == 0;
+    // this rank's part into every rank's staging half
+    if (vec) {
+        const int64_t w4 = w / 4;
+        for (int64_t i = tid; i < a.rows * w4; i += nth) {
+            const int64_t row = i / w4, off = row * a.ld + a.lo + (i - row * w4) * 4;
+            if (!px_owned(a, row)) continue;
+            const float4 v = *(const float4 *)(a.send + off);
+            for (int q = 0; q < a.world; q++) *(float4 *)(a.stage[q] + half + off) = v;
+        }
+    } else {
+        for (int64_t i = tid; i < a.rows * w; i += nth) {
+            const int64_t row = i / w, off = row * a.ld + a.lo + (i - row * w);
+            if (!px_owned(a, row)) continue;
+            const float v = a.send[off];
+            for (int q = 0; q < a.world; q++) a.stage[q][half + off] = v;
+        }
+    }
+    // the CTA's stores, ordered before its arrival by one system-scope fence after the barrier
+    // (the barrier makes them observed by thread 0, whose fence is cumulative)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        last = atomicAdd(a.done, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        __threadfence_system();
+        *a.done = 0;
+        *a.round = r;
+        for (int q = 0; q < a.world; q++) st_release_sys(a.flags[q] + a.rank, r);
+    }
+    // every rank's part of this round has arrived once all flags show it
+    if (threadIdx.x < a.world) {
+        const unsigned *f = a.flags[a.rank] + threadIdx.x;
+        unsigned long long t0 = 0;
+        for (long long it = 0; (int)(ld_acquire_sys(f) - r) < 0; it++) {
+            if (it == 256) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+            if (it > 256) {
+                unsigned long long t;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                if (t - t0 > a.wait_ns) {
+                    atomicOr(a.status, 1u);
+                    break;
+                }
+                __nanosleep(128);
+            }
+        }
+    }
+    __syncthreads();
+    const float *src = a.stage[a.rank] + half;
+    if (vec) {
+        for (int64_t i = tid; i < count / 4; i += nth) ((float4 *)a.recv)[i] = __ldcg((const float4 *)src + i);
+    } else {
+        for (int64_t i = tid; i < count; i += nth) a.recv[i] = __ldcg(src + i);
+    }
+}
+
 }  // namespace
+
+size_t peer_exchange_bytes(int64_t cap) { return px_flags_offset(cap) + 256; }
+
+unsigned *peer_status(const PeerExchange &px) {
+    return (unsigned *)((uint8_t *)px.base[px.rank] + px_flags_offset(px.cap) + 72);
+}
+
+void peer_gather(const PeerExchange &px, const float *send, float *recv, int rows, int64_t ld, int64_t lo,
+                 int64_t hi, const int32_t *top, int e0, int e1, cudaStream_t s) {
+    if (rows < 1 || ld < 1 || lo < 0 || hi > ld || lo > hi || (int64_t)rows * ld > px.cap || px.world < 1 ||
+        px.world > PX_MAX_WORLD) {
+        set_error("peer_gather: bad arguments (rows %d, ld %lld, [%lld, %lld), cap %lld)", rows, (long long)ld,
+                  (long long)lo, (long long)hi, (long long)px.cap);
+        return;
+    }
+    PxArgs a{};
+    a.send = send;
+    a.recv = recv;
+    a.ld = ld;
+    a.lo = lo;
+    a.hi = hi;
+    a.rows = rows;
+    a.top = top;
+    a.e0 = e0;
+    a.e1 = e1;
+    const size_t X = px_flags_offset(px.cap);
+    for (int q = 0; q < px.world; q++) {
+        a.stage[q] = (float *)px.base[q];
+        a.flags[q] = (unsigned *)((uint8_t *)px.base[q] + X);
+    }
+    uint8_t *own = (uint8_t *)px.base[px.rank];
+    a.done = (unsigned *)(own + X + 64);
+    a.round = (unsigned *)(own + X + 68);
+    a.status = (unsigned *)(own + X + 72);
+    a.cap = px.cap;
+    a.wait_ns = px.wait_ns;
+    a.rank = px.rank;
+    a.world = px.world;
+    const int64_t work = std::max<int64_t>((int64_t)rows * (hi - lo) * px.world, (int64_t)rows * ld) / 4;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(PX_MAX_CTAS, (work + PX_THREADS - 1) / PX_THREADS));
+    launch(peer_gather_kernel, dim3(grid), dim3(PX_THREADS), 0, s, a);
+    SDY_LAUNCHED();
+}
+
 }  // namespace sdy
 
 using namespace sdy;

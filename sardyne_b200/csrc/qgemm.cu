@@ -21,6 +21,15 @@
 // are requested with cp.async before the current superblock's MMAs are issued, so their latency
 // overlaps the MMAs and the epilogue; expansion, MMA and epilogue of one superblock still follow
 // each other.
+//
+// The 32-element formats (Q8_0, Q4_0, Q5_0; reference csrc/quant.c:148-189) go through
+// qgemm32_kernel: per block the reference forms the integer sum s of its 32 products and adds
+// (float)s * (dw * dx) to the row's total in block order (quant.c:160). A block's weight values
+// with the bias removed (Q8_0 as stored, Q4_0 q - 8, Q5_0 q - 16) are int8, so one MMA of K = 32
+// gives s for the whole 128 x 128 tile; KB = 4 blocks per step go to their own accumulators
+// (4 x 128 TMEM columns) and the epilogue adds the 4 terms per (row, token) in block order. Q8_0
+// needs no expansion beyond the copy into the core-matrix layout (the slab's 16-byte chunks of
+// 8 rows are already 8-row core matrices).
 #include "common.cuh"
 
 namespace sdy {
@@ -378,14 +387,245 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
     }
 }
 
+// ------------------------------------------------------------------- 32-element block formats
+constexpr int KB = 4;                  // blocks per step (one TMEM accumulator each)
+constexpr int APLANE32 = GM * 32;      // A bytes of one block
+constexpr int BTILE32 = GN * 32 * KB;  // B bytes of one step
+
+__host__ __device__ constexpr int g32_raw_bytes(int type) { return (GM / GROUP_ROWS) * KB * slab_bytes(type); }
+__host__ __device__ constexpr int g32_smem_bytes(int type) {
+    return KB * APLANE32 + 2 * BTILE32 + 2 * KB * GN * 4 + KB * GM * 4 + g32_raw_bytes(type) + 16;
+}
+
+// One (row, block) of the A tile: the 32 values (bias removed) as two 16-byte K chunks of the
+// block's plane, and the row's block scale. slab: the (row group, block) slab; r8: row in group.
+template <int TYPE>
+__device__ __forceinline__ void expand_block32(const uint8_t *slab, int r8, int row, uint8_t *plane, float *dw) {
+    uint4 lo, hi;
+    if constexpr (TYPE == T_Q8_0) {
+        lo = *(const uint4 *)(slab + r8 * 16);
+        hi = *(const uint4 *)(slab + 128 + r8 * 16);
+        *dw = __half2float(__ushort_as_half(*(const unsigned short *)(slab + 256 + r8 * 2)));
+    } else {
+        // element e < 16: low nibble of byte e; e >= 16: high nibble of byte e - 16 (Q5_0: bit e
+        // of qh above it)
+        const uint4 q = *(const uint4 *)(slab + r8 * 16);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        uint32_t qh = 0;
+        if constexpr (TYPE == T_Q5_0) qh = *(const uint32_t *)(slab + 128 + r8 * 4);
+        constexpr uint32_t bias = TYPE == T_Q4_0 ? 0x08080808u : 0x10101010u;
+        uint32_t l[4], h[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            l[k] = w[k] & 0x0F0F0F0Fu;
+            h[k] = (w[k] >> 4) & 0x0F0F0F0Fu;
+            if constexpr (TYPE == T_Q5_0) {
+                l[k] |= ((((qh >> (4 * k)) & 15u) * 0x00204081u) & 0x01010101u) << 4;
+                h[k] |= ((((qh >> (16 + 4 * k)) & 15u) * 0x00204081u) & 0x01010101u) << 4;
+            }
+            l[k] = __vsub4(l[k], bias);  // bytewise, no borrow between bytes
+            h[k] = __vsub4(h[k], bias);
+        }
+        lo = make_uint4(l[0], l[1], l[2], l[3]);
+        hi = make_uint4(h[0], h[1], h[2], h[3]);
+        *dw = __half2float(__ushort_as_half(*(const unsigned short *)(slab + (TYPE == T_Q4_0 ? 128 : 160) + r8 * 2)));
+    }
+    *(uint4 *)(plane + plane_off(GM, row, 0)) = lo;
+    *(uint4 *)(plane + plane_off(GM, row, 16)) = hi;
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(G_THREADS, 1) qgemm32_kernel(GemmArgs a) {
+    constexpr int SB = slab_bytes(TYPE);
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t *sa = smem, *sb = smem + KB * APLANE32;  // sa: KB block planes, sb: two B tiles
+    float *yd = (float *)(sb + 2 * BTILE32);         // [2][KB][GN] token block scales
+    float *dwr = yd + 2 * KB * GN;                   // [KB][GM] row block scales
+    uint8_t *raw = (uint8_t *)(dwr + KB * GM);       // [groups][KB] slabs of the next step
+    uint64_t *mbar = (uint64_t *)(raw + g32_raw_bytes(TYPE));
+    uint32_t *tmem_slot = (uint32_t *)(mbar + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t gt0 = a.g_begin + (int64_t)blockIdx.x * (GM / GROUP_ROWS);
+    int tok0 = blockIdx.y * GN;
+    int nv = min(GN, a.n_tok - tok0);
+    const uint8_t *slabs = a.slabs;
+    const int32_t *gslot = nullptr;
+    pdl_wait();
+    if (a.grp_off) {
+        if ((int)blockIdx.y >= a.grp_off[a.n_expert + 1]) return;
+        const int item = a.grp_tiles[blockIdx.y], e = item >> 16;
+        tok0 = (item & 0xFFFF) * GN;
+        const int g0 = a.grp_off[e];
+        nv = min(GN, a.grp_off[e + 1] - g0 - tok0);
+        gslot = a.grp_slot + g0 + tok0;
+        slabs += (size_t)e * a.gpe * a.nb * SB;
+    }
+    auto xrow = [&](int t) -> int64_t { return gslot ? gslot[t] / a.xdiv : tok0 + t; };
+    auto orow_of = [&](int t) -> int64_t { return gslot ? gslot[t] : tok0 + t; };
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+    }
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_u32(mbar)));
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    for (int i = tid; i < 2 * BTILE32 / 16; i += G_THREADS)  // padded tokens: zero activations
+        if (i % GN >= nv) ((uint4 *)sb)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < 2 * KB * GN; i += G_THREADS)
+        if (i % GN >= nv) yd[i] = 0.0f;
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t mbar_a = smem_u32(mbar);
+    const int row = tid & (GM - 1), part = tid >> 7;  // expansion: blocks 2*part, 2*part+1 of a row
+    const int64_t grow = gt0 * GROUP_ROWS + row;
+    const bool row_ok = grow < a.g_end * GROUP_ROWS;
+    const int erow = (warp & 3) * 32 + lane, ehalf = warp >> 2;  // epilogue: TMEM lane = row, 64 tokens
+    float acc[64];
+#pragma unroll
+    for (int i = 0; i < 64; i++) acc[i] = 0.0f;
+    bool ok = true;
+
+    const int ng_tile = (int)(a.g_end - gt0 < GM / GROUP_ROWS ? a.g_end - gt0 : GM / GROUP_ROWS);
+    const int steps = (a.nb + KB - 1) / KB;
+    // Step s: blocks KB*s .. KB*s + nblk - 1 (elements 128s.., inside one 256-element XQ span).
+    auto issue = [&](int st) {
+        const int b0 = st * KB, nblk = min(KB, a.nb - b0), chunks = 2 * nblk;
+        uint8_t *sbb = sb + (st & 1) * BTILE32;
+        float *ydb = yd + (st & 1) * KB * GN;
+        for (int i = tid; i < nv * chunks; i += G_THREADS) {
+            const int t = i / chunks, c = i - t * chunks;
+            cp_async16(sbb + c * (GN * 16) + t * 16, a.xqs + (size_t)xrow(t) * a.qrow + xq_pos(32 * b0) + c * 16);
+        }
+        for (int i = tid; i < nv * nblk; i += G_THREADS) {
+            const int t = i / nblk, j = i - t * nblk;
+            cp_async4(ydb + j * GN + t, a.xd + (size_t)xrow(t) * a.nbx + b0 + j);
+        }
+        constexpr int C16 = SB / 16;
+        for (int i = tid; i < ng_tile * nblk * C16; i += G_THREADS) {
+            const int gj = i / C16, c = i - gj * C16, g = gj / nblk, j = gj - g * nblk;
+            cp_async16(raw + (g * KB + j) * SB + c * 16, slabs + ((size_t)(gt0 + g) * a.nb + b0 + j) * SB + c * 16);
+        }
+        cp_async_commit();
+    };
+    issue(0);
+    for (int st = 0; st < steps && ok; st++) {
+        const int nblk = min(KB, a.nb - st * KB);
+        cp_async_wait_all();
+        __syncthreads();
+#pragma unroll
+        for (int jj = 0; jj < 2; jj++) {
+            const int j = 2 * part + jj;
+            if (j < nblk) {
+                if (row_ok) {
+                    expand_block32<TYPE>(raw + ((grow / GROUP_ROWS - gt0) * KB + j) * SB, (int)(grow % GROUP_ROWS), row,
+                                         sa + j * APLANE32, dwr + j * GM + row);
+                } else {
+                    *(uint4 *)(sa + j * APLANE32 + plane_off(GM, row, 0)) = make_uint4(0, 0, 0, 0);
+                    *(uint4 *)(sa + j * APLANE32 + plane_off(GM, row, 16)) = make_uint4(0, 0, 0, 0);
+                    dwr[j * GM + row] = 0.0f;
+                }
+            }
+        }
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        __syncthreads();
+        if (st + 1 < steps) issue(st + 1);  // raw is free; B buffer (st+1)&1 was read by MMA st-1
+        const uint8_t *sbb = sb + (st & 1) * BTILE32;
+        const float *ydb = yd + (st & 1) * KB * GN;
+        if (tid == 0) {
+            fence_after_sync();
+            for (int j = 0; j < nblk; j++)
+                mma_i8(tmem + j * GN, kmajor_desc(smem_u32(sa + j * APLANE32), GM * 16, 128),
+                       kmajor_desc(smem_u32(sbb + 2 * j * GN * 16), GN * 16, 128), 0);
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar_a)
+                         : "memory");
+        }
+        if (!mbar_wait(mbar_a, st & 1)) {
+            atomicOr(&g_qgemm_status, 1u);
+            ok = false;
+        }
+        fence_after_sync();
+        if (ok) {
+            const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
+            for (int j = 0; j < nblk; j++) {  // block order
+                const float dw = dwr[j * GM + erow];
+#pragma unroll
+                for (int cc = 0; cc < 2; cc++) {
+                    const uint32_t col = ehalf * 64 + cc * 32;
+                    int32_t v[32];
+                    tmem_ld32(tmem + lanes + j * GN + col, v);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+                    for (int i = 0; i < 32; i++)  // (float)s * (dw * dx), quant.c:160
+                        acc[cc * 32 + i] = __fadd_rn(acc[cc * 32 + i],
+                                                     __fmul_rn(__int2float_rn(v[i]), __fmul_rn(dw, ydb[j * GN + col + i])));
+                }
+            }
+        }
+        fence_before_sync();
+        __syncthreads();
+    }
+
+    cp_async_wait_all();
+    const int64_t orow = gt0 * GROUP_ROWS + erow;
+    if (ok && orow >= a.row0 && orow < a.row1) {
+#pragma unroll
+        for (int i = 0; i < 64; i++) {
+            const int t = ehalf * 64 + i;
+            if (t < nv) {
+                const size_t o = (size_t)orow_of(t) * a.ldo + (orow - a.out_row0);
+                a.out[o] = a.residual ? __fadd_rn(a.residual[o], acc[i]) : acc[i];
+            }
+        }
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        fence_after_sync();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TMEM_COLS));
+    }
+}
+
+bool is_block32(int type) { return type == T_Q8_0 || type == T_Q4_0 || type == T_Q5_0; }
+
+// The kernel of the weight type, with its shared memory.
+void launch_gemm(int type, dim3 grid, const GemmArgs &a, cudaStream_t s) {
+    switch (type) {
+#define SDY_GEMM_CASE(T, KERNEL, SMEM)                          \
+    case T: {                                                   \
+        static std::atomic<uint64_t> configured{0};            \
+        smem_limit_once(KERNEL<T>, SMEM, configured);           \
+        launch(KERNEL<T>, grid, G_THREADS, SMEM, s, a);         \
+        break;                                                  \
+    }
+        SDY_GEMM_CASE(T_Q4_K, qgemm_kernel, g_smem_bytes(3, T_Q4_K))
+        SDY_GEMM_CASE(T_Q6_K, qgemm_kernel, g_smem_bytes(2, T_Q6_K))
+        SDY_GEMM_CASE(T_Q8_0, qgemm32_kernel, g32_smem_bytes(T_Q8_0))
+        SDY_GEMM_CASE(T_Q4_0, qgemm32_kernel, g32_smem_bytes(T_Q4_0))
+        SDY_GEMM_CASE(T_Q5_0, qgemm32_kernel, g32_smem_bytes(T_Q5_0))
+#undef SDY_GEMM_CASE
+    default: set_error("qgemm: weight type %d has no tensor-core kernel", type); return;
+    }
+    SDY_LAUNCHED();
+}
+
 }  // namespace
 
-bool qgemm_supported(int type, int n_in) { return (type == T_Q4_K || type == T_Q6_K) && n_in % 256 == 0; }
+bool qgemm_supported(int type, int n_in) {
+    return ((type == T_Q4_K || type == T_Q6_K) && n_in % 256 == 0) || (is_block32(type) && n_in % 32 == 0);
+}
+
+// The activation layout the weight type multiplies with (Q8_K for the K-quants, Q8_0 otherwise).
+static int gemm_vtype(int type) { return is_block32(type) ? T_Q8_0 : T_Q8_K; }
 
 void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
            cudaStream_t s, const float *residual) {
     if (row1 <= row0 || xq.n_tok <= 0) return;
-    if (!qgemm_supported(w.type, w.n_in) || xq.vtype != T_Q8_K || xq.n_in != w.n_in) {
+    if (!qgemm_supported(w.type, w.n_in) || xq.vtype != gemm_vtype(w.type) || xq.n_in != w.n_in) {
         set_error("qgemm: unsupported weight type %d / activation layout", w.type);
         return;
     }
@@ -407,25 +647,15 @@ void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, i
     a.residual = residual;
     const int64_t tiles_m = (a.g_end - a.g_begin + GM / GROUP_ROWS - 1) / (GM / GROUP_ROWS);
     const dim3 grid((unsigned)tiles_m, (unsigned)((xq.n_tok + GN - 1) / GN));
-    if (w.type == T_Q4_K) {
-        static std::atomic<uint64_t> configured{0};
-        const int smem = g_smem_bytes(3, T_Q4_K);
-        smem_limit_once(qgemm_kernel<T_Q4_K>, smem, configured);
-        launch(qgemm_kernel<T_Q4_K>, grid, G_THREADS, smem, s, a);
-    } else {
-        static std::atomic<uint64_t> configured{0};
-        const int smem = g_smem_bytes(2, T_Q6_K);
-        smem_limit_once(qgemm_kernel<T_Q6_K>, smem, configured);
-        launch(qgemm_kernel<T_Q6_K>, grid, G_THREADS, smem, s, a);
-    }
-    SDY_LAUNCHED();
+    launch_gemm(w.type, grid, a, s);
 }
 
 void qgemm_grouped(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq, int xdiv, const int32_t *grp_off,
                    const int32_t *grp_slot, const int32_t *grp_tiles, int max_slots, int64_t rows_per_expert,
                    float *out, int64_t ldo_slot, cudaStream_t s) {
     if (max_slots <= 0 || n_expert <= 0) return;
-    if (!qgemm_supported(experts.type, experts.n_in) || xq.vtype != T_Q8_K || xq.n_in != experts.n_in) {
+    if (!qgemm_supported(experts.type, experts.n_in) || xq.vtype != gemm_vtype(experts.type) ||
+        xq.n_in != experts.n_in) {
         set_error("qgemm_grouped: unsupported weight type %d / activation layout", experts.type);
         return;
     }
@@ -453,18 +683,7 @@ void qgemm_grouped(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq,
     const int64_t tiles_m = (a.g_end + GM / GROUP_ROWS - 1) / (GM / GROUP_ROWS);
     // at most ceil(count_e / GN) tiles per expert: sum <= max_slots / GN + n_expert
     const dim3 grid((unsigned)tiles_m, (unsigned)(max_slots / GN + n_expert));
-    if (experts.type == T_Q4_K) {
-        static std::atomic<uint64_t> configured{0};
-        const int smem = g_smem_bytes(3, T_Q4_K);
-        smem_limit_once(qgemm_kernel<T_Q4_K>, smem, configured);
-        launch(qgemm_kernel<T_Q4_K>, grid, G_THREADS, smem, s, a);
-    } else {
-        static std::atomic<uint64_t> configured{0};
-        const int smem = g_smem_bytes(2, T_Q6_K);
-        smem_limit_once(qgemm_kernel<T_Q6_K>, smem, configured);
-        launch(qgemm_kernel<T_Q6_K>, grid, G_THREADS, smem, s, a);
-    }
-    SDY_LAUNCHED();
+    launch_gemm(experts.type, grid, a, s);
 }
 
 unsigned qgemm_status() {

@@ -353,7 +353,7 @@ void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0,
              cudaStream_t s, const float *residual, const ActIn *act) {
     if (row1 <= row0 || xq.n_tok <= 0) return;
     const int gmin = gemm_min_tokens();
-    if (!act && gmin > 0 && xq.n_tok >= gmin && qgemm_supported(w.type, w.n_in) && xq.vtype == T_Q8_K &&
+    if (!act && gmin > 0 && xq.n_tok >= gmin && qgemm_supported(w.type, w.n_in) && xq.vtype == vec_dot_type(w.type) &&
         xq.n_in == w.n_in) {
         qgemm(w, xq, out, ldo, row0, row1, out_row0, s, residual);
         return;
