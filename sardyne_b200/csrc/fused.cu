@@ -319,6 +319,86 @@ XQ pick(const XQ *q) {
     return a;
 }
 
+// Router logits of many tokens (prefill): the same four-accumulator dots as router_topk_kernel,
+// with the CTA's RM_EPC router rows held in shared memory while its warps stream the tokens past
+// them. Lane l of a warp runs chain a = l % 4 of expert l / 4 for the warp's current token, so a
+// warp computes 8 logits at once. Every row and the token's x are stored de-interleaved (element
+// 4g + a at plane a, index g) with a plane stride of P = G + pad floats, P = 4 (mod 32), so the
+// 16-byte loads of the 32 lanes (32 planes of the rows; 4 planes of x, broadcast) fall into
+// distinct banks. Needs dim % 16 == 0 and 16-byte aligned x rows and weights.
+constexpr int RM_EPC = 8;
+constexpr int RM_WARPS = 8;
+constexpr int RM_TPC = 32;  // tokens per CTA
+
+__host__ __device__ inline int rm_plane(int dim) {
+    const int G = dim / 4;
+    return G + ((4 - G % 32) + 32) % 32;
+}
+
+__global__ void __launch_bounds__(RM_WARPS * 32) router_many_kernel(const float *x, int64_t ldx, const void *w,
+                                                                    int wtype, int dim, int ne, int n_tok,
+                                                                    float *logits) {
+    extern __shared__ __align__(16) float sm[];
+    const int G = dim / 4, P = rm_plane(dim);
+    float *rows = sm;                           // [RM_EPC * 4][P]
+    float *xs = sm + (size_t)RM_EPC * 4 * P;    // [RM_WARPS][4][P]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int e_base = blockIdx.x * RM_EPC;
+    for (int i = tid; i < RM_EPC * G; i += blockDim.x) {
+        const int el = i / G, g = i - el * G, e = e_base + el;
+        const float4 v = e < ne ? load4_w(w, wtype, (size_t)e * dim + 4 * (size_t)g) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float *r = rows + (size_t)(4 * el) * P + g;
+        r[0] = v.x;
+        r[P] = v.y;
+        r[2 * P] = v.z;
+        r[3 * P] = v.w;
+    }
+    pdl_wait();
+    __syncthreads();
+    const int a = lane & 3, el = lane >> 2, e = e_base + el;
+    const float *wr = rows + (size_t)lane * P;  // plane 4 * el + a
+    float *xw = xs + (size_t)warp * 4 * P;
+    const int t_end = min(n_tok, (int)(blockIdx.y + 1) * RM_TPC);
+    for (int t = blockIdx.y * RM_TPC + warp; t < t_end; t += RM_WARPS) {
+        const float *xv = x + (size_t)t * ldx;
+        for (int g = lane; g < G; g += 32) {
+            const float4 v = *(const float4 *)(xv + 4 * g);
+            xw[g] = v.x;
+            xw[P + g] = v.y;
+            xw[2 * P + g] = v.z;
+            xw[3 * P + g] = v.w;
+        }
+        __syncwarp();
+        const float *xa = xw + (size_t)a * P;
+        float s = 0.0f;
+#pragma unroll 4
+        for (int g = 0; g < G; g += 4) {  // chain a over i = 4g + a, in order (ops.c:155-167)
+            const float4 xv4 = *(const float4 *)(xa + g), wv4 = *(const float4 *)(wr + g);
+            s = __fadd_rn(s, __fmul_rn(xv4.x, wv4.x));
+            s = __fadd_rn(s, __fmul_rn(xv4.y, wv4.y));
+            s = __fadd_rn(s, __fmul_rn(xv4.z, wv4.z));
+            s = __fadd_rn(s, __fmul_rn(xv4.w, wv4.w));
+        }
+        const float s1 = __shfl_down_sync(0xffffffffu, s, 1), s2 = __shfl_down_sync(0xffffffffu, s, 2),
+                    s3 = __shfl_down_sync(0xffffffffu, s, 3);
+        if (a == 0 && e < ne) logits[(size_t)t * ne + e] = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
+        __syncwarp();  // x of the next token overwrites this one
+    }
+}
+
+// Softmax and top-k of each token's logits (one CTA per token), as the router kernel's last CTA
+// runs them.
+__global__ void router_select_kernel(const float *logits, int ne, int k, int32_t *top, float *wout) {
+    extern __shared__ __align__(16) float prob[];
+    __shared__ double dpart[32];
+    __shared__ float fpart[32];
+    __shared__ float pv[64];
+    pdl_wait();
+    const int t = blockIdx.x;
+    softmax_topk_block(logits + (size_t)t * ne, prob, pv, ne, k, top + (size_t)t * k, wout + (size_t)t * k, dpart,
+                       fpart);
+}
+
 }  // namespace
 
 void rmsnorm_quant(const float *x, int64_t ldx, const float *w, int n, int rows, float eps, float *xb, int64_t ldb,
@@ -347,11 +427,14 @@ void post_qkv(const PostQKV &p, int n_tok, cudaStream_t s) {
 }
 
 namespace {
+constexpr int ROUTER_MANY_MIN_TOKENS = 8;
 size_t router_smem(int dim, int ne) {
     const size_t dp = (size_t)((dim + 3) & ~3);
     return std::max((size_t)(1 + ROUTER_EPC) * dp, (size_t)2 * ne) * 4;
 }
 }  // namespace
+
+size_t router_many_smem(int dim) { return (size_t)(RM_EPC + RM_WARPS) * 4 * rm_plane(dim) * 4; }
 
 bool router_topk_supported(int dim, int ne, int k, int n_tok, bool norm) {
     return router_smem(dim, ne) <= 200 * 1024 && n_tok <= 65535 && k <= ne && k <= 64 && (!norm || dim <= 8192);
@@ -366,10 +449,21 @@ void router_topk(const float *x, int64_t ldx, const void *w, int wtype, int dim,
         set_error("router_topk: hidden size %d / %d tokens / top-%d of %d not supported", dim, n_tok, k, ne);
         return;
     }
-    static std::atomic<uint64_t> configured{0};
-    smem_limit_once(router_topk_kernel, 200 * 1024, configured);
     const bool w_aligned = wtype == T_F32 ? ((uintptr_t)w & 15) == 0 : ((uintptr_t)w & 7) == 0;
     const int vec = dim % 16 == 0 && ldx % 4 == 0 && ((uintptr_t)x & 15) == 0 && w_aligned;
+    if (n_tok >= ROUTER_MANY_MIN_TOKENS && vec && !norm_w && router_many_smem(dim) <= 200 * 1024 && k <= 64) {
+        // many tokens: logits with the router rows resident per CTA, then one CTA per token selects
+        static std::atomic<uint64_t> configured_many{0};
+        smem_limit_once(router_many_kernel, 200 * 1024, configured_many);
+        launch(router_many_kernel, dim3((ne + RM_EPC - 1) / RM_EPC, (n_tok + RM_TPC - 1) / RM_TPC), RM_WARPS * 32,
+               router_many_smem(dim), s, x, ldx, w, wtype, dim, ne, n_tok, logits);
+        SDY_LAUNCHED();
+        launch(router_select_kernel, dim3(n_tok), 256, (size_t)ne * 4, s, logits, ne, k, top, wout);
+        SDY_LAUNCHED();
+        return;
+    }
+    static std::atomic<uint64_t> configured{0};
+    smem_limit_once(router_topk_kernel, 200 * 1024, configured);
     launch(router_topk_kernel, dim3((ne + ROUTER_EPC - 1) / ROUTER_EPC, n_tok), ROUTER_THREADS, smem, s, x, ldx, w,
            wtype, dim, ne, k, logits, counters, top, wout, vec, norm_w, norm_eps);
     SDY_LAUNCHED();

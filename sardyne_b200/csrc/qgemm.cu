@@ -74,15 +74,20 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr, uint32_t lbo, ui
            ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
 }
 
-// kind::i8 instruction descriptor: s32 accumulator, s8 A and B, both K-major, M = GM, N = GN.
-constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(GN >> 3) << 17) | ((uint32_t)(GM >> 4) << 24);
+// kind::i8 instruction descriptor: s32 accumulator, s8 A and B, both K-major, M = GM, N = the
+// tile's valid tokens rounded up to a multiple of 16 (16 .. GN; the B rows past the valid tokens
+// are zero), so a tile of few tokens (an expert's slots in MoE prefill) costs MMAs of its width.
+__device__ __forceinline__ uint32_t idesc_i8(int nv) {
+    const uint32_t n = (uint32_t)min(GN, max(16, (nv + 15) & ~15));
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((uint32_t)(GM >> 4) << 24);
+}
 
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
@@ -319,13 +324,14 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
         const float *ydb = yd + (b & 1) * GN;
         if (tid == 0) {
             fence_after_sync();
+            const uint32_t idesc = idesc_i8(nv);
 #pragma unroll
             for (int s = 0; s < 8; s++) {  // K step s: bytes 32s..32s+31 = chunk planes 2s, 2s+1
                 const uint64_t bd = kmajor_desc(smem_u32(sbb + 2 * s * GN * 16), GN * 16, 128);
 #pragma unroll
                 for (int p = 0; p < NP; p++)
                     mma_i8(tmem + p * GN, kmajor_desc(smem_u32(sa + p * PLANE + 2 * s * GM * 16), GM * 16, 128), bd,
-                           s > 0);
+                           idesc, s > 0);
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar_a)
                          : "memory");
@@ -340,6 +346,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
 #pragma unroll
             for (int cc = 0; cc < 2; cc++) {
                 const uint32_t col = ehalf * 64 + cc * 32;
+                if ((int)col >= nv) continue;  // no valid token in these columns (warp-uniform)
                 const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
                 int32_t h[32], l[32], m[32];
                 tmem_ld32(tmem + lanes + col, h);
@@ -538,9 +545,10 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm32_kernel(GemmArgs a) {
         const float *ydb = yd + (st & 1) * KB * GN;
         if (tid == 0) {
             fence_after_sync();
+            const uint32_t idesc = idesc_i8(nv);
             for (int j = 0; j < nblk; j++)
                 mma_i8(tmem + j * GN, kmajor_desc(smem_u32(sa + j * APLANE32), GM * 16, 128),
-                       kmajor_desc(smem_u32(sbb + 2 * j * GN * 16), GN * 16, 128), 0);
+                       kmajor_desc(smem_u32(sbb + 2 * j * GN * 16), GN * 16, 128), idesc, 0);
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar_a)
                          : "memory");
         }
@@ -556,6 +564,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm32_kernel(GemmArgs a) {
 #pragma unroll
                 for (int cc = 0; cc < 2; cc++) {
                     const uint32_t col = ehalf * 64 + cc * 32;
+                    if ((int)col >= nv) continue;  // no valid token in these columns (warp-uniform)
                     int32_t v[32];
                     tmem_ld32(tmem + lanes + j * GN + col, v);
                     asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
