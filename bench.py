@@ -816,8 +816,8 @@ def decode_reference(name, path, prompt):
 def measure_decode(name, args, rank, world, cpu_baseline=True):
     """Decode of a BASELINE config 3-5 model through engine_eval (host token ids in, host logits
     out): the prompt's prefill, then greedy single-token steps. Under torchrun every rank runs the
-    same token stream with its shard of the model (FFN rows / experts / vocabulary; attention
-    replicated) and the engine's NCCL collectives: strong scaling of one stream; times are the max
+    same token stream with its shard of the model (attention heads where they divide, FFN rows,
+    experts, vocabulary) and the engine's exchanges: strong scaling of one stream; times are the max
     over ranks. Returns the decode object (rank 0) or None."""
     import torch
     import torch.distributed as dist
@@ -875,6 +875,15 @@ def measure_decode(name, args, rank, world, cpu_baseline=True):
         t5 = time.perf_counter()
         if dev_tokens != tokens:
             raise RuntimeError("device greedy choice differs from numpy.argmax of the logits")
+        # two more prefills of the same prompt: prefill_tok_s is the median of four
+        prefills = [t1 - t0, t4 - t3]
+        for _ in range(2):
+            lib.engine_reset(ctx)
+            if world > 1:
+                dist.barrier()
+            ta = time.perf_counter()
+            engine_next(lib, ctx, prompt, info.n_vocab)
+            prefills.append(time.perf_counter() - ta)
     finally:
         lib.engine_ctx_free(ctx)  # graphs and NCCL communicator released before the process group
         lib.engine_model_free(model)
@@ -882,10 +891,11 @@ def measure_decode(name, args, rank, world, cpu_baseline=True):
             runtime.set_shard(0, 1)
     if world > 1:  # the slowest rank's times; every rank must agree on the tokens
         dev = torch.device("cuda", torch.cuda.current_device())
-        tt = torch.tensor([t1 - t0, t2 - t1, t5 - t4], dtype=torch.float64, device=dev)
+        tt = torch.tensor([t1 - t0, t2 - t1, t5 - t4] + prefills, dtype=torch.float64, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t0, t1, t2 = 0.0, float(tt[0]), float(tt[0] + tt[1])
         t4, t5 = 0.0, float(tt[2])
+        prefills = [float(v) for v in tt[3:]]
         toks = [None] * world
         dist.all_gather_object(toks, tokens)
         if any(tk != tokens for tk in toks):
@@ -897,13 +907,18 @@ def measure_decode(name, args, rank, world, cpu_baseline=True):
     tps = n_decode / (t2 - t1)
     out = {"metric": f"decode tok/s {name} shape (greedy, e2e through engine_eval)", "value": round(tps, 2),
            "unit": "tok/s", "n_gpus": world, "steps": n_decode, "ms_per_step": round((t2 - t1) / n_decode * 1e3, 4),
-           "prefill_tok_s": round(n_prompt / (t1 - t0), 1),
+           "prefill_tok_s": round(n_prompt / statistics.median(prefills), 1),
+           "prefill_ms_samples": [round(v * 1e3, 2) for v in prefills],
            "scaling": "strong" if world > 1 else "weak",
            "workload": f"BASELINE {name} shape{f' cut to {layers} layers' if layers else ''}: {n_prompt}-token "
                        f"prompt (uniform ids, seed 0), {n_decode} greedy decode steps, context {ctx_len}; "
                        f"random-init Q4_K_M mix",
            "model_gb": round(path.stat().st_size / 1e9, 2), "weight_bytes_per_token": wbytes,
-           "parallelism": f"ffn/expert/vocab shards x{world}, attention replicated" if world > 1 else "1 GPU",
+           "parallelism": (f"x{world}: " + ("attention replicated" if os.environ.get("SARDYNE_ATTN_TP") == "off"
+                                            else "attention heads split where they divide")
+                           + ", ffn rows / experts / vocabulary split; single-token exchanges over NVLink peer "
+                             "memory" + (" (NCCL)" if os.environ.get("SARDYNE_EXCHANGE") == "nccl" else ""))
+           if world > 1 else "1 GPU",
            "roofline": {"bound": "hbm", "achieved": round(wbytes * tps / 1e9, 1), "peak": round(peak * world, 1),
                         "unit": "GB/s", "frac": round(wbytes * tps / 1e9 / (peak * world), 4), "traffic": None,
                         "kernel": "whole decode step (weight bytes per token x tok/s, against N x peak)",

@@ -225,10 +225,13 @@ struct ActIn {
 
 // Token count from which products go to the tensor-core GEMM (0 = never).
 int gemm_min_tokens();
-// Many-token product on the tensor cores (qgemm.cu), same contract as qmatvec; Q4_K/Q6_K only.
+// Many-token product on the tensor cores (qgemm.cu), same contract as qmatvec. With split_ok, a
+// product whose tiles leave SMs idle is split along K: the CTAs store their blocks' terms in a
+// scratch buffer taken from a stream-ordered pool (outside stream capture), and a second kernel
+// adds every output's terms in block order.
 bool qgemm_supported(int type, int n_in);
 void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
-           cudaStream_t s, const float *residual = nullptr);
+           cudaStream_t s, const float *residual = nullptr, bool split_ok = true);
 unsigned qgemm_status();  // nonzero when a qgemm completion wait timed out
 // Grouped experts on the tensor cores (MoE prefill): for local expert e, the slots
 // grp_slot[grp_off[e] .. grp_off[e+1]) (device arrays from moe_group with tile GEMM_TILE_TOKENS;
@@ -239,9 +242,9 @@ void qgemm_grouped(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq,
                    const int32_t *grp_slot, const int32_t *grp_tiles, int max_slots, int64_t rows_per_expert,
                    float *out, int64_t ldo_slot, cudaStream_t s);
 // act: the input rows are prepared and quantized inside the kernel (xq then only gives the
-// activation geometry).
+// activation geometry). split_ok: the tensor-core route may take scratch memory (qgemm).
 void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
-             cudaStream_t s, const float *residual = nullptr, const ActIn *act = nullptr);
+             cudaStream_t s, const float *residual = nullptr, const ActIn *act = nullptr, bool split_ok = true);
 // Two matrices with one single-token input in one launch: outa[r] = A[r] . x, outb[r] = B[r] . x
 // over all rows (the parts of a projection whose weight types differ).
 bool qmatvec2_supported(int ta, int tb);

@@ -81,6 +81,6 @@ extern "C" int sdy_qmatvec_f32_noalloc(const void *w, const float *d_x, int n_to
     if (!scratch) return -1;
     XQ q = xq_carve(scratch, vt, m->n_in, n_tok);
     quantize_rows(vt, d_x, m->n_in, n_tok, m->n_in, q, (cudaStream_t)stream);
-    qmatvec(*m, q, d_out, ldo, row0, row1, row0, (cudaStream_t)stream);
+    qmatvec(*m, q, d_out, ldo, row0, row1, row0, (cudaStream_t)stream, nullptr, nullptr, /*split_ok=*/false);
     return last_error()[0] ? -1 : 0;
 }

@@ -22,6 +22,11 @@
 // overlaps the MMAs and the epilogue; expansion, MMA and epilogue of one superblock still follow
 // each other.
 //
+// Split along K. A product of few tiles (a 2048-row matrix at a few hundred tokens: 16-86 CTAs on
+// 148 SMs) gives each CTA of grid.z a range of superblocks; instead of adding its terms to
+// registers the epilogue stores them, terms[b][token][row], and qgemm_reduce_kernel adds each
+// output's terms in superblock order from zero, exactly the sum the single CTA forms.
+//
 // The 32-element formats (Q8_0, Q4_0, Q5_0; reference csrc/quant.c:148-189) go through
 // qgemm32_kernel: per block the reference forms the integer sum s of its 32 products and adds
 // (float)s * (dw * dx) to the row's total in block order (quant.c:160). A block's weight values
@@ -31,6 +36,10 @@
 // needs no expansion beyond the copy into the core-matrix layout (the slab's 16-byte chunks of
 // 8 rows are already 8-row core matrices).
 #include "common.cuh"
+
+#include <string.h>
+
+#include <mutex>
 
 namespace sdy {
 namespace {
@@ -228,9 +237,14 @@ struct GemmArgs {
     int n_expert;
     int xdiv;
     int64_t gpe;
+    // Split along K (grid.z > 1): CTA z takes superblocks [z * sb_per, (z + 1) * sb_per) and
+    // stores term (b, token, row) at terms[(b * n_tok + token) * t_rows + row - g_begin * 8].
+    float *terms;
+    int64_t t_rows;
+    int sb_per;
 };
 
-template <int TYPE>
+template <int TYPE, bool SPLIT = false>
 __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
     constexpr int NP = GemmPlanes<TYPE>::n;
     constexpr int SB = slab_bytes(TYPE);
@@ -306,8 +320,10 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
         }
         cp_async_commit();
     };
-    issue(0);
-    for (int b = 0; b < a.nb && ok; b++) {
+    const int b0 = SPLIT ? (int)blockIdx.z * a.sb_per : 0;
+    const int b1 = SPLIT ? min(a.nb, b0 + a.sb_per) : a.nb;
+    issue(b0);
+    for (int b = b0; b < b1 && ok; b++) {
         cp_async_wait_all();
         __syncthreads();
         if (row_ok) {
@@ -319,7 +335,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
         }
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // B (cp.async) and A for the MMA
         __syncthreads();
-        if (b + 1 < a.nb) issue(b + 1);  // the raw buffer is free, B buffer (b+1)&1 was read by MMA b-1
+        if (b + 1 < b1) issue(b + 1);  // the raw buffer is free, B buffer (b+1)&1 was read by MMA b-1
         const uint8_t *sbb = sb + (b & 1) * BTILE;
         const float *ydb = yd + (b & 1) * GN;
         if (tid == 0) {
@@ -336,13 +352,16 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar_a)
                          : "memory");
         }
-        if (!mbar_wait(mbar_a, b & 1)) {
+        if (!mbar_wait(mbar_a, (b - b0) & 1)) {
             atomicOr(&g_qgemm_status, 1u);
             ok = false;
         }
         fence_after_sync();
         if (ok) {
             const float d = dr[erow], dm = dmr[erow];
+            // split: this row's terms (rows past the matrix's groups store nothing)
+            const int64_t trow = (gt0 - a.g_begin) * GROUP_ROWS + erow;
+            float *tb = SPLIT && trow < a.t_rows ? a.terms + ((size_t)b * a.n_tok + tok0) * a.t_rows + trow : nullptr;
 #pragma unroll
             for (int cc = 0; cc < 2; cc++) {
                 const uint32_t col = ehalf * 64 + cc * 32;
@@ -365,7 +384,11 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
                         const int isum = 64 * h[i] + l[i];
                         term = __fmul_rn(__fmul_rn(y, d), __int2float_rn(isum));
                     }
-                    acc[cc * 32 + i] = __fadd_rn(acc[cc * 32 + i], term);
+                    if constexpr (SPLIT) {
+                        if (tb && (int)(col + i) < nv) tb[(size_t)(col + i) * a.t_rows] = term;
+                    } else {
+                        acc[cc * 32 + i] = __fadd_rn(acc[cc * 32 + i], term);
+                    }
                 }
             }
         }
@@ -376,7 +399,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
     cp_async_wait_all();  // nothing in flight when the CTA leaves (only after a timed-out wait)
     // outputs (rows of this tile within [row0, row1), valid tokens)
     const int64_t orow = gt0 * GROUP_ROWS + erow;
-    if (ok && orow >= a.row0 && orow < a.row1) {
+    if (ok && !SPLIT && orow >= a.row0 && orow < a.row1) {
 #pragma unroll
         for (int i = 0; i < 64; i++) {
             const int t = ehalf * 64 + i;
@@ -392,6 +415,59 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
         fence_after_sync();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TMEM_COLS));
     }
+}
+
+// out[t][r] (+ residual) = the terms of (r, t) added in superblock order from zero.
+__global__ void qgemm_reduce_kernel(const float *terms, int nb, int n_tok, int64_t t_rows, int64_t row_base,
+                                    float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
+                                    const float *residual) {
+    pdl_wait();
+    const int64_t r = row0 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int t = blockIdx.y;
+    if (r >= row1) return;
+    const float *tp = terms + (size_t)t * t_rows + (r - row_base);
+    const size_t bstride = (size_t)n_tok * t_rows;
+    const float acc = ordered_sum<8>(0.0f, nb, [&](int b) { return __ldcg(tp + (size_t)b * bstride); });
+    const size_t o = (size_t)t * ldo + (r - out_row0);
+    out[o] = residual ? __fadd_rn(residual[o], acc) : acc;
+}
+
+// Stream-ordered pool of the split products' term buffers, one per device, keeping its memory
+// between calls (release threshold: unlimited); nullptr when pools are unavailable.
+cudaMemPool_t term_pool() {
+    static cudaMemPool_t pools[64] = {};
+    static std::atomic<int> state[64];  // 0 unset, 1 ready, 2 unavailable
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    int st = state[dev].load();
+    if (st == 1) return pools[dev];
+    if (st == 2) return nullptr;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    if (state[dev].load() == 0) {
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t p = nullptr;
+        uint64_t keep = ~0ull;
+        if (cudaMemPoolCreate(&p, &props) == cudaSuccess &&
+            cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep) == cudaSuccess) {
+            pools[dev] = p;
+            state[dev].store(1);
+        } else {
+            cudaGetLastError();
+            state[dev].store(2);
+        }
+    }
+    return state[dev].load() == 1 ? pools[dev] : nullptr;
+}
+
+int device_sms() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    return n;
 }
 
 // ------------------------------------------------------------------- 32-element block formats
@@ -601,8 +677,21 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm32_kernel(GemmArgs a) {
 
 bool is_block32(int type) { return type == T_Q8_0 || type == T_Q4_0 || type == T_Q5_0; }
 
-// The kernel of the weight type, with its shared memory.
+// The kernel of the weight type, with its shared memory (a.terms set: the split K-quant kernel).
 void launch_gemm(int type, dim3 grid, const GemmArgs &a, cudaStream_t s) {
+    if (a.terms) {
+        if (type == T_Q4_K) {
+            static std::atomic<uint64_t> configured{0};
+            smem_limit_once(qgemm_kernel<T_Q4_K, true>, g_smem_bytes(3, T_Q4_K), configured);
+            launch(qgemm_kernel<T_Q4_K, true>, grid, G_THREADS, g_smem_bytes(3, T_Q4_K), s, a);
+        } else {
+            static std::atomic<uint64_t> configured{0};
+            smem_limit_once(qgemm_kernel<T_Q6_K, true>, g_smem_bytes(2, T_Q6_K), configured);
+            launch(qgemm_kernel<T_Q6_K, true>, grid, G_THREADS, g_smem_bytes(2, T_Q6_K), s, a);
+        }
+        SDY_LAUNCHED();
+        return;
+    }
     switch (type) {
 #define SDY_GEMM_CASE(T, KERNEL, SMEM)                          \
     case T: {                                                   \
@@ -632,7 +721,7 @@ bool qgemm_supported(int type, int n_in) {
 static int gemm_vtype(int type) { return is_block32(type) ? T_Q8_0 : T_Q8_K; }
 
 void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
-           cudaStream_t s, const float *residual) {
+           cudaStream_t s, const float *residual, bool split_ok) {
     if (row1 <= row0 || xq.n_tok <= 0) return;
     if (!qgemm_supported(w.type, w.n_in) || xq.vtype != gemm_vtype(w.type) || xq.n_in != w.n_in) {
         set_error("qgemm: unsupported weight type %d / activation layout", w.type);
@@ -655,8 +744,56 @@ void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, i
     a.out_row0 = out_row0;
     a.residual = residual;
     const int64_t tiles_m = (a.g_end - a.g_begin + GM / GROUP_ROWS - 1) / (GM / GROUP_ROWS);
-    const dim3 grid((unsigned)tiles_m, (unsigned)((xq.n_tok + GN - 1) / GN));
-    launch_gemm(w.type, grid, a, s);
+    const int64_t tiles_n = (xq.n_tok + GN - 1) / GN;
+    // Split along K where a simple cost model says it pays: a tile's superblock takes about
+    // SB_US (one CTA per SM), the term buffer is written and read once more at about 3 TB/s
+    // (both measured on B200), and the reduction costs a launch. At least 2 superblocks per CTA,
+    // a term buffer of at most 1 GiB, never inside a stream capture.
+    const int sms = device_sms();
+    int splits = 1;
+    const int64_t tiles = tiles_m * tiles_n;
+    static const bool split_off = [] {  // SARDYNE_GEMM_SPLIT=off: one CTA per tile always
+        const char *v = getenv("SARDYNE_GEMM_SPLIT");
+        return v && !strcmp(v, "off");
+    }();
+    if (split_ok && !split_off && !is_block32(w.type) && tiles < sms && w.nb >= 4) {
+        constexpr double SB_US = 4.5, TERM_GBS = 3000.0, REDUCE_US = 3.0;
+        const int64_t t_rows = (a.g_end - a.g_begin) * GROUP_ROWS;
+        const double term_us = 2.0 * (double)w.nb * xq.n_tok * t_rows * 4 / (TERM_GBS * 1e3);
+        double best = (double)((tiles + sms - 1) / sms) * w.nb * SB_US;
+        for (int sp = 2; sp <= w.nb / 2; sp++) {
+            const int per = (w.nb + sp - 1) / sp;
+            const double t = (double)((tiles * sp + sms - 1) / sms) * per * SB_US + term_us + REDUCE_US;
+            if (t < best) best = t, splits = sp;
+        }
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        if ((size_t)w.nb * xq.n_tok * t_rows * 4 > ((size_t)1 << 30) || cudaStreamIsCapturing(s, &cap) != cudaSuccess ||
+            cap != cudaStreamCaptureStatusNone)
+            splits = 1;
+    }
+    cudaMemPool_t pool = splits > 1 ? term_pool() : nullptr;
+    float *terms = nullptr;
+    if (pool) {
+        a.t_rows = (a.g_end - a.g_begin) * GROUP_ROWS;
+        const size_t bytes = (size_t)w.nb * xq.n_tok * a.t_rows * 4;
+        if (cudaMallocFromPoolAsync((void **)&terms, bytes, pool, s) != cudaSuccess) {
+            cudaGetLastError();  // no scratch: one CTA per tile after all
+            terms = nullptr;
+        }
+    }
+    if (!terms) {
+        launch_gemm(w.type, dim3((unsigned)tiles_m, (unsigned)tiles_n), a, s);
+        return;
+    }
+    a.terms = terms;
+    a.sb_per = (w.nb + splits - 1) / splits;
+    const int nz = (w.nb + a.sb_per - 1) / a.sb_per;
+    launch_gemm(w.type, dim3((unsigned)tiles_m, (unsigned)tiles_n, (unsigned)nz), a, s);
+    launch(qgemm_reduce_kernel, dim3((unsigned)((row1 - row0 + 255) / 256), (unsigned)xq.n_tok), 256, 0, s,
+           (const float *)terms, w.nb, xq.n_tok, a.t_rows, a.g_begin * GROUP_ROWS, out, ldo, row0, row1, out_row0,
+           residual);
+    SDY_LAUNCHED();
+    SDY_CUDA(cudaFreeAsync(terms, s));
 }
 
 void qgemm_grouped(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq, int xdiv, const int32_t *grp_off,

@@ -350,12 +350,12 @@ int gemm_min_tokens() {
 }
 
 void qmatvec(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
-             cudaStream_t s, const float *residual, const ActIn *act) {
+             cudaStream_t s, const float *residual, const ActIn *act, bool split_ok) {
     if (row1 <= row0 || xq.n_tok <= 0) return;
     const int gmin = gemm_min_tokens();
     if (!act && gmin > 0 && xq.n_tok >= gmin && qgemm_supported(w.type, w.n_in) && xq.vtype == vec_dot_type(w.type) &&
         xq.n_in == w.n_in) {
-        qgemm(w, xq, out, ldo, row0, row1, out_row0, s, residual);
+        qgemm(w, xq, out, ldo, row0, row1, out_row0, s, residual, split_ok);
         return;
     }
     if (xq.vtype != vec_dot_type(w.type) || xq.n_in != w.n_in) {
