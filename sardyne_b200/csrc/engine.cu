@@ -160,11 +160,13 @@ struct engine_model {
     gguf_file *gf = nullptr;
     engine_model_info info{};
     int dev = 0;
-    // Sharding across `world` processes, one GPU each (sdy_engine_set_shard before loading):
-    // attention and the router are replicated; this rank holds dense FFN rows [f0, f1) of gate
-    // and up, output rows [d0, d1) of down, experts [e0, e1) and vocabulary rows [v0, v1) of the
-    // output matrix. Every cross-rank exchange is an all-reduce of buffers in which each element
-    // has one nonzero contributor, so results equal the one-GPU forward bit for bit.
+    // Sharding across `world` processes, one GPU each (sdy_engine_set_shard before loading): the
+    // router is replicated; this rank holds dense FFN rows [f0, f1) of gate and up, output rows
+    // [d0, d1) of down (and of the attention output matrix when attention is split, below),
+    // experts [e0, e1) and vocabulary rows [v0, v1) of the output matrix. Every cross-rank
+    // exchange assembles parts that the ranks computed disjointly (exchange(): over peer memory at
+    // single-token sizes, else an NCCL all-reduce of buffers that are zero outside each rank's
+    // part), so results equal the one-GPU forward bit for bit.
     int rank = 0, world = 1;
     ncclComm_t comm = nullptr;
     int64_t f0 = 0, f1 = 0, d0 = 0, d1 = 0, e0 = 0, e1 = 0, v0 = 0, v1 = 0;
@@ -1321,8 +1323,8 @@ engine_model *engine_model_load(const char *path, char *err, size_t err_len) {
     shard_range(dim, m->world, m->rank, GROUP_ROWS, &m->d0, &m->d1);
     shard_range(in.n_expert, m->world, m->rank, 1, &m->e0, &m->e1);
     shard_range(in.n_vocab, m->world, m->rank, GROUP_ROWS, &m->v0, &m->v1);
-    // SARDYNE_ATTN_TP=off: attention replicated on every rank (one exchange less per attention
-    // block: lower batch-1 latency, but every rank holds all q/k/v/o rows and the whole KV cache)
+    // SARDYNE_ATTN_TP=off: attention replicated on every rank (two exchanges less per layer:
+    // lower batch-1 latency, but every rank holds all q/k/v/o rows and the whole KV cache)
     static const bool tp_off = [] {
         const char *v = getenv("SARDYNE_ATTN_TP");
         return v && !strcmp(v, "off");

@@ -133,6 +133,22 @@ def test_q0_rows_not_multiple_of_256(kind):
     assert np.array_equal(gpu_matmul_q(w, kind, xq, 3, n_in, n_out), oracle.matmul_q(w, kind, xq, 3, n_in, n_out))
 
 
+@pytest.mark.parametrize("kind", ["Q4_0", "Q5_0"])
+@pytest.mark.parametrize("n_in,n_tok", [(256, 1), (576, 3)])
+def test_q0_tall_matrix(kind, n_in, n_tok):
+    """Q4_0 / Q5_0 matrices of LM-head height (80000 rows), a row range that starts inside a row
+    group, ragged 8-block runs at 576."""
+    n_out = 80000
+    w = oracle.random_blocks(kind, n_out * n_in // 32, seed=n_in)
+    x = np.random.default_rng(n_in).standard_normal((n_tok, n_in)).astype(np.float32)
+    xq = oracle.quantize(x, "Q8_0")
+    want = oracle.matmul_q(w, kind, xq, n_tok, n_in, n_out)
+    assert np.array_equal(gpu_matmul_q(w, kind, xq, n_tok, n_in, n_out), want)
+    got = gpu_matmul_q(w, kind, xq, n_tok, n_in, n_out, row0=3, row1=79000)
+    assert np.isnan(got[:, :3]).all() and np.isnan(got[:, 79000:]).all()
+    assert np.array_equal(got[:, 3:79000], want[:, 3:79000])
+
+
 @pytest.mark.parametrize("kind", KINDS)
 def test_op_matmul_quantizes_like_the_reference(kind):
     """op_matmul (f32 activations in): quantization + product on the GPU == oracle chain."""
