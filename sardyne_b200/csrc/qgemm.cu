@@ -305,24 +305,34 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
     // Superblock b's raw slabs, B tile and token scales, requested with cp.async (B and yd into
     // buffer b & 1) so that they travel while the previous superblock is multiplied.
     const int ng_tile = (int)(a.g_end - gt0 < GM / GROUP_ROWS ? a.g_end - gt0 : GM / GROUP_ROWS);
-    auto issue = [&](int b) {
-        uint8_t *sbb = sb + (b & 1) * BTILE;
-        float *ydb = yd + (b & 1) * GN;
-        for (int i = tid; i < nv * 16; i += G_THREADS) {
-            const int t = i >> 4, c = i & 15;
-            cp_async16(sbb + c * (GN * 16) + t * 16, a.xqs + (size_t)xrow(t) * a.qrow + b * XQ_SPAN + c * 16);
-        }
-        for (int t = tid; t < nv; t += G_THREADS) cp_async4(ydb + t, a.xd + (size_t)xrow(t) * a.nbx + b);
-        constexpr int C16 = SB / 16;
-        for (int i = tid; i < ng_tile * C16; i += G_THREADS) {
-            const int g = i / C16, c = i - g * C16;
-            cp_async16(raw + g * SB + c * 16, slabs + ((size_t)(gt0 + g) * a.nb + b) * SB + c * 16);
+    // first: the first thread of the copying threads, stride their number (the first superblock's
+    // copies by every thread; later ones by warps 1-7 while warp 0 issues the MMAs)
+    auto issue = [&](int b, int first) {
+        const int me = tid - first, stride = G_THREADS - first;
+        if (me >= 0) {
+            uint8_t *sbb = sb + (b & 1) * BTILE;
+            float *ydb = yd + (b & 1) * GN;
+            for (int i = me; i < nv * 16; i += stride) {
+                const int t = i >> 4, c = i & 15;
+                cp_async16(sbb + c * (GN * 16) + t * 16, a.xqs + (size_t)xrow(t) * a.qrow + b * XQ_SPAN + c * 16);
+            }
+            for (int t = me; t < nv; t += stride) cp_async4(ydb + t, a.xd + (size_t)xrow(t) * a.nbx + b);
+            constexpr int C16 = SB / 16;
+            for (int i = me; i < ng_tile * C16; i += stride) {
+                const int g = i / C16, c = i - g * C16;
+                cp_async16(raw + g * SB + c * 16, slabs + ((size_t)(gt0 + g) * a.nb + b) * SB + c * 16);
+            }
         }
         cp_async_commit();
     };
     const int b0 = SPLIT ? (int)blockIdx.z * a.sb_per : 0;
     const int b1 = SPLIT ? min(a.nb, b0 + a.sb_per) : a.nb;
-    issue(b0);
+    issue(b0, 0);
+    // matrix descriptors of the A planes and of the two B tiles: each MMA adds its constant offset
+    // (address / 16 stays far below the field's 14 bits: shared memory is < 256 KB)
+    const uint64_t a_desc = kmajor_desc(smem_u32(sa), GM * 16, 128);
+    const uint64_t b_desc[2] = {kmajor_desc(smem_u32(sb), GN * 16, 128),
+                                kmajor_desc(smem_u32(sb + BTILE), GN * 16, 128)};
     for (int b = b0; b < b1 && ok; b++) {
         cp_async_wait_all();
         __syncthreads();
@@ -335,23 +345,22 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm_kernel(GemmArgs a) {
         }
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // B (cp.async) and A for the MMA
         __syncthreads();
-        if (b + 1 < b1) issue(b + 1);  // the raw buffer is free, B buffer (b+1)&1 was read by MMA b-1
-        const uint8_t *sbb = sb + (b & 1) * BTILE;
         const float *ydb = yd + (b & 1) * GN;
-        if (tid == 0) {
+        if (tid == 0) {  // the MMAs first, then the next superblock's copies by warps 1-7 meanwhile
             fence_after_sync();
             const uint32_t idesc = idesc_i8(nv);
+            const uint64_t bd0 = b_desc[b & 1];
 #pragma unroll
             for (int s = 0; s < 8; s++) {  // K step s: bytes 32s..32s+31 = chunk planes 2s, 2s+1
-                const uint64_t bd = kmajor_desc(smem_u32(sbb + 2 * s * GN * 16), GN * 16, 128);
+                const uint64_t bd = bd0 + ((2 * s * GN * 16) >> 4);
 #pragma unroll
                 for (int p = 0; p < NP; p++)
-                    mma_i8(tmem + p * GN, kmajor_desc(smem_u32(sa + p * PLANE + 2 * s * GM * 16), GM * 16, 128), bd,
-                           idesc, s > 0);
+                    mma_i8(tmem + p * GN, a_desc + ((p * PLANE + 2 * s * GM * 16) >> 4), bd, idesc, s > 0);
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar_a)
                          : "memory");
         }
+        if (b + 1 < b1) issue(b + 1, 32);  // the raw buffer is free, B buffer (b+1)&1 was read by MMA b-1
         if (!mbar_wait(mbar_a, (b - b0) & 1)) {
             atomicOr(&g_qgemm_status, 1u);
             ok = false;
@@ -576,26 +585,31 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm32_kernel(GemmArgs a) {
     const int ng_tile = (int)(a.g_end - gt0 < GM / GROUP_ROWS ? a.g_end - gt0 : GM / GROUP_ROWS);
     const int steps = (a.nb + KB - 1) / KB;
     // Step s: blocks KB*s .. KB*s + nblk - 1 (elements 128s.., inside one 256-element XQ span).
-    auto issue = [&](int st) {
-        const int b0 = st * KB, nblk = min(KB, a.nb - b0), chunks = 2 * nblk;
-        uint8_t *sbb = sb + (st & 1) * BTILE32;
-        float *ydb = yd + (st & 1) * KB * GN;
-        for (int i = tid; i < nv * chunks; i += G_THREADS) {
-            const int t = i / chunks, c = i - t * chunks;
-            cp_async16(sbb + c * (GN * 16) + t * 16, a.xqs + (size_t)xrow(t) * a.qrow + xq_pos(32 * b0) + c * 16);
-        }
-        for (int i = tid; i < nv * nblk; i += G_THREADS) {
-            const int t = i / nblk, j = i - t * nblk;
-            cp_async4(ydb + j * GN + t, a.xd + (size_t)xrow(t) * a.nbx + b0 + j);
-        }
-        constexpr int C16 = SB / 16;
-        for (int i = tid; i < ng_tile * nblk * C16; i += G_THREADS) {
-            const int gj = i / C16, c = i - gj * C16, g = gj / nblk, j = gj - g * nblk;
-            cp_async16(raw + (g * KB + j) * SB + c * 16, slabs + ((size_t)(gt0 + g) * a.nb + b0 + j) * SB + c * 16);
+    // first: as in qgemm_kernel (warp 0 issues the MMAs while warps 1-7 copy the next step)
+    auto issue = [&](int st, int first) {
+        const int me = tid - first, stride = G_THREADS - first;
+        if (me >= 0) {
+            const int b0 = st * KB, nblk = min(KB, a.nb - b0), chunks = 2 * nblk;
+            uint8_t *sbb = sb + (st & 1) * BTILE32;
+            float *ydb = yd + (st & 1) * KB * GN;
+            for (int i = me; i < nv * chunks; i += stride) {
+                const int t = i / chunks, c = i - t * chunks;
+                cp_async16(sbb + c * (GN * 16) + t * 16, a.xqs + (size_t)xrow(t) * a.qrow + xq_pos(32 * b0) + c * 16);
+            }
+            for (int i = me; i < nv * nblk; i += stride) {
+                const int t = i / nblk, j = i - t * nblk;
+                cp_async4(ydb + j * GN + t, a.xd + (size_t)xrow(t) * a.nbx + b0 + j);
+            }
+            constexpr int C16 = SB / 16;
+            for (int i = me; i < ng_tile * nblk * C16; i += stride) {
+                const int gj = i / C16, c = i - gj * C16, g = gj / nblk, j = gj - g * nblk;
+                cp_async16(raw + (g * KB + j) * SB + c * 16,
+                           slabs + ((size_t)(gt0 + g) * a.nb + b0 + j) * SB + c * 16);
+            }
         }
         cp_async_commit();
     };
-    issue(0);
+    issue(0, 0);
     for (int st = 0; st < steps && ok; st++) {
         const int nblk = min(KB, a.nb - st * KB);
         cp_async_wait_all();
@@ -616,7 +630,6 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm32_kernel(GemmArgs a) {
         }
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         __syncthreads();
-        if (st + 1 < steps) issue(st + 1);  // raw is free; B buffer (st+1)&1 was read by MMA st-1
         const uint8_t *sbb = sb + (st & 1) * BTILE32;
         const float *ydb = yd + (st & 1) * KB * GN;
         if (tid == 0) {
@@ -628,6 +641,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) qgemm32_kernel(GemmArgs a) {
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar_a)
                          : "memory");
         }
+        if (st + 1 < steps) issue(st + 1, 32);  // raw is free; B buffer (st+1)&1 was read by MMA st-1
         if (!mbar_wait(mbar_a, st & 1)) {
             atomicOr(&g_qgemm_status, 1u);
             ok = false;
@@ -757,7 +771,7 @@ void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, i
         return v && !strcmp(v, "off");
     }();
     if (split_ok && !split_off && !is_block32(w.type) && tiles < sms && w.nb >= 4) {
-        constexpr double SB_US = 4.5, TERM_GBS = 3000.0, REDUCE_US = 3.0;
+        constexpr double SB_US = 3.0, TERM_GBS = 3000.0, REDUCE_US = 3.0;
         const int64_t t_rows = (a.g_end - a.g_begin) * GROUP_ROWS;
         const double term_us = 2.0 * (double)w.nb * xq.n_tok * t_rows * 4 / (TERM_GBS * 1e3);
         double best = (double)((tiles + sms - 1) / sms) * w.nb * SB_US;
