@@ -58,7 +58,7 @@ def act_type(fmt):
     """The activation layout a weight format multiplies with (quant.c: vec_dot_type)."""
     return "Q8_0" if fmt in FORMATS32 else "Q8_K"
 WORKLOAD = ("BASELINE config 2 at batch 1: Q4_K and Q6_K matvec over 2048x11008, 11008x2048 and "
-            "151936x2048 ([n_out][n_in]), Q8_K activations quantized on the device once per input width")
+            "151936x2048 ([n_out][n_in]), f32 inputs resident, quantized to Q8_K inside the grouped launch")
 
 
 def log(*a):
@@ -442,13 +442,15 @@ def run_b200(args, rank, world, local_rank):
     xq_arr = (ctypes.c_void_p * len(mats))(*[d_xq[n_in].data_ptr() for _, _, n_in, _ in mats])
     out_arr = (ctypes.c_void_p * len(mats))(*[o.data_ptr() for o in d_out])
 
+    x_arr = (ctypes.c_void_p * len(mats))(*[d_x[n_in].data_ptr() for _, _, n_in, _ in mats])
+
     def grouped():
-        """This rank's products of the sweep in one launch (sdy_qmatvec_batch_dev)."""
-        if lib.sdy_qmatvec_batch_dev(len(mats), hs_arr, xq_arr, out_arr, sp) != 0:
+        """This rank's products of the sweep in one launch, each CTA quantizing its product's f32
+        input row to Q8_K itself (sdy_qmatvec_batch_f32_dev): no quantization launch."""
+        if lib.sdy_qmatvec_batch_f32_dev(len(mats), hs_arr, x_arr, out_arr, sp) != 0:
             raise RuntimeError(capi.last_error())
 
     def step():
-        quantize_inputs()
         grouped()
         if world > 1:  # every rank ends the step with every matrix's full y
             gather(sp)
@@ -502,8 +504,8 @@ def run_b200(args, rank, world, local_rank):
         del sweep_wo
     del sweep_all
 
-    # the timed step as one CUDA graph: the 2 activation quantizations, 6 matvecs (and, N > 1, the
-    # all-gather of y)
+    # the timed step as one CUDA graph: the grouped launch of the 6 products with their input
+    # quantization (and, N > 1, the all-gather of y)
     step_graph = capture(step)
     with torch.cuda.stream(stream):
         step_graph.replay()
@@ -523,7 +525,7 @@ def run_b200(args, rank, world, local_rank):
         torch.cuda.synchronize()
         barrier()
     # launches recorded in the graph once, replayed every step
-    launches_per_step = len(xs) + 1
+    launches_per_step = 1 + (1 if p2p else 0)
     # The step's dominant kernel, the grouped launch, timed per launch: eager launches each bracketed
     # by events on its stream, queued behind a ~10 ms spin kernel so that the host is ahead of the
     # GPU and no host launch gap falls inside a bracket. The single largest product (the Q6_K LM
@@ -639,7 +641,8 @@ def run_b200(args, rank, world, local_rank):
             "config": config(world, args.gather),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": f"grouped qmv: this rank's {len(mats)} products in one launch",
+                         "kernel": f"grouped qmv: this rank's {len(mats)} products and their input "
+                                   f"quantization in one launch",
                          "peak_source": peak_kind, "algorithmic_bytes": step_bytes,
                          "launch_us": round(grp_ms * 1e3, 2)},
             "roofline_single": {"bound": "hbm", "achieved": round(achieved1, 1), "peak": peak, "unit": "GB/s",

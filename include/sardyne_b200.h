@@ -184,6 +184,13 @@ int sdy_qmatvec_dev(const void *w, const void *d_xq, int n_tok, float *d_out, in
  * from sdy_quantize_rows_dev). 1 <= n <= 8, Q4_K / Q6_K weights; each result equals
  * sdy_qmatvec_dev's bit for bit. 0 or -1. */
 int sdy_qmatvec_batch_dev(int n, const void *const *w, const void *const *d_xq, float *const *d_out, void *stream);
+/* No counterpart in the reference. The same grouped products with f32 input rows d_x[i] (n_in_i
+ * floats, 16-byte aligned, n_in_i a multiple of 256): every CTA quantizes its product's row to
+ * Q8_K itself (the reference's quant_q8_K, byte-exact) while its first weights load, so no
+ * quantization launch precedes the products; results equal sdy_quantize_rows_dev followed by
+ * sdy_qmatvec_batch_dev bit for bit. 0 or -1. */
+int sdy_qmatvec_batch_f32_dev(int n, const void *const *w, const float *const *d_x, float *const *d_out,
+                              void *stream);
 
 /* No counterpart in the reference (it runs on one host). All-gather over NVLink peer memory for
  * processes that drive one GPU each: rank r's count floats (d_send) are stored by the GPU into

@@ -253,7 +253,10 @@ void qmatvec2(const QMat &wa, float *outa, const QMat &wb, float *outb, const XQ
 // Independent single-token products in one launch: out[i][r] = W_i[r] . x_i for every row of
 // each of the n (<= 8) Q4_K / Q6_K matrices, x_i the Q8_K row xq[i].
 bool qmatvec_batch_supported(int n, const QMat *const *w);
-void qmatvec_batch(int n, const QMat *const *w, const XQ *const *xq, float *const *out, cudaStream_t s);
+// acts set: product i's input row is act[i] (f32, prepared as ActIn says) and every CTA quantizes
+// it itself; xq[i] then gives the activation geometry only.
+void qmatvec_batch(int n, const QMat *const *w, const XQ *const *xq, float *const *out, cudaStream_t s,
+                   const ActIn *acts = nullptr);
 // MoE: for each slot s < n_slots, out[s*ldo_slot + r] = E[slot_expert[s]][r] . x[s / tok_div] for
 // r < rows_per_expert. `experts` holds n_expert matrices (global experts expert0 .. expert0 +
 // n_expert - 1), each padded to gpe groups; slots naming other experts are left untouched. The

@@ -567,4 +567,35 @@ int sdy_qmatvec_batch_dev(int n, const void *const *hs, const void *const *d_xq,
     return last_error()[0] ? -1 : 0;
 }
 
+int sdy_qmatvec_batch_f32_dev(int n, const void *const *hs, const float *const *d_x, float *const *d_out,
+                              void *stream) {
+    clear_error();
+    if (n < 1 || n > 8 || !hs || !d_x || !d_out) {
+        set_error("sdy_qmatvec_batch_f32_dev: 1..8 products with their weights, inputs and outputs");
+        return -1;
+    }
+    const QMat *w[8];
+    XQ q[8];
+    const XQ *qp[8];
+    ActIn act[8];
+    for (int i = 0; i < n; i++) {
+        const sdy_qmat_s *h = (const sdy_qmat_s *)hs[i];
+        if (!h || !d_x[i] || !d_out[i]) {
+            set_error("sdy_qmatvec_batch_f32_dev: product %d: null argument", i);
+            return -1;
+        }
+        if (((uintptr_t)d_x[i] & 15) || h->m.n_in % 256) {
+            set_error("sdy_qmatvec_batch_f32_dev: product %d: input must be 16-byte aligned, rows of whole "
+                      "superblocks", i);
+            return -1;
+        }
+        w[i] = &h->m;
+        q[i] = xq_carve(nullptr, vec_dot_type(h->m.type), h->m.n_in, 1);  // geometry only
+        qp[i] = &q[i];
+        act[i] = ActIn{d_x[i], h->m.n_in};
+    }
+    qmatvec_batch(n, w, qp, d_out, (cudaStream_t)stream, act);
+    return last_error()[0] ? -1 : 0;
+}
+
 }  // extern "C"

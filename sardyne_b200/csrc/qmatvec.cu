@@ -513,7 +513,8 @@ bool qmatvec_batch_supported(int n, const QMat *const *w) {
     return true;
 }
 
-void qmatvec_batch(int n, const QMat *const *w, const XQ *const *xq, float *const *out, cudaStream_t s) {
+void qmatvec_batch(int n, const QMat *const *w, const XQ *const *xq, float *const *out, cudaStream_t s,
+                   const ActIn *acts) {
     if (!qmatvec_batch_supported(n, w)) {
         set_error("qmatvec_batch: 1..%d matrices of Q4_K / Q6_K", BATCH_MAX);
         return;
@@ -537,7 +538,7 @@ void qmatvec_batch(int n, const QMat *const *w, const XQ *const *xq, float *cons
             set_error("qmatvec_batch: row of %d elements too long for one CTA", w[i]->n_in);
             return;
         }
-        b.a[i] = pair_args(*w[i], p, *xq[i], out[i], nullptr);
+        b.a[i] = pair_args(*w[i], p, *xq[i], out[i], acts ? &acts[i] : nullptr);
         b.type[i] = w[i]->type;
         b.cta0[i] = grid;
         grid += p.grid;

@@ -230,12 +230,13 @@ def test_errors_are_reported_not_crashing():
 
 def test_grouped_products_equal_single_launches():
     """sdy_qmatvec_batch_dev: independent products of both K-quant formats, different input widths
-    and row counts (ragged groups), in one launch: each equal to its own sdy_qmatvec_dev bit for bit."""
+    and row counts (ragged groups), in one launch: each equal to its own sdy_qmatvec_dev bit for bit;
+    sdy_qmatvec_batch_f32_dev (f32 rows quantized by every CTA) gives the same bits."""
     import torch
     lib_ = lib()
     shapes = [("Q4_K", 300, 2048), ("Q6_K", 1001, 2048), ("Q4_K", 77, 11008), ("Q6_K", 2048, 1024),
               ("Q4_K", 4096, 256), ("Q6_K", 9, 11008)]
-    handles, xqs, outs, want = [], [], [], []
+    handles, xqs, outs, want, xs = [], [], [], [], []
     try:
         for i, (kind, n_out, n_in) in enumerate(shapes):
             w = oracle.random_blocks(kind, n_out * n_in // 256, seed=50 + i)
@@ -243,6 +244,7 @@ def test_grouped_products_equal_single_launches():
             assert h, capi.last_error()
             handles.append(h)
             x = torch.from_numpy(np.random.default_rng(i).standard_normal(n_in).astype(np.float32)).cuda()
+            xs.append(x)
             xq = torch.empty(lib_.sdy_xq_bytes(TID["Q8_K"], n_in, 1), dtype=torch.uint8, device="cuda")
             assert lib_.sdy_quantize_rows_dev(TID["Q8_K"], ctypes.c_void_p(x.data_ptr()), 1, n_in,
                                               ctypes.c_void_p(xq.data_ptr()), None) == 0
@@ -258,6 +260,13 @@ def test_grouped_products_equal_single_launches():
                                           arr([t.data_ptr() for t in outs]), None) == 0, capi.last_error()
         torch.cuda.synchronize()
         for got, ref in zip(outs, want):
+            assert torch.equal(got, ref)
+        # f32 inputs, every CTA quantizing its row (sdy_qmatvec_batch_f32_dev): the same bits
+        outs2 = [torch.full_like(o, float("nan")) for o in outs]
+        assert lib_.sdy_qmatvec_batch_f32_dev(n, arr(handles), arr([t.data_ptr() for t in xs]),
+                                              arr([t.data_ptr() for t in outs2]), None) == 0, capi.last_error()
+        torch.cuda.synchronize()
+        for got, ref in zip(outs2, want):
             assert torch.equal(got, ref)
         # more than 8 products are refused
         assert lib_.sdy_qmatvec_batch_dev(9, arr(handles + [handles[0]] * 3), arr([0] * 9), arr([0] * 9), None) == -1
