@@ -245,7 +245,7 @@ def config(world=1, gather="p2p"):
          "l2": "inputs larger than L2: 492 MB of weights per step against a 126 MB L2",
          "weights": "N(0,0.02), package quantizer; LM heads from a pool of quantized Gaussian blocks"}
     c["parallelism"] = (f"rows of every matrix split over {world} GPUs, y all-gathered "
-                        f"({'over NVLink peer memory, own kernel' if gather == 'p2p' else 'NCCL'})"
+                        f"({'over NVLink peer memory, fused into the product launch' if gather == 'p2p' else 'NCCL'})"
                         if world > 1 else "1 GPU")
     return c
 
@@ -450,9 +450,22 @@ def run_b200(args, rank, world, local_rank):
         if lib.sdy_qmatvec_batch_f32_dev(len(mats), hs_arr, x_arr, out_arr, sp) != 0:
             raise RuntimeError(capi.last_error())
 
+    off_arr = (ctypes.c_int64 * len(mats))(*share_off)
+
+    def fused():
+        """The products with the all-gather fused into the same launch: every output value is also
+        stored into the peers' gather buffers, and the launch's last CTA exchanges round flags
+        (sdy_qmatvec_batch_f32_gather_dev)."""
+        if lib.sdy_qmatvec_batch_f32_gather_dev(len(mats), hs_arr, x_arr, off_arr, share, p2p_bases, rank, world,
+                                                sp) != 0:
+            raise RuntimeError(capi.last_error())
+
     def step():
+        if p2p:  # every rank ends the step with every matrix's full y, in one launch
+            fused()
+            return
         grouped()
-        if world > 1:  # every rank ends the step with every matrix's full y
+        if world > 1:
             gather(sp)
 
     def gathered_y(i, allv=None):
@@ -505,7 +518,8 @@ def run_b200(args, rank, world, local_rank):
     del sweep_all
 
     # the timed step as one CUDA graph: the grouped launch of the 6 products with their input
-    # quantization (and, N > 1, the all-gather of y)
+    # quantization (N > 1: and the all-gather of y, fused into the same launch; --gather nccl: an
+    # NCCL all-gather after it)
     step_graph = capture(step)
     with torch.cuda.stream(stream):
         step_graph.replay()
@@ -525,7 +539,7 @@ def run_b200(args, rank, world, local_rank):
         torch.cuda.synchronize()
         barrier()
     # launches recorded in the graph once, replayed every step
-    launches_per_step = 1 + (1 if p2p else 0)
+    launches_per_step = 1
     # The step's dominant kernel, the grouped launch, timed per launch: eager launches each bracketed
     # by events on its stream, queued behind a ~10 ms spin kernel so that the host is ahead of the
     # GPU and no host launch gap falls inside a bracket. The single largest product (the Q6_K LM

@@ -191,6 +191,16 @@ int sdy_qmatvec_batch_dev(int n, const void *const *w, const void *const *d_xq, 
  * sdy_qmatvec_batch_dev bit for bit. 0 or -1. */
 int sdy_qmatvec_batch_f32_dev(int n, const void *const *w, const float *const *d_x, float *const *d_out,
                               void *stream);
+/* No counterpart in the reference (one host). sdy_qmatvec_batch_f32_dev with the all-gather of
+ * sdy_allgather_p2p fused into the launch, for processes that drive one GPU each: product i's rows
+ * go to offset rank * count + out_off[i] of every rank's gather buffer (bases: every rank's buffer
+ * from sdy_p2p_alloc(sdy_allgather_p2p_bytes(count, world)), as mapped here; this rank's rows of
+ * each matrix, out_off[i] + rows <= count). Each output value is stored into the peers' buffers
+ * over NVLink as it is produced; the launch's last CTA then exchanges round flags with the other
+ * ranks (bounded one-second wait; sdy_kernel_status nonzero if it gave up). Every rank makes the
+ * same sequence of calls; the buffers' flags are shared with sdy_allgather_p2p. 0 or -1. */
+int sdy_qmatvec_batch_f32_gather_dev(int n, const void *const *w, const float *const *d_x, const int64_t *out_off,
+                                     int64_t count, void *const *bases, int32_t rank, int32_t world, void *stream);
 
 /* No counterpart in the reference (it runs on one host). All-gather over NVLink peer memory for
  * processes that drive one GPU each: rank r's count floats (d_send) are stored by the GPU into

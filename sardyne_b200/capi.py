@@ -119,6 +119,9 @@ EXTENSIONS = {
     "sdy_qmatvec_dev": (_i, [_vp, _vp, _i, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp]),
     "sdy_qmatvec_batch_dev": (_i, [_i, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp]),
     "sdy_qmatvec_batch_f32_dev": (_i, [_i, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp]),
+    "sdy_qmatvec_batch_f32_gather_dev": (_i, [_i, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
+                                              ctypes.POINTER(ctypes.c_int64), ctypes.c_int64, ctypes.POINTER(_vp),
+                                              ctypes.c_int32, ctypes.c_int32, _vp]),
     "sdy_allgather_p2p_bytes": (_sz, [ctypes.c_int64, ctypes.c_int32]),
     "sdy_p2p_alloc": (_vp, [_sz]),
     "sdy_p2p_free": (None, [_vp]),

@@ -255,8 +255,21 @@ void qmatvec2(const QMat &wa, float *outa, const QMat &wb, float *outb, const XQ
 bool qmatvec_batch_supported(int n, const QMat *const *w);
 // acts set: product i's input row is act[i] (f32, prepared as ActIn says) and every CTA quantizes
 // it itself; xq[i] then gives the activation geometry only.
+// tail set (processes that drive one GPU each): every output value is also stored at byte offset
+// delta[q] from its local address, in the peers' buffers (an all-gather over NVLink fused into the
+// launch); the last CTA then release-stores the next round into flags[q][rank] of every rank and
+// waits (acquire, at most one second) until its own flags show it from every rank. The buffer
+// layout and round protocol are those of sdy_allgather_p2p (p2p.cu).
+struct PeerGatherTail {
+    int64_t delta[8] = {};
+    int n_peer = 0;
+    unsigned *flags[8] = {};
+    unsigned *done = nullptr, *round = nullptr;
+    int rank = 0, world = 1;
+};
 void qmatvec_batch(int n, const QMat *const *w, const XQ *const *xq, float *const *out, cudaStream_t s,
-                   const ActIn *acts = nullptr);
+                   const ActIn *acts = nullptr, const PeerGatherTail *tail = nullptr);
+unsigned qmatvec_status();  // nonzero when a fused gather's wait gave up
 // MoE: for each slot s < n_slots, out[s*ldo_slot + r] = E[slot_expert[s]][r] . x[s / tok_div] for
 // r < rows_per_expert. `experts` holds n_expert matrices (global experts expert0 .. expert0 +
 // n_expert - 1), each padded to gpe groups; slots naming other experts are left untouched. The

@@ -157,7 +157,7 @@ const char *engine_version(void) { return "0.0.1"; }
 const char *sdy_last_error(void) { return last_error(); }
 void sdy_clear_error(void) { clear_error(); }
 uint64_t sdy_kernel_launches(void) { return g_launches.load(); }
-uint32_t sdy_kernel_status(void) { return qgemm_status(); }
+uint32_t sdy_kernel_status(void) { return qgemm_status() | qmatvec_status(); }
 
 static int g_simd = 1;
 int op_simd(void) { return g_simd; }
@@ -595,6 +595,60 @@ int sdy_qmatvec_batch_f32_dev(int n, const void *const *hs, const float *const *
         act[i] = ActIn{d_x[i], h->m.n_in};
     }
     qmatvec_batch(n, w, qp, d_out, (cudaStream_t)stream, act);
+    return last_error()[0] ? -1 : 0;
+}
+
+int sdy_qmatvec_batch_f32_gather_dev(int n, const void *const *hs, const float *const *d_x, const int64_t *out_off,
+                                     int64_t count, void *const *bases, int32_t rank, int32_t world, void *stream) {
+    clear_error();
+    if (n < 1 || n > 8 || !hs || !d_x || !out_off || count <= 0 || !bases || world < 1 || world > 8 || rank < 0 ||
+        rank >= world) {
+        set_error("sdy_qmatvec_batch_f32_gather_dev: bad arguments (1..8 products, 1 <= world <= 8)");
+        return -1;
+    }
+    for (int q = 0; q < world; q++)
+        if (!bases[q]) {
+            set_error("sdy_qmatvec_batch_f32_gather_dev: buffer of rank %d missing", q);
+            return -1;
+        }
+    // the layout of sdy_allgather_p2p: world * count floats, then the flag words
+    const size_t F = align_up((size_t)world * count * 4, 256);
+    PeerGatherTail tail;
+    tail.rank = rank;
+    tail.world = world;
+    for (int q = 0; q < world; q++) {
+        tail.flags[q] = (unsigned *)((uint8_t *)bases[q] + F);
+        if (q != rank) tail.delta[tail.n_peer++] = (int64_t)((uint8_t *)bases[q] - (uint8_t *)bases[rank]);
+    }
+    tail.done = (unsigned *)((uint8_t *)bases[rank] + F + 128);
+    tail.round = (unsigned *)((uint8_t *)bases[rank] + F + 132);
+    float *out[8];
+    for (int i = 0; i < n; i++) {
+        const sdy_qmat_s *h = (const sdy_qmat_s *)hs[i];
+        if (!h || out_off[i] < 0 || out_off[i] + h->m.n_rows > count) {
+            set_error("sdy_qmatvec_batch_f32_gather_dev: product %d: rows past this rank's %lld-float slice", i,
+                      (long long)count);
+            return -1;
+        }
+        out[i] = (float *)bases[rank] + (size_t)rank * count + out_off[i];
+    }
+    const QMat *w[8];
+    XQ q[8];
+    const XQ *qp[8];
+    ActIn act[8];
+    for (int i = 0; i < n; i++) {
+        const sdy_qmat_s *h = (const sdy_qmat_s *)hs[i];
+        if (!d_x[i] || ((uintptr_t)d_x[i] & 15) || h->m.n_in % 256) {
+            set_error("sdy_qmatvec_batch_f32_gather_dev: product %d: input must be 16-byte aligned, rows of whole "
+                      "superblocks", i);
+            return -1;
+        }
+        w[i] = &h->m;
+        q[i] = xq_carve(nullptr, vec_dot_type(h->m.type), h->m.n_in, 1);
+        qp[i] = &q[i];
+        act[i] = ActIn{d_x[i], h->m.n_in};
+    }
+    qmatvec_batch(n, w, qp, out, (cudaStream_t)stream, act, world > 1 ? &tail : nullptr);
     return last_error()[0] ? -1 : 0;
 }
 

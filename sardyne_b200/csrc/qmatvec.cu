@@ -75,7 +75,8 @@ __host__ __device__ inline Smem smem_plan(int type, int NT, int qrow, int nb, in
 
 // The CTA's work: CTA `cta` of the n_cta that share the launch's groups.
 template <int TYPE, int NT>
-__device__ __forceinline__ void qmv_body(const Args &a, int cta, int n_cta, uint8_t *smem) {
+__device__ __forceinline__ void qmv_body(const Args &a, int cta, int n_cta, uint8_t *smem,
+                                         const PeerGatherTail *pg = nullptr) {
     constexpr bool KQ = (TYPE == T_Q4_K || TYPE == T_Q6_K);
     constexpr int SB = slab_bytes(TYPE);
     const Smem plan = smem_plan(TYPE, NT, a.qrow, a.nb, a.G);
@@ -172,7 +173,10 @@ __device__ __forceinline__ void qmv_body(const Args &a, int cta, int n_cta, uint
             const float acc = ordered_sum<8>(0.0f, nb, [&](int b) { return tp[(size_t)b * rows]; });
             const size_t o = (size_t)t * a.ldo + (row - a.out_row0);
             // residual stream: x = x + W.a, the reference's `x[i] += xb[i]` (model_llama.c:804,820)
-            out[o] = a.residual ? __fadd_rn(a.residual[o], acc) : acc;
+            const float v = a.residual ? __fadd_rn(a.residual[o], acc) : acc;
+            out[o] = v;
+            if (pg)  // the same value into every peer's copy of the buffer
+                for (int q = 0; q < pg->n_peer; q++) *(float *)((char *)(out + o) + pg->delta[q]) = v;
         }
         __syncthreads();
     }
@@ -204,15 +208,62 @@ struct BatchArgs {
     int type[BATCH_MAX];
     int cta0[BATCH_MAX + 1];
     int n;
+    int gather;  // 1: pg holds a fused all-gather
+    PeerGatherTail pg;
 };
-template <int TA, int TB>
-__global__ void __launch_bounds__(THREADS) qmvb_kernel(BatchArgs b) {
+
+__device__ unsigned g_qmvb_status;
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+template <int TA, int TB, bool GATHER>
+__global__ void __launch_bounds__(THREADS) qmvb_kernel(const __grid_constant__ BatchArgs b) {
     extern __shared__ __align__(16) uint8_t smem[];
     int i = 0;
     while (i + 1 < b.n && (int)blockIdx.x >= b.cta0[i + 1]) i++;
     const int c = blockIdx.x - b.cta0[i], nc = b.cta0[i + 1] - b.cta0[i];
-    if (b.type[i] == TA) qmv_body<TA, 1>(b.a[i], c, nc, smem);
-    else qmv_body<TB, 1>(b.a[i], c, nc, smem);
+    const PeerGatherTail *pg = GATHER ? &b.pg : nullptr;
+    if (b.type[i] == TA) qmv_body<TA, 1>(b.a[i], c, nc, smem, pg);
+    else qmv_body<TB, 1>(b.a[i], c, nc, smem, pg);
+    if constexpr (!GATHER) return;
+    // fused all-gather: the CTA's peer stores ordered before its arrival (one system fence by
+    // thread 0 after the barrier, cumulative); the last CTA publishes the round and waits
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        last = atomicAdd(b.pg.done, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    __threadfence_system();
+    *b.pg.done = 0;
+    const unsigned r = *(volatile unsigned *)b.pg.round + 1;
+    *b.pg.round = r;
+    __threadfence_system();
+    for (int q = 0; q < b.pg.world; q++) st_release_sys(b.pg.flags[q] + b.pg.rank, r);
+    const unsigned *mine = b.pg.flags[b.pg.rank];
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (int q = 0; q < b.pg.world; q++) {
+        for (long long it = 0; (int)(ld_acquire_sys(mine + q) - r) < 0; it++) {
+            if (it > 256) {
+                unsigned long long t;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                if (t - t0 > 1000000000ull) {  // one second
+                    atomicOr(&g_qmvb_status, 1u);
+                    return;
+                }
+                __nanosleep(128);
+            }
+        }
+    }
 }
 
 // Raises the instantiation's dynamic shared memory limit to SMEM_LIMIT on the current device
@@ -513,8 +564,14 @@ bool qmatvec_batch_supported(int n, const QMat *const *w) {
     return true;
 }
 
+unsigned qmatvec_status() {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_qmvb_status, sizeof v) != cudaSuccess) return ~0u;
+    return v;
+}
+
 void qmatvec_batch(int n, const QMat *const *w, const XQ *const *xq, float *const *out, cudaStream_t s,
-                   const ActIn *acts) {
+                   const ActIn *acts, const PeerGatherTail *tail) {
     if (!qmatvec_batch_supported(n, w)) {
         set_error("qmatvec_batch: 1..%d matrices of Q4_K / Q6_K", BATCH_MAX);
         return;
@@ -545,9 +602,19 @@ void qmatvec_batch(int n, const QMat *const *w, const XQ *const *xq, float *cons
         smem = std::max(smem, p.smem);
     }
     b.cta0[n] = grid;
-    static std::atomic<uint64_t> configured{0};
-    smem_limit_once(qmvb_kernel<T_Q4_K, T_Q6_K>, SMEM_LIMIT, configured);
-    launch(qmvb_kernel<T_Q4_K, T_Q6_K>, dim3(grid), THREADS, smem, s, b);
+    if (tail) {
+        b.gather = 1;
+        b.pg = *tail;
+    }
+    if (b.gather) {
+        static std::atomic<uint64_t> configured{0};
+        smem_limit_once(qmvb_kernel<T_Q4_K, T_Q6_K, true>, SMEM_LIMIT, configured);
+        launch(qmvb_kernel<T_Q4_K, T_Q6_K, true>, dim3(grid), THREADS, smem, s, b);
+    } else {
+        static std::atomic<uint64_t> configured{0};
+        smem_limit_once(qmvb_kernel<T_Q4_K, T_Q6_K, false>, SMEM_LIMIT, configured);
+        launch(qmvb_kernel<T_Q4_K, T_Q6_K, false>, dim3(grid), THREADS, smem, s, b);
+    }
     SDY_LAUNCHED();
 }
 

@@ -1,4 +1,6 @@
-"""sdy_allgather_p2p: the all-gather over NVLink peer memory between two processes (one GPU each).
+"""sdy_allgather_p2p: the all-gather over NVLink peer memory between two processes (one GPU each);
+and sdy_qmatvec_batch_f32_gather_dev, the grouped products with that all-gather fused into their
+launch (each rank's row slices of every matrix, gathered, equal the one-GPU products bit for bit).
 
 Each rank shares its buffer through a CUDA IPC handle (exchanged over a gloo group), then the ranks
 run rounds of the gather with new data each round: eagerly, then replayed from a CUDA graph (the
@@ -118,3 +120,104 @@ def test_allgather_over_peer_memory():
                 continue
             want = np.concatenate([_pattern(r, rnd, count) for r in range(world)])
             assert np.array_equal(value, want), (rank, count, rnd)
+
+
+def _fused_rank(rank, world, port, q):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        import oracle
+        from sardyne_b200 import capi
+        lib = capi.lib()
+        shapes = [("Q4_K", 1000, 2048), ("Q6_K", 304, 1024), ("Q4_K", 77, 256)]
+        # this rank's rows of each matrix (whole 8-row groups) and their place in the slice
+        ranges, offs, share = [], [], 0
+        for _, n_out, _ in shapes:
+            b, e = ctypes.c_int64(), ctypes.c_int64()
+            per = []
+            for r in range(world):
+                lib.sdy_shard_range(n_out, world, r, 8, ctypes.byref(b), ctypes.byref(e))
+                per.append((b.value, e.value))
+            ranges.append(per)
+            offs.append(share)
+            share += max(e - b for b, e in per)
+        nbytes = lib.sdy_allgather_p2p_bytes(share, world)
+        buf = lib.sdy_p2p_alloc(nbytes)
+        handle = (ctypes.c_char * 64)()
+        assert buf and lib.sdy_p2p_handle(buf, handle) == 0, capi.last_error()
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle))
+        bases = [buf if r == rank else lib.sdy_p2p_open((ctypes.c_char * 64).from_buffer_copy(handles[r]))
+                 for r in range(world)]
+        assert all(bases), capi.last_error()
+        hs, xs, full = [], [], []
+        for i, (kind, n_out, n_in) in enumerate(shapes):
+            w = oracle.random_blocks(kind, n_out * n_in // 256, seed=70 + i).reshape(n_out, -1)
+            full.append(w)
+            r0, r1 = ranges[i][rank]
+            part = np.ascontiguousarray(w[r0:r1])
+            h = lib.sdy_qmat_upload(part.ctypes.data, oracle.TYPE_ID[kind], r1 - r0, n_in)
+            assert h, capi.last_error()
+            hs.append(h)
+            xs.append(torch.from_numpy(np.random.default_rng(i).standard_normal(n_in).astype(np.float32)).cuda())
+        arr = lambda vals: (ctypes.c_void_p * len(vals))(*vals)  # noqa: E731
+        offa = (ctypes.c_int64 * len(shapes))(*offs)
+        stream = torch.cuda.Stream()
+        got = np.empty(world * share, np.float32)
+        for _ in range(3):  # rounds: every one must leave the whole gathered y
+            with torch.cuda.stream(stream):
+                assert lib.sdy_qmatvec_batch_f32_gather_dev(len(shapes), arr(hs), arr([x.data_ptr() for x in xs]),
+                                                            offa, share, arr(bases), rank, world,
+                                                            ctypes.c_void_p(stream.cuda_stream)) == 0, \
+                    capi.last_error()
+            stream.synchronize()
+            lib.sdy_p2p_read(got.ctypes.data, buf, got.nbytes)
+            dist.barrier()
+        status = lib.sdy_kernel_status()
+        # the one-GPU products of the full matrices, through the oracle
+        ok = True
+        for i, (kind, n_out, n_in) in enumerate(shapes):
+            xq = oracle.quantize(xs[i].cpu().numpy()[None], "Q8_K")
+            want = oracle.matmul_q(full[i], kind, xq, 1, n_in, n_out)[0]
+            for r in range(world):
+                b, e = ranges[i][r]
+                seg = got[r * share + offs[i]: r * share + offs[i] + (e - b)]
+                ok = ok and np.array_equal(seg, want[b:e])
+        for r, p in enumerate(bases):
+            if r != rank:
+                lib.sdy_p2p_close(p)
+        dist.barrier()
+        lib.sdy_p2p_free(buf)
+        for h in hs:
+            lib.sdy_qmat_free(h)
+        q.put((rank, (ok, status)))
+    except Exception as e:
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_products_with_fused_allgather():
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_fused_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(60)
+    for rank in range(world):
+        assert not isinstance(got[rank], str), got[rank]
+        assert got[rank] == (True, 0), got[rank]
