@@ -313,6 +313,28 @@ void op_matmul(float *out, const float *x, const void *w, int wtype, int n_tok, 
     if (!dx || !dq) return;
     XQ q = xq_carve(dq, vt, n_in, n_tok);
     if (!SDY_CUDA(cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, s->st))) return;
+    const int gmin = gemm_min_tokens();
+    if (gmin <= 0 || n_tok < gmin) {
+        // below the tensor-core route: one launch, every CTA quantizing its tokens' rows itself
+        // (the same bytes as quantize_rows), so a call is copy in, one kernel, copy out
+        QMat m;
+        int64_t first;
+        if (!weights_view(s, w, wtype, n_in, 0, n_out, &m, &first)) return;
+        // a pinned (page-locked, mapped) output buffer is written by the kernel itself, during
+        // the kernel, instead of by a copy after it
+        cudaPointerAttributes at{};
+        const bool direct = cudaPointerGetAttributes(&at, out) == cudaSuccess && at.type == cudaMemoryTypeHost &&
+                            at.devicePointer != nullptr;
+        if (!direct) cudaGetLastError();  // a plain host pointer: not an error
+        float *dout = direct ? (float *)at.devicePointer : (float *)s->b[5].get((size_t)n_out * n_tok * 4);
+        if (!dout) return;
+        const ActIn act{dx, n_in};
+        qmatvec(m, q, dout, n_out, first, first + n_out, first, s->st, nullptr, &act);
+        if (!direct)
+            SDY_CUDA(cudaMemcpyAsync(out, dout, (size_t)n_out * n_tok * 4, cudaMemcpyDeviceToHost, s->st));
+        sync(s);
+        return;
+    }
     quantize_rows(vt, dx, n_in, n_tok, n_in, q, s->st);
     run_qmatvec(s, q, w, wtype, n_tok, n_in, n_out, 0, n_out, out);
 }

@@ -161,6 +161,24 @@ def test_op_matmul_quantizes_like_the_reference(kind):
     assert np.array_equal(out, oracle.matmul_q(w, kind, xq, n_tok, n_in, n_out))
 
 
+@pytest.mark.parametrize("kind", ["Q4_K", "Q6_K", "Q5_0"])
+def test_op_matmul_into_pinned_output(kind):
+    """A page-locked output buffer is written by the kernel itself (no copy after it): same bits,
+    and a pageable buffer next to it still gets the copy."""
+    import torch
+    n_in, n_out, n_tok = 2048, 1000, 2
+    w = oracle.random_blocks(kind, n_out * n_in // oracle.QK[kind], seed=13)
+    x = np.random.default_rng(13).standard_normal((n_tok, n_in)).astype(np.float32)
+    want = oracle.matmul_q(w, kind, oracle.quantize(x, oracle.VEC_DOT_TYPE[kind]), n_tok, n_in, n_out)
+    pinned = torch.full((n_tok, n_out), float("nan")).pin_memory()
+    for _ in range(2):
+        lib().op_matmul(ctypes.c_void_p(pinned.data_ptr()), ptr(x), ptr(w), TID[kind], n_tok, n_in, n_out)
+        assert np.array_equal(pinned.numpy(), want)
+    plain = np.full((n_tok, n_out), np.nan, np.float32)
+    lib().op_matmul(ptr(plain), ptr(x), ptr(w), TID[kind], n_tok, n_in, n_out)
+    assert np.array_equal(plain, want)
+
+
 @pytest.mark.parametrize("kind", KINDS)
 def test_registered_weights_read_in_place(kind):
     """Resident weights (sdy_weights_register) give the same bits as staged weights, for any
