@@ -257,7 +257,7 @@ bool qmatvec_batch_supported(int n, const QMat *const *w);
 // it itself; xq[i] then gives the activation geometry only.
 // tail set (processes that drive one GPU each): every output value is also stored at byte offset
 // delta[q] from its local address, in the peers' buffers (an all-gather over NVLink fused into the
-// launch); the last CTA then release-stores the next round into flags[q][rank] of every rank and
+// launch); the last CTA then, after one system fence, stores the next round into flags[q][rank] of every rank and
 // waits (acquire, at most one second) until its own flags show it from every rank. The buffer
 // layout and round protocol are those of sdy_allgather_p2p (p2p.cu).
 struct PeerGatherTail {
@@ -283,8 +283,8 @@ void qmatvec_gather(const QMat &experts, int64_t gpe, int n_expert, const XQ &xq
 // peer_gather assembles in `recv` the rows x ld floats of which each rank computed a disjoint part
 // in its own `send`: columns [lo, hi) of every row, and with `top` set only the rows j with
 // e0 <= top[j] < e1 (MoE slots of this rank's experts; the parts of all ranks must cover every
-// element). Each rank stores its part into every rank's staging area; the last CTA then
-// release-stores the round number into every rank's flag for this rank, and every CTA waits (at
+// element). Each rank stores its part into every rank's staging area; the last CTA then, after
+// one system fence, stores the round number into every rank's flag for this rank, and every CTA waits (at
 // most px.wait_ns, acquire loads) for all ranks' flags before copying the staging area to
 // `recv`. Two staging halves alternate by round, so a rank can run one exchange ahead of another.
 // All ranks make the same sequence of calls (eager or replayed from a graph; the round counter

@@ -12,10 +12,10 @@
 // sdy_p2p_alloc zeroes the buffer; every rank must make the same sequence of sdy_allgather_p2p
 // calls (eagerly or replayed from a CUDA graph).
 //
-// Ordering. Every thread fences its peer stores system-wide before its CTA counts itself done; the
-// last CTA then advances the round counter, release-stores it into flag `rank` of every peer and
-// waits (acquire loads, at most one second) until every peer's flag in its own buffer shows the
-// round. When
+// Ordering. Each CTA's peer stores are fenced system-wide (thread 0, after a barrier) before the
+// CTA counts itself done; the last CTA then advances the round counter and, after one more system
+// fence, stores it into flag `rank` of every peer, and waits (acquire loads, at most one second)
+// until every peer's flag in its own buffer shows the round. When
 // the kernel ends, the local buffer holds every rank's slice of this round. A wait that runs out
 // sets the status word (sdy_p2p_status) and returns.
 #include "common.cuh"
@@ -45,8 +45,10 @@ struct Gather {
 
 size_t flags_offset(int64_t count, int world) { return align_up((size_t)world * count * 4, 256); }
 
-__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+// A flag store after one system fence (fence + relaxed store is a release): a st.release.sys per
+// peer flag costs about a whole system fence each, measured ~3 us apiece over NVLink.
+__device__ __forceinline__ void st_relaxed_sys(unsigned *p, unsigned v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
     unsigned v;
@@ -69,16 +71,20 @@ __global__ void __launch_bounds__(P2P_THREADS) allgather_kernel(Gather g) {
             for (int64_t i = tid; i < g.count; i += nth) dst[i] = g.send[i];
         }
     }
-    __threadfence_system();
+    // the CTA's stores ordered before its arrival: one system fence by thread 0 after the barrier
+    // (the barrier makes them observed by thread 0, whose fence is cumulative)
     __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(g.done, 1u) == gridDim.x - 1;
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        last = atomicAdd(g.done, 1u) == gridDim.x - 1;
+    }
     __syncthreads();
     if (!last || threadIdx.x != 0) return;
     *g.done = 0;
     const unsigned r = *g.round + 1;
     *g.round = r;
-    __threadfence_system();
-    for (int q = 0; q < g.world; q++) st_release_sys(g.flags[q] + g.rank, r);
+    __threadfence_system();  // every CTA's stores (each fenced before arriving) before the flags
+    for (int q = 0; q < g.world; q++) st_relaxed_sys(g.flags[q] + g.rank, r);
     const unsigned *mine = g.flags[g.rank];
     unsigned long long t0;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
@@ -163,10 +169,10 @@ __global__ void __launch_bounds__(PX_THREADS) peer_gather_kernel(PxArgs a) {
     }
     __syncthreads();
     if (last && threadIdx.x == 0) {
-        __threadfence_system();
         *a.done = 0;
         *a.round = r;
-        for (int q = 0; q < a.world; q++) st_release_sys(a.flags[q] + a.rank, r);
+        __threadfence_system();  // every CTA's stores (each fenced before arriving) before the flags
+        for (int q = 0; q < a.world; q++) st_relaxed_sys(a.flags[q] + a.rank, r);
     }
     // every rank's part of this round has arrived once all flags show it
     if (threadIdx.x < a.world) {

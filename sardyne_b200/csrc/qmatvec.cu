@@ -213,8 +213,9 @@ struct BatchArgs {
 };
 
 __device__ unsigned g_qmvb_status;
-__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+// flag store after one system fence (see p2p.cu: a st.release.sys per flag costs a fence each)
+__device__ __forceinline__ void st_relaxed_sys(unsigned *p, unsigned v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
     unsigned v;
@@ -242,12 +243,11 @@ __global__ void __launch_bounds__(THREADS) qmvb_kernel(const __grid_constant__ B
     }
     __syncthreads();
     if (!last || threadIdx.x != 0) return;
-    __threadfence_system();
     *b.pg.done = 0;
     const unsigned r = *(volatile unsigned *)b.pg.round + 1;
     *b.pg.round = r;
-    __threadfence_system();
-    for (int q = 0; q < b.pg.world; q++) st_release_sys(b.pg.flags[q] + b.pg.rank, r);
+    __threadfence_system();  // every CTA's stores (each fenced before arriving) before the flags
+    for (int q = 0; q < b.pg.world; q++) st_relaxed_sys(b.pg.flags[q] + b.pg.rank, r);
     const unsigned *mine = b.pg.flags[b.pg.rank];
     unsigned long long t0;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
