@@ -48,3 +48,27 @@ def test_reference_symbol_table_is_covered():
         pytest.skip("the reference's Python package is not installed here")
     names = set(re.findall(r'"((?:engine|gguf|op)_[a-z0-9_]+)":', ref.read_text()))
     assert names and names <= set(capi.SIGNATURES)
+
+
+def test_grouped_and_exchange_entry_points_reject_bad_arguments():
+    """Argument checks of the grouped products, the fused gather and the exchanges return -1 with a
+    message before any CUDA call (so they run without a GPU)."""
+    lib = capi.lib()
+    vp = ctypes.c_void_p
+    none = (vp * 1)()
+    for n in (0, 9):
+        assert lib.sdy_qmatvec_batch_f32_dev(n, none, none, none, None) == -1
+        assert "1..8 products" in capi.last_error()
+        assert lib.sdy_qmatvec_batch_dev(n, none, none, none, None) == -1
+    offs = (ctypes.c_int64 * 1)(0)
+    bases = (vp * 9)()
+    for count, rank, world in ((16, 0, 9), (16, 2, 2), (0, 0, 2), (16, -1, 2)):
+        assert lib.sdy_qmatvec_batch_f32_gather_dev(1, none, none, offs, count, bases, rank, world, None) == -1
+        assert "bad arguments" in capi.last_error()
+    assert lib.sdy_qmatvec_batch_f32_gather_dev(1, (vp * 1)(1), (vp * 1)(16), offs, 16, bases, 0, 2, None) == -1
+    assert "buffer of rank 0 missing" in capi.last_error()
+    assert lib.sdy_allgather_p2p_bytes(100, 9) == 0 and lib.sdy_allgather_p2p_bytes(100, 0) == 0
+    assert lib.sdy_allgather_p2p_bytes(100, 2) >= 2 * 100 * 4
+    assert lib.sdy_allgather_p2p(None, 16, bases, 0, 2, None) == -1
+    assert lib.sdy_engine_exchange(None) == -1
+    lib.sdy_clear_error()
