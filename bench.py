@@ -58,7 +58,7 @@ def act_type(fmt):
     """The activation layout a weight format multiplies with (quant.c: vec_dot_type)."""
     return "Q8_0" if fmt in FORMATS32 else "Q8_K"
 WORKLOAD = ("BASELINE config 2 at batch 1: Q4_K and Q6_K matvec over 2048x11008, 11008x2048 and "
-            "151936x2048 ([n_out][n_in]), f32 inputs resident, quantized to Q8_K inside the grouped launch")
+            "151936x2048 ([n_out][n_in]), f32 inputs quantized to Q8_K (quant_q8_K) for the products")
 
 
 def log(*a):
