@@ -108,3 +108,22 @@ def test_attention_split_covers_every_head_once(n_head, n_kv, hd, world):
     assert len(modes) == 1  # every rank agrees on split or replicated
     if modes == {1}:
         assert owners == [1] * n_head
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sweep_slices_fit_the_fused_gather(world):
+    """bench.py's multi-GPU sweep: every rank's row slice of every matrix (whole 8-row groups)
+    fits its place in the per-rank gather slice (out_off[i] + rows <= count, the check
+    sdy_qmatvec_batch_f32_gather_dev makes), and the slices of all ranks cover every row once."""
+    import bench
+    share, offs = 0, []
+    for _, n_out, _ in [(f, o, i) for f in bench.FORMATS for o, i in bench.SHAPES]:
+        per = [bench.shard_rows(n_out, r, world) for r in range(world)]
+        assert per[0][0] == 0 and per[-1][1] == n_out
+        assert all(per[r][1] == per[r + 1][0] for r in range(world - 1))
+        assert all(b % 8 == 0 for b, _ in per)
+        offs.append((share, max(e - b for b, e in per), per))
+        share += max(e - b for b, e in per)
+    for off, width, per in offs:
+        for b, e in per:
+            assert off + (e - b) <= share and e - b <= width
