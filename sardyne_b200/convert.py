@@ -9,9 +9,11 @@ models use (sardyne_b200.synth.q4_k_m: Q4_K by default, Q6_K on attn_v, on the f
 layers and on the output matrix; rows that are not whole 256-element superblocks fall back to Q5_0
 and Q8_0), and Qwen3-MoE checkpoints (the experts' matrices stacked into the GGUF expert tensors).
 It follows the GGUF conventions the engine reads (tensor names, metadata keys, llama's q/k rows
-reordered for RoPE on adjacent pairs); norms, biases and the MoE router stay F32. Tokenizer
-metadata is not written (the engine does not read it). Tensors are read, converted and written one
-at a time.
+reordered for RoPE on adjacent pairs); norms, biases and the MoE router stay F32. When the
+directory holds a byte-level BPE tokenizer.json, the tokenizer goes into the file under the keys
+the reference's text front-ends read (tokens, token types, merges, pre-tokenizer name, chat
+template; reference sardyne/loader/convert.py:105-116), so its CLI and server run on the result.
+Tensors are read, converted and written one at a time.
 """
 import argparse
 import json
@@ -22,7 +24,7 @@ import struct
 import numpy as np
 
 from . import kquant, synth
-from .gguf_writer import GGUFWriter, f32_to_bf16
+from .gguf_writer import ARRAY, I32, STRING, GGUFWriter, f32_to_bf16
 
 ARCHS = {"LlamaForCausalLM": "llama", "Qwen2ForCausalLM": "qwen2", "Qwen3ForCausalLM": "qwen3",
          "Qwen3MoeForCausalLM": "qwen3moe"}
@@ -54,6 +56,50 @@ MODEL_TENSORS = (("model.embed_tokens.weight", "token_embd.weight"), ("model.nor
                  ("lm_head.weight", "output.weight"))
 
 _ST_DTYPES = {"F32": np.float32, "F16": np.float16, "BF16": np.uint16, "F64": np.float64}
+
+# GGUF token types (the llama.cpp numbering the reference's tokenizer reads)
+TOKEN_NORMAL, TOKEN_CONTROL, TOKEN_USER_DEFINED, TOKEN_UNUSED = 1, 3, 4, 5
+
+
+def pretokenizer_name(t: dict) -> str:
+    """tokenizer.ggml.pre for the pre-tokenizers the reference reproduces: a regex split then byte
+    level with NFC normalization ("qwen2"), or single digits then byte level without a normalizer
+    ("smollm"). (The split's regex itself is not compared.)"""
+    steps = (t.get("pre_tokenizer") or {}).get("pretokenizers", [])
+    kinds = [s.get("type") for s in steps]
+    norm = (t.get("normalizer") or {}).get("type")
+    if kinds == ["Split", "ByteLevel"] and "Regex" in (steps[0].get("pattern") or {}) and norm == "NFC":
+        return "qwen2"
+    if kinds == ["Digits", "ByteLevel"] and steps[0].get("individual_digits") and norm is None:
+        return "smollm"
+    raise NotImplementedError(f"pre-tokenizer {kinds} with normalizer {norm} is not supported")
+
+
+def tokenizer_fields(hf_dir: pathlib.Path, vocab_size: int) -> dict:
+    """The GGUF tokenizer keys of a byte-level BPE tokenizer.json: one token per id up to the
+    model's vocabulary size (vocabulary entries NORMAL, added tokens CONTROL when special else
+    USER_DEFINED, ids no entry names "[PAD<id>]" and UNUSED), merges as "left right" strings, and
+    the chat template of tokenizer_config.json when there is one."""
+    t = json.loads((hf_dir / "tokenizer.json").read_text(encoding="utf-8"))
+    model = t.get("model") or {}
+    if model.get("type") != "BPE":
+        raise NotImplementedError(f"tokenizer model {model.get('type')} is not supported")
+    text, kind = {}, {}
+    for tok, i in model["vocab"].items():
+        text[i], kind[i] = tok, TOKEN_NORMAL
+    for a in t.get("added_tokens", []):
+        text[a["id"]] = a["content"]
+        kind[a["id"]] = TOKEN_CONTROL if a.get("special") else TOKEN_USER_DEFINED
+    n = max(vocab_size, max(text) + 1)
+    fields = {"tokenizer.ggml.model": "gpt2", "tokenizer.ggml.pre": pretokenizer_name(t),
+              "tokenizer.ggml.tokens": [text.get(i, f"[PAD{i}]") for i in range(n)],
+              "tokenizer.ggml.token_type": [kind.get(i, TOKEN_UNUSED) for i in range(n)],
+              "tokenizer.ggml.merges": [m if isinstance(m, str) else " ".join(m) for m in model.get("merges", [])]}
+    cfg_path = hf_dir / "tokenizer_config.json"
+    cfg = json.loads(cfg_path.read_text(encoding="utf-8")) if cfg_path.exists() else {}
+    if cfg.get("chat_template"):
+        fields["tokenizer.chat_template"] = cfg["chat_template"]
+    return fields
 
 
 class SafeTensors:
@@ -177,6 +223,14 @@ def convert(hf_dir, out_path, outtype: str = "q4_k_m") -> pathlib.Path:
         v = v[0] if isinstance(v, list) and v else v
         if isinstance(v, int):
             w.add(gkey, v)
+    if (hf_dir / "tokenizer.json").exists():
+        for key, value in tokenizer_fields(hf_dir, cfg["vocab_size"]).items():
+            if key == "tokenizer.ggml.token_type":
+                w.add(key, value, ARRAY, I32)
+            elif isinstance(value, list):
+                w.add(key, value, ARRAY, STRING)
+            else:
+                w.add(key, value)
 
     def add(gguf_name, shape, load):
         kind = block_type(gguf_name, shape[-1], outtype, tied)

@@ -98,6 +98,12 @@ def read_gguf(path):
             if kv.type == 8:
                 n = ctypes.c_uint64()
                 kvs[key] = ctypes.string_at(lib.gguf_kv_get_str(h, i, ctypes.byref(n)), n.value).decode()
+            elif kv.type == 9 and kv.arr_type == 8:  # array of strings
+                n = ctypes.c_uint64()
+                kvs[key] = [ctypes.string_at(lib.gguf_kv_get_arr_str(h, i, j, ctypes.byref(n)), n.value).decode()
+                            for j in range(kv.n)]
+            elif kv.type == 9:  # array of 4-byte integers
+                kvs[key] = (kv.arr_type, ctypes.string_at(kv.ptr, 4 * kv.n))
             else:
                 v = ctypes.c_double()
                 u = ctypes.c_uint64()
@@ -167,3 +173,53 @@ def test_reference_engine_runs_the_conversion(tmp_path, arch, tied, min_corr):
     a, b = out["f32"].ravel(), out["q4_k_m"].ravel()
     assert np.isfinite(b).all()
     assert np.corrcoef(a, b)[0, 1] > min_corr
+
+
+def write_tokenizer(directory, style, split_regex=None):
+    """A small byte-level BPE tokenizer.json (+ tokenizer_config.json) of the two pre-tokenizer
+    styles the reference's converter accepts."""
+    vocab = {t: i for i, t in enumerate(["a", "b", "c", "ab", "abc", "\u0120", "\u0120a", "1", "2", "x"])}
+    merges = [["a", "b"], ["ab", "c"], ["\u0120", "a"]]
+    if style == "qwen2":
+        pre = {"type": "Sequence", "pretokenizers": [
+            {"type": "Split", "pattern": {"Regex": split_regex}, "behavior": "Isolated", "invert": False},
+            {"type": "ByteLevel", "add_prefix_space": False, "trim_offsets": False, "use_regex": False}]}
+        norm = {"type": "NFC"}
+        merges = [" ".join(m) for m in merges]
+    else:
+        pre = {"type": "Sequence", "pretokenizers": [
+            {"type": "Digits", "individual_digits": True},
+            {"type": "ByteLevel", "add_prefix_space": False, "trim_offsets": True, "use_regex": True}]}
+        norm = None
+    tok = {"version": "1.0", "added_tokens": [
+        {"id": 10, "content": "<|endoftext|>", "special": True},
+        {"id": 12, "content": "<tool>", "special": False}],
+        "normalizer": norm, "pre_tokenizer": pre,
+        "model": {"type": "BPE", "vocab": vocab, "merges": merges}}
+    (directory / "tokenizer.json").write_text(json.dumps(tok))
+    if style == "qwen2":
+        (directory / "tokenizer_config.json").write_text(json.dumps(
+            {"chat_template": "{% for m in messages %}{{ m['content'] }}{% endfor %}"}))
+
+
+@pytest.mark.skipif(not rt.available(), reason="the reference's Python package is not installed")
+@pytest.mark.parametrize("arch,tied,style", [("qwen2", False, "qwen2"), ("llama", True, "smollm")])
+def test_tokenizer_metadata_equals_the_reference_converter(tmp_path, arch, tied, style):
+    """With a tokenizer.json beside the checkpoint, every tokenizer.* key (tokens with [PADn] up to
+    the model's vocabulary, token types, merges, pre-tokenizer name, chat template) equals the
+    reference's converter's (sardyne/loader/convert.py:105-116)."""
+    rt.modules()
+    from sardyne.loader import convert as ref_convert  # the reference's converter
+    from sardyne.tokenizer import bpe as ref_bpe       # its pre-tokenizer regex, for the fixture
+    ck = checkpoint(tmp_path, arch, tied)
+    write_tokenizer(ck, style, ref_bpe._QWEN2)
+    _, akv = read_gguf(convert.convert(ck, tmp_path / "ours.gguf", "q4_k_m"))
+    ref_convert.convert(ck, tmp_path / "ref.gguf", "f32")
+    _, bkv = read_gguf(tmp_path / "ref.gguf")
+    want = {k: v for k, v in bkv.items() if k.startswith("tokenizer.")}
+    assert {"tokenizer.ggml.tokens", "tokenizer.ggml.token_type", "tokenizer.ggml.merges",
+            "tokenizer.ggml.pre"} <= set(want)
+    assert len(want["tokenizer.ggml.tokens"]) == 96 and want["tokenizer.ggml.tokens"][95] == "[PAD95]"
+    for key, value in want.items():
+        assert akv.get(key) == value, key
+    assert set(k for k in akv if k.startswith("tokenizer.")) == set(want)
