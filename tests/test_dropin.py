@@ -8,6 +8,11 @@ with the reference's message here; a valid one is refused on a machine without a
 engine tests drive the same runtime end to end (tests/test_gpu_engine.py,
 tests/test_gpu_baseline_shapes.py).
 """
+import os
+import pathlib
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 
@@ -55,3 +60,25 @@ def test_reference_runtime_on_a_valid_model(tmp_path):
     else:
         with pytest.raises(ValueError, match="GPU"):
             rt.model(path)
+
+
+def _reference_tests():
+    root = os.environ.get("SARDYNE_REFERENCE")
+    return pathlib.Path(root) / "tests" if root else None
+
+
+@pytest.mark.skipif(not (_reference_tests() and (_reference_tests() / "test_gguf.py").exists()),
+                    reason="set SARDYNE_REFERENCE to the reference's source tree")
+def test_reference_gguf_and_capi_tests_pass_on_this_library(tmp_path):
+    """The reference's own tests/test_gguf.py and tests/test_capi.py, unmodified, with SARDYNE_LIB
+    naming this build. Their C-reader cases go through this library's gguf_* functions: round trips,
+    custom alignment, truncated, corrupted and bad-magic/version files, the rejection rules shared
+    with the Python reader, the error messages and the binding's lifecycle. Excluded: test_capi's
+    `add`, which computes on a GPU, and the cases that need downloaded models, which skip."""
+    tests = _reference_tests()
+    env = dict(os.environ, SARDYNE_LIB=str(rt.b200_lib()), PYTHONPATH=str(tests.parent), PYTHONDONTWRITEBYTECODE="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", str(tests / "test_gguf.py"), str(tests / "test_capi.py"),
+                        "-k", "not add_matches", "-q", "-p", "no:cacheprovider"],
+                       cwd=tmp_path, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
+    assert " passed" in r.stdout and " failed" not in r.stdout, r.stdout[-2000:]
