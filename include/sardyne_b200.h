@@ -133,9 +133,12 @@ const char *sdy_last_error(void);
 void sdy_clear_error(void);
 /* Number of GPU kernels this process has launched through the library (for launch counting). */
 uint64_t sdy_kernel_launches(void);
-/* Nonzero when a kernel's bounded wait on its tensor-core completion barrier ran out (the kernel
- * then skipped its output and freed its tensor memory); synchronises the device. */
+/* Nonzero when a kernel's bounded wait ran out: a tensor-core completion barrier (the kernel then
+ * skipped its output and freed its tensor memory) or a fused gather's wait for the other ranks
+ * (sdy_qmatvec_batch_f32_gather_dev). Stays set until sdy_kernel_clear_status; synchronises the
+ * device. */
 uint32_t sdy_kernel_status(void);
+void sdy_kernel_clear_status(void);
 
 /* Sharding across processes, one GPU each (no counterpart in the reference, which runs on one
  * host). sdy_nccl_unique_id writes the 128-byte NCCL id rank 0 creates and shares with the other

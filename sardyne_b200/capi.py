@@ -102,6 +102,7 @@ EXTENSIONS = {
     "sdy_clear_error": (None, []),
     "sdy_kernel_launches": (_u64, []),
     "sdy_kernel_status": (ctypes.c_uint32, []),
+    "sdy_kernel_clear_status": (None, []),
     "sdy_nccl_unique_id": (_i, [_vp]),
     "sdy_engine_set_shard": (_i, [ctypes.c_int32, ctypes.c_int32, _vp]),
     "sdy_engine_get_shard": (None, [ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]),

@@ -233,6 +233,7 @@ bool qgemm_supported(int type, int n_in);
 void qgemm(const QMat &w, const XQ &xq, float *out, int64_t ldo, int64_t row0, int64_t row1, int64_t out_row0,
            cudaStream_t s, const float *residual = nullptr, bool split_ok = true);
 unsigned qgemm_status();  // nonzero when a qgemm completion wait timed out
+void qgemm_clear_status();
 // Grouped experts on the tensor cores (MoE prefill): for local expert e, the slots
 // grp_slot[grp_off[e] .. grp_off[e+1]) (device arrays from moe_group with tile GEMM_TILE_TOKENS;
 // at most max_slots in all) multiply expert e with activation row slot / xdiv into
@@ -270,6 +271,7 @@ struct PeerGatherTail {
 void qmatvec_batch(int n, const QMat *const *w, const XQ *const *xq, float *const *out, cudaStream_t s,
                    const ActIn *acts = nullptr, const PeerGatherTail *tail = nullptr);
 unsigned qmatvec_status();  // nonzero when a fused gather's wait gave up
+void qmatvec_clear_status();
 // MoE: for each slot s < n_slots, out[s*ldo_slot + r] = E[slot_expert[s]][r] . x[s / tok_div] for
 // r < rows_per_expert. `experts` holds n_expert matrices (global experts expert0 .. expert0 +
 // n_expert - 1), each padded to gpe groups; slots naming other experts are left untouched. The

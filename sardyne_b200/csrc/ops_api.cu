@@ -159,6 +159,11 @@ void sdy_clear_error(void) { clear_error(); }
 uint64_t sdy_kernel_launches(void) { return g_launches.load(); }
 uint32_t sdy_kernel_status(void) { return qgemm_status() | qmatvec_status(); }
 
+void sdy_kernel_clear_status(void) {
+    qgemm_clear_status();
+    qmatvec_clear_status();
+}
+
 static int g_simd = 1;
 int op_simd(void) { return g_simd; }
 int op_set_simd(int enable) {

@@ -852,4 +852,9 @@ unsigned qgemm_status() {
     return v;
 }
 
+void qgemm_clear_status() {
+    const unsigned z = 0;
+    SDY_CUDA(cudaMemcpyToSymbol(g_qgemm_status, &z, sizeof z));
+}
+
 }  // namespace sdy

@@ -570,6 +570,11 @@ unsigned qmatvec_status() {
     return v;
 }
 
+void qmatvec_clear_status() {
+    const unsigned z = 0;
+    SDY_CUDA(cudaMemcpyToSymbol(g_qmvb_status, &z, sizeof z));
+}
+
 void qmatvec_batch(int n, const QMat *const *w, const XQ *const *xq, float *const *out, cudaStream_t s,
                    const ActIn *acts, const PeerGatherTail *tail) {
     if (!qmatvec_batch_supported(n, w)) {
