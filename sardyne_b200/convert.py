@@ -60,15 +60,22 @@ _ST_DTYPES = {"F32": np.float32, "F16": np.float16, "BF16": np.uint16, "F64": np
 # GGUF token types (the llama.cpp numbering the reference's tokenizer reads)
 TOKEN_NORMAL, TOKEN_CONTROL, TOKEN_USER_DEFINED, TOKEN_UNUSED = 1, 3, 4, 5
 
+# The split pattern of Qwen2's byte-level BPE tokenizer.json (a published format constant); the
+# reference's tokenizer reproduces exactly this pattern under the name "qwen2"
+# (sardyne/tokenizer/bpe.py:28-29).
+QWEN2_SPLIT = ("(?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\\r\\n\\p{L}\\p{N}]?\\p{L}+|\\p{N}| ?[^\\s\\p{L}\\p{N}]+[\\r\\n]*"
+               "|\\s*[\\r\\n]+|\\s+(?!\\S)|\\s+")
+
 
 def pretokenizer_name(t: dict) -> str:
-    """tokenizer.ggml.pre for the pre-tokenizers the reference reproduces: a regex split then byte
-    level with NFC normalization ("qwen2"), or single digits then byte level without a normalizer
-    ("smollm"). (The split's regex itself is not compared.)"""
+    """tokenizer.ggml.pre for the pre-tokenizers the reference reproduces (sardyne/tokenizer/bpe.py:
+    192-201): Qwen2's regex split then byte level with NFC normalization ("qwen2"), or single digits
+    then byte level without a normalizer ("smollm"); anything else is refused."""
     steps = (t.get("pre_tokenizer") or {}).get("pretokenizers", [])
     kinds = [s.get("type") for s in steps]
     norm = (t.get("normalizer") or {}).get("type")
-    if kinds == ["Split", "ByteLevel"] and "Regex" in (steps[0].get("pattern") or {}) and norm == "NFC":
+    if kinds == ["Split", "ByteLevel"] and (steps[0].get("pattern") or {}).get("Regex") == QWEN2_SPLIT \
+            and norm == "NFC":
         return "qwen2"
     if kinds == ["Digits", "ByteLevel"] and steps[0].get("individual_digits") and norm is None:
         return "smollm"

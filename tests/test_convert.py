@@ -210,9 +210,10 @@ def test_tokenizer_metadata_equals_the_reference_converter(tmp_path, arch, tied,
     reference's converter's (sardyne/loader/convert.py:105-116)."""
     rt.modules()
     from sardyne.loader import convert as ref_convert  # the reference's converter
-    from sardyne.tokenizer import bpe as ref_bpe       # its pre-tokenizer regex, for the fixture
+    from sardyne.tokenizer import bpe as ref_bpe       # its pre-tokenizer regex
+    assert convert.QWEN2_SPLIT == ref_bpe._QWEN2
     ck = checkpoint(tmp_path, arch, tied)
-    write_tokenizer(ck, style, ref_bpe._QWEN2)
+    write_tokenizer(ck, style, convert.QWEN2_SPLIT)
     _, akv = read_gguf(convert.convert(ck, tmp_path / "ours.gguf", "q4_k_m"))
     ref_convert.convert(ck, tmp_path / "ref.gguf", "f32")
     _, bkv = read_gguf(tmp_path / "ref.gguf")
@@ -223,3 +224,26 @@ def test_tokenizer_metadata_equals_the_reference_converter(tmp_path, arch, tied,
     for key, value in want.items():
         assert akv.get(key) == value, key
     assert set(k for k in akv if k.startswith("tokenizer.")) == set(want)
+
+
+@pytest.mark.skipif(not rt.available(), reason="the reference's Python package is not installed")
+def test_unsupported_pretokenizers_are_refused_like_the_reference(tmp_path):
+    """A split regex other than Qwen2's, or a tokenizer model other than BPE, is refused by both
+    converters (sardyne/tokenizer/bpe.py:104-105,192-201) instead of being written under a
+    pre-tokenizer name that would tokenize differently."""
+    rt.modules()
+    from sardyne.loader import convert as ref_convert
+    ck = checkpoint(tmp_path, "qwen2", False)
+    write_tokenizer(ck, "qwen2", r"\p{L}+|\s+")
+    with pytest.raises(NotImplementedError):
+        convert.convert(ck, tmp_path / "ours.gguf", "f32")
+    assert not list(tmp_path.glob("ours.gguf*"))  # nothing written, not even a temporary file
+    with pytest.raises(NotImplementedError):
+        ref_convert.convert(ck, tmp_path / "ref.gguf", "f32")
+    tok = json.loads((ck / "tokenizer.json").read_text())
+    tok["model"]["type"] = "Unigram"
+    (ck / "tokenizer.json").write_text(json.dumps(tok))
+    with pytest.raises(NotImplementedError):
+        convert.convert(ck, tmp_path / "ours.gguf", "f32")
+    with pytest.raises(NotImplementedError):
+        ref_convert.convert(ck, tmp_path / "ref.gguf", "f32")
