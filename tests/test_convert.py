@@ -224,6 +224,15 @@ def test_tokenizer_metadata_equals_the_reference_converter(tmp_path, arch, tied,
     for key, value in want.items():
         assert akv.get(key) == value, key
     assert set(k for k in akv if k.startswith("tokenizer.")) == set(want)
+    # the reference's text front-end reads the file: its tokenizer loaded from our GGUF encodes like
+    # the same tokenizer loaded from tokenizer.json (special tokens, digits, spaces, unknown bytes)
+    from sardyne.tokenizer.bpe import BPETokenizer
+    ours = BPETokenizer.load(model=tmp_path / "ours.gguf")
+    hf = BPETokenizer.load(hf_dir=ck)
+    assert ours.pre == hf.pre == style and ours.eos_ids == hf.eos_ids
+    for text in ["abc ab a", "a12 cab<|endoftext|>abc<tool> x", " a  abc\nb", "zz\u00e9 12"]:
+        assert ours.encode(text) == hf.encode(text), text
+        assert ours.decode(ours.encode(text)) == hf.decode(hf.encode(text))
 
 
 @pytest.mark.skipif(not rt.available(), reason="the reference's Python package is not installed")
