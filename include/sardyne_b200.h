@@ -235,8 +235,7 @@ void sdy_p2p_clear_status(void);
  * array inside the library (held by every GPU that loads it until exit): requests that need
  * more (sdy_xq_bytes(vtype, n_in, n_tok) > 512 KiB; for 16384-element rows, more than 26 tokens)
  * return -1 with a message and launch nothing. The first call on a device looks up the array's
- * address with that device current and keeps it: make it before any stream capture, and do not
- * reset the device afterwards. All calls on a device share the array: calls whose GPU work may
+ * address with that device current and keeps it: do not reset the device afterwards. All calls on a device share the array: calls whose GPU work may
  * overlap (unordered streams) race. 0 or -1 (sdy_last_error). */
 int sdy_qmatvec_f32_noalloc(const void *w, const float *d_x, int n_tok, float *d_out, int64_t ldo, int64_t row0,
                             int64_t row1, void *stream);

@@ -16,9 +16,8 @@
 //     16384-element rows that is 26 tokens); larger requests fail with -1 and a message in
 //     sdy_last_error, before anything is launched;
 //   * the first call on a device looks up the array's device address (cudaGetSymbolAddress)
-//     with that device current and keeps it for the process: make that first call before any
-//     stream capture begins, and do not reset the device (cudaDeviceReset) afterwards, since
-//     the kept address would then be stale;
+//     with that device current and keeps it for the process: do not reset the device
+//     (cudaDeviceReset) afterwards, since the kept address would then be stale;
 //   * every call on a device shares the one array, so calls whose GPU work overlaps in time
 //     (different streams, no ordering between them) race on it and must not be issued;
 //   * the array keeps whatever the last call left there. Nothing needs clearing: each call
