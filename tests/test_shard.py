@@ -127,3 +127,53 @@ def test_sweep_slices_fit_the_fused_gather(world):
     for off, width, per in offs:
         for b, e in per:
             assert off + (e - b) <= share and e - b <= width
+
+
+def _failing_worker(rank, world, port, mode, q):
+    import datetime
+    import time
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    if rank == 1:  # the failing rank: leaves at once, or stays but never takes part
+        if mode == "silent":
+            time.sleep(8)
+        os._exit(0)
+    from sardyne_b200 import runtime
+    t0 = time.time()
+    try:
+        runtime.shard_from_torch()
+        outcome = "returned"
+    except RuntimeError:
+        outcome = "raised"
+    r, w = ctypes.c_int32(), ctypes.c_int32()
+    capi.lib().sdy_engine_get_shard(ctypes.byref(r), ctypes.byref(w))
+    q.put((outcome, time.time() - t0, r.value, w.value))
+    q.close()
+    q.join_thread()  # the queue's feeder thread sends the result before the process ends
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["exits", "silent"])
+def test_shard_setup_fails_when_a_rank_is_gone(mode):
+    """Failure detection on the host (gloo, CPU only): when another rank has exited, or stays alive
+    without taking part, shard_from_torch raises within the process group's timeout (3 s here)
+    instead of waiting, and this process's shard stays unset (world 1), so no sharded load
+    starts."""
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    outcome, seconds, rank, world = q.get(timeout=120)
+    for p in procs:
+        p.join(60)
+    assert outcome == "raised" and seconds < 30, (outcome, seconds)
+    assert (rank, world) == (0, 1)
