@@ -176,11 +176,27 @@ def sample_bytes(sample):
     return sum(alg_bytes(fmt, n_out, n_in) for fmt, n_out, n_in, _ in sample)
 
 
+def host_cores():
+    """Threads for the CPU baselines: the CPUs this process may run on (its affinity mask), capped
+    by a cgroup v2 CPU quota when one is set (a container's share of a larger host)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        n = os.cpu_count() or 1
+    try:
+        quota, period = pathlib.Path("/sys/fs/cgroup/cpu.max").read_text().split()[:2]
+        if quota != "max":
+            n = min(n, -(-int(quota) // int(period)))
+    except (OSError, ValueError):
+        pass
+    return max(1, n)
+
+
 def time_reference(mats, xs, min_seconds=3.0, threads=None):
     import oracle
     ref = oracle.ref()
     ref.op_set_simd(1)
-    threads = threads or os.cpu_count() or 1
+    threads = threads or host_cores()
     sample = cpu_sample(mats)
     nbytes = sample_bytes(sample)
     best, spent, n = float("inf"), 0.0, 0
@@ -207,7 +223,7 @@ def run_reference_arm(args, rank, world):
     mats, xs = make_inputs()
     ref = oracle.ref()
     ref.op_set_simd(1)
-    threads = os.cpu_count() or 1
+    threads = host_cores()
     sample = cpu_sample(mats)
     nbytes = sample_bytes(sample)
     with cf.ThreadPoolExecutor(threads) as pool:
@@ -812,7 +828,8 @@ def decode_reference(name, path, prompt):
     n_prompt, n_decode = REF_DECODE_SAMPLE
     ref = oracle.ref()
     ref.op_set_simd(1)
-    model, ctx, info = engine_open(ref, path, n_prompt + n_decode + 1, n_prompt)
+    cores = min(host_cores(), 256)  # the reference's thread pool takes 1..256 (csrc/model_llama.c:475-487)
+    model, ctx, info = engine_open(ref, path, n_prompt + n_decode + 1, n_prompt, n_threads=cores)
     try:
         t0 = time.perf_counter()
         nxt = engine_next(ref, ctx, prompt[:n_prompt], info.n_vocab)
@@ -823,7 +840,6 @@ def decode_reference(name, path, prompt):
     finally:
         ref.engine_ctx_free(ctx)
         ref.engine_model_free(model)
-    cores = os.cpu_count() or 1
     return {"value": round(n_decode / (t2 - t1), 3), "unit": "tok/s", "cores": cores, "kind": "reference",
             "prefill_tok_s": round(n_prompt / (t1 - t0), 2),
             "sample": f"reference engine_eval (oracle/_ref, AVX2, {cores} threads) on the same model: "

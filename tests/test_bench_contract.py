@@ -35,3 +35,12 @@ def test_reference_arm_prints_one_contract_line():
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+    assert cb["cores"] <= (os.cpu_count() or 1)
+
+
+def test_cpu_baselines_use_the_cpus_this_process_may_run_on():
+    """The CPU baselines' thread count: at least one, at most the CPUs the process may run on."""
+    sys.path.insert(0, ROOT)
+    import bench
+    n = bench.host_cores()
+    assert 1 <= n <= len(os.sched_getaffinity(0))
