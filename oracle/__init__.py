@@ -126,6 +126,22 @@ def random_blocks(kind: str, n_blocks: int, seed: int = 0) -> np.ndarray:
     return b
 
 
+def special_rows(n: int) -> np.ndarray:
+    """Activation rows of special values (n a multiple of 512): signed zeros, blocks whose largest
+    magnitude is so small (subnormal, below ~3.7e-37) that the quantizers' inverse scale overflows
+    to infinity, values near the float maximum, a negative maximum, and normal blocks beside tiny
+    ones in the same row. The reference's quantizers give defined bytes for all of them."""
+    rows = [np.full(n, -0.0, np.float32)]
+    r = np.zeros(n, np.float32); r[5], r[7], r[40] = 1e-40, -3e-41, 2e-45; rows.append(r)
+    r = np.full(n, 1.5e-39, np.float32); r[::3] *= -1; rows.append(r)
+    r = np.full(n, -2e-38, np.float32); r[1::2] = 1e-38; rows.append(r)  # negative maximum, tiny
+    r = np.zeros(n, np.float32); r[1], r[2], r[3] = 3.0e38, -1e-30, 1.0; rows.append(r)
+    r = np.linspace(-2.0, 1.0, n).astype(np.float32); rows.append(r)
+    r = np.random.default_rng(0).standard_normal(n).astype(np.float32)
+    r[256:512] *= 1e-38; r[300] = -4e-39; rows.append(r)  # a normal block, then tiny ones
+    return np.ascontiguousarray(np.stack(rows))
+
+
 # ---------------------------------------------------------------- the reference library itself
 
 def ref_available() -> bool:

@@ -8,6 +8,22 @@
 
 namespace sdy {
 
+// The reference's integer conversions as its x86 host computes them, including the rows whose
+// largest magnitude is so small (below ~3.7e-37) that the inverse scale overflows to infinity.
+// nearest_int (quant.c:111-116): the integer left in the mantissa bits by adding 1.5 * 2^23,
+// i.e. round half to even for |p| < 2^22; +-inf leave 0 mantissa bits (-2^22), and the NaN of
+// inf * 0 is the x86 default NaN, whose mantissa bits give 0.
+__device__ __forceinline__ int nearest_int_ref(float p) {
+    if (isnan(p)) return 0;
+    return (__float_as_int(__fadd_rn(p, 12582912.0f)) & 0x007FFFFF) - 0x00400000;
+}
+// (int8_t)roundf(p) (quant.c:106): the x86 conversion of a value outside the int range, or NaN,
+// gives INT_MIN, whose low byte is 0.
+__device__ __forceinline__ int8_t round_to_int8_ref(float p) {
+    const float r = roundf(p);
+    return r >= -2147483648.0f && r < 2147483648.0f ? (int8_t)(int)r : (int8_t)0;
+}
+
 // Q8_K (quant.c:118-144) of one 256-element block whose 8 values per lane are in v. The scale
 // comes from the FIRST element of largest magnitude, with its sign.
 __device__ __forceinline__ void quant_q8k_vals(const float v[8], int t, int blk, const XQ &xq) {
@@ -37,8 +53,8 @@ __device__ __forceinline__ void quant_q8k_vals(const float v[8], int t, int blk,
     const float iscale = __fdiv_rn(-127.0f, vmax);
     int q[8], sum = 0;
     for (int i = 0; i < 8; i++) {
-        int r = __float2int_rn(__fmul_rn(iscale, v[i]));  // round half to even (quant.c:111-116)
-        q[i] = r < 127 ? r : 127;
+        const int r = nearest_int_ref(__fmul_rn(iscale, v[i]));
+        q[i] = (int8_t)(r < 127 ? r : 127);  // the stored byte; the sums add the stored values
         sum += q[i];
     }
     uint32_t lo = (q[0] & 255) | ((q[1] & 255) << 8) | ((q[2] & 255) << 16) | ((uint32_t)(q[3] & 255) << 24);
@@ -62,7 +78,7 @@ __device__ __forceinline__ void quant_q80_vals(const float v[8], bool live, int 
     float d = __fdiv_rn(amax, 127.0f);
     float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     int q[8], sum = 0;
-    for (int i = 0; i < 8; i++) { q[i] = live ? (int)roundf(__fmul_rn(v[i], id)) : 0; sum += q[i]; }
+    for (int i = 0; i < 8; i++) { q[i] = live ? round_to_int8_ref(__fmul_rn(v[i], id)) : 0; sum += q[i]; }
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     if (!live) return;

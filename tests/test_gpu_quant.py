@@ -75,6 +75,38 @@ def test_activation_quantization_random(vt, n):
     assert out.tobytes() == oracle.quantize(x, vt).tobytes()
 
 
+def same_floats(got, want):
+    """Bit-equal, except that NaNs (whose bit patterns differ between the host and the GPU) need
+    only sit in the same places."""
+    nan = np.isnan(want)
+    return np.array_equal(np.isnan(got), nan) and np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32))
+
+
+@pytest.mark.parametrize("vt", ["Q8_0", "Q8_K"])
+def test_activation_quantization_special_values(vt):
+    """Signed zeros, blocks whose inverse scale overflows to infinity (subnormal maxima: the
+    reference's conversions then store zeros), values near the float maximum, a negative maximum:
+    the bytes of the reference's host (oracle.special_rows, pinned to the reference library)."""
+    x = oracle.special_rows(512)
+    out = np.zeros(lib().op_row_size(TID[vt], 512) * len(x), np.uint8)
+    lib().op_quantize_rows(TID[vt], ptr(x), ptr(out), 512, 0, len(x))
+    assert out.tobytes() == oracle.quantize(x, vt).tobytes()
+
+
+@pytest.mark.parametrize("n_copies", [1, 5])  # 7 tokens: matvec; 35: the tensor-core GEMM
+@pytest.mark.parametrize("kind", ["Q4_K", "Q6_K", "Q8_0", "Q4_0"])
+def test_products_of_special_rows(kind, n_copies):
+    """op_matmul on the special rows (quantized inside the product's kernels) equals the oracle's
+    product of the oracle's quantization."""
+    x = np.ascontiguousarray(np.tile(oracle.special_rows(512), (n_copies, 1)))
+    n_tok, n_in, n_out = x.shape[0], 512, 40
+    w = oracle.random_blocks(kind, n_out * n_in // oracle.QK[kind], seed=9)
+    got = np.full((n_tok, n_out), np.nan, np.float32)
+    lib().op_matmul(ptr(got), ptr(x), ptr(w), TID[kind], n_tok, n_in, n_out)
+    want = oracle.matmul_q(w, kind, oracle.quantize(x, oracle.VEC_DOT_TYPE[kind]), n_tok, n_in, n_out)
+    assert same_floats(got, want)
+
+
 @pytest.mark.parametrize("kind", KINDS)
 def test_vec_dot_matches_reference(golden, kind):
     w, xq = golden[f"dot_{kind}_w"], golden[f"dot_{kind}_xq"]

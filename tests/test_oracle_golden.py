@@ -92,3 +92,14 @@ def test_oracle_equals_reference_library_on_fresh_inputs(kind):
             assert np.array_equal(oracle.matmul_q(w, kind, xq, n_tok, n_in, n_out), want)
     finally:
         ref.op_set_simd(1)
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference library not built here")
+@pytest.mark.parametrize("vt", ["Q8_0", "Q8_K"])
+def test_oracle_quantizers_equal_reference_on_special_values(vt):
+    """Signed zeros, blocks whose inverse scale overflows to infinity (subnormal maxima), values near
+    the float maximum: the oracle's bytes are the reference library's."""
+    x = oracle.special_rows(512)
+    want = np.zeros(oracle.row_bytes(vt, 512) * len(x), np.uint8)
+    oracle.ref().op_quantize_rows(oracle.TYPE_ID[vt], x.ctypes.data, want.ctypes.data, 512, 0, len(x))
+    assert oracle.quantize(x, vt).tobytes() == want.tobytes()
