@@ -1,9 +1,10 @@
 """The HF -> GGUF converter with K-quants (sardyne_b200.convert), on the CPU.
 
 Tiny llama / qwen2 / qwen3moe checkpoints are written as safetensors here. Checked:
-  * at F32 the output equals the reference's own converter's (sardyne/loader/convert.py) tensor for
-    tensor, byte for byte (names, shapes, llama's q/k row order), with the same model metadata
-    (the reference's converter has no MoE, so qwen3moe is checked against its checkpoint directly);
+  * at every type the reference's own converter writes (sardyne/loader/convert.py: f32, f16, bf16,
+    q8_0, q4_0) the output equals its output tensor for tensor, byte for byte (names, types,
+    shapes, llama's q/k row order), with every metadata entry equal (the reference's converter has
+    no MoE, so qwen3moe is checked against its checkpoint directly);
   * in the Q4_K_M mix every tensor gets the type the mix names, and dequantizes (oracle) to the
     checkpoint's weights within the reference's own error bounds for published files
     (tests/test_quant.py:53: Q4_K < 0.11, Q6_K < 0.03, Q5_0 < 0.07 relative RMS; Q8_0 < 0.01);
@@ -81,7 +82,8 @@ def checkpoint(tmp_path, arch, tied, dtype="F32"):
 
 
 def read_gguf(path):
-    """{name: (type name, ne, bytes)} and {key: raw value bytes or str} through this library's reader."""
+    """{name: (type name, ne, bytes)} and {key: value} through this library's reader (strings and
+    string arrays as str; other arrays as (element type, raw bytes); scalars as (GGUF type, value))."""
     lib = capi.lib()
     err = ctypes.create_string_buffer(256)
     h = lib.gguf_open(str(path).encode(), err, len(err))
@@ -107,8 +109,8 @@ def read_gguf(path):
             else:
                 v = ctypes.c_double()
                 u = ctypes.c_uint64()
-                kvs[key] = u.value if lib.gguf_kv_get_u64(h, i, ctypes.byref(u)) == 0 else \
-                    (v.value if lib.gguf_kv_get_f64(h, i, ctypes.byref(v)) == 0 else None)
+                kvs[key] = (kv.type, u.value if lib.gguf_kv_get_u64(h, i, ctypes.byref(u)) == 0 else
+                            (v.value if lib.gguf_kv_get_f64(h, i, ctypes.byref(v)) == 0 else None))
     finally:
         lib.gguf_close(h)
     return tensors, kvs
@@ -124,21 +126,22 @@ def floats(kind, ne, raw):
 
 
 @pytest.mark.skipif(not rt.available(), reason="the reference's Python package is not installed")
+@pytest.mark.parametrize("outtype", ["f32", "f16", "bf16", "q8_0", "q4_0"])
 @pytest.mark.parametrize("arch,tied", [("llama", True), ("qwen2", False)])
-def test_f32_equals_the_reference_converter(tmp_path, arch, tied):
+def test_equals_the_reference_converter(tmp_path, arch, tied, outtype):
+    """At every type the reference's converter writes (sardyne/loader/convert.py:30-31), every
+    tensor (name, type, shape, bytes) and every metadata entry equal its output."""
     rt.modules()
     from sardyne.loader import convert as ref_convert  # the reference's converter
     ck = checkpoint(tmp_path, arch, tied)
-    ours = convert.convert(ck, tmp_path / "ours.gguf", "f32")
-    ref_convert.convert(ck, tmp_path / "ref.gguf", "f32")
+    ours = convert.convert(ck, tmp_path / "ours.gguf", outtype)
+    ref_convert.convert(ck, tmp_path / "ref.gguf", outtype)
     a, akv = read_gguf(ours)
     b, bkv = read_gguf(tmp_path / "ref.gguf")
     assert a.keys() == b.keys()
     for name in a:
         assert a[name] == b[name], name
-    for key, value in bkv.items():
-        if key.startswith(arch + ".") or key in ("general.architecture",):
-            assert akv.get(key) == value, key
+    assert akv == bkv
 
 
 @pytest.mark.parametrize("arch,tied,dtype", [("llama", True, "F32"), ("qwen2", False, "BF16"),
@@ -147,7 +150,7 @@ def test_q4_k_m_mix_and_error_bounds(tmp_path, arch, tied, dtype):
     ck = checkpoint(tmp_path, arch, tied, dtype)
     f32, _ = read_gguf(convert.convert(ck, tmp_path / "f32.gguf", "f32"))
     q, kv = read_gguf(convert.convert(ck, tmp_path / "q.gguf", "q4_k_m"))
-    assert kv["general.file_type"] == 15 and q.keys() == f32.keys()
+    assert kv["general.file_type"][1] == 15 and q.keys() == f32.keys()
     mix = synth.mix_q4_k_m_tied if tied else synth.mix_q4_k_m_untied
     for name, (kind, ne, raw) in q.items():
         want_kind = "F32" if len(ne) == 1 or "gate_inp" in name else mix(name, ne[0])
