@@ -183,10 +183,18 @@ def block_type(gguf_name: str, n_in: int, outtype: str, tied: bool) -> str:
     return kind
 
 
-def encode(data: np.ndarray, kind: str):
+F16_MAX = float(np.finfo(np.float16).max)
+
+
+def encode(name: str, data: np.ndarray, kind: str):
     if kind == "F32":
         return np.ascontiguousarray(data, np.float32).view(np.uint8)
     if kind == "F16":
+        # a value beyond the f16 range is refused rather than written as infinity (NaNs fail the
+        # comparison and stay NaN), as the reference's converter does (sardyne/loader/convert.py:97-101)
+        big = float(np.abs(data).max()) if data.size else 0.0
+        if big > F16_MAX:
+            raise ValueError(f"{name}: value {big:g} beyond the f16 maximum ({F16_MAX:g}); use --outtype bf16")
         return np.ascontiguousarray(data, np.float16).view(np.uint8)
     if kind == "BF16":
         return f32_to_bf16(data).view(np.uint8)
@@ -242,8 +250,8 @@ def convert(hf_dir, out_path, outtype: str = "q4_k_m") -> pathlib.Path:
     def add(gguf_name, shape, load):
         kind = block_type(gguf_name, shape[-1], outtype, tied)
 
-        def produce(load=load, kind=kind):
-            return encode(load(), kind).tobytes()
+        def produce(load=load, kind=kind, name=gguf_name):
+            return encode(name, load(), kind).tobytes()
 
         w.add_lazy_tensor(gguf_name, tuple(reversed(shape)), kind, produce)
 

@@ -115,14 +115,18 @@ class GGUFWriter:
             head += struct.pack("<IQ", GGML_TYPES[kind], o)
         head += b"\0" * (-len(head) % self.alignment)
         tmp = self.path.with_name(f"{self.path.name}.{os.getpid()}.tmp")
-        with open(tmp, "wb") as f:
-            f.write(head)
-            for name, ne, kind, raw in self.tensors:
-                if callable(raw):
-                    raw = raw()
-                    if len(raw) != self._nbytes(ne, kind):
-                        raise ValueError(f"{name}: produced {len(raw)} bytes, expected {self._nbytes(ne, kind)}")
-                f.write(raw)
-                f.write(b"\0" * (-len(raw) % self.alignment))
+        try:
+            with open(tmp, "wb") as f:
+                f.write(head)
+                for name, ne, kind, raw in self.tensors:
+                    if callable(raw):
+                        raw = raw()
+                        if len(raw) != self._nbytes(ne, kind):
+                            raise ValueError(f"{name}: produced {len(raw)} bytes, expected {self._nbytes(ne, kind)}")
+                    f.write(raw)
+                    f.write(b"\0" * (-len(raw) % self.alignment))
+        except BaseException:
+            tmp.unlink(missing_ok=True)  # a tensor that cannot be produced leaves no partial file
+            raise
         os.replace(tmp, self.path)
         return self.path

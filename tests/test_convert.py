@@ -29,7 +29,8 @@ def write_safetensors(path, tensors, dtype="F32"):
     header, blobs, off = {}, [], 0
     for name, a in tensors.items():
         a = np.ascontiguousarray(a, np.float32)
-        raw = ((a.view(np.uint32) + 0x8000) >> 16).astype(np.uint16).tobytes() if dtype == "BF16" else a.tobytes()
+        raw = ((a.view(np.uint32) + 0x8000) >> 16).astype(np.uint16).tobytes() if dtype == "BF16" else \
+            a.astype(np.float16).tobytes() if dtype == "F16" else a.tobytes()
         header[name] = {"dtype": dtype, "shape": list(a.shape), "data_offsets": [off, off + len(raw)]}
         blobs.append(raw)
         off += len(raw)
@@ -127,13 +128,15 @@ def floats(kind, ne, raw):
 
 @pytest.mark.skipif(not rt.available(), reason="the reference's Python package is not installed")
 @pytest.mark.parametrize("outtype", ["f32", "f16", "bf16", "q8_0", "q4_0"])
-@pytest.mark.parametrize("arch,tied", [("llama", True), ("qwen2", False)])
-def test_equals_the_reference_converter(tmp_path, arch, tied, outtype):
-    """At every type the reference's converter writes (sardyne/loader/convert.py:30-31), every
-    tensor (name, type, shape, bytes) and every metadata entry equal its output."""
+@pytest.mark.parametrize("arch,tied,dtype", [("llama", True, "F32"), ("qwen2", False, "F32"),
+                                             ("qwen2", False, "BF16"), ("llama", True, "F16")])
+def test_equals_the_reference_converter(tmp_path, arch, tied, dtype, outtype):
+    """At every type the reference's converter writes (sardyne/loader/convert.py:30-31), from
+    checkpoints stored in F32, BF16 or F16, every tensor (name, type, shape, bytes) and every
+    metadata entry equal its output."""
     rt.modules()
     from sardyne.loader import convert as ref_convert  # the reference's converter
-    ck = checkpoint(tmp_path, arch, tied)
+    ck = checkpoint(tmp_path, arch, tied, dtype)
     ours = convert.convert(ck, tmp_path / "ours.gguf", outtype)
     ref_convert.convert(ck, tmp_path / "ref.gguf", outtype)
     a, akv = read_gguf(ours)
@@ -259,3 +262,26 @@ def test_unsupported_pretokenizers_are_refused_like_the_reference(tmp_path):
         convert.convert(ck, tmp_path / "ours.gguf", "f32")
     with pytest.raises(NotImplementedError):
         ref_convert.convert(ck, tmp_path / "ref.gguf", "f32")
+
+
+@pytest.mark.skipif(not rt.available(), reason="the reference's Python package is not installed")
+def test_f16_overflow_is_refused_like_the_reference(tmp_path):
+    """A matrix value beyond the f16 range is refused at f16 (the reference's message names the
+    tensor and "f16"), leaving neither the output nor a temporary file; bf16 converts it
+    (reference tests/test_convert.py:142-152)."""
+    rt.modules()
+    from sardyne.loader import convert as ref_convert
+    ck = checkpoint(tmp_path, "llama", True)
+    raw = (ck / "model.safetensors").read_bytes()
+    n = struct.unpack("<Q", raw[:8])[0]
+    off = json.loads(raw[8:8 + n])["model.layers.0.mlp.up_proj.weight"]["data_offsets"][0] + 8 + n
+    (ck / "model.safetensors").write_bytes(raw[:off] + struct.pack("<f", 70000.0) + raw[off + 4:])
+    out = tmp_path / "out"
+    out.mkdir()
+    for fn, name in ((convert.convert, "ours.gguf"), (ref_convert.convert, "ref.gguf")):
+        with pytest.raises(ValueError, match="blk.0.ffn_up.weight.*f16"):
+            fn(ck, out / name, "f16")
+    assert not list(out.iterdir())
+    a, _ = read_gguf(convert.convert(ck, out / "ours.gguf", "bf16"))
+    ref_convert.convert(ck, out / "ref.gguf", "bf16")
+    assert a == read_gguf(out / "ref.gguf")[0]
