@@ -285,3 +285,26 @@ def test_f16_overflow_is_refused_like_the_reference(tmp_path):
     a, _ = read_gguf(convert.convert(ck, out / "ours.gguf", "bf16"))
     ref_convert.convert(ck, out / "ref.gguf", "bf16")
     assert a == read_gguf(out / "ref.gguf")[0]
+
+
+ROPE_CASES = [{}, {"rope_theta": 5e5}, {"rope_parameters": {"rope_theta": 1e4, "rope_type": "yarn"}},
+              {"rope_parameters": {"full_attention": {"rope_theta": 3.0}}},
+              {"rope_scaling": {"rope_type": "llama3", "factor": 8.0}}, {"rope_scaling": {"type": "linear", "factor": 2.0}},
+              {"rope_scaling": None, "rope_theta": 1e6}, {"rope_parameters": {"rope_theta": 2e4, "rope_type": "default"}},
+              {"rope_scaling": {"rope_type": "default"}, "rope_theta": 7.0}]
+
+
+@pytest.mark.skipif(not rt.available(), reason="the reference's Python package is not installed")
+@pytest.mark.parametrize("cfg", ROPE_CASES)
+def test_rope_theta_and_scaling_refusals_match_the_reference(cfg):
+    """The RoPE base read from config.json, and the refusal of scaled RoPE variants, as the
+    reference's hf_config.rope_theta (reference tests/test_convert.py:112-121)."""
+    rt.modules()
+    from sardyne.loader import hf_config
+
+    def outcome(fn):
+        try:
+            return fn(cfg)
+        except NotImplementedError:
+            return "refused"
+    assert outcome(convert.rope_theta) == outcome(hf_config.rope_theta)
