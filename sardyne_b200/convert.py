@@ -109,27 +109,60 @@ def tokenizer_fields(hf_dir: pathlib.Path, vocab_size: int) -> dict:
     return fields
 
 
+class SafeTensorsError(ValueError):
+    """A .safetensors file whose header does not describe its data."""
+
+
+def _check_entry(where: str, info, data_len: int) -> tuple:
+    """(dtype, shape, begin, end) of one header entry, or SafeTensorsError: a known dtype,
+    non-negative integer dimensions, two offsets inside the data, and as many bytes as the shape
+    needs."""
+    if not isinstance(info, dict):
+        raise SafeTensorsError(f"{where}: entry is not an object")
+    dtype, shape, offs = info.get("dtype"), info.get("shape"), info.get("data_offsets")
+    if dtype not in _ST_DTYPES:
+        raise SafeTensorsError(f"{where}: dtype {dtype} not supported")
+    if not isinstance(shape, list) or not all(type(d) is int and d >= 0 for d in shape):
+        raise SafeTensorsError(f"{where}: bad shape {shape!r}")
+    if not isinstance(offs, list) or len(offs) != 2 or not all(type(o) is int for o in offs):
+        raise SafeTensorsError(f"{where}: bad data_offsets {offs!r}")
+    b, e = offs
+    if not 0 <= b <= e <= data_len:
+        raise SafeTensorsError(f"{where}: data [{b}, {e}) outside the file's {data_len} data bytes")
+    if e - b != int(np.prod(shape, dtype=np.int64)) * np.dtype(_ST_DTYPES[dtype]).itemsize:
+        raise SafeTensorsError(f"{where}: {e - b} bytes do not hold shape {shape} of {dtype}")
+    return dtype, tuple(shape), b, e
+
+
 class SafeTensors:
     """The tensors of every *.safetensors file of a directory (8-byte header length, JSON header,
-    raw row-major data), mapped read-only; get() returns float32."""
+    raw row-major data), mapped read-only; get() returns float32. Every header entry is checked
+    against the file when it is opened (SafeTensorsError)."""
 
     def __init__(self, directory):
         self.index = {}
         self._maps = []
         for path in sorted(pathlib.Path(directory).glob("*.safetensors")):
-            f = open(path, "rb")
-            mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
-            f.close()
+            size = path.stat().st_size
+            if size < 8:
+                raise SafeTensorsError(f"{path.name}: {size} bytes, shorter than the header length")
+            with open(path, "rb") as f:
+                mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
             (hlen,) = struct.unpack("<Q", mm[:8])
-            header = json.loads(mm[8:8 + hlen])
+            if hlen > size - 8:  # checked before anything is read or allocated
+                raise SafeTensorsError(f"{path.name}: header length {hlen} beyond the file")
+            try:
+                header = json.loads(mm[8:8 + hlen])
+            except (UnicodeDecodeError, json.JSONDecodeError) as e:
+                raise SafeTensorsError(f"{path.name}: header is not JSON ({e})") from None
+            if not isinstance(header, dict):
+                raise SafeTensorsError(f"{path.name}: header is not an object")
             base = 8 + hlen
             for name, info in header.items():
                 if name == "__metadata__":
                     continue
-                if info["dtype"] not in _ST_DTYPES:
-                    raise ValueError(f"{path.name}: {name}: dtype {info['dtype']} not supported")
-                b, e = info["data_offsets"]
-                self.index[name] = (mm, info["dtype"], tuple(info["shape"]), base + b, base + e)
+                dtype, shape, b, e = _check_entry(f"{path.name}: {name}", info, size - base)
+                self.index[name] = (mm, dtype, shape, base + b, base + e)
             self._maps.append(mm)
         if not self.index:
             raise FileNotFoundError(f"no *.safetensors in {directory}")

@@ -308,3 +308,44 @@ def test_rope_theta_and_scaling_refusals_match_the_reference(cfg):
         except NotImplementedError:
             return "refused"
     assert outcome(convert.rope_theta) == outcome(hf_config.rope_theta)
+
+
+def _st_file(directory, header, data=b"", header_len=None):
+    directory.mkdir()
+    h = json.dumps(header).encode()
+    (directory / "m.safetensors").write_bytes(struct.pack("<Q", len(h) if header_len is None else header_len) + h + data)
+    return directory
+
+
+@pytest.mark.parametrize("header,data", [
+    ({"a": {"dtype": "F32", "shape": [2], "data_offsets": [-8, 0]}}, b"\0" * 8),   # negative offset
+    ({"a": {"dtype": "F32", "shape": [4], "data_offsets": [0, 16]}}, b"\0" * 8),   # past the file
+    ({"a": {"dtype": "F32", "shape": [3], "data_offsets": [0, 8]}}, b"\0" * 8),    # shape and size differ
+    ({"a": {"dtype": "F8_E4M3", "shape": [8], "data_offsets": [0, 8]}}, b"\0" * 8),  # unknown dtype
+    ({"a": {"dtype": "F32", "shape": [-2], "data_offsets": [0, 8]}}, b"\0" * 8),   # negative dimension
+    ({"a": {"dtype": "F32", "shape": [2], "data_offsets": [0]}}, b"\0" * 8),       # one offset
+    ({"a": {"dtype": "F32", "shape": [2], "data_offsets": [8, 0]}}, b"\0" * 8),    # end before begin
+    ({"a": "x"}, b""),                                                             # entry not an object
+    ([1, 2], b""),                                                                 # header not an object
+])
+def test_safetensors_headers_are_checked_when_opened(tmp_path, header, data):
+    """The converter's safetensors reader refuses a header that does not describe its data (the
+    cases of reference tests/test_safetensors.py:29-41) with SafeTensorsError, a ValueError."""
+    with pytest.raises(convert.SafeTensorsError):
+        convert.SafeTensors(_st_file(tmp_path / "ck", header, data))
+
+
+def test_safetensors_lengths_and_json(tmp_path):
+    (tmp_path / "short").mkdir()
+    (tmp_path / "short" / "m.safetensors").write_bytes(b"\1\2\3")
+    with pytest.raises(convert.SafeTensorsError):
+        convert.SafeTensors(tmp_path / "short")
+    with pytest.raises(convert.SafeTensorsError):  # a huge header length allocates nothing
+        convert.SafeTensors(_st_file(tmp_path / "huge", {}, header_len=2 ** 62))
+    (tmp_path / "json").mkdir()
+    (tmp_path / "json" / "m.safetensors").write_bytes(struct.pack("<Q", 3) + b"{x}")
+    with pytest.raises(convert.SafeTensorsError):
+        convert.SafeTensors(tmp_path / "json")
+    ok = convert.SafeTensors(_st_file(tmp_path / "ok", {"a": {"dtype": "F32", "shape": [2, 3], "data_offsets": [0, 24]}},
+                                      np.arange(6, dtype=np.float32).tobytes()))
+    assert ok.shape("a") == (2, 3) and np.array_equal(ok.get("a"), np.arange(6, dtype=np.float32).reshape(2, 3))
