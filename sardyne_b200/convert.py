@@ -135,37 +135,68 @@ def _check_entry(where: str, info, data_len: int) -> tuple:
 
 
 class SafeTensors:
-    """The tensors of every *.safetensors file of a directory (8-byte header length, JSON header,
-    raw row-major data), mapped read-only; get() returns float32. Every header entry is checked
-    against the file when it is opened (SafeTensorsError)."""
+    """The tensors of a Hugging Face checkpoint directory, mapped read-only; get() returns float32.
+    With model.safetensors.index.json the shards it names (plain file names inside the directory)
+    and the tensors it places in them, as the reference's loader reads them
+    (sardyne/loader/safetensors.py:110-131); otherwise every *.safetensors file of the directory,
+    each name in one file only. Every header entry is checked against its file when the file is
+    opened (SafeTensorsError)."""
 
     def __init__(self, directory):
+        directory = pathlib.Path(directory)
         self.index = {}
         self._maps = []
-        for path in sorted(pathlib.Path(directory).glob("*.safetensors")):
-            size = path.stat().st_size
-            if size < 8:
-                raise SafeTensorsError(f"{path.name}: {size} bytes, shorter than the header length")
-            with open(path, "rb") as f:
-                mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
-            (hlen,) = struct.unpack("<Q", mm[:8])
-            if hlen > size - 8:  # checked before anything is read or allocated
-                raise SafeTensorsError(f"{path.name}: header length {hlen} beyond the file")
+        index = directory / "model.safetensors.index.json"
+        if index.exists():
             try:
-                header = json.loads(mm[8:8 + hlen])
-            except (UnicodeDecodeError, json.JSONDecodeError) as e:
-                raise SafeTensorsError(f"{path.name}: header is not JSON ({e})") from None
-            if not isinstance(header, dict):
-                raise SafeTensorsError(f"{path.name}: header is not an object")
-            base = 8 + hlen
-            for name, info in header.items():
-                if name == "__metadata__":
-                    continue
-                dtype, shape, b, e = _check_entry(f"{path.name}: {name}", info, size - base)
-                self.index[name] = (mm, dtype, shape, base + b, base + e)
-            self._maps.append(mm)
+                weight_map = json.loads(index.read_text())["weight_map"]
+            except (ValueError, KeyError, TypeError) as e:
+                raise SafeTensorsError(f"{index.name}: no weight_map ({e})") from None
+            if not isinstance(weight_map, dict):
+                raise SafeTensorsError(f"{index.name}: weight_map is not an object")
+            shards = {}
+            for f in sorted(set(map(str, weight_map.values()))):
+                # the index comes with the download: its shards must be files of this directory
+                if pathlib.Path(f).name != f or not f.endswith(".safetensors"):
+                    raise SafeTensorsError(f"{index.name}: shard name {f!r} is not a file of the model directory")
+                shards[f] = self._open(directory / f)
+            for name, f in weight_map.items():
+                if name not in shards[str(f)]:
+                    raise SafeTensorsError(f"{index.name}: {name} placed in {f}, which does not hold it")
+                self.index[name] = shards[str(f)][name]
+        else:
+            for path in sorted(directory.glob("*.safetensors")):
+                for name, entry in self._open(path).items():
+                    if name in self.index:
+                        raise SafeTensorsError(f"{path.name}: {name} is also in another file")
+                    self.index[name] = entry
         if not self.index:
             raise FileNotFoundError(f"no *.safetensors in {directory}")
+
+    def _open(self, path) -> dict:
+        """{name: (map, dtype, shape, begin, end)} of one file, every entry checked."""
+        size = path.stat().st_size
+        if size < 8:
+            raise SafeTensorsError(f"{path.name}: {size} bytes, shorter than the header length")
+        with open(path, "rb") as f:
+            mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+        (hlen,) = struct.unpack("<Q", mm[:8])
+        if hlen > size - 8:  # checked before anything is read or allocated
+            raise SafeTensorsError(f"{path.name}: header length {hlen} beyond the file")
+        try:
+            header = json.loads(mm[8:8 + hlen])
+        except (UnicodeDecodeError, json.JSONDecodeError) as e:
+            raise SafeTensorsError(f"{path.name}: header is not JSON ({e})") from None
+        if not isinstance(header, dict):
+            raise SafeTensorsError(f"{path.name}: header is not an object")
+        base, out = 8 + hlen, {}
+        for name, info in header.items():
+            if name == "__metadata__":
+                continue
+            dtype, shape, b, e = _check_entry(f"{path.name}: {name}", info, size - base)
+            out[name] = (mm, dtype, shape, base + b, base + e)
+        self._maps.append(mm)
+        return out
 
     def __contains__(self, name):
         return name in self.index

@@ -349,3 +349,52 @@ def test_safetensors_lengths_and_json(tmp_path):
     ok = convert.SafeTensors(_st_file(tmp_path / "ok", {"a": {"dtype": "F32", "shape": [2, 3], "data_offsets": [0, 24]}},
                                       np.arange(6, dtype=np.float32).tobytes()))
     assert ok.shape("a") == (2, 3) and np.array_equal(ok.get("a"), np.arange(6, dtype=np.float32).reshape(2, 3))
+
+
+def shard_checkpoint(ck, out):
+    """The checkpoint `ck` split over two shards with a model.safetensors.index.json, in `out`."""
+    out.mkdir()
+    (out / "config.json").write_text((ck / "config.json").read_text())
+    st = convert.SafeTensors(ck)
+    names = sorted(st.index)
+    halves = {"model-00001-of-00002.safetensors": names[::2], "model-00002-of-00002.safetensors": names[1::2]}
+    for fname, part in halves.items():
+        write_safetensors(out / fname, {n: st.get(n) for n in part})
+    (out / "model.safetensors.index.json").write_text(json.dumps(
+        {"metadata": {}, "weight_map": {n: f for f, part in halves.items() for n in part}}))
+    return out
+
+
+@pytest.mark.skipif(not rt.available(), reason="the reference's Python package is not installed")
+def test_sharded_checkpoint_converts_like_the_single_file(tmp_path):
+    rt.modules()
+    from sardyne.loader import convert as ref_convert
+    ck = checkpoint(tmp_path, "qwen2", False)
+    sh = shard_checkpoint(ck, tmp_path / "sharded")
+    a, akv = read_gguf(convert.convert(ck, tmp_path / "single.gguf", "q8_0"))
+    b, bkv = read_gguf(convert.convert(sh, tmp_path / "sharded.gguf", "q8_0"))
+    ref_convert.convert(sh, tmp_path / "ref.gguf", "q8_0")
+    c, ckv = read_gguf(tmp_path / "ref.gguf")
+    assert a == b and b == c and bkv == ckv
+    assert {k: v for k, v in akv.items() if k != "general.name"} == {k: v for k, v in bkv.items() if k != "general.name"}
+
+
+def test_shard_index_is_checked(tmp_path):
+    """Index entries must name files of the model directory that hold the tensor (reference
+    tests/test_safetensors.py:51-62); without an index a tensor name may appear in one file only."""
+    ck = checkpoint(tmp_path, "llama", True)
+    sh = shard_checkpoint(ck, tmp_path / "sharded")
+    index = json.loads((sh / "model.safetensors.index.json").read_text())
+    name = next(iter(index["weight_map"]))
+    for bad in ("../outside.safetensors", "/abs/model.safetensors", "model.bin"):
+        (sh / "model.safetensors.index.json").write_text(json.dumps({"weight_map": {**index["weight_map"], name: bad}}))
+        with pytest.raises(convert.SafeTensorsError, match="not a file of the model directory"):
+            convert.SafeTensors(sh)
+    other = next(f for f in set(index["weight_map"].values()) if f != index["weight_map"][name])
+    (sh / "model.safetensors.index.json").write_text(json.dumps({"weight_map": {**index["weight_map"], name: other}}))
+    with pytest.raises(convert.SafeTensorsError, match="does not hold it"):
+        convert.SafeTensors(sh)
+    (sh / "model.safetensors.index.json").unlink()
+    write_safetensors(sh / "extra.safetensors", {name: np.zeros(convert.SafeTensors(ck).shape(name), np.float32)})
+    with pytest.raises(convert.SafeTensorsError, match="also in another file"):
+        convert.SafeTensors(sh)
