@@ -72,3 +72,25 @@ def test_grouped_and_exchange_entry_points_reject_bad_arguments():
     assert lib.sdy_allgather_p2p(None, 16, bases, 0, 2, None) == -1
     assert lib.sdy_engine_exchange(None) == -1
     lib.sdy_clear_error()
+
+
+def test_host_side_entry_points_equal_the_reference_library():
+    """The entry points that need no GPU (row sizes of every type id and length, the kernel-set
+    switch) answer as the reference library built from its sources (csrc/ops.c:211-255,189-209)."""
+    import oracle
+    if not oracle.ref_available():
+        pytest.skip("reference library not built")
+    ours, ref = ctypes.CDLL(str(capi.lib_path())), oracle.ref()
+    for lib in (ours, ref):
+        lib.op_row_size.restype = ctypes.c_size_t
+        lib.op_row_size.argtypes = [ctypes.c_int, ctypes.c_int]
+    for t in range(-2, 45):
+        for n in (0, 1, 31, 32, 33, 255, 256, 512, 2048, 11008):
+            assert ours.op_row_size(t, n) == ref.op_row_size(t, n), (t, n)
+    try:
+        for enable in (0, 1, 0):
+            assert ours.op_set_simd(enable) == ref.op_set_simd(enable)
+            assert ours.op_simd() == ref.op_simd()
+    finally:
+        ours.op_set_simd(1)
+        ref.op_set_simd(1)
