@@ -42,12 +42,15 @@ def write_safetensors(path, tensors, dtype="F32"):
 def checkpoint(tmp_path, arch, tied, dtype="F32"):
     rng = np.random.default_rng(len(arch))
     dim, n_head, n_kv, hd, ffn, vocab, n_layer = 256, 4, 2, 64, 512, 96, 2
-    hf = {"llama": "LlamaForCausalLM", "qwen2": "Qwen2ForCausalLM", "qwen3moe": "Qwen3MoeForCausalLM"}[arch]
+    hf = {"llama": "LlamaForCausalLM", "qwen2": "Qwen2ForCausalLM", "qwen3": "Qwen3ForCausalLM",
+          "qwen3moe": "Qwen3MoeForCausalLM"}[arch]
     cfg = {"architectures": [hf], "hidden_size": dim, "num_hidden_layers": n_layer, "num_attention_heads": n_head,
            "num_key_value_heads": n_kv, "intermediate_size": ffn, "vocab_size": vocab, "rms_norm_eps": 1e-6,
            "rope_theta": 10000.0, "max_position_embeddings": 128, "tie_word_embeddings": tied}
     if arch == "qwen3moe":
         cfg.update(num_experts=4, num_experts_per_tok=2, moe_intermediate_size=256, head_dim=hd)
+    if arch == "qwen3":
+        cfg.update(head_dim=hd)
     t = {"model.embed_tokens.weight": rng.standard_normal((vocab, dim)) * 0.02,
          "model.norm.weight": 1 + rng.standard_normal(dim) * 0.1}
     if not tied:
@@ -63,9 +66,10 @@ def checkpoint(tmp_path, arch, tied, dtype="F32"):
         if arch == "qwen2":
             for n, r in (("q", n_head * hd), ("k", n_kv * hd), ("v", n_kv * hd)):
                 t[p + f"self_attn.{n}_proj.bias"] = rng.standard_normal(r) * 0.1
-        if arch == "qwen3moe":
+        if arch in ("qwen3", "qwen3moe"):
             t[p + "self_attn.q_norm.weight"] = 1 + rng.standard_normal(hd) * 0.1
             t[p + "self_attn.k_norm.weight"] = 1 + rng.standard_normal(hd) * 0.1
+        if arch == "qwen3moe":
             t[p + "mlp.gate.weight"] = rng.standard_normal((4, dim)) * 0.1
             for e in range(4):
                 t[p + f"mlp.experts.{e}.gate_proj.weight"] = rng.standard_normal((256, dim)) * 0.02
@@ -128,7 +132,7 @@ def floats(kind, ne, raw):
 
 @pytest.mark.skipif(not rt.available(), reason="the reference's Python package is not installed")
 @pytest.mark.parametrize("outtype", ["f32", "f16", "bf16", "q8_0", "q4_0"])
-@pytest.mark.parametrize("arch,tied,dtype", [("llama", True, "F32"), ("qwen2", False, "F32"),
+@pytest.mark.parametrize("arch,tied,dtype", [("llama", True, "F32"), ("qwen2", False, "F32"), ("qwen3", True, "F32"),
                                              ("qwen2", False, "BF16"), ("llama", True, "F16")])
 def test_equals_the_reference_converter(tmp_path, arch, tied, dtype, outtype):
     """At every type the reference's converter writes (sardyne/loader/convert.py:30-31), from
