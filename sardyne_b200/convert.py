@@ -156,8 +156,10 @@ class SafeTensors:
                 raise SafeTensorsError(f"{index.name}: weight_map is not an object")
             shards = {}
             for f in sorted(set(map(str, weight_map.values()))):
-                # the index comes with the download: its shards must be files of this directory
-                if pathlib.Path(f).name != f or not f.endswith(".safetensors"):
+                # the index comes with the download: a shard is one path component of this
+                # directory (no separators, no "." or ".."; symlinks, as in a hub cache, are fine)
+                parts = pathlib.PurePath(f).parts
+                if len(parts) != 1 or parts[0] in (".", "..") or pathlib.PurePath(f).suffix != ".safetensors":
                     raise SafeTensorsError(f"{index.name}: shard name {f!r} is not a file of the model directory")
                 shards[f] = self._open(directory / f)
             for name, f in weight_map.items():
