@@ -91,17 +91,17 @@ def tokenizer_fields(hf_dir: pathlib.Path, vocab_size: int) -> dict:
     model = t.get("model") or {}
     if model.get("type") != "BPE":
         raise NotImplementedError(f"tokenizer model {model.get('type')} is not supported")
-    text, kind = {}, {}
-    for tok, i in model["vocab"].items():
-        text[i], kind[i] = tok, TOKEN_NORMAL
+    # id -> (text, type); added tokens override vocabulary entries of the same id
+    table = {i: (tok, TOKEN_NORMAL) for tok, i in model["vocab"].items()}
     for a in t.get("added_tokens", []):
-        text[a["id"]] = a["content"]
-        kind[a["id"]] = TOKEN_CONTROL if a.get("special") else TOKEN_USER_DEFINED
-    n = max(vocab_size, max(text) + 1)
+        table[a["id"]] = (a["content"], TOKEN_CONTROL if a.get("special") else TOKEN_USER_DEFINED)
+    rows = [table.get(i, (f"[PAD{i}]", TOKEN_UNUSED)) for i in range(max(vocab_size, max(table) + 1))]
+    # merges come as "left right" strings (older files) or as [left, right] pairs (newer ones)
+    merges = [m if isinstance(m, str) else f"{m[0]} {m[1]}" for m in model.get("merges", [])]
     fields = {"tokenizer.ggml.model": "gpt2", "tokenizer.ggml.pre": pretokenizer_name(t),
-              "tokenizer.ggml.tokens": [text.get(i, f"[PAD{i}]") for i in range(n)],
-              "tokenizer.ggml.token_type": [kind.get(i, TOKEN_UNUSED) for i in range(n)],
-              "tokenizer.ggml.merges": [m if isinstance(m, str) else " ".join(m) for m in model.get("merges", [])]}
+              "tokenizer.ggml.tokens": [text for text, _ in rows],
+              "tokenizer.ggml.token_type": [kind for _, kind in rows],
+              "tokenizer.ggml.merges": merges}
     cfg_path = hf_dir / "tokenizer_config.json"
     cfg = json.loads(cfg_path.read_text(encoding="utf-8")) if cfg_path.exists() else {}
     if cfg.get("chat_template"):
