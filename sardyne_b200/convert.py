@@ -256,11 +256,12 @@ def encode(name: str, data: np.ndarray, kind: str):
     if kind == "F32":
         return np.ascontiguousarray(data, np.float32).view(np.uint8)
     if kind == "F16":
-        # a value beyond the f16 range is refused rather than written as infinity (NaNs fail the
-        # comparison and stay NaN), as the reference's converter does (sardyne/loader/convert.py:97-101)
-        big = float(np.abs(data).max()) if data.size else 0.0
-        if big > F16_MAX:
-            raise ValueError(f"{name}: value {big:g} beyond the f16 maximum ({F16_MAX:g}); use --outtype bf16")
+        # a value beyond the f16 range is refused rather than written as infinity, as the
+        # reference's converter does (sardyne/loader/convert.py:97-101); the maximum of a tensor
+        # holding a NaN is NaN, which passes, and its NaNs stay NaN
+        peak = float(np.max(np.abs(data), initial=0.0))
+        if peak > F16_MAX:
+            raise ValueError(f"{name}: value {peak:g} beyond the f16 maximum ({F16_MAX:g}); use --outtype bf16")
         return np.ascontiguousarray(data, np.float16).view(np.uint8)
     if kind == "BF16":
         return f32_to_bf16(data).view(np.uint8)
