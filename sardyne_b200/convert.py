@@ -67,19 +67,24 @@ QWEN2_SPLIT = ("(?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\\r\\n\\p{L}\\p{N}]?\\p{L}+|\\p{N
                "|\\s*[\\r\\n]+|\\s+(?!\\S)|\\s+")
 
 
+# The pre-tokenizers the reference's tokenizer reproduces (sardyne/tokenizer/bpe.py:192-201), as
+# (pre-tokenizer step types, normalizer type, check of the first step, tokenizer.ggml.pre).
+PRETOKENIZERS = (
+    (("Split", "ByteLevel"), "NFC", lambda step: (step.get("pattern") or {}).get("Regex") == QWEN2_SPLIT, "qwen2"),
+    (("Digits", "ByteLevel"), None, lambda step: bool(step.get("individual_digits")), "smollm"),
+)
+
+
 def pretokenizer_name(t: dict) -> str:
-    """tokenizer.ggml.pre for the pre-tokenizers the reference reproduces (sardyne/tokenizer/bpe.py:
-    192-201): Qwen2's regex split then byte level with NFC normalization ("qwen2"), or single digits
-    then byte level without a normalizer ("smollm"); anything else is refused."""
-    steps = (t.get("pre_tokenizer") or {}).get("pretokenizers", [])
-    kinds = [s.get("type") for s in steps]
-    norm = (t.get("normalizer") or {}).get("type")
-    if kinds == ["Split", "ByteLevel"] and (steps[0].get("pattern") or {}).get("Regex") == QWEN2_SPLIT \
-            and norm == "NFC":
-        return "qwen2"
-    if kinds == ["Digits", "ByteLevel"] and steps[0].get("individual_digits") and norm is None:
-        return "smollm"
-    raise NotImplementedError(f"pre-tokenizer {kinds} with normalizer {norm} is not supported")
+    """tokenizer.ggml.pre of a tokenizer.json whose pre-tokenizer is one of PRETOKENIZERS; any
+    other is refused (NotImplementedError)."""
+    sequence = (t.get("pre_tokenizer") or {}).get("pretokenizers") or []
+    types = tuple(step.get("type") for step in sequence)
+    normalizer = (t.get("normalizer") or {}).get("type")
+    for want_types, want_normalizer, first_ok, name in PRETOKENIZERS:
+        if types == want_types and normalizer == want_normalizer and first_ok(sequence[0]):
+            return name
+    raise NotImplementedError(f"pre-tokenizer {list(types)} with normalizer {normalizer} is not supported")
 
 
 def tokenizer_fields(hf_dir: pathlib.Path, vocab_size: int) -> dict:
