@@ -221,15 +221,20 @@ class SafeTensors:
 
 
 def rope_theta(cfg) -> float:
-    """RoPE base; scaled RoPE variants are refused (the engine runs plain RoPE only)."""
-    params = cfg.get("rope_parameters") or {}
-    if params and all(isinstance(v, dict) for v in params.values()):
-        params = params.get("full_attention", {})
-    for p in (params, cfg.get("rope_scaling") or {}):
-        kind = p.get("rope_type", p.get("type", "default"))
-        if kind not in ("default", None):
-            raise NotImplementedError(f"RoPE scaling '{kind}' is not supported")
-    return float(params.get("rope_theta", cfg.get("rope_theta", 10000.0)))
+    """The RoPE base of config.json; scaled RoPE variants are refused (NotImplementedError: the
+    engine runs plain RoPE), with the reference's config reader's rules
+    (sardyne/loader/hf_config.py:12-27)."""
+    given = cfg.get("rope_parameters") or {}
+    # newer configs nest the parameters per attention kind; only full attention is supported
+    per_kind = bool(given) and all(isinstance(v, dict) for v in given.values())
+    if per_kind and "full_attention" not in given:
+        raise NotImplementedError(f"RoPE parameters per layer kind {sorted(given)} are not supported")
+    rope = given["full_attention"] if per_kind else given
+    for source in (rope, cfg.get("rope_scaling") or {}):
+        variant = source["rope_type"] if "rope_type" in source else source.get("type", "default")
+        if variant is not None and variant != "default":
+            raise NotImplementedError(f"RoPE scaling '{variant}' is not supported")
+    return float(rope["rope_theta"] if "rope_theta" in rope else cfg.get("rope_theta", 10000.0))
 
 
 def interleave_rope_rows(w: np.ndarray, n_head: int) -> np.ndarray:

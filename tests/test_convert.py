@@ -295,7 +295,10 @@ ROPE_CASES = [{}, {"rope_theta": 5e5}, {"rope_parameters": {"rope_theta": 1e4, "
               {"rope_parameters": {"full_attention": {"rope_theta": 3.0}}},
               {"rope_scaling": {"rope_type": "llama3", "factor": 8.0}}, {"rope_scaling": {"type": "linear", "factor": 2.0}},
               {"rope_scaling": None, "rope_theta": 1e6}, {"rope_parameters": {"rope_theta": 2e4, "rope_type": "default"}},
-              {"rope_scaling": {"rope_type": "default"}, "rope_theta": 7.0}]
+              {"rope_scaling": {"rope_type": "default"}, "rope_theta": 7.0},
+              {"rope_parameters": {"sliding_attention": {"rope_theta": 1.0}}},
+              {"rope_parameters": {"full_attention": {"rope_theta": 2.0}, "sliding_attention": {"rope_theta": 1.0}}},
+              {"rope_parameters": {"rope_type": None, "rope_theta": 9.0}}]
 
 
 @pytest.mark.skipif(not rt.available(), reason="the reference's Python package is not installed")
