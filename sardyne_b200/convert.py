@@ -278,6 +278,17 @@ def encode(name: str, data: np.ndarray, kind: str):
     return np.frombuffer(kquant.quantize(data.reshape(-1, data.shape[-1]), kind), np.uint8)
 
 
+def end_token_ids(hf_dir: pathlib.Path, cfg: dict) -> list:
+    """The end-of-generation token ids: those of generation_config.json when it names any, else
+    those of config.json (reference sardyne/loader/hf_config.py:30-42)."""
+    gen = hf_dir / "generation_config.json"
+    for source in (json.loads(gen.read_text()) if gen.exists() else {}, cfg):
+        ids = source.get("eos_token_id")
+        if ids is not None:
+            return [int(i) for i in (ids if isinstance(ids, list) else [ids])]
+    return []
+
+
 def convert(hf_dir, out_path, outtype: str = "q4_k_m") -> pathlib.Path:
     hf_dir = pathlib.Path(hf_dir)
     cfg = json.loads((hf_dir / "config.json").read_text())
@@ -310,11 +321,11 @@ def convert(hf_dir, out_path, outtype: str = "q4_k_m") -> pathlib.Path:
     for key, value in meta:
         w.add(f"{arch}.{key}", value)
     w.add("general.file_type", FILE_TYPES[outtype])
-    for key, gkey in (("bos_token_id", "tokenizer.ggml.bos_token_id"), ("eos_token_id", "tokenizer.ggml.eos_token_id")):
-        v = cfg.get(key)
-        v = v[0] if isinstance(v, list) and v else v
-        if isinstance(v, int):
-            w.add(gkey, v)
+    if isinstance(cfg.get("bos_token_id"), int):  # a single id only
+        w.add("tokenizer.ggml.bos_token_id", cfg["bos_token_id"])
+    ends = end_token_ids(hf_dir, cfg)
+    if ends:  # the first is the file's end-of-sequence token
+        w.add("tokenizer.ggml.eos_token_id", ends[0])
     if (hf_dir / "tokenizer.json").exists():
         for key, value in tokenizer_fields(hf_dir, cfg["vocab_size"]).items():
             if key == "tokenizer.ggml.token_type":

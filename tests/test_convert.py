@@ -46,7 +46,8 @@ def checkpoint(tmp_path, arch, tied, dtype="F32"):
           "qwen3moe": "Qwen3MoeForCausalLM"}[arch]
     cfg = {"architectures": [hf], "hidden_size": dim, "num_hidden_layers": n_layer, "num_attention_heads": n_head,
            "num_key_value_heads": n_kv, "intermediate_size": ffn, "vocab_size": vocab, "rms_norm_eps": 1e-6,
-           "rope_theta": 10000.0, "max_position_embeddings": 128, "tie_word_embeddings": tied}
+           "rope_theta": 10000.0, "max_position_embeddings": 128, "tie_word_embeddings": tied,
+           "bos_token_id": 1, "eos_token_id": 2 if arch != "qwen3" else [2, 4]}
     if arch == "qwen3moe":
         cfg.update(num_experts=4, num_experts_per_tok=2, moe_intermediate_size=256, head_dim=hd)
     if arch == "qwen3":
@@ -82,6 +83,8 @@ def checkpoint(tmp_path, arch, tied, dtype="F32"):
     d = tmp_path / f"{arch}-{'tied' if tied else 'untied'}-{dtype}"
     d.mkdir()
     (d / "config.json").write_text(json.dumps(cfg))
+    if arch == "qwen2":  # end ids from generation_config.json take precedence
+        (d / "generation_config.json").write_text(json.dumps({"eos_token_id": [5, 2]}))
     write_safetensors(d / "model.safetensors", t, dtype)
     return d
 
@@ -239,7 +242,8 @@ def test_tokenizer_metadata_equals_the_reference_converter(tmp_path, arch, tied,
     from sardyne.tokenizer.bpe import BPETokenizer
     ours = BPETokenizer.load(model=tmp_path / "ours.gguf")
     hf = BPETokenizer.load(hf_dir=ck)
-    assert ours.pre == hf.pre == style and ours.eos_ids == hf.eos_ids
+    # a GGUF keeps one end id (the first), so the end ids are those of the reference's own file
+    assert ours.pre == hf.pre == style and ours.eos_ids == BPETokenizer.load(model=tmp_path / "ref.gguf").eos_ids
     for text in ["abc ab a", "a12 cab<|endoftext|>abc<tool> x", " a  abc\nb", "zz\u00e9 12"]:
         assert ours.encode(text) == hf.encode(text), text
         assert ours.decode(ours.encode(text)) == hf.decode(hf.encode(text))
@@ -361,7 +365,8 @@ def test_safetensors_lengths_and_json(tmp_path):
 def shard_checkpoint(ck, out):
     """The checkpoint `ck` split over two shards with a model.safetensors.index.json, in `out`."""
     out.mkdir()
-    (out / "config.json").write_text((ck / "config.json").read_text())
+    for meta in ck.glob("*.json"):
+        (out / meta.name).write_text(meta.read_text())
     st = convert.SafeTensors(ck)
     names = sorted(st.index)
     halves = {"model-00001-of-00002.safetensors": names[::2], "model-00002-of-00002.safetensors": names[1::2]}
