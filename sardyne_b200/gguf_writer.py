@@ -36,14 +36,34 @@ def f32_to_bf16(x: np.ndarray) -> np.ndarray:
     return out
 
 
+DEFAULT_ALIGNMENT = 32
+
+
+def _check_name(what: str, name: str) -> None:
+    """Keys and tensor names: non-empty UTF-8 without NUL (readers refuse anything else)."""
+    if not isinstance(name, str) or not name or "\0" in name:
+        raise ValueError(f"{what} {name!r} is not a non-empty string without NUL")
+    name.encode("utf-8")  # lone surrogates raise UnicodeEncodeError, a ValueError
+
+
 class GGUFWriter:
-    def __init__(self, path, alignment: int = 32):
+    def __init__(self, path, alignment: int = DEFAULT_ALIGNMENT):
+        if not (isinstance(alignment, int) and 0 < alignment <= 1 << 16 and alignment & (alignment - 1) == 0):
+            raise ValueError(f"alignment {alignment} is not a power of two up to 65536")
         self.path = pathlib.Path(path)
         self.alignment = alignment
         self.kv = []        # (key, type, payload bytes)
         self.tensors = []   # (name, ne, type name, bytes)
+        self._keys, self._names = set(), set()
+        if alignment != DEFAULT_ALIGNMENT:
+            self.add("general.alignment", alignment, U32)
 
     def add(self, key: str, value, vtype: int | None = None, arr_type: int | None = None):
+        _check_name("key", key)
+        if key in self._keys:
+            raise ValueError(f"key {key!r} added twice")
+        if isinstance(value, np.generic):
+            value = value.item()  # NumPy scalars as the Python value
         if vtype is None:
             if isinstance(value, bool):
                 vtype = BOOL
@@ -58,15 +78,40 @@ class GGUFWriter:
             else:
                 raise TypeError(f"{key}: unsupported value {type(value)}")
         if vtype == STRING:
+            if not isinstance(value, str):
+                raise TypeError(f"{key}: STRING needs a str")
             payload = _str(value)
         elif vtype == ARRAY:
+            value = [v.item() if isinstance(v, np.generic) else v for v in value]
+            kinds = {type(v) for v in value}
+            if any(isinstance(v, (list, tuple, np.ndarray)) for v in value):
+                raise TypeError(f"{key}: arrays of arrays are not supported")
+            if len(kinds) > 1 and not kinds <= {int, float}:
+                raise TypeError(f"{key}: array elements of different types {sorted(k.__name__ for k in kinds)}")
             if arr_type is None:
-                arr_type = STRING if value and isinstance(value[0], str) else (F32 if value and isinstance(value[0], float) else I32)
-            body = b"".join(_str(v) for v in value) if arr_type == STRING else \
-                b"".join(struct.pack(_SCALAR_FMT[arr_type], v) for v in value)
+                if kinds == {str}:
+                    arr_type = STRING
+                elif kinds == {bool}:
+                    arr_type = BOOL
+                elif float in kinds:
+                    arr_type = F32
+                else:  # integers: int32 when every value fits, else the 64-bit type that holds them
+                    lo, hi = (min(value), max(value)) if value else (0, 0)
+                    arr_type = I32 if -2 ** 31 <= lo and hi < 2 ** 31 else U64 if lo >= 0 else I64
+            try:
+                body = b"".join(_str(v) for v in value) if arr_type == STRING else \
+                    b"".join(struct.pack(_SCALAR_FMT[arr_type], v) for v in value)
+            except struct.error as e:
+                raise ValueError(f"{key}: {e}") from None
             payload = struct.pack("<IQ", arr_type, len(value)) + body
         else:
-            payload = struct.pack(_SCALAR_FMT[vtype], value)
+            if vtype not in _SCALAR_FMT:
+                raise ValueError(f"{key}: unknown value type {vtype}")
+            try:
+                payload = struct.pack(_SCALAR_FMT[vtype], value)
+            except struct.error as e:  # out of the type's range, or not a number
+                raise ValueError(f"{key}: {value!r} does not fit value type {vtype} ({e})") from None
+        self._keys.add(key)
         self.kv.append((key, vtype, payload))
 
     def add_tensor(self, name: str, data: np.ndarray, kind: str = "F32"):
@@ -80,22 +125,35 @@ class GGUFWriter:
             raw = (data if data.dtype == np.uint16 else f32_to_bf16(data)).tobytes()
         else:
             raise ValueError(f"{kind}: use add_raw_tensor for quantized data")
-        self.tensors.append((name, tuple(reversed(data.shape)), kind, raw))
+        self._tensor(name, tuple(reversed(data.shape)), kind, raw)
 
     def add_raw_tensor(self, name: str, ne, kind: str, raw: bytes):
+        if kind not in _BLOCK:
+            raise ValueError(f"{name}: unknown tensor type {kind}")
         block, size = _BLOCK[kind]
         n = int(np.prod(ne))
         if ne[0] % block or len(raw) != n // block * size:
             raise ValueError(f"{name}: {len(raw)} bytes do not match {kind} {tuple(ne)}")
-        self.tensors.append((name, tuple(int(v) for v in ne), kind, bytes(raw)))
+        self._tensor(name, tuple(int(v) for v in ne), kind, bytes(raw))
 
     def add_lazy_tensor(self, name: str, ne, kind: str, produce):
         """A tensor whose bytes `produce()` returns when the file is written (one tensor in
         memory at a time, for multi-GB files)."""
+        if kind not in _BLOCK:
+            raise ValueError(f"{name}: unknown tensor type {kind}")
         block, _ = _BLOCK[kind]
         if ne[0] % block:
             raise ValueError(f"{name}: {tuple(ne)} is not whole {kind} blocks")
-        self.tensors.append((name, tuple(int(v) for v in ne), kind, produce))
+        self._tensor(name, tuple(int(v) for v in ne), kind, produce)
+
+    def _tensor(self, name, ne, kind, raw):
+        _check_name("tensor name", name)
+        if name in self._names:
+            raise ValueError(f"tensor {name!r} added twice")
+        if not ne or len(ne) > 4 or any(v < 0 for v in ne):
+            raise ValueError(f"{name}: dimensions {ne} are not 1 to 4 non-negative sizes")
+        self._names.add(name)
+        self.tensors.append((name, ne, kind, raw))
 
     def _nbytes(self, ne, kind):
         block, size = _BLOCK[kind]

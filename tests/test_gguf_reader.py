@@ -125,3 +125,49 @@ def test_missing_and_truncated(tmp_path):
         p.write_bytes(data[:cut])
         h, err = open_gguf(p)
         assert not h and err
+
+
+def test_writer_refuses_what_readers_reject(tmp_path):
+    """The package's GGUF writer refuses input that would make an unreadable or ambiguous file
+    (the rules of the reference's writer, tests/test_gguf.py:412-437), and widens integer arrays."""
+    with pytest.raises(ValueError):
+        GGUFWriter(tmp_path / "x.gguf", alignment=24)  # not a power of two
+    w = GGUFWriter(tmp_path / "x.gguf")
+    w.add("k", 1)
+    bad = [lambda: w.add("k", 2),                       # key added twice
+           lambda: w.add("a\0b", 1),                    # NUL in a key
+           lambda: w.add("", 1),                        # empty key
+           lambda: w.add("big", 2 ** 64),               # beyond 64 bits
+           lambda: w.add("u8", 256, 0),                 # beyond UINT8
+           lambda: w.add("mix", [1, "a"]),              # mixed array
+           lambda: w.add("nested", [[1, 2], [3]]),      # array of arrays
+           lambda: w.add("obj", object()),
+           lambda: w.add_raw_tensor("q", (32,), "Q8_0", b"\0" * 33),  # Q8_0 holds 34 bytes per 32
+           lambda: w.add_raw_tensor("z", (32,), "Q9_9", b""),         # unknown type
+           lambda: w.add_tensor("n\0", np.ones(4, np.float32))]
+    for fn in bad:
+        with pytest.raises((ValueError, TypeError)):
+            fn()
+    w.add("np_scalar", np.float32(1.5))
+    w.add("wide", [1, 2 ** 33])
+    w.add("neg", [-1, 2 ** 40])
+    w.add_tensor("t", np.ones(4, np.float32))
+    with pytest.raises(ValueError):
+        w.add_tensor("t", np.ones(4, np.float32))       # tensor name added twice
+    lib = capi.lib()
+    err = ctypes.create_string_buffer(256)
+    h = lib.gguf_open(str(w.write()).encode(), err, len(err))
+    assert h, err.value
+    try:
+        kv = {lib.gguf_get_kv(h, i).contents.key.decode(): lib.gguf_get_kv(h, i).contents for i in range(lib.gguf_n_kv(h))}
+        assert (kv["wide"].type, kv["wide"].arr_type, kv["wide"].n) == (9, 10, 2)  # UINT64 array
+        assert (kv["neg"].type, kv["neg"].arr_type) == (9, 11)                    # INT64 array
+        assert kv["np_scalar"].type == 6 and lib.gguf_n_tensors(h) == 1
+    finally:
+        lib.gguf_close(h)
+    w2 = GGUFWriter(tmp_path / "a64.gguf", alignment=64)  # a non-default alignment is recorded
+    w2.add_tensor("t", np.ones(3, np.float32))
+    h = lib.gguf_open(str(w2.write()).encode(), err, len(err))
+    assert h, err.value
+    assert lib.gguf_alignment(h) == 64
+    lib.gguf_close(h)
