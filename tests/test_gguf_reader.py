@@ -171,3 +171,21 @@ def test_writer_refuses_what_readers_reject(tmp_path):
     assert h, err.value
     assert lib.gguf_alignment(h) == 64
     lib.gguf_close(h)
+
+
+def test_writer_failure_leaves_the_existing_file(tmp_path):
+    """A tensor that cannot be produced while the file is written leaves the previous file intact
+    and no temporary file (reference tests/test_gguf.py:440-461)."""
+    path = tmp_path / "m.gguf"
+    w = GGUFWriter(path)
+    w.add_tensor("t", np.arange(8, dtype=np.float32))
+    before = w.write().read_bytes()
+
+    def boom():
+        raise RuntimeError("cannot produce")
+
+    w2 = GGUFWriter(path)
+    w2.add_lazy_tensor("t", (4,), "F32", boom)
+    with pytest.raises(RuntimeError):
+        w2.write()
+    assert path.read_bytes() == before and [p.name for p in tmp_path.iterdir()] == ["m.gguf"]
