@@ -75,8 +75,10 @@ def alg_bytes(fmt, n_out, n_in):
     return weight_bytes(fmt, n_out, n_in) + 4 * n_in + 4 * n_out
 
 
-def make_inputs(seed=0, only=None, formats=FORMATS):
-    """The sweep's matrices; `only` ("Q6_K:151936") keeps one format/row count (profiling runs)."""
+INPUTS_VERSION = 1  # bump when the generated matrices change
+
+
+def _generate_inputs(seed, only, formats):
     from sardyne_b200 import kquant
     rng = np.random.default_rng(seed)
     mats = []
@@ -90,7 +92,39 @@ def make_inputs(seed=0, only=None, formats=FORMATS):
             else:
                 raw = kquant.synth_tensor(fmt, n_out, n_in, rng)
             mats.append((fmt, n_out, n_in, np.frombuffer(raw, np.uint8).reshape(n_out, -1).copy()))
+    return mats
+
+
+def inputs_cache_path(seed=0, only=None, formats=FORMATS) -> pathlib.Path:
+    from sardyne_b200 import synth
+    tag = "-".join(formats) + (f"-{only.replace(':', '_')}" if only else "")
+    return pathlib.Path(synth.model_cache_dir()) / f"sardyne-sweep-v{INPUTS_VERSION}-s{seed}-{tag}.npz"
+
+
+def make_inputs(seed=0, only=None, formats=FORMATS):
+    """The sweep's matrices; `only` ("Q6_K:151936") keeps one format/row count (profiling runs).
+    Quantizing ~0.5 GB takes minutes on the host, so the bytes are kept in the synthetic-model
+    cache directory (written atomically; a cache whose arrays do not have the expected sizes is
+    rebuilt)."""
+    from sardyne_b200 import kquant
     xs = {n_in: np.random.default_rng(1).standard_normal(n_in).astype(np.float32) for _, n_in in SHAPES}
+    wanted = [(fmt, n_out, n_in) for fmt in formats for n_out, n_in in SHAPES if not only or only == f"{fmt}:{n_out}"]
+    path = inputs_cache_path(seed, only, formats)
+    try:
+        with np.load(path) as z:
+            mats = [(fmt, n_out, n_in, z[f"{fmt}_{n_out}_{n_in}"]) for fmt, n_out, n_in in wanted]
+        if all(w.shape == (n_out, n_in // kquant.QK[fmt] * kquant.BLOCK_BYTES[fmt]) for fmt, n_out, n_in, w in mats):
+            return mats, xs
+    except Exception:  # noqa: BLE001 -- absent, truncated or foreign: generated again below
+        pass
+    mats = _generate_inputs(seed, only, formats)
+    tmp = path.with_name(f"{path.name}.{os.getpid()}.tmp")
+    try:
+        with open(tmp, "wb") as f:
+            np.savez(f, **{f"{fmt}_{n_out}_{n_in}": w for fmt, n_out, n_in, w in mats})
+        os.replace(tmp, path)
+    except OSError:  # no room or no permission: run without the cache
+        tmp.unlink(missing_ok=True)
     return mats, xs
 
 

@@ -14,10 +14,11 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 @pytest.mark.skipif(not oracle.ref_available(), reason="reference library not built")
-def test_reference_arm_prints_one_contract_line():
+def test_reference_arm_prints_one_contract_line(tmp_path):
     r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0",
                         "--no-decode"],
-                       cwd=ROOT, capture_output=True, text=True, timeout=600)
+                       cwd=ROOT, capture_output=True, text=True, timeout=600,
+                       env=dict(os.environ, SARDYNE_MODEL_DIR=str(tmp_path)))  # caches stay in the test's directory
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [l for l in r.stdout.splitlines() if l.strip()]
     assert len(lines) == 1, r.stdout
@@ -44,3 +45,26 @@ def test_cpu_baselines_use_the_cpus_this_process_may_run_on():
     import bench
     n = bench.host_cores()
     assert 1 <= n <= len(os.sched_getaffinity(0))
+
+
+def test_sweep_inputs_are_cached_and_rebuilt_when_damaged(tmp_path, monkeypatch):
+    """bench.make_inputs keeps the quantized matrices in the model cache directory: a second call
+    returns the same bytes from the cache, and a truncated cache file is rebuilt."""
+    monkeypatch.setenv("SARDYNE_MODEL_DIR", str(tmp_path))
+    sys.path.insert(0, ROOT)
+    import numpy as np
+
+    import bench
+    monkeypatch.setattr(bench, "SHAPES", [(16, 256), (40, 512)])  # small matrices: the same code
+    first, xs = bench.make_inputs(only="Q4_K:16")
+    path = bench.inputs_cache_path(only="Q4_K:16")
+    assert path.exists() and [p.name for p in tmp_path.iterdir()] == [path.name]
+    again, _ = bench.make_inputs(only="Q4_K:16")
+    assert [m[:3] for m in again] == [m[:3] for m in first] == [("Q4_K", 16, 256)]
+    assert all(np.array_equal(a[3], b[3]) for a, b in zip(first, again))
+    path.write_bytes(path.read_bytes()[:100])
+    rebuilt, _ = bench.make_inputs(only="Q4_K:16")
+    assert np.array_equal(rebuilt[0][3], first[0][3]) and path.stat().st_size > 100
+    full, _ = bench.make_inputs()  # every format and shape, one file each set
+    assert [m[:3] for m in full] == [(f, n, k) for f in bench.FORMATS for n, k in bench.SHAPES]
+    assert all(np.array_equal(a[3], b[3]) for a, b in zip(full, bench.make_inputs()[0]))
